@@ -1,0 +1,358 @@
+// Varlen packed flash attention on tcgen05 for the text backbone: bidirectional, scale 1,
+// inclusive sliding window (radius `window`) or global, block-diagonal over packed sequences.
+//
+// Replaces the reference's bf16 flash kernels `flash_attn_d256_packed_bb` and `flash_attn_d512_bb`
+// (kernels_sm80.cu:236-416, :474-684; mma.sync) and their launchers (src/gpu/mod.rs:1217-1241,
+// :1547-1599); semantics of src/ops.rs:364-444.
+//
+// One CTA per (query tile, K/V head, output half). A query tile packs the G = nh / nkv query heads
+// that share a K/V head into the 128 MMA rows: row r = token (r / G), head (g * G + r % G), so
+// each K/V tile loaded serves all G heads. Sliding layers (G = 2) take 64 tokens per tile, global
+// layers (G = 4) 32. The output is produced 256 channels at a time: head_dim 512 runs two CTAs per
+// tile, each computing the full S = Q K^T and its half of O (TMEM holds 512 fp32 columns, too few
+// for S and a 512-wide O together).
+//
+//   warp 0      TMA: Q once (head_dim / 64 swizzled [128 x 64] boxes), then per 64-key tile the
+//               K chunks (ring of 4 x [64 x 64]) and the V tile [64 keys x 256] (VB buffers)
+//   warp 1      TMEM owner; lane 0 issues S = Q K^T (M 128, N 64, K 16) into S[j % 2] and
+//               O += P V (M 128, N 256, K 16, V read MN-major) and commits
+//   warps 2..5  softmax: thread = row; reads S from TMEM, masks, online max / sum in the log2
+//               domain, writes P (bf16, swizzled K-major) to P[j % 2]; O is rescaled in TMEM only
+//               when a row max grows by more than 2^8 (else the stale max is kept, which is exact);
+//               at the end O / l is stored as bf16.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace eg2 {
+
+constexpr int ATT_THREADS = 192;
+constexpr int ATT_BN = 64;       // keys per tile
+constexpr int ATT_DV = 256;      // output channels per CTA
+constexpr int ATT_KST = 4;       // K chunk ring
+constexpr float ATT_RESCALE_LOG2 = 8.f;
+
+template <int DQK, int VB>
+struct AttCfg {
+    static constexpr int Q_BYTES = (DQK / 64) * 128 * 128;
+    static constexpr int K_SLOT = ATT_BN * 128;          // [64 keys x 64 ch] bf16
+    static constexpr int V_BYTES = (ATT_DV / 64) * ATT_BN * 128;
+    static constexpr int P_BYTES = 128 * ATT_BN * 2;     // [128 rows x 64 keys] bf16
+    static constexpr int OFF_K = Q_BYTES;
+    static constexpr int OFF_V = OFF_K + ATT_KST * K_SLOT;
+    static constexpr int OFF_P = OFF_V + VB * V_BYTES;
+    static constexpr int OFF_BAR = OFF_P + 2 * P_BYTES;
+    static constexpr int SMEM = 1024 + OFF_BAR + 256;
+};
+
+struct AttParams {
+    const AttnTile* tiles;
+    bf16_t* out;
+    int nh, nkv, hd, window, G, tq, nsplit;
+};
+
+template <int DQK, int VB>
+__global__ void __launch_bounds__(ATT_THREADS, 1)
+    attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                        const __grid_constant__ CUtensorMap tmV, AttParams prm) {
+    using Cfg = AttCfg<DQK, VB>;
+    constexpr int QCH = DQK / 64;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::OFF_BAR);
+    uint64_t* q_full = bars;
+    uint64_t* k_full = bars + 1;
+    uint64_t* k_empty = k_full + ATT_KST;
+    uint64_t* v_full = k_empty + ATT_KST;
+    uint64_t* v_empty = v_full + VB;
+    uint64_t* s_full = v_empty + VB;
+    uint64_t* s_empty = s_full + 2;
+    uint64_t* p_full = s_empty + 2;
+    uint64_t* pv_done = p_full + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pv_done + 2);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int tile_idx = blockIdx.x / (prm.nkv * prm.nsplit);
+    const int rem = blockIdx.x % (prm.nkv * prm.nsplit);
+    const int g = rem / prm.nsplit, dsplit = rem % prm.nsplit;
+    const AttnTile tile = prm.tiles[tile_idx];
+    const int G = prm.G, W = prm.window;
+    const int q_last = min(tile.q0 + prm.tq, tile.len) - 1;
+    const int k_lo = (W >= 0) ? max(0, tile.q0 - W) : 0;
+    const int k_hi = (W >= 0) ? min(tile.len, q_last + W + 1) : tile.len;
+    const int n_kt = tile.len > 0 ? (k_hi - k_lo + ATT_BN - 1) / ATT_BN : 0;
+
+    if (threadIdx.x == 0) {
+        mbar_init(q_full, 1);
+        for (int s = 0; s < ATT_KST; s++) {
+            mbar_init(&k_full[s], 1);
+            mbar_init(&k_empty[s], 1);
+        }
+        for (int s = 0; s < VB; s++) {
+            mbar_init(&v_full[s], 1);
+            mbar_init(&v_empty[s], 1);
+        }
+        for (int s = 0; s < 2; s++) {
+            mbar_init(&s_full[s], 1);
+            mbar_init(&s_empty[s], 128);
+            mbar_init(&p_full[s], 128);
+            mbar_init(&pv_done[s], 1);
+        }
+        *abort_flag = 0;
+        fence_mbarrier_init();
+    }
+    if (warp == 1) tmem_alloc(tmem_slot, 512);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const uint32_t t_s = tmem;          // S[0] cols [0, 64), S[1] cols [64, 128)
+    const uint32_t t_o = tmem + 256;    // O cols [256, 512)
+
+    if (n_kt == 0) goto done;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // Q: the G heads of K/V head g for tokens [q0, q0 + tq), 128 rows of 64 channels per box.
+            mbar_arrive_expect_tx(q_full, Cfg::Q_BYTES);
+            for (int c = 0; c < QCH; c++)
+                tma_load_3d(smem + c * 128 * 128, &tmQ, q_full, c * 64, g * G, tile.row0 + tile.q0);
+            int ks = 0, vs = 0;
+            uint32_t kph = 0, vph = 0;
+            for (int j = 0; j < n_kt; j++) {
+                const int key0 = tile.row0 + k_lo + j * ATT_BN;
+                for (int c = 0; c < QCH; c++) {
+                    if (!mbar_wait(&k_empty[ks], kph ^ 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) goto done;
+                    mbar_arrive_expect_tx(&k_full[ks], Cfg::K_SLOT);
+                    tma_load_3d(smem + Cfg::OFF_K + ks * Cfg::K_SLOT, &tmK, &k_full[ks], c * 64, g, key0);
+                    if (++ks == ATT_KST) {
+                        ks = 0;
+                        kph ^= 1;
+                    }
+                }
+                if (!mbar_wait(&v_empty[vs], vph ^ 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) goto done;
+                mbar_arrive_expect_tx(&v_full[vs], Cfg::V_BYTES);
+                for (int c = 0; c < ATT_DV / 64; c++)
+                    tma_load_3d(smem + Cfg::OFF_V + vs * Cfg::V_BYTES + c * ATT_BN * 128, &tmV, &v_full[vs],
+                                dsplit * ATT_DV + c * 64, g, key0);
+                if (++vs == VB) {
+                    vs = 0;
+                    vph ^= 1;
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            constexpr uint32_t idesc_s = umma_idesc(128, ATT_BN, 1);
+            constexpr uint32_t idesc_o = umma_idesc(128, ATT_DV, 1, /*b_mn_major=*/true);
+            const uint32_t sq = smem_u32(smem);
+            int ks = 0, vs = 0;
+            uint32_t kph = 0, vph = 0;
+            if (!mbar_wait(q_full, 0, EG2_DEV_TIMEOUT_ATTN, abort_flag)) goto done;
+            // S[j % 2] = Q K_j^T over head_dim in 64-channel chunks.
+            auto issue_qk = [&](int j) -> bool {
+                const int sb = j & 1;
+                if (!mbar_wait(&s_empty[sb], ((j >> 1) & 1) ^ 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) return false;
+                tc_fence_after();
+                for (int c = 0; c < QCH; c++) {
+                    if (!mbar_wait(&k_full[ks], kph, EG2_DEV_TIMEOUT_ATTN, abort_flag)) return false;
+                    tc_fence_after();
+                    const uint32_t sk = smem_u32(smem + Cfg::OFF_K + ks * Cfg::K_SLOT);
+#pragma unroll
+                    for (int kk = 0; kk < 4; kk++)
+                        mma_bf16(t_s + sb * ATT_BN, umma_desc_sw128(sq + c * 128 * 128 + kk * 32, 16, 1024),
+                                 umma_desc_sw128(sk + kk * 32, 16, 1024), idesc_s, (c | kk) != 0);
+                    mma_commit(&k_empty[ks]);
+                    if (++ks == ATT_KST) {
+                        ks = 0;
+                        kph ^= 1;
+                    }
+                }
+                mma_commit(&s_full[sb]);
+                return true;
+            };
+            if (!issue_qk(0)) goto done;
+            for (int j = 0; j < n_kt; j++) {
+                if (j + 1 < n_kt && !issue_qk(j + 1)) goto done;
+                const int pb = j & 1;
+                if (!mbar_wait(&p_full[pb], (j >> 1) & 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) goto done;
+                if (!mbar_wait(&v_full[vs], vph, EG2_DEV_TIMEOUT_ATTN, abort_flag)) goto done;
+                tc_fence_after();
+                const uint32_t sp = smem_u32(smem + Cfg::OFF_P + pb * Cfg::P_BYTES);
+                const uint32_t sv = smem_u32(smem + Cfg::OFF_V + vs * Cfg::V_BYTES);
+#pragma unroll
+                for (int kk = 0; kk < ATT_BN / 16; kk++)
+                    mma_bf16(t_o, umma_desc_sw128(sp + kk * 32, 16, 1024),
+                             umma_desc_sw128(sv + kk * 2048, ATT_BN * 128, 1024), idesc_o, (j | kk) != 0);
+                mma_commit(&v_empty[vs]);
+                mma_commit(&pv_done[pb]);
+                if (++vs == VB) {
+                    vs = 0;
+                    vph ^= 1;
+                }
+            }
+        }
+    } else {
+        // Softmax / epilogue warps: row r = 32 * (warp % 4) + lane of the 128-row tile.
+        const int e = warp & 3;
+        const int r = 32 * e + lane;
+        const int tok = tile.q0 + r / G;  // position within the sequence
+        const bool row_valid = tok < tile.len;
+        const uint32_t lane_off = (uint32_t)(32 * e) << 16;
+        const float LOG2E = 1.4426950408889634f;
+        float m_used = -INFINITY, l = 0.f;
+        for (int j = 0; j < n_kt; j++) {
+            const int sb = j & 1;
+            if (!mbar_wait(&s_full[sb], (j >> 1) & 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) break;
+            tc_fence_after();
+            uint32_t s0[32], s1[32];
+            tmem_ld32(t_s + sb * ATT_BN + lane_off, s0);
+            tmem_ld32(t_s + sb * ATT_BN + 32 + lane_off, s1);
+            tmem_ld_wait();
+            tc_fence_before();
+            mbar_arrive(&s_empty[sb]);
+            const int kbase = k_lo + j * ATT_BN;  // key position of column 0 within the sequence
+            float sv[64];
+            float mt = -INFINITY;
+#pragma unroll
+            for (int c = 0; c < 64; c++) {
+                const int kp = kbase + c;
+                bool ok = kp < tile.len;
+                if (W >= 0 && row_valid) ok = ok && (kp >= tok - W) && (kp <= tok + W);
+                const float x = __uint_as_float(c < 32 ? s0[c] : s1[c - 32]) * LOG2E;
+                sv[c] = ok ? x : -INFINITY;
+                mt = fmaxf(mt, sv[c]);
+            }
+            // Decide the reference max: keep the stale one unless the new max exceeds it by 2^8.
+            float factor = 1.f;
+            bool need = false;
+            if (mt > m_used) {
+                if (m_used == -INFINITY) {
+                    m_used = mt;  // O rows so far are exactly 0 (all earlier P were 0)
+                } else if (mt - m_used > ATT_RESCALE_LOG2) {
+                    factor = exp2f(m_used - mt);
+                    m_used = mt;
+                    need = true;
+                }
+            }
+            // P buffer reuse: PV(j - 2) must be done. Rescaling O also needs PV(j - 1) done.
+            if (j >= 2 && !mbar_wait(&pv_done[sb], ((j - 2) >> 1) & 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) break;
+            const bool warp_need = __any_sync(0xffffffffu, need);
+            if (warp_need && j >= 1) {
+                if (!mbar_wait(&pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) break;
+                tc_fence_after();
+#pragma unroll 1
+                for (int c = 0; c < ATT_DV / 32; c++) {
+                    uint32_t o[32];
+                    tmem_ld32(t_o + c * 32 + lane_off, o);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int q = 0; q < 32; q++) o[q] = __float_as_uint(__uint_as_float(o[q]) * factor);
+                    tmem_st32(t_o + c * 32 + lane_off, o);
+                }
+                tmem_st_wait();
+            }
+            l *= factor;
+            // p = 2^(s - m_used), summed in f32; stored bf16 into the swizzled K-major P tile.
+            uint8_t* prow = smem + Cfg::OFF_P + sb * Cfg::P_BYTES + r * 128;
+            const bool any = m_used != -INFINITY;
+#pragma unroll
+            for (int ch = 0; ch < 8; ch++) {
+                float p8[8];
+#pragma unroll
+                for (int q = 0; q < 8; q++) {
+                    const float x = sv[ch * 8 + q];
+                    p8[q] = (any && x != -INFINITY) ? exp2f(x - m_used) : 0.f;
+                    l += p8[q];
+                }
+                uint4 pk = make_uint4(pack_bf16x2(p8[0], p8[1]), pack_bf16x2(p8[2], p8[3]), pack_bf16x2(p8[4], p8[5]),
+                                      pack_bf16x2(p8[6], p8[7]));
+                *reinterpret_cast<uint4*>(prow + ((ch ^ (r & 7)) << 4)) = pk;
+            }
+            fence_proxy_async();
+            tc_fence_before();
+            mbar_arrive(&p_full[sb]);
+        }
+        // Epilogue: O / l for this row's 256 channels.
+        if (!*abort_flag && mbar_wait(&pv_done[(n_kt - 1) & 1], ((n_kt - 1) >> 1) & 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) {
+            tc_fence_after();
+            const float inv = (l > 0.f) ? 1.f / l : 0.f;
+            const int head = g * G + r % G;
+            bf16_t* orow = prm.out + ((long)(tile.row0 + tok) * prm.nh + head) * prm.hd + dsplit * ATT_DV;
+#pragma unroll 1
+            for (int c = 0; c < ATT_DV / 32; c++) {
+                uint32_t o[32];
+                tmem_ld32(t_o + c * 32 + lane_off, o);
+                tmem_ld_wait();
+                if (row_valid) {
+                    uint4* d = reinterpret_cast<uint4*>(orow + c * 32);
+#pragma unroll
+                    for (int q = 0; q < 4; q++)
+                        d[q] = make_uint4(pack_bf16x2(__uint_as_float(o[8 * q + 0]) * inv, __uint_as_float(o[8 * q + 1]) * inv),
+                                          pack_bf16x2(__uint_as_float(o[8 * q + 2]) * inv, __uint_as_float(o[8 * q + 3]) * inv),
+                                          pack_bf16x2(__uint_as_float(o[8 * q + 4]) * inv, __uint_as_float(o[8 * q + 5]) * inv),
+                                          pack_bf16x2(__uint_as_float(o[8 * q + 6]) * inv, __uint_as_float(o[8 * q + 7]) * inv));
+                }
+            }
+        }
+    }
+done:
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 512);
+    }
+}
+
+int attention_tc_tile_tokens(int nh, int nkv) {
+    if (nkv <= 0 || nh % nkv) return 0;
+    const int G = nh / nkv;
+    if (128 % G) return 0;
+    return 128 / G;
+}
+
+template <int DQK, int VB>
+static int launch_att(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, const AttParams& prm,
+                      int n_tiles, cudaStream_t s) {
+    using Cfg = AttCfg<DQK, VB>;
+    auto kern = attention_tc_kernel<DQK, VB>;
+    static bool attr = false;
+    if (!attr) {
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM) != cudaSuccess) return -3;
+        attr = true;
+    }
+    const long grid = (long)n_tiles * prm.nkv * prm.nsplit;
+    if (grid <= 0) return 0;
+    kern<<<(unsigned)grid, ATT_THREADS, Cfg::SMEM, s>>>(tq, tk, tv, prm);
+    return cudaGetLastError() == cudaSuccess ? 0 : -3;
+}
+
+int attention_tc(const bf16_t* q, const bf16_t* k, const bf16_t* v, bf16_t* out, long rows, const AttnTile* tiles,
+                 int n_tiles, int nh, int nkv, int hd, int window, cudaStream_t s) {
+    if (rows <= 0 || n_tiles <= 0) return 0;
+    const int tq = attention_tc_tile_tokens(nh, nkv);
+    if (!tq || (hd != 256 && hd != 512)) return -1;
+    const int G = nh / nkv;
+    CUtensorMap mq, mk, mv;
+    const CUtensorMapDataType dt = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+    // q [rows, nh, hd]: box (64 ch, G heads, tq tokens) -> 128 rows of 128 B.
+    if (make_tmap_3d(&mq, dt, q, hd, nh, rows, (uint64_t)hd * 2, (uint64_t)nh * hd * 2, 64, G, tq) ||
+        make_tmap_3d(&mk, dt, k, hd, nkv, rows, (uint64_t)hd * 2, (uint64_t)nkv * hd * 2, 64, 1, ATT_BN) ||
+        make_tmap_3d(&mv, dt, v, hd, nkv, rows, (uint64_t)hd * 2, (uint64_t)nkv * hd * 2, 64, 1, ATT_BN))
+        return -1;
+    AttParams prm;
+    prm.tiles = tiles;
+    prm.out = out;
+    prm.nh = nh;
+    prm.nkv = nkv;
+    prm.hd = hd;
+    prm.window = window;
+    prm.G = G;
+    prm.tq = tq;
+    prm.nsplit = hd / ATT_DV;
+    if (hd == 256) return launch_att<256, 2>(mq, mk, mv, prm, n_tiles, s);
+    return launch_att<512, 1>(mq, mk, mv, prm, n_tiles, s);
+}
+
+}  // namespace eg2

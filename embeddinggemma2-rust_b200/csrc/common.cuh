@@ -1,0 +1,245 @@
+// Shared device helpers for the sm_100a kernels: bf16 conversion, mbarriers with bounded waits,
+// TMA tile loads, tcgen05 (TMEM allocation, MMA issue, commit, TMEM loads) and UMMA descriptors.
+//
+// Every wait on an mbarrier is bounded by wall time (%globaltimer). A wait that runs out records
+// an error code in eg2_dev_status (read back by the host after the launch) and returns false, so
+// a kernel with a broken pipeline ends with an error status instead of hanging the GPU.
+#pragma once
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+typedef uint16_t bf16_t;
+
+#define EG2_DEV __device__ __forceinline__
+
+// Device-side status word: 0 = fine, otherwise the first error code recorded by any kernel.
+__device__ int eg2_dev_status = 0;
+
+enum Eg2DevError : int {
+    EG2_DEV_OK = 0,
+    EG2_DEV_TIMEOUT_GEMM = 1,
+    EG2_DEV_TIMEOUT_ATTN = 2,
+    EG2_DEV_BAD_ARGS = 3,
+};
+
+// Upper bound of any single wait: 2 s. A healthy pipeline waits microseconds.
+#define EG2_WAIT_LIMIT_NS 2000000000ull
+
+EG2_DEV void eg2_record_error(int code) { atomicCAS(&eg2_dev_status, 0, code); }
+
+// ---------------------------------------------------------------------------------------------
+// bf16
+// ---------------------------------------------------------------------------------------------
+EG2_DEV float bf16_to_f32(bf16_t b) { return __uint_as_float(((uint32_t)b) << 16); }
+EG2_DEV bf16_t f32_to_bf16(float f) { return __bfloat16_as_ushort(__float2bfloat16_rn(f)); }
+EG2_DEV uint32_t pack_bf16x2(float lo, float hi) {
+    return (uint32_t)f32_to_bf16(lo) | ((uint32_t)f32_to_bf16(hi) << 16);
+}
+
+// GELU with the tanh approximation (the reference's gelu_tanh, constants as written there).
+EG2_DEV float gelu_tanh_f(float x) {
+    const float beta = 0.79788456f, kappa = 0.044715f;
+    float inner = beta * (x + kappa * x * x * x);
+    return 0.5f * x * (1.f + tanhf(inner));
+}
+
+// Load / store one element of f32 or bf16 storage as f32.
+template <typename T>
+EG2_DEV float ldf(const T* p, long i);
+template <>
+EG2_DEV float ldf<float>(const float* p, long i) {
+    return p[i];
+}
+template <>
+EG2_DEV float ldf<bf16_t>(const bf16_t* p, long i) {
+    return bf16_to_f32(p[i]);
+}
+template <typename T>
+EG2_DEV void stf(T* p, long i, float v);
+template <>
+EG2_DEV void stf<float>(float* p, long i, float v) {
+    p[i] = v;
+}
+template <>
+EG2_DEV void stf<bf16_t>(bf16_t* p, long i, float v) {
+    p[i] = f32_to_bf16(v);
+}
+
+EG2_DEV float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+EG2_DEV uint64_t globaltimer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+EG2_DEV uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+// ---------------------------------------------------------------------------------------------
+// mbarrier
+// ---------------------------------------------------------------------------------------------
+EG2_DEV void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+EG2_DEV void fence_mbarrier_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+EG2_DEV void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+EG2_DEV void mbar_arrive(uint64_t* bar) {
+    asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(smem_u32(bar)) : "memory");
+}
+EG2_DEV void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}" ::"r"(smem_u32(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+EG2_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Bounded wait for the phase with the given parity to complete. Returns false (and records
+// `code`) if it does not complete within EG2_WAIT_LIMIT_NS, or if `abort` is already set.
+EG2_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, int code, volatile int* abort) {
+    if (mbar_try_wait(bar, parity)) return true;
+    uint64_t t0 = globaltimer_ns();
+    for (uint32_t it = 0;; ++it) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((it & 255u) == 255u) {
+            if (abort && *abort) return false;
+            // Another CTA already gave up: stop waiting too, so a broken launch ends in ~2 s.
+            if (*(volatile int*)&eg2_dev_status != 0) {
+                if (abort) *abort = 1;
+                return false;
+            }
+            if (globaltimer_ns() - t0 > EG2_WAIT_LIMIT_NS) {
+                eg2_record_error(code);
+                if (abort) *abort = 1;
+                return false;
+            }
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------------------------
+// TMA (tiled tensor loads into this CTA's shared memory; no cluster multicast anywhere)
+// ---------------------------------------------------------------------------------------------
+EG2_DEV void tma_prefetch_desc(const CUtensorMap* m) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");
+}
+EG2_DEV void tma_load_2d(void* dst, const CUtensorMap* m, uint64_t* bar, int x, int y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+            smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(m)), "r"(smem_u32(bar)), "r"(x), "r"(y)
+        : "memory");
+}
+EG2_DEV void tma_load_3d(void* dst, const CUtensorMap* m, uint64_t* bar, int x, int y, int z) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(
+            smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(m)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
+        : "memory");
+}
+
+// ---------------------------------------------------------------------------------------------
+// tcgen05
+// ---------------------------------------------------------------------------------------------
+// Allocate `ncols` TMEM columns (power of two >= 32); the whole warp executes this.
+EG2_DEV void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)), "r"(ncols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::);
+}
+EG2_DEV void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols));
+}
+EG2_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+EG2_DEV void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// D[tmem] (+)= A[smem] * B[smem], kind::f16 (bf16 inputs here), fp32 accumulation.
+EG2_DEV void mma_bf16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+// Same with TF32 inputs (f32 data in shared memory).
+EG2_DEV void mma_tf32(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+template <typename TIn>
+EG2_DEV void mma_bf16_or_tf32(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate);
+template <>
+EG2_DEV void mma_bf16_or_tf32<bf16_t>(uint32_t d, uint64_t a, uint64_t b, uint32_t i, uint32_t acc) {
+    mma_bf16(d, a, b, i, acc);
+}
+template <>
+EG2_DEV void mma_bf16_or_tf32<float>(uint32_t d, uint64_t a, uint64_t b, uint32_t i, uint32_t acc) {
+    mma_tf32(d, a, b, i, acc);
+}
+// Arrive on `bar` once every MMA issued so far by this thread has completed.
+EG2_DEV void mma_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+// 32 lanes x 32 consecutive 32-bit columns: thread i of the warp gets lane (base lane + i).
+EG2_DEV void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+          "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+          "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+}
+EG2_DEV void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+        "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+        "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),
+        "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
+        "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31]));
+}
+EG2_DEV void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+EG2_DEV void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// ---------------------------------------------------------------------------------------------
+// UMMA descriptors
+// ---------------------------------------------------------------------------------------------
+// Shared-memory matrix descriptor for a tile stored with the 128-byte swizzle (rows of 128 B,
+// 8-row / 1024-byte swizzle atoms, tile base 1024-byte aligned).
+//   K-major operand: lbo unused (1), sbo = 1024 B between 8-row groups.
+//   MN-major operand: lbo = byte stride between 64-element (128 B) chunks along M/N,
+//                     sbo = 1024 B between 8-row groups along K.
+EG2_DEV uint64_t umma_desc_sw128(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr & 0x3FFFFu) >> 4);
+    d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16;
+    d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32;
+    d |= (uint64_t)1 << 46;  // descriptor version for sm_100
+    d |= (uint64_t)2 << 61;  // 128-byte swizzle
+    return d;
+}
+
+// Instruction descriptor: D f32, A/B format (1 = bf16, 2 = tf32), both K-major unless b_mn.
+__host__ __device__ constexpr uint32_t umma_idesc(int M, int N, uint32_t ab_format, bool b_mn_major = false) {
+    return (1u << 4) | (ab_format << 7) | (ab_format << 10) | ((b_mn_major ? 1u : 0u) << 16) |
+           ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}

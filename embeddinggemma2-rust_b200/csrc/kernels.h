@@ -1,0 +1,91 @@
+// Internal host-side interface of the kernels (not part of the C ABI; see include/eg2.h for that).
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace eg2 {
+
+typedef uint16_t bf16_t;
+
+enum GemmKind : int { GEMM_BF16 = 0, GEMM_TF32 = 1, GEMM_F32 = 2 };
+
+enum EpiMode : int {
+    EPI_STORE = 0,     // out = acc * scale (bf16 or f32)
+    EPI_GELU_GU = 1,   // weights interleaved in 128-row gate / up halves per 256-row block: out = gelu(g) * u
+    EPI_PLE_GATE = 2,  // out = gelu(acc) * aux[row * aux_ld + aux_off + col]
+};
+
+struct GemmEpilogue {
+    int mode = EPI_STORE;
+    int out_f32 = 0;          // EPI_STORE with bf16 inputs: write f32 instead of bf16
+    void* out = nullptr;      // [M, ldo] (EPI_GELU_GU: N/2 valid columns)
+    long ldo = 0;
+    const float* aux = nullptr;
+    long aux_ld = 0;
+    int aux_off = 0;
+    float scale = 1.f;
+};
+
+// Number of SMs of the current device (cached per device).
+int num_sms();
+
+// 2-D K-major tensor map with 128-byte swizzle: `inner` elements per row (the K extent),
+// `outer` rows, `row_bytes` between rows; box = box_inner x box_outer.
+int make_tmap_2d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t inner, uint64_t outer,
+                 uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer);
+// 3-D variant: dims (d0, d1, d2) with byte strides s1 (dim 1) and s2 (dim 2); box (b0, b1, b2).
+int make_tmap_3d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t d0, uint64_t d1, uint64_t d2,
+                 uint64_t s1, uint64_t s2, uint32_t b0, uint32_t b1, uint32_t b2);
+
+// C = A . W^T on tcgen05 (bf16 or tf32 inputs). N must be a multiple of 256, K of 64 (bf16) / 32 (tf32).
+int gemm_tc(GemmKind kind, const void* A, long lda, const void* W, long ldw, int M, int N, int K,
+            const GemmEpilogue& epi, cudaStream_t s);
+// f32 CUDA-core GEMM (the float32 precision path): out f32 [M, ldo] = scale * A . W^T.
+int gemm_f32(const float* A, long lda, const float* W, long ldw, float* out, long ldo, int M, int N, int K, float scale,
+             cudaStream_t s);
+
+// ---- row kernels (rowops.cu) ----
+template <typename TO>
+int rms_norm_rows(const float* x, TO* out, const float* w, long rows, int dim, float eps, float pre, cudaStream_t s);
+int rms_norm_inplace(float* x, const float* w, long rows, int dim, float eps, float pre, cudaStream_t s);
+// h = (h + rmsnorm(o) * w1) * scalar; then optionally t = rmsnorm(h) * w2 (w2 == nullptr: t = h copy).
+template <typename TI, typename TT>
+int add_norm(float* h, const TI* o, const float* w1, TT* t, const float* w2, long rows, int dim, float eps,
+             float scalar, cudaStream_t s);
+// Per-head RMSNorm (q, k weighted; v not) and RoPE on q and k, from the fused projection output
+// qkv[row, (nh + 2 nkv) * hd]. cs/sn: [positions, rope_w] tables; part = rotation width (hd or hd / 2).
+template <typename TI, typename TO>
+int qkv_post(const TI* qkv, TO* q, TO* k, TO* v, const float* wq, const float* wk, const float* cs, const float* sn,
+             int rope_w, const int* pos, long rows, int nh, int nkv, int hd, int part, float eps, cudaStream_t s);
+template <typename TI, typename TO>
+int gelu_gu(const TI* gu, TO* out, long rows, int ff, cudaStream_t s);
+template <typename TI, typename TO>
+int ple_gate(const TI* g, TO* out, const float* ple, long rows, int p, int n_layers, int layer, cudaStream_t s);
+// dims_dev: device array of n_dims cut widths (the first is normally dim itself); out row stride out_stride.
+int pool_rows(const float* x, const int* seq_start, const int* seq_len, int n_seq, int dim, const int* dims_dev,
+              int n_dims, int out_stride, float* out, cudaStream_t s);
+int embed_gather(const bf16_t* table, long vocab, int h, const uint32_t* ids, long n, float scale, float* out,
+                 int* bad, cudaStream_t s);
+template <typename TO>
+int cast_rows(const float* x, TO* out, long n, float mul, float add, cudaStream_t s);
+int widen_bf16(const bf16_t* x, float* out, long n, cudaStream_t s);
+int vision_add_positions(float* h, const float* table, const int* pos, long n, int hdim, int pe, cudaStream_t s);
+int vision_pool(const float* x, float* out, int gh, int gw, int hdim, int k, float root, cudaStream_t s);
+
+// ---- attention ----
+// Tile list for the tensor-core kernel: one entry per (sequence, query tile): {row0, len, q0}.
+struct AttnTile {
+    int row0, len, q0;
+};
+// Tensor-core flash attention, bf16 q/k/v/out, GQA-packed query tiles (attention_tc.cu).
+int attention_tc(const bf16_t* q, const bf16_t* k, const bf16_t* v, bf16_t* out, long rows, const AttnTile* tiles,
+                 int n_tiles, int nh, int nkv, int hd, int window, cudaStream_t s);
+// Query tokens per tile of attention_tc for a head configuration.
+int attention_tc_tile_tokens(int nh, int nkv);
+// CUDA-core attention (f32 arithmetic; bf16 or f32 storage), one warp per (row, head).
+template <typename T>
+int attention_simt(const T* q, const T* k, const T* v, T* out, const int* seq_start, const int* seq_len, long rows,
+                   int nh, int nkv, int hd, int window, cudaStream_t s);
+
+}  // namespace eg2

@@ -1,0 +1,385 @@
+// Row-wise and elementwise kernels of the forward pass. All arithmetic is f32; storage is f32 or
+// bf16 as the template parameters say. HBM-bound: one warp per row (dim 512 or 768 here), 16-byte
+// vector loads, no shared-memory staging except where a row's elements are exchanged (RoPE).
+//
+// Reference semantics (paths inside the reference project):
+//   rms_norm_rows   src/ops.rs:211-238 (`rms_norm`), with the PLE pre-scale of src/text.rs:147-149
+//   add_norm        src/text.rs:203-230 (post-norm + residual (+ layer_scalar), then the next pre-norm);
+//                   GPU counterpart kernels.cu:131-172 (`add_norm_row`)
+//   qkv_post        src/text.rs:171-175, src/vision.rs:241-245, src/ops.rs:319-338;
+//                   GPU counterpart kernels.cu:183-237
+//   gelu_gu         src/text.rs:210-212; kernels.cu:239-246
+//   ple_gate        src/text.rs:218-224; kernels.cu:294-299
+//   pool_rows       src/model.rs:530-535 + :677-688 (mean and L2 in f64, Matryoshka cuts)
+//   embed_gather    src/text.rs:53-64
+//   vision_*        src/vision.rs:73-89, :140-163; kernels.cu:249-282
+#include "common.cuh"
+#include "kernels.h"
+
+namespace eg2 {
+
+// Load 16 consecutive-in-stride elements of a 512-wide row: element (lane * 4 + 128 * j + c).
+template <typename T>
+EG2_DEV void load_row(const T* r, int dim, float* v) {
+    for (int j = 0; j < dim / 128; j++)
+#pragma unroll
+        for (int c = 0; c < 4; c++) v[4 * j + c] = ldf(r, (long)(threadIdx.x & 31) * 4 + 128 * j + c);
+}
+
+constexpr int ROW_MAX_VALS = 24;  // dims up to 768
+
+// ---------------------------------------------------------------------------------------------
+template <typename TO>
+__global__ void rms_norm_kernel(const float* __restrict__ x, TO* __restrict__ out, const float* __restrict__ w, long rows,
+                                int dim, float eps, float pre) {
+    long row = (long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (row >= rows) return;
+    const int lane = threadIdx.x & 31;
+    const float* r = x + row * dim;
+    float v[ROW_MAX_VALS];
+    const int nj = dim / 128;
+    float ss = 0.f;
+    for (int j = 0; j < nj; j++) {
+        float4 a = *reinterpret_cast<const float4*>(r + lane * 4 + 128 * j);
+        v[4 * j + 0] = a.x * pre;
+        v[4 * j + 1] = a.y * pre;
+        v[4 * j + 2] = a.z * pre;
+        v[4 * j + 3] = a.w * pre;
+#pragma unroll
+        for (int c = 0; c < 4; c++) ss = fmaf(v[4 * j + c], v[4 * j + c], ss);
+    }
+    ss = warp_sum(ss);
+    const float inv = 1.0f / sqrtf(ss / (float)dim + eps);
+    TO* o = out + row * dim;
+    for (int j = 0; j < nj; j++)
+#pragma unroll
+        for (int c = 0; c < 4; c++) {
+            const int col = lane * 4 + 128 * j + c;
+            float n = v[4 * j + c] * inv;
+            if (w) n *= w[col];
+            stf(o, col, n);
+        }
+}
+
+template <typename TO>
+int rms_norm_rows(const float* x, TO* out, const float* w, long rows, int dim, float eps, float pre, cudaStream_t s) {
+    if (rows <= 0) return 0;
+    if (dim % 128 || dim > 128 * (ROW_MAX_VALS / 4)) return -1;
+    const int wpb = 8;
+    rms_norm_kernel<TO><<<(unsigned)((rows + wpb - 1) / wpb), 32 * wpb, 0, s>>>(x, out, w, rows, dim, eps, pre);
+    return cudaGetLastError() == cudaSuccess ? 0 : -3;
+}
+template int rms_norm_rows<float>(const float*, float*, const float*, long, int, float, float, cudaStream_t);
+template int rms_norm_rows<bf16_t>(const float*, bf16_t*, const float*, long, int, float, float, cudaStream_t);
+
+int rms_norm_inplace(float* x, const float* w, long rows, int dim, float eps, float pre, cudaStream_t s) {
+    return rms_norm_rows<float>(x, x, w, rows, dim, eps, pre, s);
+}
+
+// ---------------------------------------------------------------------------------------------
+template <typename TI, typename TT>
+__global__ void add_norm_kernel(float* __restrict__ h, const TI* __restrict__ o, const float* __restrict__ w1,
+                                TT* __restrict__ t, const float* __restrict__ w2, long rows, int dim, float eps,
+                                float scalar) {
+    long row = (long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (row >= rows) return;
+    const int lane = threadIdx.x & 31;
+    const int nj = dim / 128;
+    float v[ROW_MAX_VALS];
+    load_row(o + row * dim, dim, v);
+    float ss = 0.f;
+    for (int i = 0; i < 4 * nj; i++) ss = fmaf(v[i], v[i], ss);
+    ss = warp_sum(ss);
+    const float inv1 = 1.0f / sqrtf(ss / (float)dim + eps);
+    float* hr = h + row * dim;
+    float ss2 = 0.f;
+    for (int j = 0; j < nj; j++) {
+        float4 hv = *reinterpret_cast<float4*>(hr + lane * 4 + 128 * j);
+        float hh[4] = {hv.x, hv.y, hv.z, hv.w};
+#pragma unroll
+        for (int c = 0; c < 4; c++) {
+            const int col = lane * 4 + 128 * j + c;
+            const float n = v[4 * j + c] * inv1 * w1[col];
+            hh[c] = (hh[c] + n) * scalar;
+            v[4 * j + c] = hh[c];
+            ss2 = fmaf(hh[c], hh[c], ss2);
+        }
+        *reinterpret_cast<float4*>(hr + lane * 4 + 128 * j) = make_float4(hh[0], hh[1], hh[2], hh[3]);
+    }
+    if (!t) return;
+    TT* tr = t + row * dim;
+    float inv2 = 1.f;
+    if (w2) {
+        ss2 = warp_sum(ss2);
+        inv2 = 1.0f / sqrtf(ss2 / (float)dim + eps);
+    }
+    for (int j = 0; j < nj; j++)
+#pragma unroll
+        for (int c = 0; c < 4; c++) {
+            const int col = lane * 4 + 128 * j + c;
+            stf(tr, col, w2 ? v[4 * j + c] * inv2 * w2[col] : v[4 * j + c]);
+        }
+}
+
+template <typename TI, typename TT>
+int add_norm(float* h, const TI* o, const float* w1, TT* t, const float* w2, long rows, int dim, float eps, float scalar,
+             cudaStream_t s) {
+    if (rows <= 0) return 0;
+    if (dim % 128 || dim > 128 * (ROW_MAX_VALS / 4)) return -1;
+    const int wpb = 8;
+    add_norm_kernel<TI, TT><<<(unsigned)((rows + wpb - 1) / wpb), 32 * wpb, 0, s>>>(h, o, w1, t, w2, rows, dim, eps, scalar);
+    return cudaGetLastError() == cudaSuccess ? 0 : -3;
+}
+template int add_norm<float, float>(float*, const float*, const float*, float*, const float*, long, int, float, float, cudaStream_t);
+template int add_norm<bf16_t, bf16_t>(float*, const bf16_t*, const float*, bf16_t*, const float*, long, int, float, float, cudaStream_t);
+template int add_norm<float, bf16_t>(float*, const float*, const float*, bf16_t*, const float*, long, int, float, float, cudaStream_t);
+
+// ---------------------------------------------------------------------------------------------
+// One warp per (row, head slot) over [q heads | k heads | v heads]. The normalised head goes
+// through shared memory so RoPE can pair element i with i + part/2 whatever the lane layout.
+// Tables hold the unique half of the reference's duplicated-halves layout: entry
+// [pos, pi * (part / 2) + j] is the angle of rotation part pi, frequency j; rope_w = hd / 2.
+template <typename TI, typename TO>
+__global__ void qkv_post_kernel(const TI* __restrict__ qkv, TO* __restrict__ q, TO* __restrict__ k, TO* __restrict__ v,
+                                const float* __restrict__ wq, const float* __restrict__ wk, const float* __restrict__ cs,
+                                const float* __restrict__ sn, int rope_w, const int* __restrict__ pos, long rows, int nh,
+                                int nkv, int hd, int part, float eps) {
+    extern __shared__ float sbuf[];
+    const int S = nh + 2 * nkv;
+    const long item = (long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (item >= rows * S) return;
+    const long row = item / S;
+    const int slot = (int)(item % S);
+    const int lane = threadIdx.x & 31;
+    float* buf = sbuf + (threadIdx.x >> 5) * hd;
+    const TI* src = qkv + row * (long)S * hd + (long)slot * hd;
+    const float* w;
+    TO* dst;
+    bool rot;
+    if (slot < nh) {
+        dst = q + (row * nh + slot) * hd;
+        w = wq;
+        rot = true;
+    } else if (slot < nh + nkv) {
+        dst = k + (row * nkv + (slot - nh)) * hd;
+        w = wk;
+        rot = true;
+    } else {
+        dst = v + (row * nkv + (slot - nh - nkv)) * hd;
+        w = nullptr;
+        rot = false;
+    }
+    float ss = 0.f;
+    for (int i = lane; i < hd; i += 32) {
+        const float x = ldf(src, i);
+        buf[i] = x;
+        ss = fmaf(x, x, ss);
+    }
+    ss = warp_sum(ss);
+    const float inv = 1.0f / sqrtf(ss / (float)hd + eps);
+    for (int i = lane; i < hd; i += 32) {
+        float n = buf[i] * inv;
+        if (w) n *= w[i];
+        buf[i] = n;
+    }
+    __syncwarp();
+    if (!rot) {
+        for (int i = lane; i < hd; i += 32) stf(dst, i, buf[i]);
+        return;
+    }
+    const int half = part / 2;
+    const long p = pos ? pos[row] : row;
+    const float* c = cs + p * rope_w;
+    const float* sv = sn + p * rope_w;
+    for (int idx = lane; idx < hd / 2; idx += 32) {
+        const int pi = idx / half, j = idx % half;
+        const int b = pi * part;
+        const float x1 = buf[b + j], x2 = buf[b + half + j];
+        const float cj = c[pi * half + j], sj = sv[pi * half + j];
+        stf(dst, b + j, x1 * cj - x2 * sj);
+        stf(dst, b + half + j, x2 * cj + x1 * sj);
+    }
+}
+
+template <typename TI, typename TO>
+int qkv_post(const TI* qkv, TO* q, TO* k, TO* v, const float* wq, const float* wk, const float* cs, const float* sn,
+             int rope_w, const int* pos, long rows, int nh, int nkv, int hd, int part, float eps, cudaStream_t s) {
+    if (rows <= 0) return 0;
+    if (hd % 32 || hd > 1024 || part <= 0 || hd % part || part % 2) return -1;
+    const int wpb = 8;
+    const long items = rows * (nh + 2 * nkv);
+    qkv_post_kernel<TI, TO><<<(unsigned)((items + wpb - 1) / wpb), 32 * wpb, wpb * hd * sizeof(float), s>>>(
+        qkv, q, k, v, wq, wk, cs, sn, rope_w, pos, rows, nh, nkv, hd, part, eps);
+    return cudaGetLastError() == cudaSuccess ? 0 : -3;
+}
+template int qkv_post<bf16_t, bf16_t>(const bf16_t*, bf16_t*, bf16_t*, bf16_t*, const float*, const float*, const float*,
+                                      const float*, int, const int*, long, int, int, int, int, float, cudaStream_t);
+template int qkv_post<float, float>(const float*, float*, float*, float*, const float*, const float*, const float*,
+                                    const float*, int, const int*, long, int, int, int, int, float, cudaStream_t);
+
+// ---------------------------------------------------------------------------------------------
+// gate|up rows in the interleaved layout of EPI_GELU_GU: per 256 columns, 128 gate then 128 up.
+template <typename TI, typename TO>
+__global__ void gelu_gu_kernel(const TI* __restrict__ gu, TO* __restrict__ out, long rows, int ff) {
+    const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= rows * ff) return;
+    const long r = i / ff;
+    const int c = (int)(i % ff);
+    const long base = r * 2L * ff + (c / 128) * 256 + (c % 128);
+    stf(out, i, gelu_tanh_f(ldf(gu, base)) * ldf(gu, base + 128));
+}
+template <typename TI, typename TO>
+int gelu_gu(const TI* gu, TO* out, long rows, int ff, cudaStream_t s) {
+    if (rows <= 0) return 0;
+    if (ff % 128) return -1;
+    const long n = rows * ff;
+    gelu_gu_kernel<TI, TO><<<(unsigned)((n + 255) / 256), 256, 0, s>>>(gu, out, rows, ff);
+    return cudaGetLastError() == cudaSuccess ? 0 : -3;
+}
+template int gelu_gu<float, float>(const float*, float*, long, int, cudaStream_t);
+
+template <typename TI, typename TO>
+__global__ void ple_gate_kernel(const TI* __restrict__ g, TO* __restrict__ out, const float* __restrict__ ple, long rows,
+                                int p, int n_layers, int layer) {
+    const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= rows * p) return;
+    const long r = i / p;
+    const int c = (int)(i % p);
+    stf(out, i, gelu_tanh_f(ldf(g, i)) * ple[(r * n_layers + layer) * p + c]);
+}
+template <typename TI, typename TO>
+int ple_gate(const TI* g, TO* out, const float* ple, long rows, int p, int n_layers, int layer, cudaStream_t s) {
+    if (rows <= 0) return 0;
+    const long n = rows * p;
+    ple_gate_kernel<TI, TO><<<(unsigned)((n + 255) / 256), 256, 0, s>>>(g, out, ple, rows, p, n_layers, layer);
+    return cudaGetLastError() == cudaSuccess ? 0 : -3;
+}
+template int ple_gate<float, float>(const float*, float*, const float*, long, int, int, int, cudaStream_t);
+
+// ---------------------------------------------------------------------------------------------
+// Mean over a sequence's rows (f64 sums), L2 normalisation (f64) and Matryoshka cuts: for each
+// sequence the output holds, back to back, the normalised first dims[d] components for each d.
+__global__ void pool_kernel(const float* __restrict__ x, const int* __restrict__ seq_start, const int* __restrict__ seq_len,
+                            int dim, const int* __restrict__ dims, int n_dims, int out_stride, float* __restrict__ out) {
+    extern __shared__ double dsh[];  // dim means + 32 partials
+    double* mean = dsh;
+    double* part = dsh + dim;
+    const int sidx = blockIdx.x;
+    const long r0 = seq_start[sidx];
+    const int len = seq_len[sidx];
+    for (int c = threadIdx.x; c < dim; c += blockDim.x) {
+        double acc = 0.0;
+        const float* col = x + r0 * dim + c;
+        for (int r = 0; r < len; r++) acc += (double)col[(long)r * dim];
+        mean[c] = (double)(float)(acc / (double)len);
+    }
+    __syncthreads();
+    float* o = out + (long)sidx * out_stride;
+    int off = 0;
+    for (int d = 0; d < n_dims; d++) {
+        const int nd = dims[d];
+        double ss = 0.0;
+        for (int c = threadIdx.x; c < nd; c += blockDim.x) ss += mean[c] * mean[c];
+#pragma unroll
+        for (int sh = 16; sh > 0; sh >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, sh);
+        if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = ss;
+        __syncthreads();
+        double tot = 0.0;
+        for (int wv = 0; wv < (int)(blockDim.x >> 5); wv++) tot += part[wv];
+        const double norm = fmax(sqrt(tot), 1e-12);
+        for (int c = threadIdx.x; c < nd; c += blockDim.x) o[off + c] = (float)(mean[c] / norm);
+        __syncthreads();
+        off += nd;
+    }
+}
+
+int pool_rows(const float* x, const int* seq_start, const int* seq_len, int n_seq, int dim, const int* dims_dev,
+                  int n_dims, int out_stride, float* out, cudaStream_t s) {
+    if (n_seq <= 0) return 0;
+    pool_kernel<<<n_seq, 256, (dim + 32) * sizeof(double), s>>>(x, seq_start, seq_len, dim, dims_dev, n_dims, out_stride, out);
+    return cudaGetLastError() == cudaSuccess ? 0 : -3;
+}
+
+// ---------------------------------------------------------------------------------------------
+__global__ void embed_gather_kernel(const bf16_t* __restrict__ table, long vocab, int h, const uint32_t* __restrict__ ids,
+                                    long n, float scale, float* __restrict__ out, int* bad) {
+    const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n * h) return;
+    const long t = i / h;
+    const int c = (int)(i % h);
+    const uint32_t id = ids[t];
+    if ((long)id >= vocab) {
+        if (c == 0) atomicExch(bad, 1);
+        out[i] = 0.f;
+        return;
+    }
+    out[i] = bf16_to_f32(table[(long)id * h + c]) * scale;
+}
+int embed_gather(const bf16_t* table, long vocab, int h, const uint32_t* ids, long n, float scale, float* out, int* bad,
+                 cudaStream_t s) {
+    if (n <= 0) return 0;
+    const long tot = n * h;
+    embed_gather_kernel<<<(unsigned)((tot + 255) / 256), 256, 0, s>>>(table, vocab, h, ids, n, scale, out, bad);
+    return cudaGetLastError() == cudaSuccess ? 0 : -3;
+}
+
+template <typename TO>
+__global__ void cast_kernel(const float* __restrict__ x, TO* __restrict__ out, long n, float mul, float add) {
+    const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) stf(out, i, (x[i] + add) * mul);
+}
+template <typename TO>
+int cast_rows(const float* x, TO* out, long n, float mul, float add, cudaStream_t s) {
+    if (n <= 0) return 0;
+    cast_kernel<TO><<<(unsigned)((n + 255) / 256), 256, 0, s>>>(x, out, n, mul, add);
+    return cudaGetLastError() == cudaSuccess ? 0 : -3;
+}
+template int cast_rows<float>(const float*, float*, long, float, float, cudaStream_t);
+template int cast_rows<bf16_t>(const float*, bf16_t*, long, float, float, cudaStream_t);
+
+__global__ void widen_bf16_kernel(const bf16_t* __restrict__ x, float* __restrict__ out, long n) {
+    const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) out[i] = bf16_to_f32(x[i]);
+}
+int widen_bf16(const bf16_t* x, float* out, long n, cudaStream_t s) {
+    if (n <= 0) return 0;
+    widen_bf16_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(x, out, n);
+    return cudaGetLastError() == cudaSuccess ? 0 : -3;
+}
+
+__global__ void vision_pos_kernel(float* __restrict__ h, const float* __restrict__ table, const int* __restrict__ pos, long n,
+                                  int hdim, int pe) {
+    const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n * hdim) return;
+    const long t = i / hdim;
+    const int c = (int)(i % hdim);
+    h[i] += table[(long)pos[2 * t] * hdim + c] + table[((long)pe + pos[2 * t + 1]) * hdim + c];
+}
+int vision_add_positions(float* h, const float* table, const int* pos, long n, int hdim, int pe, cudaStream_t s) {
+    if (n <= 0) return 0;
+    vision_pos_kernel<<<(unsigned)((n * hdim + 255) / 256), 256, 0, s>>>(h, table, pos, n, hdim, pe);
+    return cudaGetLastError() == cudaSuccess ? 0 : -3;
+}
+
+__global__ void vision_pool_kernel(const float* __restrict__ x, float* __restrict__ out, int gh, int gw, int hdim, int k,
+                                   float root) {
+    const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+    const int ow = gw / k;
+    const long n = (long)(gh / k) * ow * hdim;
+    if (i >= n) return;
+    const long o = i / hdim;
+    const int c = (int)(i % hdim);
+    const int oy = (int)(o / ow), ox = (int)(o % ow);
+    float acc = 0.f;
+    for (int dy = 0; dy < k; dy++)
+        for (int dx = 0; dx < k; dx++) acc += x[((long)(oy * k + dy) * gw + ox * k + dx) * hdim + c];
+    out[i] = (acc / (float)(k * k)) * root;
+}
+int vision_pool(const float* x, float* out, int gh, int gw, int hdim, int k, float root, cudaStream_t s) {
+    const long n = (long)(gh / k) * (gw / k) * hdim;
+    if (n <= 0) return 0;
+    vision_pool_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(x, out, gh, gw, hdim, k, root);
+    return cudaGetLastError() == cudaSuccess ? 0 : -3;
+}
+
+}  // namespace eg2

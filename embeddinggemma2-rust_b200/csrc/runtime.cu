@@ -1,0 +1,1366 @@
+// Host runtime of the library: checkpoint loading, device weights, per-pass workspace, the text
+// backbone and vision tower launch sequences, and the C ABI of include/eg2.h.
+//
+// Reference counterparts (paths inside the reference project):
+//   context + weights upload   Gpu::new, GpuText::from_cpu (src/gpu/mod.rs:281-403, src/gpu/text.rs:177-219)
+//   layer launch sequence      GpuText::enqueue (src/gpu/text.rs:350-433)
+//   forward_packed             GpuText::forward_packed (src/gpu/text.rs:436-529)
+//   RoPE tables                GpuText::ensure_rope (src/gpu/text.rs:227-242), src/ops.rs:293-314
+//   vision                     GpuVision::encode (src/gpu/vision.rs:97-219), VisionHead (src/vision.rs:47-170)
+//   safetensors                Weights::open (src/weights.rs:46-86)
+#include <fcntl.h>
+#include <sys/mman.h>
+#include <sys/stat.h>
+#include <unistd.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/eg2.h"
+#include "json.h"
+#include "kernels.h"
+
+namespace eg2 {
+
+// ---------------------------------------------------------------------------------------------
+// Driver helpers
+// ---------------------------------------------------------------------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_tiled() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = (EncodeTiledFn)p;
+    });
+    return fn;
+}
+
+int make_tmap_2d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t inner, uint64_t outer,
+                 uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer) {
+    EncodeTiledFn fn = encode_tiled();
+    if (!fn) return -3;
+    cuuint64_t dims[2] = {inner, outer};
+    cuuint64_t strides[1] = {row_bytes};
+    cuuint32_t box[2] = {box_inner, box_outer};
+    cuuint32_t es[2] = {1, 1};
+    CUresult r = fn(m, dt, 2, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? 0 : -1;
+}
+
+int make_tmap_3d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t d0, uint64_t d1, uint64_t d2,
+                 uint64_t s1, uint64_t s2, uint32_t b0, uint32_t b1, uint32_t b2) {
+    EncodeTiledFn fn = encode_tiled();
+    if (!fn) return -3;
+    cuuint64_t dims[3] = {d0, d1, d2};
+    cuuint64_t strides[2] = {s1, s2};
+    cuuint32_t box[3] = {b0, b1, b2};
+    cuuint32_t es[3] = {1, 1, 1};
+    CUresult r = fn(m, dt, 3, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? 0 : -1;
+}
+
+int num_sms() {
+    static int cache[64] = {0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) return 148;
+    if (!cache[dev]) {
+        int n = 0;
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        cache[dev] = n > 0 ? n : 148;
+    }
+    return cache[dev];
+}
+
+// ---------------------------------------------------------------------------------------------
+// Errors
+// ---------------------------------------------------------------------------------------------
+struct Fail {
+    int code;
+    std::string msg;
+};
+[[noreturn]] static void fail(int code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    throw Fail{code, buf};
+}
+#define CK(call)                                                                                      \
+    do {                                                                                              \
+        cudaError_t e_ = (call);                                                                      \
+        if (e_ != cudaSuccess)                                                                        \
+            fail(e_ == cudaErrorMemoryAllocation ? EG2_ERR_OOM : EG2_ERR_CUDA, "%s: %s (%s:%d)", #call, \
+                 cudaGetErrorString(e_), __FILE__, __LINE__);                                         \
+    } while (0)
+#define KL(call, what)                                                                         \
+    do {                                                                                       \
+        int r_ = (call);                                                                       \
+        if (r_ != 0) fail(r_ == -1 ? EG2_ERR_INVALID : EG2_ERR_CUDA, "launch of %s failed", what); \
+    } while (0)
+
+// ---------------------------------------------------------------------------------------------
+// Safetensors (mmap, BF16 / F16 / F32), checks as src/weights.rs:46-86
+// ---------------------------------------------------------------------------------------------
+struct TensorInfo {
+    std::string dtype;
+    std::vector<long> shape;
+    size_t start = 0, end = 0;
+    long numel() const {
+        long n = 1;
+        for (long d : shape) n *= d;
+        return n;
+    }
+};
+
+struct SafeTensors {
+    void* map = nullptr;
+    size_t size = 0;
+    size_t data_start = 0;
+    std::map<std::string, TensorInfo> index;
+
+    explicit SafeTensors(const std::string& path) {
+        int fd = ::open(path.c_str(), O_RDONLY);
+        if (fd < 0) fail(EG2_ERR_IO, "opening %s", path.c_str());
+        struct stat st;
+        fstat(fd, &st);
+        size = (size_t)st.st_size;
+        map = size ? mmap(nullptr, size, PROT_READ, MAP_PRIVATE, fd, 0) : MAP_FAILED;
+        ::close(fd);
+        if (map == MAP_FAILED) fail(EG2_ERR_IO, "mapping %s", path.c_str());
+        if (size < 8) fail(EG2_ERR_IO, "safetensors file too small");
+        uint64_t hlen;
+        memcpy(&hlen, map, 8);
+        if (hlen > size - 8) fail(EG2_ERR_IO, "corrupt safetensors header length in %s", path.c_str());
+        data_start = 8 + hlen;
+        Json h;
+        try {
+            h = Json::parse((const char*)map + 8, hlen);
+        } catch (std::exception& e) {
+            fail(EG2_ERR_IO, "parsing the header of %s: %s", path.c_str(), e.what());
+        }
+        for (auto& kv : h.obj) {
+            if (kv.first == "__metadata__") continue;
+            TensorInfo t;
+            t.dtype = kv.second.at("dtype").string();
+            for (auto& d : kv.second.at("shape").arr) t.shape.push_back(d.integer());
+            const auto& off = kv.second.at("data_offsets").arr;
+            t.start = (size_t)off.at(0).integer();
+            t.end = (size_t)off.at(1).integer();
+            long esz = t.dtype == "F32" ? 4 : (t.dtype == "BF16" || t.dtype == "F16") ? 2 : 0;
+            if (!esz) fail(EG2_ERR_IO, "tensor %s: unsupported dtype %s", kv.first.c_str(), t.dtype.c_str());
+            if (t.end < t.start || data_start + t.end > size || (size_t)(t.numel() * esz) != t.end - t.start)
+                fail(EG2_ERR_IO, "tensor %s: bad offsets", kv.first.c_str());
+            index[kv.first] = t;
+        }
+    }
+    ~SafeTensors() {
+        if (map && map != MAP_FAILED) munmap(map, size);
+    }
+    bool has(const std::string& n) const { return index.count(n) > 0; }
+    const TensorInfo& info(const std::string& n, std::initializer_list<long> shape) const {
+        auto it = index.find(n);
+        if (it == index.end()) fail(EG2_ERR_IO, "missing tensor `%s`", n.c_str());
+        std::vector<long> want(shape);
+        if (!want.empty() && it->second.shape != want) {
+            // Accept a scalar stored as [] or [1].
+            if (!(want.size() == 1 && want[0] == 1 && it->second.numel() == 1))
+                fail(EG2_ERR_IO, "tensor `%s` has an unexpected shape", n.c_str());
+        }
+        return it->second;
+    }
+    const uint8_t* bytes(const TensorInfo& t) const { return (const uint8_t*)map + data_start + t.start; }
+    // Whole tensor as host f32 (BF16 widened exactly as bf16_to_f32, src/weights.rs:189-191).
+    std::vector<float> f32(const std::string& n, std::initializer_list<long> shape) const {
+        const TensorInfo& t = info(n, shape);
+        std::vector<float> out(t.numel());
+        const uint8_t* b = bytes(t);
+        if (t.dtype == "F32") {
+            memcpy(out.data(), b, out.size() * 4);
+        } else if (t.dtype == "BF16") {
+            for (size_t i = 0; i < out.size(); i++) {
+                uint32_t u = (uint32_t)(b[2 * i] | (b[2 * i + 1] << 8)) << 16;
+                memcpy(&out[i], &u, 4);
+            }
+        } else {
+            fail(EG2_ERR_IO, "tensor %s: F16 not supported here", n.c_str());
+        }
+        return out;
+    }
+};
+
+static uint16_t f32_to_bf16_host(float f) {
+    uint32_t u;
+    memcpy(&u, &f, 4);
+    if ((u & 0x7fffffffu) > 0x7f800000u) return (uint16_t)((u >> 16) | 0x40u);
+    u += 0x7fffu + ((u >> 16) & 1u);
+    return (uint16_t)(u >> 16);
+}
+
+// ---------------------------------------------------------------------------------------------
+// Configuration (src/config.rs:21-66)
+// ---------------------------------------------------------------------------------------------
+struct TextCfg {
+    long vocab = 0;
+    int hidden = 0, inter = 0, layers = 0, nh = 0, ple = 0, emb = 0, window = 0;
+    float eps = 1e-6f;
+    std::vector<int> hd, nkv, sliding;
+    std::vector<double> theta;
+};
+struct VisionCfg {
+    bool present = false;
+    int hidden = 0, inter = 0, layers = 0, nh = 0, nkv = 0, hd = 0, patch = 0, pool = 0, pos_size = 0;
+    float eps = 1e-6f;
+    double theta = 100.0;
+};
+
+static std::string read_file(const std::string& path) {
+    FILE* f = fopen(path.c_str(), "rb");
+    if (!f) fail(EG2_ERR_IO, "reading %s", path.c_str());
+    std::string s;
+    char buf[65536];
+    size_t n;
+    while ((n = fread(buf, 1, sizeof buf, f)) > 0) s.append(buf, n);
+    fclose(f);
+    return s;
+}
+
+static void parse_config(const std::string& dir, TextCfg& tc, VisionCfg& vc) {
+    std::string raw = read_file(dir + "/config.json");
+    Json j;
+    try {
+        j = Json::parse(raw.data(), raw.size());
+        const Json& t = j.at("text_config");
+        if (t.has("attention_bias") && t.at("attention_bias").kind == Json::Bool && t.at("attention_bias").b)
+            fail(EG2_ERR_IO, "attention_bias=true is not supported");
+        tc.vocab = t.at("vocab_size").integer();
+        tc.hidden = (int)t.at("hidden_size").integer();
+        tc.inter = (int)t.at("intermediate_size").integer();
+        tc.layers = (int)t.at("num_hidden_layers").integer();
+        tc.nh = (int)t.at("num_attention_heads").integer();
+        tc.ple = (int)t.at("hidden_size_per_layer_input").integer();
+        tc.emb = (int)t.at("embedding_dim").integer();
+        tc.window = (int)t.at("sliding_window").integer();
+        tc.eps = (float)t.at("rms_norm_eps").number();
+        const int hd0 = (int)t.at("head_dim").integer(), nkv0 = (int)t.at("num_key_value_heads").integer();
+        const Json& lt = t.at("layer_types");
+        const Json& rp = t.at("rope_parameters");
+        for (int i = 0; i < tc.layers; i++) {
+            const bool sl = lt.arr.at(i).string() == "sliding_attention";
+            int hd = hd0, nkv = nkv0;
+            if (t.has("per_layer_config")) {
+                char k2[16], k1[16];
+                snprintf(k2, sizeof k2, "%02d", i);
+                snprintf(k1, sizeof k1, "%d", i);
+                const Json& plc = t.at("per_layer_config");
+                const Json* ov = plc.has(k2) ? &plc.at(k2) : plc.has(k1) ? &plc.at(k1) : nullptr;
+                if (ov) {
+                    if (ov->has("head_dim") && ov->at("head_dim").kind == Json::Num) hd = (int)ov->at("head_dim").integer();
+                    if (ov->has("num_key_value_heads") && ov->at("num_key_value_heads").kind == Json::Num)
+                        nkv = (int)ov->at("num_key_value_heads").integer();
+                }
+            }
+            tc.hd.push_back(hd);
+            tc.nkv.push_back(nkv);
+            tc.sliding.push_back(sl ? 1 : 0);
+            tc.theta.push_back(rp.at(sl ? "sliding_attention" : "full_attention").at("rope_theta").number());
+        }
+        if (j.has("vision_config") && j.at("vision_config").kind == Json::Obj) {
+            const Json& v = j.at("vision_config");
+            vc.present = true;
+            vc.hidden = (int)v.at("hidden_size").integer();
+            vc.inter = (int)v.at("intermediate_size").integer();
+            vc.layers = (int)v.at("num_hidden_layers").integer();
+            vc.nh = (int)v.at("num_attention_heads").integer();
+            vc.nkv = (int)v.at("num_key_value_heads").integer();
+            vc.hd = (int)v.at("head_dim").integer();
+            vc.patch = (int)v.at("patch_size").integer();
+            vc.pool = (int)v.at("pooling_kernel_size").integer();
+            vc.pos_size = (int)v.at("position_embedding_size").integer();
+            vc.eps = (float)v.at("rms_norm_eps").number();
+            vc.theta = v.at("rope_parameters").at("rope_theta").number();
+            if (v.has("standardize") && v.at("standardize").kind == Json::Bool && v.at("standardize").b)
+                fail(EG2_ERR_IO, "vision_config.standardize=true is not supported");
+        }
+    } catch (Fail&) {
+        throw;
+    } catch (std::exception& e) {
+        fail(EG2_ERR_IO, "config.json: %s", e.what());
+    }
+}
+
+// ---------------------------------------------------------------------------------------------
+// RoPE tables (unique halves): [len, hd / 2], angle = pos * inv_freq[i] in f32 (src/ops.rs:293-314)
+// ---------------------------------------------------------------------------------------------
+static std::vector<float> rope_inv_freq(double base, int dim) {
+    std::vector<float> inv(dim / 2);
+    for (int i = 0; i < dim / 2; i++) inv[i] = 1.0f / powf((float)base, (float)(2 * i) / (float)dim);
+    return inv;
+}
+
+struct RopeTab {
+    double theta = 0;
+    int hd = 0;
+    long len = 0;
+    float* cs = nullptr;
+    float* sn = nullptr;
+};
+
+// ---------------------------------------------------------------------------------------------
+// Context
+// ---------------------------------------------------------------------------------------------
+struct LayerW {
+    void *qkv = nullptr, *o = nullptr, *gu = nullptr, *down = nullptr, *pg = nullptr, *pp = nullptr;
+    float *input_ln, *post_attn_ln, *pre_ff_ln, *post_ff_ln, *q_norm, *k_norm, *ple_post_norm;
+    float layer_scalar = 1.f;
+    int hd = 0, nkv = 0, sliding = 0, rope = 0;
+};
+
+struct VLayerW {
+    void *qkv = nullptr, *o = nullptr, *gu = nullptr, *down = nullptr;
+    float *input_ln, *post_attn_ln, *pre_ff_ln, *post_ff_ln, *q_norm, *k_norm;
+};
+
+struct Work {
+    long cap = 0;
+    float *hidden = nullptr, *ple = nullptr, *out = nullptr, *x_in = nullptr;
+    void *t = nullptr, *qkv = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *a = nullptr, *o = nullptr,
+         *gate = nullptr, *pg = nullptr, *gu = nullptr;
+    int *pos = nullptr, *seq_start = nullptr, *seq_len = nullptr;
+    uint32_t* ids = nullptr;
+    long tiles_cap = 0;
+    AttnTile* tiles = nullptr;
+    long pooled_cap = 0;
+    float* pooled = nullptr;
+    int* dims = nullptr;
+    int seq_meta_cap = 0;
+    int* seq_meta = nullptr;
+};
+
+}  // namespace eg2
+
+struct eg2_ctx {
+    int device = 0;
+    int precision = EG2_BF16;
+    std::mutex mu;
+    std::string err;
+    cudaStream_t own_stream = nullptr;
+    cudaStream_t stream = nullptr;
+    eg2::TextCfg tc;
+    eg2::VisionCfg vc;
+    std::vector<void*> allocs;
+    // text weights
+    std::vector<eg2::LayerW> layers;
+    void *ple_proj = nullptr, *emb_proj = nullptr;
+    float *ple_norm = nullptr, *final_norm = nullptr;
+    uint16_t* embed_table = nullptr;  // bf16 [vocab, hidden] on the device
+    std::vector<eg2::RopeTab> ropes;
+    // vision weights
+    std::vector<eg2::VLayerW> vlayers;
+    void *v_input_proj = nullptr, *v_embed_proj = nullptr;
+    float* v_pos_table = nullptr;
+    eg2::Work w;
+    // vision workspace
+    long vcap = 0;
+    float *v_hidden = nullptr, *v_pooled = nullptr, *v_cs = nullptr, *v_sn = nullptr, *v_soft = nullptr;
+    void *v_x = nullptr, *v_t = nullptr, *v_qkv = nullptr, *v_q = nullptr, *v_k = nullptr, *v_v = nullptr, *v_a = nullptr,
+         *v_o = nullptr, *v_gate = nullptr, *v_gu = nullptr;
+    int *v_pos = nullptr, *v_seq_start = nullptr, *v_seq_len = nullptr;
+    eg2::AttnTile* v_tiles = nullptr;
+    long v_tiles_cap = 0;
+    int* bad_flag = nullptr;
+    // profiling
+    bool profiling = false;
+    std::vector<std::pair<std::string, cudaEvent_t>> marks;
+    std::vector<cudaEvent_t> event_pool;
+    std::map<std::string, std::pair<double, long>> prof;
+    bool use_tc_attention = true;
+
+    ~eg2_ctx();
+};
+
+namespace eg2 {
+
+static void* dalloc(eg2_ctx* c, size_t bytes) {
+    void* p = nullptr;
+    if (bytes == 0) bytes = 16;
+    cudaError_t e = cudaMalloc(&p, bytes);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        fail(e == cudaErrorMemoryAllocation ? EG2_ERR_OOM : EG2_ERR_CUDA, "cudaMalloc(%zu): %s", bytes, cudaGetErrorString(e));
+    }
+    c->allocs.push_back(p);
+    return p;
+}
+static void dfree(eg2_ctx* c, void* p) {
+    if (!p) return;
+    auto it = std::find(c->allocs.begin(), c->allocs.end(), p);
+    if (it != c->allocs.end()) c->allocs.erase(it);
+    cudaFree(p);
+}
+
+static bool bf16_mode(const eg2_ctx* c) { return c->precision == EG2_BF16; }
+static size_t act_size(const eg2_ctx* c) { return bf16_mode(c) ? 2 : 4; }
+
+// Upload one weight matrix as the context's GEMM storage (bf16 or f32) into dst (+ row offset).
+static void upload_rows(eg2_ctx* c, const SafeTensors& st, const std::string& name, std::initializer_list<long> shape,
+                        void* dst, long dst_row0, long row0, long nrows) {
+    const TensorInfo& t = st.info(name, shape);
+    if (t.dtype != "BF16" && t.dtype != "F32") fail(EG2_ERR_IO, "tensor %s: unsupported dtype", name.c_str());
+    const long cols = t.shape.size() >= 2 ? t.shape.back() : 1;
+    const uint8_t* src = st.bytes(t);
+    const size_t es = act_size(c);
+    std::vector<uint8_t> tmp;
+    const size_t n = (size_t)nrows * cols;
+    if (t.dtype == "BF16" && es == 2) {
+        CK(cudaMemcpy((uint8_t*)dst + dst_row0 * cols * 2, src + row0 * cols * 2, n * 2, cudaMemcpyHostToDevice));
+        return;
+    }
+    tmp.resize(n * es);
+    for (size_t i = 0; i < n; i++) {
+        float f;
+        if (t.dtype == "BF16") {
+            const uint8_t* b = src + (row0 * cols + i) * 2;
+            uint32_t u = (uint32_t)(b[0] | (b[1] << 8)) << 16;
+            memcpy(&f, &u, 4);
+        } else {
+            memcpy(&f, src + (row0 * cols + i) * 4, 4);
+        }
+        if (es == 4) {
+            memcpy(&tmp[i * 4], &f, 4);
+        } else {
+            uint16_t h = f32_to_bf16_host(f);
+            memcpy(&tmp[i * 2], &h, 2);
+        }
+    }
+    CK(cudaMemcpy((uint8_t*)dst + dst_row0 * cols * es, tmp.data(), n * es, cudaMemcpyHostToDevice));
+}
+
+static float* upload_vec(eg2_ctx* c, const SafeTensors& st, const std::string& name, long n) {
+    std::vector<float> v = st.f32(name, {n});
+    float* d = (float*)dalloc(c, n * 4);
+    CK(cudaMemcpy(d, v.data(), n * 4, cudaMemcpyHostToDevice));
+    return d;
+}
+
+// gate|up into one [2 ff, K] matrix, interleaved per 128 features: rows [256 b, 256 b + 128) hold
+// gate rows [128 b, 128 b + 128), the next 128 the matching up rows (the EPI_GELU_GU layout).
+static void* upload_gate_up(eg2_ctx* c, const SafeTensors& st, const std::string& gate, const std::string& up, long ff,
+                            long k) {
+    void* d = dalloc(c, 2 * ff * k * act_size(c));
+    for (long b = 0; b < ff / 128; b++) {
+        upload_rows(c, st, gate, {ff, k}, d, 256 * b, 128 * b, 128);
+        upload_rows(c, st, up, {ff, k}, d, 256 * b + 128, 128 * b, 128);
+    }
+    return d;
+}
+
+static void load_text(eg2_ctx* c, const SafeTensors& st) {
+    const TextCfg& tc = c->tc;
+    const long h = tc.hidden, p = tc.ple, ff = tc.inter, nh = tc.nh;
+    if (h % 128 || h > 768 || ff % 128 || p % 256 || tc.emb % 256)
+        fail(EG2_ERR_IO, "unsupported text dimensions (hidden %ld, ff %ld, ple %ld)", h, ff, p);
+    for (int i = 0; i < tc.layers; i++) {
+        LayerW L;
+        L.hd = tc.hd[i];
+        L.nkv = tc.nkv[i];
+        L.sliding = tc.sliding[i];
+        const long hd = L.hd, nkv = L.nkv;
+        char pre[64];
+        snprintf(pre, sizeof pre, "language_model.layers.%d.", i);
+        std::string P(pre);
+        const long nqkv = (nh + 2 * nkv) * hd;
+        L.qkv = dalloc(c, nqkv * h * act_size(c));
+        upload_rows(c, st, P + "self_attn.q_proj.weight", {nh * hd, h}, L.qkv, 0, 0, nh * hd);
+        upload_rows(c, st, P + "self_attn.k_proj.weight", {nkv * hd, h}, L.qkv, nh * hd, 0, nkv * hd);
+        upload_rows(c, st, P + "self_attn.v_proj.weight", {nkv * hd, h}, L.qkv, (nh + nkv) * hd, 0, nkv * hd);
+        L.o = dalloc(c, h * nh * hd * act_size(c));
+        upload_rows(c, st, P + "self_attn.o_proj.weight", {h, nh * hd}, L.o, 0, 0, h);
+        L.gu = upload_gate_up(c, st, P + "mlp.gate_proj.weight", P + "mlp.up_proj.weight", ff, h);
+        L.down = dalloc(c, h * ff * act_size(c));
+        upload_rows(c, st, P + "mlp.down_proj.weight", {h, ff}, L.down, 0, 0, h);
+        L.pg = dalloc(c, p * h * act_size(c));
+        upload_rows(c, st, P + "ple_block.per_layer_input_gate.weight", {p, h}, L.pg, 0, 0, p);
+        L.pp = dalloc(c, h * p * act_size(c));
+        upload_rows(c, st, P + "ple_block.per_layer_projection.weight", {h, p}, L.pp, 0, 0, h);
+        L.input_ln = upload_vec(c, st, P + "input_layernorm.weight", h);
+        L.post_attn_ln = upload_vec(c, st, P + "post_attention_layernorm.weight", h);
+        L.pre_ff_ln = upload_vec(c, st, P + "pre_feedforward_layernorm.weight", h);
+        L.post_ff_ln = upload_vec(c, st, P + "post_feedforward_layernorm.weight", h);
+        L.q_norm = upload_vec(c, st, P + "self_attn.q_norm.weight", hd);
+        L.k_norm = upload_vec(c, st, P + "self_attn.k_norm.weight", hd);
+        L.ple_post_norm = upload_vec(c, st, P + "ple_block.post_per_layer_input_norm.weight", h);
+        L.layer_scalar = st.f32(P + "layer_scalar", {1})[0];
+        // RoPE table slot per distinct (theta, head_dim), as the reference's rope cache.
+        int slot = -1;
+        for (size_t r = 0; r < c->ropes.size(); r++)
+            if (c->ropes[r].theta == tc.theta[i] && c->ropes[r].hd == L.hd) slot = (int)r;
+        if (slot < 0) {
+            RopeTab rt;
+            rt.theta = tc.theta[i];
+            rt.hd = L.hd;
+            c->ropes.push_back(rt);
+            slot = (int)c->ropes.size() - 1;
+        }
+        L.rope = slot;
+        c->layers.push_back(L);
+    }
+    c->ple_proj = dalloc(c, (long)tc.layers * p * h * act_size(c));
+    upload_rows(c, st, "language_model.ple.per_layer_model_projection.weight", {(long)tc.layers * p, h}, c->ple_proj, 0, 0,
+                (long)tc.layers * p);
+    c->emb_proj = dalloc(c, (long)tc.emb * h * act_size(c));
+    upload_rows(c, st, "language_model.embedding_projection.weight", {(long)tc.emb, h}, c->emb_proj, 0, 0, tc.emb);
+    c->ple_norm = upload_vec(c, st, "language_model.ple.per_layer_projection_norm.weight", p);
+    c->final_norm = upload_vec(c, st, "language_model.norm.weight", h);
+    // Token-embedding table stays bf16 on the device (the device-side gather of eg2_embed_packed).
+    const TensorInfo& et = st.info("language_model.embed_tokens.weight", {tc.vocab, h});
+    if (et.dtype != "BF16") fail(EG2_ERR_IO, "embed_tokens must be BF16");
+    c->embed_table = (uint16_t*)dalloc(c, (size_t)tc.vocab * h * 2);
+    CK(cudaMemcpy(c->embed_table, st.bytes(et), (size_t)tc.vocab * h * 2, cudaMemcpyHostToDevice));
+}
+
+static void load_vision(eg2_ctx* c, const SafeTensors& st) {
+    VisionCfg& vc = c->vc;
+    if (!vc.present || !st.has("vision_tower.patch_embedder.input_proj.weight")) {
+        vc.present = false;
+        return;
+    }
+    const long h = vc.hidden, ff = vc.inter, nh = vc.nh, nkv = vc.nkv, hd = vc.hd, pd = 3L * vc.patch * vc.patch;
+    if (h % 256 || ff % 128 || pd % 64 || ((nh + 2 * nkv) * hd) % 256 || (nh * hd) % 64) {
+        vc.present = false;
+        return;
+    }
+    for (int i = 0; i < vc.layers; i++) {
+        VLayerW L;
+        char pre[64];
+        snprintf(pre, sizeof pre, "vision_tower.encoder.layers.%d.", i);
+        std::string P(pre);
+        L.qkv = dalloc(c, (nh + 2 * nkv) * hd * h * act_size(c));
+        upload_rows(c, st, P + "self_attn.q_proj.linear.weight", {nh * hd, h}, L.qkv, 0, 0, nh * hd);
+        upload_rows(c, st, P + "self_attn.k_proj.linear.weight", {nkv * hd, h}, L.qkv, nh * hd, 0, nkv * hd);
+        upload_rows(c, st, P + "self_attn.v_proj.linear.weight", {nkv * hd, h}, L.qkv, (nh + nkv) * hd, 0, nkv * hd);
+        L.o = dalloc(c, h * nh * hd * act_size(c));
+        upload_rows(c, st, P + "self_attn.o_proj.linear.weight", {h, nh * hd}, L.o, 0, 0, h);
+        L.gu = upload_gate_up(c, st, P + "mlp.gate_proj.linear.weight", P + "mlp.up_proj.linear.weight", ff, h);
+        L.down = dalloc(c, h * ff * act_size(c));
+        upload_rows(c, st, P + "mlp.down_proj.linear.weight", {h, ff}, L.down, 0, 0, h);
+        L.input_ln = upload_vec(c, st, P + "input_layernorm.weight", h);
+        L.post_attn_ln = upload_vec(c, st, P + "post_attention_layernorm.weight", h);
+        L.pre_ff_ln = upload_vec(c, st, P + "pre_feedforward_layernorm.weight", h);
+        L.post_ff_ln = upload_vec(c, st, P + "post_feedforward_layernorm.weight", h);
+        L.q_norm = upload_vec(c, st, P + "self_attn.q_norm.weight", hd);
+        L.k_norm = upload_vec(c, st, P + "self_attn.k_norm.weight", hd);
+        c->vlayers.push_back(L);
+    }
+    c->v_input_proj = dalloc(c, h * pd * act_size(c));
+    upload_rows(c, st, "vision_tower.patch_embedder.input_proj.weight", {h, pd}, c->v_input_proj, 0, 0, h);
+    // The multimodal embedder's projection stays f32 (it runs on the f32 CUDA-core GEMM: N = 512
+    // soft-token width is small and the reference runs it on the host in f32).
+    {
+        std::vector<float> w = st.f32("embed_vision.embedding_projection.weight", {(long)c->tc.hidden, h});
+        c->v_embed_proj = dalloc(c, w.size() * 4);
+        CK(cudaMemcpy(c->v_embed_proj, w.data(), w.size() * 4, cudaMemcpyHostToDevice));
+    }
+    std::vector<float> pt = st.f32("vision_tower.patch_embedder.position_embedding_table", {2, (long)vc.pos_size, h});
+    c->v_pos_table = (float*)dalloc(c, pt.size() * 4);
+    CK(cudaMemcpy(c->v_pos_table, pt.data(), pt.size() * 4, cudaMemcpyHostToDevice));
+}
+
+// Grow-only RoPE tables covering positions [0, max_len).
+static void ensure_rope(eg2_ctx* c, long max_len) {
+    for (RopeTab& r : c->ropes) {
+        if (r.len >= max_len) continue;
+        long len = ((max_len + 1023) / 1024) * 1024;
+        if (len < 4096) len = 4096;
+        std::vector<float> inv = rope_inv_freq(r.theta, r.hd);
+        const int half = r.hd / 2;
+        std::vector<float> cs((size_t)len * half), sn((size_t)len * half);
+        for (long t = 0; t < len; t++)
+            for (int i = 0; i < half; i++) {
+                const float f = (float)t * inv[i];
+                cs[(size_t)t * half + i] = cosf(f);
+                sn[(size_t)t * half + i] = sinf(f);
+            }
+        CK(cudaStreamSynchronize(c->stream));
+        dfree(c, r.cs);
+        dfree(c, r.sn);
+        r.cs = (float*)dalloc(c, cs.size() * 4);
+        r.sn = (float*)dalloc(c, sn.size() * 4);
+        CK(cudaMemcpy(r.cs, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice));
+        CK(cudaMemcpy(r.sn, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice));
+        r.len = len;
+    }
+}
+
+static void ensure_work(eg2_ctx* c, long rows, long n_tiles) {
+    Work& w = c->w;
+    const TextCfg& tc = c->tc;
+    if (rows > w.cap) {
+        CK(cudaStreamSynchronize(c->stream));
+        long cap = ((rows + 1023) / 1024) * 1024;
+        void** bufs[] = {(void**)&w.hidden, (void**)&w.ple, (void**)&w.out, (void**)&w.t, (void**)&w.qkv, (void**)&w.q,
+                         (void**)&w.k, (void**)&w.v, (void**)&w.a, (void**)&w.o, (void**)&w.gate, (void**)&w.pg,
+                         (void**)&w.gu, (void**)&w.pos, (void**)&w.seq_start, (void**)&w.seq_len, (void**)&w.ids};
+        for (void** b : bufs) {
+            dfree(c, *b);
+            *b = nullptr;
+        }
+        int max_q = 0, max_kv = 0, max_qkv = 0;
+        for (auto& L : c->layers) {
+            max_q = std::max(max_q, tc.nh * L.hd);
+            max_kv = std::max(max_kv, L.nkv * L.hd);
+            max_qkv = std::max(max_qkv, (tc.nh + 2 * L.nkv) * L.hd);
+        }
+        const size_t as = act_size(c);
+        w.hidden = (float*)dalloc(c, cap * tc.hidden * 4);
+        w.ple = (float*)dalloc(c, cap * (long)tc.layers * tc.ple * 4);
+        w.out = (float*)dalloc(c, cap * tc.emb * 4);
+        w.t = dalloc(c, cap * tc.hidden * as);
+        w.qkv = dalloc(c, cap * max_qkv * as);
+        w.q = dalloc(c, cap * max_q * as);
+        w.k = dalloc(c, cap * max_kv * as);
+        w.v = dalloc(c, cap * max_kv * as);
+        w.a = dalloc(c, cap * max_q * as);
+        w.o = dalloc(c, cap * tc.hidden * as);
+        w.gate = dalloc(c, cap * tc.inter * as);
+        w.pg = dalloc(c, cap * tc.ple * as);
+        w.gu = c->precision == EG2_F32 ? dalloc(c, cap * 2L * tc.inter * 4) : nullptr;
+        w.pos = (int*)dalloc(c, cap * 4);
+        w.seq_start = (int*)dalloc(c, cap * 4);
+        w.seq_len = (int*)dalloc(c, cap * 4);
+        w.ids = (uint32_t*)dalloc(c, cap * 4);
+        w.cap = cap;
+    }
+    if (n_tiles > w.tiles_cap) {
+        CK(cudaStreamSynchronize(c->stream));
+        dfree(c, w.tiles);
+        w.tiles_cap = std::max(n_tiles, 1024L);
+        w.tiles = (AttnTile*)dalloc(c, w.tiles_cap * sizeof(AttnTile));
+    }
+}
+
+// ---------------------------------------------------------------------------------------------
+// Profiling marks
+// ---------------------------------------------------------------------------------------------
+static void mark(eg2_ctx* c, const char* label) {
+    if (!c->profiling) return;
+    cudaEvent_t e;
+    if (c->event_pool.empty()) {
+        CK(cudaEventCreate(&e));
+    } else {
+        e = c->event_pool.back();
+        c->event_pool.pop_back();
+    }
+    CK(cudaEventRecord(e, c->stream));
+    c->marks.push_back({label, e});
+}
+static void collect_marks(eg2_ctx* c) {
+    if (c->marks.empty()) return;
+    CK(cudaEventSynchronize(c->marks.back().second));
+    for (size_t i = 1; i < c->marks.size(); i++) {
+        float ms = 0;
+        cudaEventElapsedTime(&ms, c->marks[i - 1].second, c->marks[i].second);
+        auto& p = c->prof[c->marks[i].first];
+        p.first += ms;
+        p.second += 1;
+    }
+    for (auto& m : c->marks) c->event_pool.push_back(m.second);
+    c->marks.clear();
+}
+
+// ---------------------------------------------------------------------------------------------
+// GEMM dispatch by precision
+// ---------------------------------------------------------------------------------------------
+// y = x . W^T with the context's precision. Modes: EPI_STORE (y act, or f32 when out_f32),
+// EPI_GELU_GU (y = gelu(gate) * up, N/2 columns), EPI_PLE_GATE (y = gelu(acc) * ple[:, layer]).
+static void gemm(eg2_ctx* c, const void* x, long ldx, const void* W, int M, int N, int K, void* y, long ldy, int mode,
+                 bool out_f32, float scale = 1.f, const float* aux = nullptr, long aux_ld = 0, int aux_off = 0,
+                 void* tmp_f32 = nullptr) {
+    if (c->precision == EG2_F32) {
+        const float* A = (const float*)x;
+        if (mode == EPI_STORE) {
+            KL(gemm_f32(A, ldx, (const float*)W, K, (float*)y, ldy, M, N, K, scale, c->stream), "gemm_f32");
+        } else if (mode == EPI_GELU_GU) {
+            KL(gemm_f32(A, ldx, (const float*)W, K, (float*)tmp_f32, N, M, N, K, 1.f, c->stream), "gemm_f32");
+            KL((gelu_gu<float, float>((const float*)tmp_f32, (float*)y, M, N / 2, c->stream)), "gelu_gu");
+        } else {
+            KL(gemm_f32(A, ldx, (const float*)W, K, (float*)y, ldy, M, N, K, 1.f, c->stream), "gemm_f32");
+            KL((ple_gate<float, float>((const float*)y, (float*)y, aux, M, N, c->tc.layers, aux_off / N, c->stream)),
+               "ple_gate");
+        }
+        return;
+    }
+    GemmEpilogue e;
+    e.mode = mode;
+    e.out_f32 = out_f32 ? 1 : 0;
+    e.out = y;
+    e.ldo = ldy;
+    e.aux = aux;
+    e.aux_ld = aux_ld;
+    e.aux_off = aux_off;
+    e.scale = scale;
+    KL(gemm_tc(bf16_mode(c) ? GEMM_BF16 : GEMM_TF32, x, ldx, W, K, M, N, K, e, c->stream), "gemm_tc");
+}
+
+template <typename T>
+static void attention(eg2_ctx* c, const T* q, const T* k, const T* v, T* out, long rows, int nh, int nkv, int hd,
+                      int window, const int* seq_start, const int* seq_len, const AttnTile* tiles, int n_tiles);
+template <>
+void attention<float>(eg2_ctx* c, const float* q, const float* k, const float* v, float* out, long rows, int nh, int nkv,
+                      int hd, int window, const int* seq_start, const int* seq_len, const AttnTile*, int) {
+    KL(attention_simt<float>(q, k, v, out, seq_start, seq_len, rows, nh, nkv, hd, window, c->stream), "attention_simt");
+}
+template <>
+void attention<bf16_t>(eg2_ctx* c, const bf16_t* q, const bf16_t* k, const bf16_t* v, bf16_t* out, long rows, int nh,
+                       int nkv, int hd, int window, const int* seq_start, const int* seq_len, const AttnTile* tiles,
+                       int n_tiles) {
+    if (c->use_tc_attention && tiles)
+        KL(attention_tc(q, k, v, out, rows, tiles, n_tiles, nh, nkv, hd, window, c->stream), "attention_tc");
+    else
+        KL(attention_simt<bf16_t>(q, k, v, out, seq_start, seq_len, rows, nh, nkv, hd, window, c->stream), "attention_simt");
+}
+
+// ---------------------------------------------------------------------------------------------
+// Text backbone over w.hidden (rows x hidden f32, already holding the input embeddings).
+// Per-layer tile lists: tiles_by_cfg[k] covers layers whose (nkv) matches tile_nkv[k].
+// ---------------------------------------------------------------------------------------------
+struct TileSet {
+    int nkv;
+    long offset;  // into w.tiles
+    int count;
+};
+
+template <typename T>
+static void enqueue_text(eg2_ctx* c, long rows, const std::vector<TileSet>& tsets) {
+    const TextCfg& tc = c->tc;
+    Work& w = c->w;
+    const int h = tc.hidden, p = tc.ple, nl = tc.layers, nh = tc.nh, ff = tc.inter;
+    const float eps = tc.eps;
+    const bool f32 = std::is_same<T, float>::value;
+    T* t = (T*)w.t;
+    mark(c, "start");
+    // PLE prologue: ple = rmsnorm(embeds . W_ple^T * h^-0.5) * ple_norm per (token, layer) row.
+    const void* x_in = w.hidden;
+    if (!f32) {
+        KL(cast_rows<bf16_t>(w.hidden, (bf16_t*)w.t, rows * h, 1.f, 0.f, c->stream), "cast");
+        x_in = w.t;
+    }
+    gemm(c, x_in, h, c->ple_proj, (int)rows, nl * p, h, w.ple, (long)nl * p, EPI_STORE, true, powf((float)h, -0.5f));
+    mark(c, "gemm ple_model");
+    KL(rms_norm_inplace(w.ple, c->ple_norm, rows * nl, p, eps, 1.f, c->stream), "rms_norm ple");
+    KL(rms_norm_rows<T>(w.hidden, t, c->layers[0].input_ln, rows, h, eps, 1.f, c->stream), "rms_norm");
+    mark(c, "norms (ple, first)");
+    for (int i = 0; i < nl; i++) {
+        const LayerW& L = c->layers[i];
+        const int hd = L.hd, nkv = L.nkv;
+        const int nqkv = (nh + 2 * nkv) * hd;
+        const RopeTab& rt = c->ropes[L.rope];
+        gemm(c, t, h, L.qkv, (int)rows, nqkv, h, w.qkv, nqkv, EPI_STORE, f32);
+        mark(c, "gemm qkv");
+        KL((qkv_post<T, T>((const T*)w.qkv, (T*)w.q, (T*)w.k, (T*)w.v, L.q_norm, L.k_norm, rt.cs, rt.sn, hd / 2, w.pos,
+                           rows, nh, nkv, hd, hd, eps, c->stream)),
+           "qkv_post");
+        mark(c, "qkv_post");
+        const AttnTile* tiles = nullptr;
+        int n_tiles = 0;
+        for (const TileSet& s : tsets)
+            if (s.nkv == nkv) {
+                tiles = w.tiles + s.offset;
+                n_tiles = s.count;
+            }
+        attention<T>(c, (const T*)w.q, (const T*)w.k, (const T*)w.v, (T*)w.a, rows, nh, nkv, hd,
+                     L.sliding ? tc.window : -1, w.seq_start, w.seq_len, tiles, n_tiles);
+        mark(c, hd == 256 ? "attention d256" : "attention d512");
+        gemm(c, w.a, nh * hd, L.o, (int)rows, h, nh * hd, w.o, h, EPI_STORE, f32);
+        mark(c, "gemm o");
+        KL((add_norm<T, T>(w.hidden, (const T*)w.o, L.post_attn_ln, t, L.pre_ff_ln, rows, h, eps, 1.f, c->stream)), "add_norm");
+        mark(c, "add_norm");
+        gemm(c, t, h, L.gu, (int)rows, 2 * ff, h, w.gate, ff, EPI_GELU_GU, f32, 1.f, nullptr, 0, 0, w.gu);
+        mark(c, "gemm gate|up + gelu");
+        gemm(c, w.gate, ff, L.down, (int)rows, h, ff, w.o, h, EPI_STORE, f32);
+        mark(c, "gemm down");
+        // t = hidden (as the per-layer-input gate's input, bf16 in bf16 mode).
+        KL((add_norm<T, T>(w.hidden, (const T*)w.o, L.post_ff_ln, t, nullptr, rows, h, eps, 1.f, c->stream)), "add_norm");
+        mark(c, "add_norm");
+        gemm(c, t, h, L.pg, (int)rows, p, h, w.pg, p, EPI_PLE_GATE, f32, 1.f, w.ple, (long)nl * p, i * p);
+        mark(c, "gemm ple_gate");
+        gemm(c, w.pg, p, L.pp, (int)rows, h, p, w.o, h, EPI_STORE, f32);
+        mark(c, "gemm ple_proj");
+        const float* next_w = (i + 1 < nl) ? c->layers[i + 1].input_ln : c->final_norm;
+        KL((add_norm<T, T>(w.hidden, (const T*)w.o, L.ple_post_norm, t, next_w, rows, h, eps, L.layer_scalar, c->stream)),
+           "add_norm");
+        mark(c, "add_norm");
+    }
+    gemm(c, t, h, c->emb_proj, (int)rows, tc.emb, h, w.out, tc.emb, EPI_STORE, true);
+    mark(c, "gemm embed_proj");
+}
+
+// Row metadata and attention tile lists for sequences packed back to back.
+static std::vector<TileSet> prepare_pass(eg2_ctx* c, const int32_t* lens, int n_seq, long rows) {
+    const TextCfg& tc = c->tc;
+    std::vector<int> pos(rows), st(rows), ln(rows);
+    long r = 0;
+    long max_len = 0;
+    for (int s = 0; s < n_seq; s++) {
+        for (int i = 0; i < lens[s]; i++, r++) {
+            pos[r] = i;
+            st[r] = (int)(r - i);
+            ln[r] = lens[s];
+        }
+        max_len = std::max<long>(max_len, lens[s]);
+    }
+    std::vector<int> kinds;
+    for (auto& L : c->layers)
+        if (std::find(kinds.begin(), kinds.end(), L.nkv) == kinds.end()) kinds.push_back(L.nkv);
+    std::vector<TileSet> sets;
+    std::vector<AttnTile> tiles;
+    if (bf16_mode(c) && c->use_tc_attention) {
+        for (int nkv : kinds) {
+            TileSet ts;
+            ts.nkv = nkv;
+            ts.offset = (long)tiles.size();
+            const int tq = attention_tc_tile_tokens(tc.nh, nkv);
+            long row0 = 0;
+            for (int s = 0; s < n_seq; s++) {
+                for (int q0 = 0; q0 < lens[s]; q0 += tq) tiles.push_back(AttnTile{(int)row0, lens[s], q0});
+                row0 += lens[s];
+            }
+            ts.count = (int)(tiles.size() - ts.offset);
+            sets.push_back(ts);
+        }
+    }
+    ensure_work(c, rows, (long)tiles.size());
+    ensure_rope(c, max_len);
+    Work& w = c->w;
+    CK(cudaMemcpyAsync(w.pos, pos.data(), rows * 4, cudaMemcpyHostToDevice, c->stream));
+    CK(cudaMemcpyAsync(w.seq_start, st.data(), rows * 4, cudaMemcpyHostToDevice, c->stream));
+    CK(cudaMemcpyAsync(w.seq_len, ln.data(), rows * 4, cudaMemcpyHostToDevice, c->stream));
+    if (!tiles.empty())
+        CK(cudaMemcpyAsync(w.tiles, tiles.data(), tiles.size() * sizeof(AttnTile), cudaMemcpyHostToDevice, c->stream));
+    // The host vectors die at return: make the copies complete first.
+    CK(cudaStreamSynchronize(c->stream));
+    return sets;
+}
+
+static long check_lens(const int32_t* lens, int n_seq) {
+    if (n_seq < 0 || (n_seq > 0 && !lens)) fail(EG2_ERR_INVALID, "bad sequence list");
+    long rows = 0;
+    for (int s = 0; s < n_seq; s++) {
+        if (lens[s] <= 0) fail(EG2_ERR_INVALID, "empty token sequence (index %d)", s);
+        rows += lens[s];
+    }
+    if (rows > (1L << 30)) fail(EG2_ERR_INVALID, "too many rows");
+    return rows;
+}
+
+static void check_device_status(eg2_ctx* c) {
+    int st = 0;
+    CK(cudaStreamSynchronize(c->stream));
+    CK(cudaMemcpyFromSymbol(&st, eg2_dev_status, sizeof(int)));
+    if (st) {
+        int zero = 0;
+        cudaMemcpyToSymbol(eg2_dev_status, &zero, sizeof(int));
+        fail(EG2_ERR_TIMEOUT, "a device-side wait ran out (code %d)", st);
+    }
+}
+
+static void run_text(eg2_ctx* c, long rows, const std::vector<TileSet>& sets) {
+    if (bf16_mode(c))
+        enqueue_text<bf16_t>(c, rows, sets);
+    else
+        enqueue_text<float>(c, rows, sets);
+}
+
+// ---------------------------------------------------------------------------------------------
+// Vision tower (src/vision.rs:223-273)
+// ---------------------------------------------------------------------------------------------
+template <typename T>
+static void enqueue_vision(eg2_ctx* c, long n, int gh, int gw) {
+    const VisionCfg& vc = c->vc;
+    const int h = vc.hidden, ff = vc.inter, nh = vc.nh, nkv = vc.nkv, hd = vc.hd, pd = 3 * vc.patch * vc.patch;
+    const bool f32 = std::is_same<T, float>::value;
+    const float eps = vc.eps;
+    T* t = (T*)c->v_t;
+    mark(c, "start");
+    // v_t holds 2 (x - 0.5) in the GEMM storage type (written by the caller).
+    gemm(c, c->v_t, pd, c->v_input_proj, (int)n, h, pd, c->v_hidden, h, EPI_STORE, true);
+    KL(vision_add_positions(c->v_hidden, c->v_pos_table, c->v_pos, n, h, vc.pos_size, c->stream), "positions");
+    mark(c, "vision input");
+    KL(rms_norm_rows<T>(c->v_hidden, t, c->vlayers[0].input_ln, n, h, eps, 1.f, c->stream), "rms_norm");
+    const int nqkv = (nh + 2 * nkv) * hd;
+    for (int l = 0; l < vc.layers; l++) {
+        const VLayerW& L = c->vlayers[l];
+        gemm(c, t, h, L.qkv, (int)n, nqkv, h, c->v_qkv, nqkv, EPI_STORE, f32);
+        KL((qkv_post<T, T>((const T*)c->v_qkv, (T*)c->v_q, (T*)c->v_k, (T*)c->v_v, L.q_norm, L.k_norm, c->v_cs, c->v_sn,
+                           hd / 2, nullptr, n, nh, nkv, hd, hd / 2, eps, c->stream)),
+           "qkv_post");
+        mark(c, "vision qkv");
+        if (f32)
+            KL(attention_simt<float>((const float*)c->v_q, (const float*)c->v_k, (const float*)c->v_v, (float*)c->v_a,
+                                     c->v_seq_start, c->v_seq_len, n, nh, nkv, hd, -1, c->stream),
+               "attention");
+        else
+            KL(attention_simt<bf16_t>((const bf16_t*)c->v_q, (const bf16_t*)c->v_k, (const bf16_t*)c->v_v, (bf16_t*)c->v_a,
+                                      c->v_seq_start, c->v_seq_len, n, nh, nkv, hd, -1, c->stream),
+               "attention");
+        mark(c, "vision attention");
+        gemm(c, c->v_a, nh * hd, L.o, (int)n, h, nh * hd, c->v_o, h, EPI_STORE, f32);
+        KL((add_norm<T, T>(c->v_hidden, (const T*)c->v_o, L.post_attn_ln, t, L.pre_ff_ln, n, h, eps, 1.f, c->stream)), "add_norm");
+        gemm(c, t, h, L.gu, (int)n, 2 * ff, h, c->v_gate, ff, EPI_GELU_GU, f32, 1.f, nullptr, 0, 0, c->v_gu);
+        gemm(c, c->v_gate, ff, L.down, (int)n, h, ff, c->v_o, h, EPI_STORE, f32);
+        const float* next_w = (l + 1 < vc.layers) ? c->vlayers[l + 1].input_ln : nullptr;
+        KL((add_norm<T, T>(c->v_hidden, (const T*)c->v_o, L.post_ff_ln, next_w ? t : (T*)nullptr, next_w, n, h, eps, 1.f,
+                           c->stream)),
+           "add_norm");
+        mark(c, "vision mlp");
+    }
+    const int oh = gh / vc.pool, ow = gw / vc.pool;
+    KL(vision_pool(c->v_hidden, c->v_pooled, gh, gw, h, vc.pool, sqrtf((float)h), c->stream), "vision_pool");
+    // Multimodal embedder: scale-free RMSNorm, then 768 -> text hidden in f32 (src/vision.rs:167-170).
+    float* normed = (float*)c->v_o;  // reuse: oh*ow*h f32 fits (act buffer sized n*h*4)
+    KL(rms_norm_rows<float>(c->v_pooled, normed, nullptr, (long)oh * ow, h, eps, 1.f, c->stream), "rms_norm");
+    KL(gemm_f32(normed, h, (const float*)c->v_embed_proj, h, c->v_soft, c->tc.hidden, oh * ow, c->tc.hidden, h, 1.f,
+                c->stream),
+       "gemm_f32");
+    mark(c, "vision pool + embed");
+}
+
+}  // namespace eg2
+
+using namespace eg2;
+
+eg2_ctx::~eg2_ctx() {
+    if (stream) cudaStreamSynchronize(stream);
+    for (void* p : allocs) cudaFree(p);
+    for (auto& m : marks) cudaEventDestroy(m.second);
+    for (auto e : event_pool) cudaEventDestroy(e);
+    if (own_stream) cudaStreamDestroy(own_stream);
+}
+
+static thread_local std::string g_open_error;
+
+template <typename F>
+static int guarded(eg2_ctx* c, F&& f) {
+    if (!c) return EG2_ERR_INVALID;
+    std::lock_guard<std::mutex> lk(c->mu);
+    int prev = 0;
+    cudaGetDevice(&prev);
+    if (prev != c->device) cudaSetDevice(c->device);
+    int rc = EG2_OK;
+    try {
+        f();
+    } catch (Fail& e) {
+        c->err = e.msg;
+        rc = e.code;
+        c->marks.clear();
+    } catch (std::exception& e) {
+        c->err = e.what();
+        rc = EG2_ERR_INVALID;
+    }
+    if (prev != c->device) cudaSetDevice(prev);
+    return rc;
+}
+
+extern "C" {
+
+int eg2_open(int device, int precision, const char* model_dir, eg2_ctx** out) {
+    if (!out || !model_dir || precision < EG2_F32 || precision > EG2_BF16) {
+        g_open_error = "invalid argument";
+        return EG2_ERR_INVALID;
+    }
+    *out = nullptr;
+    eg2_ctx* c = new eg2_ctx();
+    c->device = device;
+    c->precision = precision;
+    int prev = 0;
+    cudaGetDevice(&prev);
+    try {
+        CK(cudaSetDevice(device));
+        int major = 0, minor = 0;
+        CK(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device));
+        CK(cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, device));
+        if (major != 10 || minor != 0) fail(EG2_ERR_CUDA, "device %d is sm_%d%d; this library is built for sm_100a", device, major, minor);
+        CK(cudaStreamCreateWithFlags(&c->own_stream, cudaStreamNonBlocking));
+        c->stream = c->own_stream;
+        std::string dir(model_dir);
+        parse_config(dir, c->tc, c->vc);
+        SafeTensors st(dir + "/model.safetensors");
+        load_text(c, st);
+        load_vision(c, st);
+        c->bad_flag = (int*)dalloc(c, 4);
+        CK(cudaMemset(c->bad_flag, 0, 4));
+        const char* env = getenv("EG2_SIMT_ATTENTION");
+        if (env && env[0] == '1') c->use_tc_attention = false;
+        CK(cudaDeviceSynchronize());
+    } catch (Fail& e) {
+        g_open_error = e.msg;
+        delete c;
+        cudaSetDevice(prev);
+        return e.code;
+    } catch (std::exception& e) {
+        g_open_error = e.what();
+        delete c;
+        cudaSetDevice(prev);
+        return EG2_ERR_IO;
+    }
+    cudaSetDevice(prev);
+    *out = c;
+    return EG2_OK;
+}
+
+void eg2_close(eg2_ctx* c) {
+    if (!c) return;
+    int prev = 0;
+    cudaGetDevice(&prev);
+    cudaSetDevice(c->device);
+    delete c;
+    cudaSetDevice(prev);
+}
+
+const char* eg2_last_error(const eg2_ctx* c) { return c ? c->err.c_str() : g_open_error.c_str(); }
+
+int eg2_text_dims(const eg2_ctx* c, int* hidden, int* emb, int64_t* vocab, int* layers) {
+    if (!c) return EG2_ERR_INVALID;
+    if (hidden) *hidden = c->tc.hidden;
+    if (emb) *emb = c->tc.emb;
+    if (vocab) *vocab = c->tc.vocab;
+    if (layers) *layers = c->tc.layers;
+    return EG2_OK;
+}
+
+int eg2_set_stream(eg2_ctx* c, void* stream) {
+    return guarded(c, [&] {
+        CK(cudaStreamSynchronize(c->stream));
+        c->stream = stream ? (cudaStream_t)stream : c->own_stream;
+    });
+}
+
+int eg2_embed_tokens(eg2_ctx* c, const uint32_t* ids, int64_t n, float* out) {
+    return guarded(c, [&] {
+        if (n < 0 || (n > 0 && (!ids || !out))) fail(EG2_ERR_INVALID, "bad arguments");
+        if (n == 0) return;
+        for (int64_t i = 0; i < n; i++)
+            if ((int64_t)ids[i] >= c->tc.vocab) fail(EG2_ERR_INVALID, "token id %u out of range", ids[i]);
+        ensure_work(c, n, 0);
+        Work& w = c->w;
+        CK(cudaMemcpyAsync(w.ids, ids, n * 4, cudaMemcpyHostToDevice, c->stream));
+        KL(embed_gather(c->embed_table, c->tc.vocab, c->tc.hidden, w.ids, n, sqrtf((float)c->tc.hidden), w.hidden,
+                        c->bad_flag, c->stream),
+           "embed_gather");
+        CK(cudaMemcpyAsync(out, w.hidden, n * c->tc.hidden * 4, cudaMemcpyDeviceToHost, c->stream));
+        CK(cudaStreamSynchronize(c->stream));
+    });
+}
+
+static int forward_impl(eg2_ctx* c, const float* embeds, const int32_t* lens, int n_seq, float* out, void* stream,
+                        bool device_ptrs) {
+    return guarded(c, [&] {
+        cudaStream_t saved = c->stream;
+        if (stream) c->stream = (cudaStream_t)stream;
+        struct Restore {
+            eg2_ctx* c;
+            cudaStream_t s;
+            ~Restore() { c->stream = s; }
+        } restore{c, saved};
+        const long rows = check_lens(lens, n_seq);
+        if (rows == 0) return;
+        if (!embeds || !out) fail(EG2_ERR_INVALID, "null buffer");
+        auto sets = prepare_pass(c, lens, n_seq, rows);
+        Work& w = c->w;
+        CK(cudaMemcpyAsync(w.hidden, embeds, rows * c->tc.hidden * 4,
+                           device_ptrs ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, c->stream));
+        run_text(c, rows, sets);
+        CK(cudaMemcpyAsync(out, w.out, rows * c->tc.emb * 4, device_ptrs ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost,
+                           c->stream));
+        check_device_status(c);
+        collect_marks(c);
+    });
+}
+
+int eg2_forward_packed(eg2_ctx* c, const float* embeds, const int32_t* lens, int n_seq, float* out) {
+    return forward_impl(c, embeds, lens, n_seq, out, nullptr, false);
+}
+int eg2_forward_packed_device(eg2_ctx* c, const float* embeds, const int32_t* lens, int n_seq, float* out, void* stream) {
+    return forward_impl(c, embeds, lens, n_seq, out, stream, true);
+}
+
+static int embed_impl(eg2_ctx* c, const uint32_t* ids, const int32_t* lens, int n_seq, const int32_t* dims, int n_dims,
+                      float* out, void* stream, bool device_ptrs) {
+    return guarded(c, [&] {
+        cudaStream_t saved = c->stream;
+        if (stream) c->stream = (cudaStream_t)stream;
+        struct Restore {
+            eg2_ctx* c;
+            cudaStream_t s;
+            ~Restore() { c->stream = s; }
+        } restore{c, saved};
+        const long rows = check_lens(lens, n_seq);
+        if (rows == 0) return;
+        if (!ids || !out || !dims || n_dims <= 0 || n_dims > 16) fail(EG2_ERR_INVALID, "bad arguments");
+        int total = 0;
+        for (int d = 0; d < n_dims; d++) {
+            if (dims[d] <= 0 || dims[d] > c->tc.emb) fail(EG2_ERR_INVALID, "truncate_dim %d out of range 1..=%d", dims[d], c->tc.emb);
+            total += dims[d];
+        }
+        if (!device_ptrs)
+            for (long i = 0; i < rows; i++)
+                if ((int64_t)ids[i] >= c->tc.vocab) fail(EG2_ERR_INVALID, "token id %u out of range", ids[i]);
+        auto sets = prepare_pass(c, lens, n_seq, rows);
+        Work& w = c->w;
+        if ((long)n_seq * total > w.pooled_cap || !w.dims) {
+            CK(cudaStreamSynchronize(c->stream));
+            dfree(c, w.pooled);
+            w.pooled_cap = std::max((long)n_seq * total, 4096L);
+            w.pooled = (float*)dalloc(c, w.pooled_cap * 4);
+            if (!w.dims) w.dims = (int*)dalloc(c, 64);
+        }
+        std::vector<int> st(n_seq), ln(n_seq);
+        long r = 0;
+        for (int s = 0; s < n_seq; s++) {
+            st[s] = (int)r;
+            ln[s] = lens[s];
+            r += lens[s];
+        }
+        // Per-sequence start / length for the pool kernel.
+        if (n_seq > w.seq_meta_cap) {
+            CK(cudaStreamSynchronize(c->stream));
+            dfree(c, w.seq_meta);
+            w.seq_meta_cap = std::max(n_seq, 1024);
+            w.seq_meta = (int*)dalloc(c, 2L * w.seq_meta_cap * 4);
+        }
+        int* seq_meta = w.seq_meta;
+        CK(cudaMemcpyAsync(seq_meta, st.data(), n_seq * 4, cudaMemcpyHostToDevice, c->stream));
+        CK(cudaMemcpyAsync(seq_meta + n_seq, ln.data(), n_seq * 4, cudaMemcpyHostToDevice, c->stream));
+        CK(cudaMemcpyAsync(w.dims, dims, n_dims * 4, cudaMemcpyHostToDevice, c->stream));
+        CK(cudaMemsetAsync(c->bad_flag, 0, 4, c->stream));
+        CK(cudaMemcpyAsync(w.ids, ids, rows * 4, device_ptrs ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, c->stream));
+        KL(embed_gather(c->embed_table, c->tc.vocab, c->tc.hidden, w.ids, rows, sqrtf((float)c->tc.hidden), w.hidden,
+                        c->bad_flag, c->stream),
+           "embed_gather");
+        run_text(c, rows, sets);
+        KL(pool_rows(w.out, seq_meta, seq_meta + n_seq, n_seq, c->tc.emb, w.dims, n_dims, total, w.pooled, c->stream), "pool");
+        mark(c, "pool");
+        CK(cudaMemcpyAsync(out, w.pooled, (size_t)n_seq * total * 4,
+                           device_ptrs ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost, c->stream));
+        int bad = 0;
+        CK(cudaMemcpyAsync(&bad, c->bad_flag, 4, cudaMemcpyDeviceToHost, c->stream));
+        check_device_status(c);
+        collect_marks(c);
+        if (bad) fail(EG2_ERR_INVALID, "token id out of range");
+    });
+}
+
+int eg2_embed_packed(eg2_ctx* c, const uint32_t* ids, const int32_t* lens, int n_seq, const int32_t* dims, int n_dims,
+                     float* out) {
+    return embed_impl(c, ids, lens, n_seq, dims, n_dims, out, nullptr, false);
+}
+int eg2_embed_packed_device(eg2_ctx* c, const uint32_t* ids, const int32_t* lens, int n_seq, const int32_t* dims,
+                            int n_dims, float* out, void* stream) {
+    return embed_impl(c, ids, lens, n_seq, dims, n_dims, out, stream, true);
+}
+
+int eg2_vision_encode(eg2_ctx* c, const float* patches, const int32_t* pos_xy, int gh, int gw, float* out_pooled,
+                      float* out_soft) {
+    return guarded(c, [&] {
+        VisionCfg& vc = c->vc;
+        if (!vc.present) fail(EG2_ERR_INVALID, "the checkpoint has no vision tower");
+        const int k = vc.pool;
+        const long n = (long)gh * gw;
+        if (gh <= 0 || gw <= 0 || gh % k || gw % k)
+            fail(EG2_ERR_INVALID, "patch grid %dx%d is empty or not divisible by the pooling kernel %d", gh, gw, k);
+        if (!patches || !pos_xy) fail(EG2_ERR_INVALID, "null buffer");
+        for (long t = 0; t < n; t++)
+            if (pos_xy[2 * t] < 0 || pos_xy[2 * t] >= vc.pos_size || pos_xy[2 * t + 1] < 0 || pos_xy[2 * t + 1] >= vc.pos_size)
+                fail(EG2_ERR_INVALID, "patch position outside the %d-entry position table", vc.pos_size);
+        const int h = vc.hidden, ff = vc.inter, nh = vc.nh, nkv = vc.nkv, hd = vc.hd, pd = 3 * vc.patch * vc.patch;
+        const size_t as = act_size(c);
+        if (n > c->vcap) {
+            CK(cudaStreamSynchronize(c->stream));
+            void** bufs[] = {(void**)&c->v_hidden, (void**)&c->v_pooled, (void**)&c->v_cs, (void**)&c->v_sn, (void**)&c->v_soft,
+                             &c->v_x, &c->v_t, &c->v_qkv, &c->v_q, &c->v_k, &c->v_v, &c->v_a, &c->v_o, &c->v_gate, &c->v_gu,
+                             (void**)&c->v_pos, (void**)&c->v_seq_start, (void**)&c->v_seq_len};
+            for (void** b : bufs) {
+                dfree(c, *b);
+                *b = nullptr;
+            }
+            const long cap = ((n + 1023) / 1024) * 1024;
+            c->v_hidden = (float*)dalloc(c, cap * h * 4);
+            c->v_pooled = (float*)dalloc(c, cap * h * 4);
+            c->v_soft = (float*)dalloc(c, cap * c->tc.hidden * 4);
+            c->v_cs = (float*)dalloc(c, cap * (hd / 2) * 4);
+            c->v_sn = (float*)dalloc(c, cap * (hd / 2) * 4);
+            c->v_x = dalloc(c, cap * pd * 4);
+            c->v_t = dalloc(c, cap * std::max(h, pd) * as);
+            c->v_qkv = dalloc(c, cap * (nh + 2 * nkv) * hd * as);
+            c->v_q = dalloc(c, cap * nh * hd * as);
+            c->v_k = dalloc(c, cap * nkv * hd * as);
+            c->v_v = dalloc(c, cap * nkv * hd * as);
+            c->v_a = dalloc(c, cap * nh * hd * as);
+            c->v_o = dalloc(c, cap * h * 4);
+            c->v_gate = dalloc(c, cap * ff * as);
+            c->v_gu = c->precision == EG2_F32 ? dalloc(c, cap * 2L * ff * 4) : nullptr;
+            c->v_pos = (int*)dalloc(c, cap * 2 * 4);
+            c->v_seq_start = (int*)dalloc(c, cap * 4);
+            c->v_seq_len = (int*)dalloc(c, cap * 4);
+            c->vcap = cap;
+        }
+        // Axial RoPE tables [n, hd / 2]: x angles in the first hd / 4 entries, y in the next (src/vision.rs:114-136).
+        std::vector<float> inv = rope_inv_freq(vc.theta, hd / 2);
+        const int q4 = hd / 4;
+        std::vector<float> cs((size_t)n * (hd / 2)), sn((size_t)n * (hd / 2));
+        for (long t = 0; t < n; t++)
+            for (int axis = 0; axis < 2; axis++)
+                for (int i = 0; i < q4; i++) {
+                    const float f = (float)pos_xy[2 * t + axis] * inv[i];
+                    cs[(size_t)t * (hd / 2) + axis * q4 + i] = cosf(f);
+                    sn[(size_t)t * (hd / 2) + axis * q4 + i] = sinf(f);
+                }
+        std::vector<int> zeros(n, 0), lens_v(n, (int)n);
+        CK(cudaMemcpyAsync(c->v_cs, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice, c->stream));
+        CK(cudaMemcpyAsync(c->v_sn, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice, c->stream));
+        CK(cudaMemcpyAsync(c->v_pos, pos_xy, n * 2 * 4, cudaMemcpyHostToDevice, c->stream));
+        CK(cudaMemcpyAsync(c->v_seq_start, zeros.data(), n * 4, cudaMemcpyHostToDevice, c->stream));
+        CK(cudaMemcpyAsync(c->v_seq_len, lens_v.data(), n * 4, cudaMemcpyHostToDevice, c->stream));
+        CK(cudaMemcpyAsync(c->v_x, patches, n * pd * 4, cudaMemcpyHostToDevice, c->stream));
+        // 2 (x - 0.5) into the GEMM input buffer in the storage type.
+        if (bf16_mode(c))
+            KL(cast_rows<bf16_t>((const float*)c->v_x, (bf16_t*)c->v_t, n * pd, 2.f, -0.5f, c->stream), "cast");
+        else
+            KL(cast_rows<float>((const float*)c->v_x, (float*)c->v_t, n * pd, 2.f, -0.5f, c->stream), "cast");
+        if (bf16_mode(c))
+            enqueue_vision<bf16_t>(c, n, gh, gw);
+        else
+            enqueue_vision<float>(c, n, gh, gw);
+        const long no = (long)(gh / k) * (gw / k);
+        if (out_pooled) CK(cudaMemcpyAsync(out_pooled, c->v_pooled, no * h * 4, cudaMemcpyDeviceToHost, c->stream));
+        if (out_soft) CK(cudaMemcpyAsync(out_soft, c->v_soft, no * c->tc.hidden * 4, cudaMemcpyDeviceToHost, c->stream));
+        check_device_status(c);
+        collect_marks(c);
+    });
+}
+
+int eg2_profile(eg2_ctx* c, int enable) {
+    return guarded(c, [&] {
+        c->profiling = enable != 0;
+        c->prof.clear();
+    });
+}
+
+int eg2_profile_read(eg2_ctx* c, char* buf, int cap) {
+    return guarded(c, [&] {
+        std::string s = "{";
+        bool first = true;
+        for (auto& kv : c->prof) {
+            char item[256];
+            snprintf(item, sizeof item, "%s\"%s\": [%.6f, %ld]", first ? "" : ", ", kv.first.c_str(), kv.second.first,
+                     kv.second.second);
+            s += item;
+            first = false;
+        }
+        s += "}";
+        if (!buf || cap <= (int)s.size()) fail(EG2_ERR_INVALID, "buffer too small (%zu bytes needed)", s.size() + 1);
+        memcpy(buf, s.c_str(), s.size() + 1);
+    });
+}
+
+int eg2_gemm(int kind, const void* A, int64_t lda, const void* W, int64_t ldw, void* C, int64_t ldc, int M, int N, int K,
+             int out_f32, void* stream) {
+    if (!A || !W || !C || M < 0 || N <= 0 || K <= 0) return EG2_ERR_INVALID;
+    cudaStream_t s = (cudaStream_t)stream;
+    int rc;
+    if (kind == EG2_F32) {
+        rc = gemm_f32((const float*)A, lda, (const float*)W, ldw, (float*)C, ldc, M, N, K, 1.f, s);
+    } else if (kind == EG2_BF16 || kind == EG2_TF32) {
+        GemmEpilogue e;
+        e.mode = EPI_STORE;
+        e.out_f32 = (kind == EG2_TF32 || out_f32) ? 1 : 0;
+        e.out = C;
+        e.ldo = ldc;
+        rc = gemm_tc(kind == EG2_BF16 ? GEMM_BF16 : GEMM_TF32, A, lda, W, ldw, M, N, K, e, s);
+    } else {
+        return EG2_ERR_INVALID;
+    }
+    if (rc == -1) return EG2_ERR_INVALID;
+    return rc ? EG2_ERR_CUDA : EG2_OK;
+}
+
+int eg2_attention(int kind, const void* q, const void* k, const void* v, void* out, const int32_t* lens, int n_seq, int nh,
+                  int nkv, int hd, int window, void* stream) {
+    if (!q || !k || !v || !out || !lens || n_seq <= 0 || nh <= 0 || nkv <= 0 || nh % nkv) return EG2_ERR_INVALID;
+    cudaStream_t s = (cudaStream_t)stream;
+    long rows = 0;
+    for (int i = 0; i < n_seq; i++) {
+        if (lens[i] <= 0) return EG2_ERR_INVALID;
+        rows += lens[i];
+    }
+    std::vector<int> st(rows), ln(rows);
+    std::vector<AttnTile> tiles;
+    long r = 0;
+    const int tq = kind == EG2_BF16 ? attention_tc_tile_tokens(nh, nkv) : 0;
+    if (kind == EG2_BF16 && tq <= 0) return EG2_ERR_INVALID;
+    for (int i = 0; i < n_seq; i++) {
+        for (int j = 0; j < lens[i]; j++) {
+            st[r + j] = (int)r;
+            ln[r + j] = lens[i];
+        }
+        if (tq > 0)
+            for (int q0 = 0; q0 < lens[i]; q0 += tq) tiles.push_back(AttnTile{(int)r, lens[i], q0});
+        r += lens[i];
+    }
+    int* meta = nullptr;
+    AttnTile* dt = nullptr;
+    if (cudaMalloc(&meta, 2 * rows * 4) != cudaSuccess) return EG2_ERR_OOM;
+    if (!tiles.empty() && cudaMalloc(&dt, tiles.size() * sizeof(AttnTile)) != cudaSuccess) {
+        cudaFree(meta);
+        return EG2_ERR_OOM;
+    }
+    cudaMemcpyAsync(meta, st.data(), rows * 4, cudaMemcpyHostToDevice, s);
+    cudaMemcpyAsync(meta + rows, ln.data(), rows * 4, cudaMemcpyHostToDevice, s);
+    if (dt) cudaMemcpyAsync(dt, tiles.data(), tiles.size() * sizeof(AttnTile), cudaMemcpyHostToDevice, s);
+    int rc;
+    if (kind == EG2_F32)
+        rc = attention_simt<float>((const float*)q, (const float*)k, (const float*)v, (float*)out, meta, meta + rows, rows, nh,
+                                   nkv, hd, window, s);
+    else if (kind == EG2_BF16)
+        rc = attention_tc((const bf16_t*)q, (const bf16_t*)k, (const bf16_t*)v, (bf16_t*)out, rows, dt, (int)tiles.size(),
+                          nh, nkv, hd, window, s);
+    else
+        rc = -1;
+    cudaStreamSynchronize(s);
+    cudaFree(meta);
+    if (dt) cudaFree(dt);
+    if (rc == -1) return EG2_ERR_INVALID;
+    if (rc) return EG2_ERR_CUDA;
+    int stv = 0;
+    cudaMemcpyFromSymbol(&stv, eg2_dev_status, sizeof(int));
+    return stv ? EG2_ERR_TIMEOUT : EG2_OK;
+}
+
+int eg2_device_status(void) {
+    int st = 0;
+    cudaMemcpyFromSymbol(&st, eg2_dev_status, sizeof(int));
+    return st;
+}
+void eg2_device_status_reset(void) {
+    int zero = 0;
+    cudaMemcpyToSymbol(eg2_dev_status, &zero, sizeof(int));
+}
+
+}  // extern "C"

@@ -1,0 +1,122 @@
+/*
+ * eg2.h -- C ABI of the B200-native EmbeddingGemma 2 text-backbone and vision-tower library
+ * (libeg2_b200.so, built for sm_100a).
+ *
+ * It is the drop-in for the reference engine's device backends. Each entry point names the
+ * reference interface it replaces (paths inside the reference project):
+ *
+ *   eg2_open / eg2_close          GpuText::from_cpu + Gpu::new (src/gpu/text.rs:177-219,
+ *                                 src/gpu/mod.rs:281-403), reading the checkpoint like
+ *                                 Weights::open + TextModel::load (src/weights.rs:46-86, src/text.rs:67-114)
+ *   eg2_embed_tokens              TextBackend::embed_tokens (src/backend.rs:64-70, src/text.rs:53-64)
+ *   eg2_forward_packed            TextBackend::forward_packed (src/backend.rs:73-79,
+ *                                 src/gpu/text.rs:436-529): [rows, 512] f32 in, [rows, 768] f32 out
+ *   eg2_embed_packed              EmbeddingGemma2::embed_prepared's text tail + truncate_and_normalize
+ *                                 (src/model.rs:508-540, :677-688): ids in, pooled L2-normalised
+ *                                 embeddings (and Matryoshka cuts) out, all on the device
+ *   eg2_vision_encode             VisionBackend::encode (src/backend.rs:88-95, src/gpu/vision.rs:97-219)
+ *   eg2_gemm                      Gpu::gemm_bf16 / Gpu::matmul_nt (src/gpu/mod.rs:554-630)
+ *   eg2_attention                 Gpu::attention_act / attention_flash_packed (src/gpu/mod.rs:1217-1599)
+ *
+ * Conventions: every function returns 0 on success or a negative EG2_ERR_* code; the message of
+ * the last failure is available from eg2_last_error. A failure before the result is written
+ * leaves the output untouched. Calls on one context are serialised internally (the reference
+ * holds one lock per device, src/gpu/mod.rs:472-475); different contexts (GPUs) may be driven
+ * concurrently from different host threads. Host pointers are plain host memory; "_device"
+ * variants take device pointers and an optional CUDA stream (NULL: the context's own stream).
+ */
+#ifndef EG2_H
+#define EG2_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct eg2_ctx eg2_ctx;
+
+/* Precision of the matrix products (src/backend.rs:17-27). */
+enum {
+    EG2_F32 = 0,  /* f32 CUDA-core GEMMs and attention: float32 profile */
+    EG2_TF32 = 1, /* TF32 tensor-core GEMMs, f32 activations: tf32 profile */
+    EG2_BF16 = 2  /* bf16 tensor-core GEMMs and attention, f32 residual / norms: bf16 profile */
+};
+
+enum {
+    EG2_OK = 0,
+    EG2_ERR_INVALID = -1, /* bad argument (sizes, ids out of range, empty sequence) */
+    EG2_ERR_OOM = -2,     /* device or pinned host memory exhausted */
+    EG2_ERR_CUDA = -3,    /* a CUDA call failed */
+    EG2_ERR_TIMEOUT = -4, /* a bounded device wait ran out (the kernel returned an error status) */
+    EG2_ERR_IO = -5       /* checkpoint or config unreadable / malformed */
+};
+
+/* Open `model_dir` (config.json + model.safetensors in the reference's layout) on CUDA device
+ * `device`. Loads the text tower; the vision tower is loaded when present. */
+int eg2_open(int device, int precision, const char* model_dir, eg2_ctx** out);
+void eg2_close(eg2_ctx* ctx);
+/* Message of the last failure on `ctx` (or of the last failed eg2_open when ctx is NULL). */
+const char* eg2_last_error(const eg2_ctx* ctx);
+
+/* Model dimensions: hidden size, output (embedding) width, vocabulary size, layers. */
+int eg2_text_dims(const eg2_ctx* ctx, int* hidden, int* embedding_dim, int64_t* vocab, int* layers);
+
+/* Scaled token embeddings embed_tokens[id] * sqrt(hidden) for `n` ids into out [n, hidden]. */
+int eg2_embed_tokens(eg2_ctx* ctx, const uint32_t* ids, int64_t n, float* out);
+
+/* Per-token states [rows, embedding_dim] for `n_seq` sequences packed back to back
+ * (rows = sum(lens)); embeds [rows, hidden]. Host buffers. */
+int eg2_forward_packed(eg2_ctx* ctx, const float* embeds, const int32_t* lens, int n_seq, float* out);
+/* Same with device buffers; `lens` stays a host array. Work is enqueued on `stream` (or the
+ * context's stream) and the call returns after it completes. */
+int eg2_forward_packed_device(eg2_ctx* ctx, const float* embeds, const int32_t* lens, int n_seq, float* out,
+                              void* stream);
+
+/* Token ids of `n_seq` sequences packed back to back -> per sequence, the L2-normalised mean of
+ * the per-token states, followed by its Matryoshka cuts: for each dims[i] (dims[0] is normally
+ * embedding_dim) the first dims[i] components re-normalised. out [n_seq, sum(dims)]. Host buffers. */
+int eg2_embed_packed(eg2_ctx* ctx, const uint32_t* ids, const int32_t* lens, int n_seq, const int32_t* dims,
+                     int n_dims, float* out);
+int eg2_embed_packed_device(eg2_ctx* ctx, const uint32_t* ids, const int32_t* lens, int n_seq, const int32_t* dims,
+                            int n_dims, float* out, void* stream);
+
+/* Vision tower over one patched image: patches [n, 3*p*p] in [0, 1], pos_xy [n, 2] (x, y),
+ * n = grid_h * grid_w. out_pooled [n/k^2, vision_hidden] (3x3-pooled states * sqrt(hidden), the
+ * reference GPU tower's output) and out_soft [n/k^2, text_hidden] (after the multimodal
+ * embedder); either may be NULL. */
+int eg2_vision_encode(eg2_ctx* ctx, const float* patches, const int32_t* pos_xy, int grid_h, int grid_w,
+                      float* out_pooled, float* out_soft);
+
+/* Run on a caller-owned CUDA stream (cudaStream_t); NULL restores the context's own stream. */
+int eg2_set_stream(eg2_ctx* ctx, void* stream);
+
+/* Per-op device timing (CUDA events around each launch group, like the reference's
+ * EGEMMA2_PROFILE marks, src/gpu/mod.rs:437-469). eg2_profile_read writes a JSON object
+ * {"label": [ms_total, count], ...} accumulated since enabling. */
+int eg2_profile(eg2_ctx* ctx, int enable);
+int eg2_profile_read(eg2_ctx* ctx, char* buf, int cap);
+
+/* ---- single ops on device pointers (GEMM sweep and attention checks) ---- */
+
+/* C[M, N] = A[M, K] . W[N, K]^T. kind: EG2_BF16 (bf16 A/W, tcgen05), EG2_TF32 (f32 A/W,
+ * tcgen05 TF32), EG2_F32 (f32 CUDA cores). C is f32 when out_f32 != 0 or kind != EG2_BF16,
+ * else bf16. N must be a multiple of 256 and K of 64 on the tensor-core kinds. */
+int eg2_gemm(int kind, const void* A, int64_t lda, const void* W, int64_t ldw, void* C, int64_t ldc, int M, int N,
+             int K, int out_f32, void* stream);
+
+/* Block-diagonal bidirectional attention, scale 1, window radius `window` (< 0: global).
+ * q [rows, nh, hd], k / v [rows, nkv, hd], out [rows, nh, hd]; lens host array.
+ * kind: EG2_BF16 (bf16 storage, tcgen05 flash kernel), EG2_F32 (f32 CUDA cores). */
+int eg2_attention(int kind, const void* q, const void* k, const void* v, void* out, const int32_t* lens, int n_seq,
+                  int nh, int nkv, int hd, int window, void* stream);
+
+/* First error code recorded by a device-side bounded wait since the last reset (0: none). */
+int eg2_device_status(void);
+void eg2_device_status_reset(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* EG2_H */

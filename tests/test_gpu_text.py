@@ -1,0 +1,118 @@
+"""Text backbone parity through the C ABI against the CPU oracle, per precision profile
+(src/verify.rs:66-110): embeddings and their 512/256/128 Matryoshka cuts."""
+import json
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+import oracle as O
+from conftest import pkg
+
+B = pkg("backend")
+V = pkg("verify")
+L = pkg("lib")
+
+pytestmark = pytest.mark.gpu
+GOLDEN = Path(__file__).parent / "golden" / "golden_text.json"
+
+
+def ids_for(lens, seed):
+    rng = np.random.default_rng(seed)
+    return [rng.integers(0, 262144, size=n).astype(np.uint32) for n in lens]
+
+
+def check_embeddings(got: dict, want: np.ndarray, profile, label):
+    worst = 0.0
+    for i in range(want.shape[0]):
+        c = V.vec_check(f"{label}[{i}]", got[768][i], want[i], profile.embedding)
+        assert c.passed(), str(c)
+        worst = max(worst, c.max_abs)
+        for d in (512, 256, 128):
+            cut = O.truncate_and_normalize(want[i:i + 1], d)[0]
+            c = V.vec_check(f"{label}[{i}]@{d}", got[d][i], cut, profile.embedding)
+            assert c.passed(), str(c)
+    return worst
+
+
+@pytest.fixture(scope="module")
+def cases(oracle_text):
+    out = {}
+    for name, lens in {"short": [17, 3, 27, 1], "doc": [700], "mixed": [130, 600, 64, 65, 1100]}.items():
+        seqs = ids_for(lens, hash(name) % 1000)
+        out[name] = (seqs, oracle_text.embed_ids(seqs))
+    return out
+
+
+@pytest.mark.parametrize("prec", ["bf16", "tf32", "f32"])
+def test_embed_ids_parity(prec, cases, request):
+    dev = request.getfixturevalue(f"dev_{prec}")
+    tb = B.TextBackend(dev)
+    prof = V.for_precision(prec)
+    for name, (seqs, want) in cases.items():
+        got = tb.embed_ids(seqs)
+        w = check_embeddings(got, want, prof, f"{prec}/{name}")
+        print(f"{prec} {name}: worst max|d| {w:.2e}")
+
+
+@pytest.mark.parametrize("prec", ["bf16", "f32"])
+def test_forward_packed_rows(prec, oracle_text, request):
+    """The drop-in call itself: per-token states [rows, 768] for host embeddings."""
+    dev = request.getfixturevalue(f"dev_{prec}")
+    tb = B.TextBackend(dev)
+    lens = [5, 64, 200]
+    seqs = ids_for(lens, 9)
+    ids = np.concatenate(seqs)
+    e = oracle_text.embed_tokens(ids)
+    np.testing.assert_array_equal(tb.embed_tokens(ids), e)
+    got = tb.forward_packed(e, lens)
+    want = oracle_text.forward_packed(e, lens)
+    tol = 2e-5 if prec == "f32" else 0.08
+    assert np.abs(got - want).max() < tol * max(1.0, float(np.abs(want).max()))
+    if prec != "f32":
+        assert V.cosine(got, want) > 0.9999
+
+
+def test_golden_through_gpu(dev_bf16):
+    g = json.loads(GOLDEN.read_text())
+    tb = B.TextBackend(dev_bf16)
+    for case in g["cases"]:
+        got = tb.embed_ids([np.asarray(x, dtype=np.uint32) for x in case["ids"]])
+        for i, o in enumerate(case["outputs"]):
+            for key, d in (("emb", 768), ("emb512", 512), ("emb256", 256), ("emb128", 128)):
+                c = V.vec_check(f"golden {case['name']}[{i}]@{d}", got[d][i], o[key], V.BF16.embedding)
+                assert c.passed(), str(c)
+
+
+def test_long_documents_bf16(dev_bf16, oracle_text):
+    """Two 2208-token documents (the metric's length) against the oracle."""
+    seqs = ids_for([2208, 2208], 21)
+    want = oracle_text.embed_ids(seqs)
+    got = B.TextBackend(dev_bf16).embed_ids(seqs)
+    check_embeddings(got, want, V.BF16, "bf16/2208")
+
+
+def test_errors_leave_output_untouched(dev_bf16):
+    tb = B.TextBackend(dev_bf16)
+    with pytest.raises(L.Eg2Error):
+        tb.embed_ids([np.array([1, 2], np.uint32), np.array([], np.uint32)])
+    with pytest.raises(L.Eg2Error):
+        tb.embed_ids([np.array([1, 262144], np.uint32)])
+    with pytest.raises(L.Eg2Error):
+        tb.embed_ids([np.array([1, 2], np.uint32)], dims=(769,))
+    out = np.full((2, 768), 7.0, np.float32)
+    lib = L.load()
+    rc = lib.eg2_forward_packed(dev_bf16.handle, np.zeros((2, 512), np.float32).ctypes.data, L.i32_array([2, 0]), 2,
+                                out.ctypes.data)
+    assert rc == -1 and np.all(out == 7.0)
+    # The context stays usable after errors.
+    got = tb.embed_ids([np.array([5, 6, 7], np.uint32)])
+    assert np.isfinite(got[768]).all()
+
+
+def test_repeated_calls_are_deterministic(dev_bf16):
+    tb = B.TextBackend(dev_bf16)
+    seqs = ids_for([300, 17], 4)
+    a = tb.embed_ids(seqs)[768].copy()
+    b = tb.embed_ids(seqs)[768].copy()
+    np.testing.assert_array_equal(a, b)

@@ -1,0 +1,31 @@
+"""Vision tower parity (soft tokens) against the CPU oracle per profile."""
+import numpy as np
+import pytest
+
+from conftest import pkg
+
+B = pkg("backend")
+V = pkg("verify")
+
+pytestmark = pytest.mark.gpu
+
+
+def image(gh, gw, seed):
+    rng = np.random.default_rng(seed)
+    patches = rng.random((gh * gw, 768), dtype=np.float32)
+    pos = np.array([[x, y] for y in range(gh) for x in range(gw)], dtype=np.int32)
+    return patches, pos
+
+
+@pytest.mark.parametrize("prec", ["bf16", "f32"])
+def test_vision_soft_tokens(prec, oracle_vision, request):
+    dev = request.getfixturevalue(f"dev_{prec}")
+    vb = B.VisionBackend(dev)
+    prof = V.for_precision(prec)
+    for gh, gw in ((12, 12), (6, 21)):
+        patches, pos = image(gh, gw, gh * 100 + gw)
+        pooled_want, soft_want = oracle_vision.encode(patches, pos, gh, gw)
+        soft, pooled = vb.encode(patches, pos, gh, gw, pooled=True)
+        c = V.vec_check(f"{prec} soft {gh}x{gw}", soft, soft_want, prof.soft_tokens)
+        assert c.passed(), str(c)
+        print(c)
