@@ -1,0 +1,365 @@
+"""Benchmark: bf16 docs/s at 2,208 tokens through the full 24-layer EmbeddingGemma 2 text backbone
+(+ mean pool, L2, Matryoshka cuts) on 1..8 B200s, one process per GPU.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--docs-per-gpu B] [--impl ours|reference]
+
+Each rank embeds its own B documents of 2,208 seeded uniform token ids per step (weak scaling: the
+workload shards by document, no collective on the data path). ``value`` is documents per second of
+the whole job with the token ids already on the device, timed with CUDA events on the launching
+stream, max over ranks. ``e2e`` is the same metric through the host-buffer C-ABI call
+``eg2_embed_packed`` (ids H2D and pooled embeddings D2H inside the timed region). Weights are the
+seeded random-init checkpoint (no real weights exist here). ``--impl reference`` times the CPU
+restatement of the reference's CPU f32 path (the Rust reference cannot be built here) on the
+host cores, on a bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import importlib
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+PKG = "embeddinggemma2-rust_b200"
+SEQ_LEN = 2208
+DIMS = (768, 512, 256, 128)
+METRIC = "bf16 docs/sec @2,208 tok (24-layer text backbone + pool)"
+
+
+def pkg(mod):
+    return importlib.import_module(f"{PKG}.{mod}")
+
+
+# ---------------------------------------------------------------------------------------------
+# Algorithmic work (per document of L tokens)
+# ---------------------------------------------------------------------------------------------
+def layer_shapes(cfg):
+    """(name, N, K) of every projection GEMM per text layer, plus the once-per-pass ones."""
+    tc = cfg.text
+    h, p, ff, nh = tc.hidden_size, tc.hidden_size_per_layer_input, tc.intermediate_size, tc.num_attention_heads
+    out = []
+    for i in range(tc.num_hidden_layers):
+        hd, nkv = tc.layer_dims(i)
+        out += [("qkv", (nh + 2 * nkv) * hd, h), ("o", h, nh * hd), ("gate|up", 2 * ff, h), ("down", h, ff),
+                ("ple_gate", p, h), ("ple_proj", h, p)]
+    out += [("ple_model", tc.num_hidden_layers * p, h), ("embed_proj", tc.embedding_dim, h)]
+    return out
+
+
+def gemm_flops_per_token(cfg):
+    return sum(2 * n * k for _, n, k in layer_shapes(cfg))
+
+
+def attention_flops(cfg, L):
+    """Unmasked (query, key) pairs only: 4 * hd FLOP per pair per query head (QK^T and PV)."""
+    tc = cfg.text
+    W = tc.sliding_window
+    i = np.arange(L)
+    keys_sliding = int((np.minimum(i + W, L - 1) - np.maximum(i - W, 0) + 1).sum())
+    total = 0
+    for l in range(tc.num_hidden_layers):
+        hd, _ = tc.layer_dims(l)
+        pairs = keys_sliding if tc.is_sliding(l) else L * L
+        total += tc.num_attention_heads * 4 * hd * pairs
+    return total
+
+
+# ---------------------------------------------------------------------------------------------
+def clocks_sampler(device_index: int):
+    """nvidia-smi samples (200 ms) during the timed region; returns a stop() -> summary function."""
+    q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    try:
+        proc = subprocess.Popen(["nvidia-smi", f"--id={device_index}", f"--query-gpu={q}", "--format=csv,noheader,nounits",
+                                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+    except OSError:
+        return lambda: None
+    lines: list[str] = []
+    t = threading.Thread(target=lambda: lines.extend(iter(proc.stdout.readline, "")), daemon=True)
+    t.start()
+
+    def stop():
+        proc.terminate()
+        try:
+            proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            proc.kill()
+        t.join(timeout=2)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+    return stop
+
+
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d, "measured"
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+def ncu_traffic(kernel_label: str):
+    """DRAM bytes per launch of a kernel, from the committed ncu summary (profiles/*.md lines
+    `traffic <label>: <bytes> bytes/launch`), else None."""
+    for f in sorted((ROOT / "profiles").glob("*.md")):
+        for ln in f.read_text().splitlines():
+            if ln.startswith(f"traffic {kernel_label}:"):
+                try:
+                    return float(ln.split(":")[1].split()[0])
+                except (IndexError, ValueError):
+                    pass
+    return None
+
+
+def make_checkpoint(dirpath: Path):
+    pkg("weights").make_random_checkpoint(dirpath, seed=0, vision=False)
+
+
+# ---------------------------------------------------------------------------------------------
+def cpu_baseline_run(model_dir: Path, docs: int, seed: int):
+    """The oracle (C restatement of the reference CPU f32 path) on `docs` documents of SEQ_LEN."""
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import oracle as O
+
+    m = O.OracleText(model_dir)
+    rng = np.random.default_rng(seed)
+    seqs = [rng.integers(0, 262144, size=SEQ_LEN).astype(np.uint32) for _ in range(docs)]
+    t0 = time.perf_counter()
+    m.embed_ids(seqs)
+    return time.perf_counter() - t0, O.num_threads()
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        print(json.dumps({"impl": "reference", "rank": rank, "skipped": "rank 0 runs the CPU reference"}), file=sys.stderr)
+        return
+    with tempfile.TemporaryDirectory() as d:
+        make_checkpoint(Path(d))
+        per_doc, threads = cpu_baseline_run(Path(d), 1, 99)  # warm-up + size probe
+        budget = 150.0
+        steps = max(1, min(args.steps, int(budget / max(per_doc, 1e-3))))
+        times = []
+        for s in range(steps):
+            dt, threads = cpu_baseline_run(Path(d), 1, 100 + s)
+            times.append(dt)
+    value = len(times) / sum(times)
+    sample = f"{len(times)} step(s) of 1 document x {SEQ_LEN} tokens (full 24-layer f32 forward + pool)"
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "docs/s", "n_gpus": args.gpus,
+        "steps": len(times), "warmup": 1, "ms_per_step": 1000 * sum(times) / len(times), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"documents of {SEQ_LEN} seeded uniform token ids, random-init checkpoint", "seq_len": SEQ_LEN},
+        "cpu_baseline": {"value": value, "unit": "docs/s", "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": "docs/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "the Rust reference cannot be built here (no cargo); its CPU f32 path is timed as the C restatement in oracle/",
+    }
+    print(json.dumps(line))
+
+
+# ---------------------------------------------------------------------------------------------
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--docs-per-gpu", type=int, default=64)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    B, V = pkg("backend"), pkg("verify")
+    L = pkg("lib")
+    tmp = Path(tempfile.gettempdir()) / f"eg2_bench_ckpt_{os.environ.get('MASTER_PORT', 'solo')}"
+    if rank == 0:
+        tmp.mkdir(parents=True, exist_ok=True)
+        make_checkpoint(tmp)
+    barrier()
+    dev = B.Device(tmp, local, "bf16")
+    tb = B.TextBackend(dev)
+    cfg = dev.cfg
+    n_docs = args.docs_per_gpu
+    rows = n_docs * SEQ_LEN
+    rng = np.random.default_rng(1000 + rank)
+    ids_host = rng.integers(0, cfg.text.vocab_size, size=rows).astype(np.uint32)
+    lens = [SEQ_LEN] * n_docs
+    total_dims = sum(DIMS)
+    stream = torch.cuda.current_stream()
+    dev.set_stream(stream.cuda_stream)
+    ids_dev = torch.from_numpy(ids_host.view(np.int32)).cuda()
+    out_dev = torch.empty((n_docs, total_dims), dtype=torch.float32, device="cuda")
+
+    def step_device():
+        tb.embed_ids_device(ids_dev.data_ptr(), lens, DIMS, out_dev.data_ptr(), stream.cuda_stream)
+
+    # ---- device-resident throughput (value) ----
+    for _ in range(max(3, args.warmup)):
+        step_device()
+    torch.cuda.synchronize()
+    launches0 = L.load().eg2_launch_count()
+    stop_clocks = clocks_sampler(local)
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step_device()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    clocks = stop_clocks()
+    ms_local = e0.elapsed_time(e1)
+    launches = (L.load().eg2_launch_count() - launches0) // max(1, args.steps)
+    ms = max_over_ranks(ms_local)
+    value = world * n_docs * args.steps / (ms / 1000.0)
+
+    # ---- end to end through the host-buffer C ABI (ids in, pooled embeddings out) ----
+    dev.set_stream(None)
+    ids_pinned = torch.from_numpy(ids_host.view(np.int32)).pin_memory()
+    out_pinned = torch.empty((n_docs, total_dims), dtype=torch.float32).pin_memory()
+    lib = L.load()
+    import ctypes as C
+
+    def step_host():
+        dev.check(lib.eg2_embed_packed(dev.handle, C.c_void_p(ids_pinned.data_ptr()), L.i32_array(lens), n_docs,
+                                       L.i32_array(DIMS), len(DIMS), C.c_void_p(out_pinned.data_ptr())))
+
+    step_host()
+    barrier()
+    t0 = time.perf_counter()
+    e2e_steps = max(1, args.steps)
+    for _ in range(e2e_steps):
+        step_host()
+    t_e2e = max_over_ranks(time.perf_counter() - t0)
+    barrier()
+    e2e_value = world * n_docs * e2e_steps / t_e2e
+
+    # ---- per-op device time shares (CUDA events around each op, one profiled step) ----
+    dev.set_stream(stream.cuda_stream)
+    dev.profile(True)
+    step_device()
+    torch.cuda.synchronize()
+    prof = dev.profile_read()
+    dev.profile(False)
+    gemm_labels = [k for k in prof if k.startswith("gemm")]
+    per_tok = gemm_flops_per_token(cfg)
+    gemm_ms = sum(prof[k][0] for k in gemm_labels)
+    attn_flops = attention_flops(cfg, SEQ_LEN) * n_docs
+    total_ms = sum(v[0] for v in prof.values())
+    # Dominant kernel: the op label with the largest share.
+    top = max(prof, key=lambda k: prof[k][0])
+    peaks, peak_kind = measured_peaks()
+    shapes = {n: (N, K) for n, N, K in layer_shapes(cfg)}
+    label_shape = {"gemm gate|up + gelu": "gate|up", "gemm qkv": "qkv", "gemm o": "o", "gemm down": "down",
+                   "gemm ple_gate": "ple_gate", "gemm ple_proj": "ple_proj", "gemm ple_model": "ple_model",
+                   "gemm embed_proj": "embed_proj"}
+    if top.startswith("attention"):
+        hd = 256 if "256" in top else 512
+        n_layers = sum(1 for l in range(cfg.text.num_hidden_layers) if cfg.text.layer_dims(l)[0] == hd)
+        i = np.arange(SEQ_LEN)
+        W = cfg.text.sliding_window
+        pairs = int((np.minimum(i + W, SEQ_LEN - 1) - np.maximum(i - W, 0) + 1).sum()) if hd == 256 else SEQ_LEN * SEQ_LEN
+        flops_launch = cfg.text.num_attention_heads * 4 * hd * pairs * n_docs
+    else:
+        name = label_shape.get(top, "gate|up")
+        # qkv / o differ per layer kind: average over the layers' launches.
+        per = [2 * N * K for nm, N, K in layer_shapes(cfg) if nm == name]
+        flops_launch = (sum(per) / len(per)) * rows
+    ms_launch = prof[top][0] / prof[top][1]
+    achieved = flops_launch / (ms_launch / 1000.0) / 1e12
+    peak = peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops"))
+    traffic = ncu_traffic(top)
+    roofline = {
+        "kernel": top, "bound": "tensor", "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
+        "frac": round(achieved / peak, 4), "traffic": traffic, "peak_source": f"{peak_kind} (bf16_tflops_sustained)",
+        "time_share": round(prof[top][0] / total_ms, 4),
+        "all_gemms": {"tflops": round(per_tok * rows / (gemm_ms / 1000.0) / 1e12, 1),
+                      "frac": round(per_tok * rows / (gemm_ms / 1000.0) / 1e12 / peak, 4),
+                      "time_share": round(gemm_ms / total_ms, 4)},
+        "op_ms": {k: round(v[0], 3) for k, v in sorted(prof.items(), key=lambda kv: -kv[1][0])},
+    }
+    total_flops_doc = per_tok * SEQ_LEN + attention_flops(cfg, SEQ_LEN)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        dt, threads = cpu_baseline_run(tmp, 1, 7)
+        cpu = {"value": 1.0 / dt, "unit": "docs/s", "cores": threads, "kind": "port",
+               "sample": f"1 document x {SEQ_LEN} tokens through the oracle (C restatement of the reference CPU f32 path), {threads} threads"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "docs/s", "n_gpus": world, "steps": args.steps,
+            "warmup": max(3, args.warmup), "ms_per_step": round(ms / args.steps, 3), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded uniform token ids, random-init weights)",
+            "config": {"workload": f"{n_docs} documents x {SEQ_LEN} tokens per GPU, full 24-layer text backbone + mean pool + L2 + Matryoshka 512/256/128",
+                       "docs_per_gpu": n_docs, "seq_len": SEQ_LEN, "global_batch": n_docs * world,
+                       "parallelism": f"dp{world} (documents sharded per GPU, no collective)",
+                       "l2": "inputs larger than L2 (141k-row activations, 274 MB of weights per pass)"},
+            "tflops_per_gpu": round(total_flops_doc * n_docs * args.steps / (ms / 1000.0) / 1e12, 1),
+            "roofline": roofline,
+            "e2e": {"value": round(e2e_value, 2), "unit": "docs/s", "h2d_bytes_per_step": int(rows * 4),
+                    "d2h_bytes_per_step": int(n_docs * total_dims * 4), "call": "eg2_embed_packed (host ids -> host embeddings)"},
+            "gpu_launches": int(launches),
+            "clocks": clocks,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line))
+    dev.close()
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -383,3 +383,8 @@ int vision_pool(const float* x, float* out, int gh, int gw, int hdim, int k, flo
 }
 
 }  // namespace eg2
+
+namespace eg2 {
+template int qkv_post<float, bf16_t>(const float*, bf16_t*, bf16_t*, bf16_t*, const float*, const float*, const float*,
+                                     const float*, int, const int*, long, int, int, int, int, float, cudaStream_t);
+}  // namespace eg2

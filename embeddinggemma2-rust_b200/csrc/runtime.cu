@@ -19,6 +19,7 @@
 #include <cstdio>
 #include <cstring>
 #include <map>
+#include <atomic>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -110,10 +111,13 @@ struct Fail {
             fail(e_ == cudaErrorMemoryAllocation ? EG2_ERR_OOM : EG2_ERR_CUDA, "%s: %s (%s:%d)", #call, \
                  cudaGetErrorString(e_), __FILE__, __LINE__);                                         \
     } while (0)
+// Kernel launches issued by this library (all contexts), for the benchmark's launch count.
+static std::atomic<long long> g_launches{0};
 #define KL(call, what)                                                                         \
     do {                                                                                       \
         int r_ = (call);                                                                       \
         if (r_ != 0) fail(r_ == -1 ? EG2_ERR_INVALID : EG2_ERR_CUDA, "launch of %s failed", what); \
+        g_launches.fetch_add(1, std::memory_order_relaxed);                                    \
     } while (0)
 
 // ---------------------------------------------------------------------------------------------
@@ -633,12 +637,12 @@ static void ensure_work(eg2_ctx* c, long rows, long n_tiles) {
         w.ple = (float*)dalloc(c, cap * (long)tc.layers * tc.ple * 4);
         w.out = (float*)dalloc(c, cap * tc.emb * 4);
         w.t = dalloc(c, cap * tc.hidden * as);
-        w.qkv = dalloc(c, cap * max_qkv * as);
+        w.qkv = dalloc(c, cap * max_qkv * 4);
         w.q = dalloc(c, cap * max_q * as);
         w.k = dalloc(c, cap * max_kv * as);
         w.v = dalloc(c, cap * max_kv * as);
         w.a = dalloc(c, cap * max_q * as);
-        w.o = dalloc(c, cap * tc.hidden * as);
+        w.o = dalloc(c, cap * tc.hidden * 4);
         w.gate = dalloc(c, cap * tc.inter * as);
         w.pg = dalloc(c, cap * tc.ple * as);
         w.gu = c->precision == EG2_F32 ? dalloc(c, cap * 2L * tc.inter * 4) : nullptr;
@@ -772,9 +776,9 @@ static void enqueue_text(eg2_ctx* c, long rows, const std::vector<TileSet>& tset
         const int hd = L.hd, nkv = L.nkv;
         const int nqkv = (nh + 2 * nkv) * hd;
         const RopeTab& rt = c->ropes[L.rope];
-        gemm(c, t, h, L.qkv, (int)rows, nqkv, h, w.qkv, nqkv, EPI_STORE, f32);
+        gemm(c, t, h, L.qkv, (int)rows, nqkv, h, w.qkv, nqkv, EPI_STORE, true);
         mark(c, "gemm qkv");
-        KL((qkv_post<T, T>((const T*)w.qkv, (T*)w.q, (T*)w.k, (T*)w.v, L.q_norm, L.k_norm, rt.cs, rt.sn, hd / 2, w.pos,
+        KL((qkv_post<float, T>((const float*)w.qkv, (T*)w.q, (T*)w.k, (T*)w.v, L.q_norm, L.k_norm, rt.cs, rt.sn, hd / 2, w.pos,
                            rows, nh, nkv, hd, hd, eps, c->stream)),
            "qkv_post");
         mark(c, "qkv_post");
@@ -788,23 +792,23 @@ static void enqueue_text(eg2_ctx* c, long rows, const std::vector<TileSet>& tset
         attention<T>(c, (const T*)w.q, (const T*)w.k, (const T*)w.v, (T*)w.a, rows, nh, nkv, hd,
                      L.sliding ? tc.window : -1, w.seq_start, w.seq_len, tiles, n_tiles);
         mark(c, hd == 256 ? "attention d256" : "attention d512");
-        gemm(c, w.a, nh * hd, L.o, (int)rows, h, nh * hd, w.o, h, EPI_STORE, f32);
+        gemm(c, w.a, nh * hd, L.o, (int)rows, h, nh * hd, w.o, h, EPI_STORE, true);
         mark(c, "gemm o");
-        KL((add_norm<T, T>(w.hidden, (const T*)w.o, L.post_attn_ln, t, L.pre_ff_ln, rows, h, eps, 1.f, c->stream)), "add_norm");
+        KL((add_norm<float, T>(w.hidden, (const float*)w.o, L.post_attn_ln, t, L.pre_ff_ln, rows, h, eps, 1.f, c->stream)), "add_norm");
         mark(c, "add_norm");
         gemm(c, t, h, L.gu, (int)rows, 2 * ff, h, w.gate, ff, EPI_GELU_GU, f32, 1.f, nullptr, 0, 0, w.gu);
         mark(c, "gemm gate|up + gelu");
-        gemm(c, w.gate, ff, L.down, (int)rows, h, ff, w.o, h, EPI_STORE, f32);
+        gemm(c, w.gate, ff, L.down, (int)rows, h, ff, w.o, h, EPI_STORE, true);
         mark(c, "gemm down");
         // t = hidden (as the per-layer-input gate's input, bf16 in bf16 mode).
-        KL((add_norm<T, T>(w.hidden, (const T*)w.o, L.post_ff_ln, t, nullptr, rows, h, eps, 1.f, c->stream)), "add_norm");
+        KL((add_norm<float, T>(w.hidden, (const float*)w.o, L.post_ff_ln, t, nullptr, rows, h, eps, 1.f, c->stream)), "add_norm");
         mark(c, "add_norm");
         gemm(c, t, h, L.pg, (int)rows, p, h, w.pg, p, EPI_PLE_GATE, f32, 1.f, w.ple, (long)nl * p, i * p);
         mark(c, "gemm ple_gate");
-        gemm(c, w.pg, p, L.pp, (int)rows, h, p, w.o, h, EPI_STORE, f32);
+        gemm(c, w.pg, p, L.pp, (int)rows, h, p, w.o, h, EPI_STORE, true);
         mark(c, "gemm ple_proj");
         const float* next_w = (i + 1 < nl) ? c->layers[i + 1].input_ln : c->final_norm;
-        KL((add_norm<T, T>(w.hidden, (const T*)w.o, L.ple_post_norm, t, next_w, rows, h, eps, L.layer_scalar, c->stream)),
+        KL((add_norm<float, T>(w.hidden, (const float*)w.o, L.ple_post_norm, t, next_w, rows, h, eps, L.layer_scalar, c->stream)),
            "add_norm");
         mark(c, "add_norm");
     }
@@ -907,8 +911,8 @@ static void enqueue_vision(eg2_ctx* c, long n, int gh, int gw) {
     const int nqkv = (nh + 2 * nkv) * hd;
     for (int l = 0; l < vc.layers; l++) {
         const VLayerW& L = c->vlayers[l];
-        gemm(c, t, h, L.qkv, (int)n, nqkv, h, c->v_qkv, nqkv, EPI_STORE, f32);
-        KL((qkv_post<T, T>((const T*)c->v_qkv, (T*)c->v_q, (T*)c->v_k, (T*)c->v_v, L.q_norm, L.k_norm, c->v_cs, c->v_sn,
+        gemm(c, t, h, L.qkv, (int)n, nqkv, h, c->v_qkv, nqkv, EPI_STORE, true);
+        KL((qkv_post<float, T>((const float*)c->v_qkv, (T*)c->v_q, (T*)c->v_k, (T*)c->v_v, L.q_norm, L.k_norm, c->v_cs, c->v_sn,
                            hd / 2, nullptr, n, nh, nkv, hd, hd / 2, eps, c->stream)),
            "qkv_post");
         mark(c, "vision qkv");
@@ -921,12 +925,12 @@ static void enqueue_vision(eg2_ctx* c, long n, int gh, int gw) {
                                       c->v_seq_start, c->v_seq_len, n, nh, nkv, hd, -1, c->stream),
                "attention");
         mark(c, "vision attention");
-        gemm(c, c->v_a, nh * hd, L.o, (int)n, h, nh * hd, c->v_o, h, EPI_STORE, f32);
-        KL((add_norm<T, T>(c->v_hidden, (const T*)c->v_o, L.post_attn_ln, t, L.pre_ff_ln, n, h, eps, 1.f, c->stream)), "add_norm");
+        gemm(c, c->v_a, nh * hd, L.o, (int)n, h, nh * hd, c->v_o, h, EPI_STORE, true);
+        KL((add_norm<float, T>(c->v_hidden, (const float*)c->v_o, L.post_attn_ln, t, L.pre_ff_ln, n, h, eps, 1.f, c->stream)), "add_norm");
         gemm(c, t, h, L.gu, (int)n, 2 * ff, h, c->v_gate, ff, EPI_GELU_GU, f32, 1.f, nullptr, 0, 0, c->v_gu);
-        gemm(c, c->v_gate, ff, L.down, (int)n, h, ff, c->v_o, h, EPI_STORE, f32);
+        gemm(c, c->v_gate, ff, L.down, (int)n, h, ff, c->v_o, h, EPI_STORE, true);
         const float* next_w = (l + 1 < vc.layers) ? c->vlayers[l + 1].input_ln : nullptr;
-        KL((add_norm<T, T>(c->v_hidden, (const T*)c->v_o, L.post_ff_ln, next_w ? t : (T*)nullptr, next_w, n, h, eps, 1.f,
+        KL((add_norm<float, T>(c->v_hidden, (const float*)c->v_o, L.post_ff_ln, next_w ? t : (T*)nullptr, next_w, n, h, eps, 1.f,
                            c->stream)),
            "add_norm");
         mark(c, "vision mlp");
@@ -1208,7 +1212,7 @@ int eg2_vision_encode(eg2_ctx* c, const float* patches, const int32_t* pos_xy, i
             c->v_sn = (float*)dalloc(c, cap * (hd / 2) * 4);
             c->v_x = dalloc(c, cap * pd * 4);
             c->v_t = dalloc(c, cap * std::max(h, pd) * as);
-            c->v_qkv = dalloc(c, cap * (nh + 2 * nkv) * hd * as);
+            c->v_qkv = dalloc(c, cap * (nh + 2 * nkv) * hd * 4);
             c->v_q = dalloc(c, cap * nh * hd * as);
             c->v_k = dalloc(c, cap * nkv * hd * as);
             c->v_v = dalloc(c, cap * nkv * hd * as);
@@ -1352,6 +1356,8 @@ int eg2_attention(int kind, const void* q, const void* k, const void* v, void* o
     cudaMemcpyFromSymbol(&stv, eg2_dev_status, sizeof(int));
     return stv ? EG2_ERR_TIMEOUT : EG2_OK;
 }
+
+long long eg2_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
 
 int eg2_device_status(void) {
     int st = 0;

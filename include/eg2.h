@@ -111,6 +111,9 @@ int eg2_gemm(int kind, const void* A, int64_t lda, const void* W, int64_t ldw, v
 int eg2_attention(int kind, const void* q, const void* k, const void* v, void* out, const int32_t* lens, int n_seq,
                   int nh, int nkv, int hd, int window, void* stream);
 
+/* Number of kernel launches this library has issued in the process (all contexts). */
+long long eg2_launch_count(void);
+
 /* First error code recorded by a device-side bounded wait since the last reset (0: none). */
 int eg2_device_status(void);
 void eg2_device_status_reset(void);

@@ -23,15 +23,18 @@ def ids_for(lens, seed):
 
 
 def check_embeddings(got: dict, want: np.ndarray, profile, label):
-    worst = 0.0
+    """Checks every vector and cut, prints the worst margins, then fails on any violation."""
+    checks = []
     for i in range(want.shape[0]):
-        c = V.vec_check(f"{label}[{i}]", got[768][i], want[i], profile.embedding)
-        assert c.passed(), str(c)
-        worst = max(worst, c.max_abs)
+        checks.append(V.vec_check(f"{label}[{i}]", got[768][i], want[i], profile.embedding))
         for d in (512, 256, 128):
             cut = O.truncate_and_normalize(want[i:i + 1], d)[0]
-            c = V.vec_check(f"{label}[{i}]@{d}", got[d][i], cut, profile.embedding)
-            assert c.passed(), str(c)
+            checks.append(V.vec_check(f"{label}[{i}]@{d}", got[d][i], cut, profile.embedding))
+    worst = max(c.max_abs for c in checks)
+    min_cos = min(c.cos for c in checks if c.cos is not None)
+    print(f"{label}: n={len(checks)} worst max|d|={worst:.3e} min cos={min_cos:.8f}")
+    bad = [str(c) for c in checks if not c.passed()]
+    assert not bad, "\n".join(bad)
     return worst
 
 
