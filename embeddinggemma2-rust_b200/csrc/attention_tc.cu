@@ -25,10 +25,14 @@
 
 namespace eg2 {
 
-constexpr int ATT_THREADS = 192;
+constexpr int ATT_THREADS = 224;  // warp 0 Q/K loads, 1 MMA, 2..5 softmax, 6 V loads
+constexpr int ATT_V_WARP = 6;
 constexpr int ATT_BN = 64;       // keys per tile
 constexpr int ATT_DV = 256;      // output channels per CTA
-constexpr int ATT_KST = 4;       // K chunk ring
+// K chunk ring depth (slots of [64 keys x 64 channels]): as deep as shared memory allows, since
+// the kernel is bound by the latency of the K loads when fewer than ~2 key tiles are in flight.
+template <int DQK>
+constexpr int att_kst() { return DQK == 256 ? 8 : 4; }
 constexpr float ATT_RESCALE_LOG2 = 8.f;
 
 template <int DQK, int VB>
@@ -36,11 +40,9 @@ struct AttCfg {
     static constexpr int Q_BYTES = (DQK / 64) * 128 * 128;
     static constexpr int K_SLOT = ATT_BN * 128;          // [64 keys x 64 ch] bf16
     static constexpr int V_BYTES = (ATT_DV / 64) * ATT_BN * 128;
-    static constexpr int P_BYTES = 128 * ATT_BN * 2;     // [128 rows x 64 keys] bf16
     static constexpr int OFF_K = Q_BYTES;
-    static constexpr int OFF_V = OFF_K + ATT_KST * K_SLOT;
-    static constexpr int OFF_P = OFF_V + VB * V_BYTES;
-    static constexpr int OFF_BAR = OFF_P + 2 * P_BYTES;
+    static constexpr int OFF_V = OFF_K + att_kst<DQK>() * K_SLOT;
+    static constexpr int OFF_BAR = OFF_V + VB * V_BYTES;
     static constexpr int SMEM = 1024 + OFF_BAR + 256;
 };
 
@@ -61,8 +63,8 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::OFF_BAR);
     uint64_t* q_full = bars;
     uint64_t* k_full = bars + 1;
-    uint64_t* k_empty = k_full + ATT_KST;
-    uint64_t* v_full = k_empty + ATT_KST;
+    uint64_t* k_empty = k_full + att_kst<DQK>();
+    uint64_t* v_full = k_empty + att_kst<DQK>();
     uint64_t* v_empty = v_full + VB;
     uint64_t* s_full = v_empty + VB;
     uint64_t* s_empty = s_full + 2;
@@ -84,7 +86,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
 
     if (threadIdx.x == 0) {
         mbar_init(q_full, 1);
-        for (int s = 0; s < ATT_KST; s++) {
+        for (int s = 0; s < att_kst<DQK>(); s++) {
             mbar_init(&k_full[s], 1);
             mbar_init(&k_empty[s], 1);
         }
@@ -107,29 +109,40 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
     const uint32_t t_s = tmem;          // S[0] cols [0, 64), S[1] cols [64, 128)
+    const uint32_t t_p = tmem + 128;    // P[0] cols [128, 160), P[1] cols [160, 192) (bf16 pairs)
     const uint32_t t_o = tmem + 256;    // O cols [256, 512)
 
     if (n_kt == 0) goto done;
 
     if (warp == 0) {
+        // K producer (with Q first). K and V have producers of their own so that a wait for a free
+        // V buffer never holds back the K loads the next S = Q K^T needs.
         if (lane == 0) {
             // Q: the G heads of K/V head g for tokens [q0, q0 + tq), 128 rows of 64 channels per box.
             mbar_arrive_expect_tx(q_full, Cfg::Q_BYTES);
             for (int c = 0; c < QCH; c++)
                 tma_load_3d(smem + c * 128 * 128, &tmQ, q_full, c * 64, g * G, tile.row0 + tile.q0);
-            int ks = 0, vs = 0;
-            uint32_t kph = 0, vph = 0;
+            int ks = 0;
+            uint32_t kph = 0;
             for (int j = 0; j < n_kt; j++) {
                 const int key0 = tile.row0 + k_lo + j * ATT_BN;
                 for (int c = 0; c < QCH; c++) {
                     if (!mbar_wait(&k_empty[ks], kph ^ 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) goto done;
                     mbar_arrive_expect_tx(&k_full[ks], Cfg::K_SLOT);
                     tma_load_3d(smem + Cfg::OFF_K + ks * Cfg::K_SLOT, &tmK, &k_full[ks], c * 64, g, key0);
-                    if (++ks == ATT_KST) {
+                    if (++ks == att_kst<DQK>()) {
                         ks = 0;
                         kph ^= 1;
                     }
                 }
+            }
+        }
+    } else if (warp == ATT_V_WARP) {
+        if (lane == 0) {
+            int vs = 0;
+            uint32_t vph = 0;
+            for (int j = 0; j < n_kt; j++) {
+                const int key0 = tile.row0 + k_lo + j * ATT_BN;
                 if (!mbar_wait(&v_empty[vs], vph ^ 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) goto done;
                 mbar_arrive_expect_tx(&v_full[vs], Cfg::V_BYTES);
                 for (int c = 0; c < ATT_DV / 64; c++)
@@ -145,25 +158,31 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         if (lane == 0) {
             constexpr uint32_t idesc_s = umma_idesc(128, ATT_BN, 1);
             constexpr uint32_t idesc_o = umma_idesc(128, ATT_DV, 1, /*b_mn_major=*/true);
-            const uint32_t sq = smem_u32(smem);
+            // Descriptors are built once; moving within a tile only adds (byte offset >> 4) to the
+            // start-address field. A single thread issues every MMA, so anything between two
+            // tcgen05.mma instructions is issue latency the tensor pipe waits for.
+            const uint64_t dq0 = umma_desc_sw128(smem_u32(smem), 16, 1024);
+            const uint64_t dk0 = umma_desc_sw128(smem_u32(smem + Cfg::OFF_K), 16, 1024);
+            const uint64_t dv0 = umma_desc_sw128(smem_u32(smem + Cfg::OFF_V), ATT_BN * 128, 1024);
             int ks = 0, vs = 0;
             uint32_t kph = 0, vph = 0;
             if (!mbar_wait(q_full, 0, EG2_DEV_TIMEOUT_ATTN, abort_flag)) goto done;
             // S[j % 2] = Q K_j^T over head_dim in 64-channel chunks.
             auto issue_qk = [&](int j) -> bool {
                 const int sb = j & 1;
+                const uint32_t ts = t_s + sb * ATT_BN;
                 if (!mbar_wait(&s_empty[sb], ((j >> 1) & 1) ^ 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) return false;
                 tc_fence_after();
                 for (int c = 0; c < QCH; c++) {
                     if (!mbar_wait(&k_full[ks], kph, EG2_DEV_TIMEOUT_ATTN, abort_flag)) return false;
                     tc_fence_after();
-                    const uint32_t sk = smem_u32(smem + Cfg::OFF_K + ks * Cfg::K_SLOT);
+                    const uint64_t da = dq0 + (uint64_t)(c * (128 * 128 >> 4));
+                    const uint64_t db = dk0 + (uint64_t)(ks * (Cfg::K_SLOT >> 4));
+                    mma_bf16(ts, da, db, idesc_s, c != 0);
 #pragma unroll
-                    for (int kk = 0; kk < 4; kk++)
-                        mma_bf16(t_s + sb * ATT_BN, umma_desc_sw128(sq + c * 128 * 128 + kk * 32, 16, 1024),
-                                 umma_desc_sw128(sk + kk * 32, 16, 1024), idesc_s, (c | kk) != 0);
+                    for (int kk = 1; kk < 4; kk++) mma_bf16(ts, da + 2 * kk, db + 2 * kk, idesc_s, 1);
                     mma_commit(&k_empty[ks]);
-                    if (++ks == ATT_KST) {
+                    if (++ks == att_kst<DQK>()) {
                         ks = 0;
                         kph ^= 1;
                     }
@@ -178,12 +197,12 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
                 if (!mbar_wait(&p_full[pb], (j >> 1) & 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) goto done;
                 if (!mbar_wait(&v_full[vs], vph, EG2_DEV_TIMEOUT_ATTN, abort_flag)) goto done;
                 tc_fence_after();
-                const uint32_t sp = smem_u32(smem + Cfg::OFF_P + pb * Cfg::P_BYTES);
-                const uint32_t sv = smem_u32(smem + Cfg::OFF_V + vs * Cfg::V_BYTES);
+                const uint64_t dv = dv0 + (uint64_t)(vs * (Cfg::V_BYTES >> 4));
+                const uint32_t tp = t_p + pb * (ATT_BN / 2);
+                // 16 keys per MMA = 8 packed P columns and 16 V rows (2048 bytes).
+                mma_bf16_ts(t_o, tp, dv, idesc_o, j != 0);
 #pragma unroll
-                for (int kk = 0; kk < ATT_BN / 16; kk++)
-                    mma_bf16(t_o, umma_desc_sw128(sp + kk * 32, 16, 1024),
-                             umma_desc_sw128(sv + kk * 2048, ATT_BN * 128, 1024), idesc_o, (j | kk) != 0);
+                for (int kk = 1; kk < ATT_BN / 16; kk++) mma_bf16_ts(t_o, tp + kk * 8, dv + kk * (2048 >> 4), idesc_o, 1);
                 mma_commit(&v_empty[vs]);
                 mma_commit(&pv_done[pb]);
                 if (++vs == VB) {
@@ -211,26 +230,36 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
             tmem_ld_wait();
             tc_fence_before();
             mbar_arrive(&s_empty[sb]);
+            // Valid key columns of this row in this tile: [lo_c, hi_c). Interior tiles (every row of
+            // the warp fully valid) skip the masking pass.
             const int kbase = k_lo + j * ATT_BN;  // key position of column 0 within the sequence
-            float sv[64];
-            float mt = -INFINITY;
-#pragma unroll
-            for (int c = 0; c < 64; c++) {
-                const int kp = kbase + c;
-                bool ok = kp < tile.len;
-                if (W >= 0 && row_valid) ok = ok && (kp >= tok - W) && (kp <= tok + W);
-                const float x = __uint_as_float(c < 32 ? s0[c] : s1[c - 32]) * LOG2E;
-                sv[c] = ok ? x : -INFINITY;
-                mt = fmaxf(mt, sv[c]);
+            int lo_c = 0, hi_c = min(ATT_BN, tile.len - kbase);
+            if (W >= 0 && row_valid) {
+                lo_c = max(lo_c, tok - W - kbase);
+                hi_c = min(hi_c, tok + W + 1 - kbase);
             }
-            // Decide the reference max: keep the stale one unless the new max exceeds it by 2^8.
+            float sv[64];
+#pragma unroll
+            for (int c = 0; c < 32; c++) {
+                sv[c] = __uint_as_float(s0[c]);
+                sv[32 + c] = __uint_as_float(s1[c]);
+            }
+            if (!__all_sync(0xffffffffu, lo_c <= 0 && hi_c >= ATT_BN)) {
+#pragma unroll
+                for (int c = 0; c < 64; c++) sv[c] = (c >= lo_c && c < hi_c) ? sv[c] : -INFINITY;
+            }
+            float mt = sv[0];
+#pragma unroll
+            for (int c = 1; c < 64; c++) mt = fmaxf(mt, sv[c]);
+            // Reference max (raw logit units): keep the stale one unless the new max exceeds it by
+            // 2^8 in probability, so O is rescaled only rarely (the result is exact either way).
             float factor = 1.f;
             bool need = false;
             if (mt > m_used) {
                 if (m_used == -INFINITY) {
                     m_used = mt;  // O rows so far are exactly 0 (all earlier P were 0)
-                } else if (mt - m_used > ATT_RESCALE_LOG2) {
-                    factor = exp2f(m_used - mt);
+                } else if ((mt - m_used) * LOG2E > ATT_RESCALE_LOG2) {
+                    factor = ex2_approx((m_used - mt) * LOG2E);
                     m_used = mt;
                     need = true;
                 }
@@ -253,23 +282,23 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
                 tmem_st_wait();
             }
             l *= factor;
-            // p = 2^(s - m_used), summed in f32; stored bf16 into the swizzled K-major P tile.
-            uint8_t* prow = smem + Cfg::OFF_P + sb * Cfg::P_BYTES + r * 128;
-            const bool any = m_used != -INFINITY;
+            // p = 2^((s - m_used) log2 e): one FFMA + one MUFU op per element; masked entries are
+            // -inf and give 0 (a row with no valid key yet has m_used = -inf: bias 0 keeps it 0).
+            // Summed in f32, stored as packed bf16 pairs into P[j % 2] in TMEM (lane = row, column c
+            // holds keys 2c and 2c + 1: the A-operand layout of the P V product).
+            const float bias = (m_used == -INFINITY) ? 0.f : -m_used * LOG2E;
+            float lsum[4] = {0.f, 0.f, 0.f, 0.f};
+            uint32_t pk[32];
 #pragma unroll
-            for (int ch = 0; ch < 8; ch++) {
-                float p8[8];
-#pragma unroll
-                for (int q = 0; q < 8; q++) {
-                    const float x = sv[ch * 8 + q];
-                    p8[q] = (any && x != -INFINITY) ? exp2f(x - m_used) : 0.f;
-                    l += p8[q];
-                }
-                uint4 pk = make_uint4(pack_bf16x2(p8[0], p8[1]), pack_bf16x2(p8[2], p8[3]), pack_bf16x2(p8[4], p8[5]),
-                                      pack_bf16x2(p8[6], p8[7]));
-                *reinterpret_cast<uint4*>(prow + ((ch ^ (r & 7)) << 4)) = pk;
+            for (int q = 0; q < 32; q++) {
+                const float p0 = ex2_approx(fmaf(sv[2 * q], LOG2E, bias));
+                const float p1 = ex2_approx(fmaf(sv[2 * q + 1], LOG2E, bias));
+                lsum[q & 3] += p0 + p1;
+                pk[q] = bf16x2_bits(p0, p1);
             }
-            fence_proxy_async();
+            l += (lsum[0] + lsum[1]) + (lsum[2] + lsum[3]);
+            tmem_st32(t_p + sb * (ATT_BN / 2) + lane_off, pk);
+            tmem_st_wait();
             tc_fence_before();
             mbar_arrive(&p_full[sb]);
         }
@@ -351,8 +380,9 @@ int attention_tc(const bf16_t* q, const bf16_t* k, const bf16_t* v, bf16_t* out,
     prm.G = G;
     prm.tq = tq;
     prm.nsplit = hd / ATT_DV;
-    if (hd == 256) return launch_att<256, 2>(mq, mk, mv, prm, n_tiles, s);
-    return launch_att<512, 1>(mq, mk, mv, prm, n_tiles, s);
+    // V buffers: as many as shared memory holds next to Q and the K ring (224 KB in both cases).
+    if (hd == 256) return launch_att<256, 3>(mq, mk, mv, prm, n_tiles, s);
+    return launch_att<512, 2>(mq, mk, mv, prm, n_tiles, s);
 }
 
 }  // namespace eg2

@@ -38,6 +38,29 @@ EG2_DEV uint32_t pack_bf16x2(float lo, float hi) {
     return (uint32_t)f32_to_bf16(lo) | ((uint32_t)f32_to_bf16(hi) << 16);
 }
 
+// 2^x on the MUFU unit (flush-to-zero; ex2(-inf) = +0).
+EG2_DEV float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+// Two floats to packed bf16 (round to nearest even) in one cvt: lo in bits 0-15.
+EG2_DEV uint32_t bf16x2_bits(float lo, float hi) {
+    __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&v);
+}
+
+// sin and cos of an angle of moderate size (|a| < 2^12 * 2 pi): Cody-Waite reduction by 2 pi
+// (6.28125 has 8 significant bits, so k * 6.28125 is exact for |k| < 2^15), then the MUFU
+// approximations, which are accurate to ~4e-7 absolute on [-pi, pi].
+EG2_DEV void sincos_reduced(float a, float& s, float& c) {
+    const float k = rintf(a * 0.15915494309189535f);
+    float r = fmaf(-k, 6.28125f, a);
+    r = fmaf(-k, 1.9353071795864769e-3f, r);
+    s = __sinf(r);
+    c = __cosf(r);
+}
+
 // GELU with the tanh approximation (the reference's gelu_tanh, constants as written there).
 EG2_DEV float gelu_tanh_f(float x) {
     const float beta = 0.79788456f, kappa = 0.044715f;
@@ -173,6 +196,14 @@ EG2_DEV void mma_bf16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t 
         "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
         "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+// D[tmem] (+)= A[tmem] * B[smem], kind::f16: A read from tensor memory (row i in lane i, column c
+// holding the K-adjacent bf16 pair (2c, 2c + 1)), B from a shared-memory descriptor.
+EG2_DEV void mma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate));
 }
 // Same with TF32 inputs (f32 data in shared memory).
 EG2_DEV void mma_tf32(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {

@@ -38,25 +38,143 @@ struct GemmCfg {
     static constexpr int B_BYTES = BN * 128;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
     static constexpr int STAGES = (BN == 256) ? 4 : 6;
-    static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + 256;
+    static constexpr int OFF_STAGE = STAGES * STAGE_BYTES + 256;  // after the barriers
+    static constexpr int STAGE_WARP = 32 * (128 + 16);            // 32 rows x 32 f32 + 16 B pad
+    static constexpr int OFF_W = OFF_STAGE + 4 * STAGE_WARP;      // EPI_QKV: q / k norm weights
+    static constexpr int SMEM_BYTES = 1024 + OFF_W + 3072;
     static constexpr uint32_t TMEM_COLS = 2 * BN;
 };
 
+// Warp-cooperative store of a 32-row x 32-column output chunk (lane i holds row row0 + i):
+// the chunk goes through a padded shared-memory tile, then each store instruction writes whole
+// 64 / 128-byte row segments of 8 / 4 rows (instead of 32 scattered 16-byte pieces). Rows >= M
+// are skipped. All 32 lanes must call it.
 template <typename TOut>
-EG2_DEV void store32(TOut* dst, const float (&v)[32]);
-template <>
-EG2_DEV void store32<bf16_t>(bf16_t* dst, const float (&v)[32]) {
-    uint4* d = reinterpret_cast<uint4*>(dst);
+EG2_DEV void warp_store32(TOut* out, long ldo, int row0, int M, long col, const float (&v)[32], uint8_t* stage) {
+    const int lane = threadIdx.x & 31;
+    constexpr int ROWB = 32 * (int)sizeof(TOut), STRIDE = ROWB + 16, PIECES = ROWB / 16;
+    uint8_t* my = stage + lane * STRIDE;
+    if constexpr (sizeof(TOut) == 2) {
 #pragma unroll
-    for (int q = 0; q < 4; q++)
-        d[q] = make_uint4(pack_bf16x2(v[8 * q + 0], v[8 * q + 1]), pack_bf16x2(v[8 * q + 2], v[8 * q + 3]),
-                          pack_bf16x2(v[8 * q + 4], v[8 * q + 5]), pack_bf16x2(v[8 * q + 6], v[8 * q + 7]));
+        for (int q = 0; q < 4; q++)
+            *reinterpret_cast<uint4*>(my + q * 16) = make_uint4(bf16x2_bits(v[8 * q + 0], v[8 * q + 1]), bf16x2_bits(v[8 * q + 2], v[8 * q + 3]),
+                                                                bf16x2_bits(v[8 * q + 4], v[8 * q + 5]), bf16x2_bits(v[8 * q + 6], v[8 * q + 7]));
+    } else {
+#pragma unroll
+        for (int q = 0; q < 8; q++)
+            *reinterpret_cast<float4*>(my + q * 16) = make_float4(v[4 * q + 0], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+    }
+    __syncwarp();
+#pragma unroll
+    for (int p = lane; p < 32 * PIECES; p += 32) {
+        const int r = p / PIECES, sg = p % PIECES;
+        if (row0 + r < M)
+            *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(out + (long)(row0 + r) * ldo + col) + sg * 16) =
+                *reinterpret_cast<const uint4*>(stage + r * STRIDE + sg * 16);
+    }
+    __syncwarp();
 }
-template <>
-EG2_DEV void store32<float>(float* dst, const float (&v)[32]) {
-    float4* d = reinterpret_cast<float4*>(dst);
+
+// EPI_QKV: the tile's BN columns are whole heads of one kind (q, k or v). Pass 1 reads the
+// accumulator for the per-head sums of squares; pass 2 reads it again, normalises (q / k times
+// their norm weights), applies RoPE to q / k (split-halves rule, pairs i and i + part / 2) and
+// stores the heads. Mirrors qkv_post_kernel (rowops.cu) operation for operation. All 32 lanes
+// run every tcgen05.ld; rows past M only skip the stores.
+template <typename TOut, int BN>
+EG2_DEV void epilogue_qkv(const GemmEpilogue& epi, uint32_t tbase, int row0, int M, int n0, uint8_t* stage,
+                          const float* wsm) {
+    const int row = row0 + (int)(threadIdx.x & 31);
+    const QkvEpilogue& Q = epi.qkv;
+    const int hd = Q.hd, qw = Q.nh * hd, kw = Q.nkv * hd;
+    TOut* base;
+    int nheads, head0;
+    const float* w;
+    bool rot;
+    if (n0 < qw) {
+        base = (TOut*)Q.q, nheads = Q.nh, head0 = n0 / hd, w = wsm, rot = true;
+    } else if (n0 < qw + kw) {
+        base = (TOut*)Q.k, nheads = Q.nkv, head0 = (n0 - qw) / hd, w = wsm + hd, rot = true;
+    } else {
+        base = (TOut*)Q.v, nheads = Q.nkv, head0 = (n0 - qw - kw) / hd, w = nullptr, rot = false;
+    }
+    float ss0 = 0.f, ss1 = 0.f, ss2 = 0.f, ss3 = 0.f;
+#pragma unroll 1
+    for (int c = 0; c < BN / 32; c++) {
+        uint32_t r[32];
+        tmem_ld32(tbase + c * 32, r);
+        tmem_ld_wait();
+        float s = 0.f;
 #pragma unroll
-    for (int q = 0; q < 8; q++) d[q] = make_float4(v[4 * q + 0], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+        for (int j = 0; j < 32; j++) s = fmaf(__uint_as_float(r[j]), __uint_as_float(r[j]), s);
+        const int hi = (c * 32) / hd;
+        if (hi == 0) ss0 += s;
+        else if (hi == 1) ss1 += s;
+        else if (hi == 2) ss2 += s;
+        else ss3 += s;
+    }
+    const float inv0 = 1.0f / sqrtf(ss0 / (float)hd + Q.eps), inv1 = 1.0f / sqrtf(ss1 / (float)hd + Q.eps);
+    const float inv2 = 1.0f / sqrtf(ss2 / (float)hd + Q.eps), inv3 = 1.0f / sqrtf(ss3 / (float)hd + Q.eps);
+    const bool live = row < M;
+    // Frequency-major tables: entry (f, pos) at f * tstride + pos, so the 32 lanes (consecutive
+    // rows, mostly consecutive positions) of a warp read neighbouring addresses.
+    // RoPE angles: position * inv_freq in f32 exactly as the reference's tables (src/ops.rs:303-306),
+    // then sin / cos after a Cody-Waite reduction to [-pi, pi] on the MUFU unit (abs. error < 1e-6).
+    const int half = Q.part / 2;
+    const float* invs = wsm + 2 * hd;
+    const long ldo = (long)nheads * hd;
+#pragma unroll 1
+    for (int c = 0; c < BN / 32; c++) {
+        const int col0 = c * 32, hi = col0 / hd, hc = col0 % hd;
+        const float inv = hi == 0 ? inv0 : hi == 1 ? inv1 : hi == 2 ? inv2 : inv3;
+        const long col_base = (long)(head0 + hi) * hd;
+        if (!rot) {
+            uint32_t r[32];
+            tmem_ld32(tbase + col0, r);
+            tmem_ld_wait();
+            float o[32];
+#pragma unroll
+            for (int t = 0; t < 32; t++) o[t] = __uint_as_float(r[t]) * inv;
+            warp_store32<TOut>(base, ldo, row0, M, col_base + hc, o, stage);
+        } else if (half >= 32) {
+            if ((hc % Q.part) >= half) continue;  // written together with its partner chunk
+            uint32_t a[32], b[32];
+            tmem_ld32(tbase + col0, a);
+            tmem_ld32(tbase + col0 + half, b);
+            tmem_ld_wait();
+            const int pi = hc / Q.part, j0 = hc % Q.part;
+            const float pf = live ? (float)(Q.pos ? Q.pos[(long)row * Q.pos_stride + pi] : row) : 0.f;
+            float o1[32], o2[32];
+#pragma unroll
+            for (int t = 0; t < 32; t++) {
+                const float x1 = __uint_as_float(a[t]) * inv * w[hc + t];
+                const float x2 = __uint_as_float(b[t]) * inv * w[hc + half + t];
+                float sj, cj;
+                sincos_reduced(pf * invs[j0 + t], sj, cj);
+                o1[t] = x1 * cj - x2 * sj;
+                o2[t] = x2 * cj + x1 * sj;
+            }
+            warp_store32<TOut>(base, ldo, row0, M, col_base + hc, o1, stage);
+            warp_store32<TOut>(base, ldo, row0, M, col_base + hc + half, o2, stage);
+        } else {
+            // part == 32: both halves of each rotated pair lie in this chunk.
+            uint32_t a[32];
+            tmem_ld32(tbase + col0, a);
+            tmem_ld_wait();
+            const int pi = hc / Q.part;
+            const float pf = live ? (float)(Q.pos ? Q.pos[(long)row * Q.pos_stride + pi] : row) : 0.f;
+            float o[32];
+#pragma unroll
+            for (int t = 0; t < 16; t++) {
+                const float x1 = __uint_as_float(a[t]) * inv * w[hc + t];
+                const float x2 = __uint_as_float(a[t + 16]) * inv * w[hc + 16 + t];
+                float sj, cj;
+                sincos_reduced(pf * invs[t], sj, cj);
+                o[t] = x1 * cj - x2 * sj;
+                o[t + 16] = x2 * cj + x1 * sj;
+            }
+            warp_store32<TOut>(base, ldo, row0, M, col_base + hc, o, stage);
+        }
+    }
 }
 
 template <typename TIn, int BN, int EPI, typename TOut>
@@ -122,6 +240,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     } else if (warp == 1) {
         if (lane == 0) {
             constexpr uint32_t idesc = umma_idesc(GEMM_BM, BN, InTraits<TIn>::FMT);
+            const uint64_t da0 = umma_desc_sw128(smem_u32(smem), 16, 1024);
             int stage = 0;
             uint32_t phase = 0;
             int local = 0;
@@ -134,14 +253,12 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
                 for (int kb = 0; kb < kblocks; kb++) {
                     if (!mbar_wait(&full[stage], phase, EG2_DEV_TIMEOUT_GEMM, abort_flag)) goto done;
                     tc_fence_after();
-                    const uint32_t sa = smem_u32(smem + stage * Cfg::STAGE_BYTES);
-                    const uint32_t sb = sa + Cfg::A_BYTES;
+                    // One add per MMA on prebuilt descriptors (32-byte K steps = 2 address units).
+                    const uint64_t ad = da0 + (uint64_t)(stage * (Cfg::STAGE_BYTES >> 4));
+                    const uint64_t bd = ad + (uint64_t)(Cfg::A_BYTES >> 4);
+                    mma_bf16_or_tf32<TIn>(d_tmem, ad, bd, idesc, kb != 0);
 #pragma unroll
-                    for (int kk = 0; kk < 4; kk++) {
-                        const uint64_t ad = umma_desc_sw128(sa + kk * 32, 16, 1024);
-                        const uint64_t bd = umma_desc_sw128(sb + kk * 32, 16, 1024);
-                        mma_bf16_or_tf32<TIn>(d_tmem, ad, bd, idesc, (kb | kk) != 0);
-                    }
+                    for (int kk = 1; kk < 4; kk++) mma_bf16_or_tf32<TIn>(d_tmem, ad + 2 * kk, bd + 2 * kk, idesc, 1);
                     mma_commit(&empty[stage]);
                     if (++stage == STAGES) {
                         stage = 0;
@@ -153,6 +270,15 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         }
     } else {
         const int e = warp & 3;  // TMEM lane quadrant this warp may access
+        float* wsm = reinterpret_cast<float*>(smem + Cfg::OFF_W);
+        if constexpr (EPI == EPI_QKV) {
+            // q_norm / k_norm weights once per CTA (the 4 epilogue warps share them).
+            const int hd = epi.qkv.hd;
+            const int nf = epi.qkv.part / 2;  // distinct inverse frequencies
+            for (int i = threadIdx.x - 64; i < 2 * hd + nf; i += 128)
+                wsm[i] = i < hd ? epi.qkv.wq[i] : i < 2 * hd ? epi.qkv.wk[i - hd] : epi.qkv.inv_freq[i - 2 * hd];
+            asm volatile("bar.sync 1, 128;" ::: "memory");
+        }
         int local = 0;
         for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, local++) {
             const int acc = local & 1;
@@ -160,9 +286,12 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             if (!mbar_wait(&tfull[acc], acc_phase, EG2_DEV_TIMEOUT_GEMM, abort_flag)) break;
             tc_fence_after();
             const int m0 = (tile / tiles_n) * GEMM_BM, n0 = (tile % tiles_n) * BN;
-            const int row = m0 + 32 * e + lane;
+            const int row0 = m0 + 32 * e, row = row0 + lane;
+            uint8_t* stage = smem + Cfg::OFF_STAGE + e * Cfg::STAGE_WARP;
             const uint32_t tbase = tmem_base + ((uint32_t)(32 * e) << 16) + acc * BN;
-            if constexpr (EPI == EPI_GELU_GU) {
+            if constexpr (EPI == EPI_QKV) {
+                epilogue_qkv<TOut, BN>(epi, tbase, row0, M, n0, stage, wsm);
+            } else if constexpr (EPI == EPI_GELU_GU) {
                 // Tile columns [0, BN/2) are gate features, [BN/2, BN) the matching up features.
                 TOut* out = reinterpret_cast<TOut*>(epi.out);
 #pragma unroll 1
@@ -174,7 +303,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
                     float v[32];
 #pragma unroll
                     for (int j = 0; j < 32; j++) v[j] = gelu_tanh_f(__uint_as_float(g[j])) * __uint_as_float(u[j]);
-                    if (row < M) store32<TOut>(out + (long)row * epi.ldo + n0 / 2 + c * 32, v);
+                    warp_store32<TOut>(out, epi.ldo, row0, M, n0 / 2 + c * 32, v, stage);
                 }
             } else {
                 TOut* out = reinterpret_cast<TOut*>(epi.out);
@@ -189,7 +318,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
                             const float4* pl = reinterpret_cast<const float4*>(epi.aux + (long)row * epi.aux_ld + epi.aux_off + n0 + c * 32);
 #pragma unroll
                             for (int q = 0; q < 8; q++) {
-                                float4 p4 = pl[q];
+                                const float4 p4 = pl[q];
                                 v[4 * q + 0] = gelu_tanh_f(__uint_as_float(r[4 * q + 0])) * p4.x;
                                 v[4 * q + 1] = gelu_tanh_f(__uint_as_float(r[4 * q + 1])) * p4.y;
                                 v[4 * q + 2] = gelu_tanh_f(__uint_as_float(r[4 * q + 2])) * p4.z;
@@ -200,7 +329,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
 #pragma unroll
                         for (int j = 0; j < 32; j++) v[j] = __uint_as_float(r[j]) * epi.scale;
                     }
-                    if (row < M) store32<TOut>(out + (long)row * epi.ldo + n0 + c * 32, v);
+                    warp_store32<TOut>(out, epi.ldo, row0, M, n0 + c * 32, v, stage);
                 }
             }
             tc_fence_before();
@@ -237,6 +366,13 @@ static int launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N,
     return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
 
+bool qkv_fusable(const QkvEpilogue& q) {
+    const int hd = q.hd, half = q.part / 2;
+    if (hd <= 0 || hd % 32 || 256 % hd || q.part <= 0 || hd % q.part) return false;
+    if ((q.nh * hd) % 256 || (q.nkv * hd) % 256) return false;
+    return q.part == 32 || (half >= 32 && half % 32 == 0);
+}
+
 int gemm_tc(GemmKind kind, const void* A, long lda, const void* W, long ldw, int M, int N, int K,
             const GemmEpilogue& epi, cudaStream_t s) {
     if (M <= 0) return 0;
@@ -245,6 +381,7 @@ int gemm_tc(GemmKind kind, const void* A, long lda, const void* W, long ldw, int
     const int esize = tf32 ? 4 : 2;
     const int BK = 128 / esize;
     if (N % BN || K % BK || lda % (16 / esize) || ldw % (16 / esize)) return -1;
+    if (epi.mode == EPI_QKV && !qkv_fusable(epi.qkv)) return -1;
     CUtensorMap ta, tb;
     const CUtensorMapDataType dt = tf32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
     if (make_tmap_2d(&ta, dt, A, K, M, lda * esize, BK, GEMM_BM) || make_tmap_2d(&tb, dt, W, K, N, ldw * esize, BK, BN))
@@ -258,8 +395,11 @@ int gemm_tc(GemmKind kind, const void* A, long lda, const void* W, long ldw, int
                 return launch_tc<bf16_t, BN, EPI_GELU_GU, bf16_t>(ta, tb, M, N, K, epi, s);
             case EPI_PLE_GATE:
                 return launch_tc<bf16_t, BN, EPI_PLE_GATE, bf16_t>(ta, tb, M, N, K, epi, s);
+            case EPI_QKV:
+                return launch_tc<bf16_t, BN, EPI_QKV, bf16_t>(ta, tb, M, N, K, epi, s);
         }
     } else {
+        if (epi.mode == EPI_QKV) return launch_tc<float, BN, EPI_QKV, float>(ta, tb, M, N, K, epi, s);
         switch (epi.mode) {
             case EPI_STORE:
                 return launch_tc<float, BN, EPI_STORE, float>(ta, tb, M, N, K, epi, s);

@@ -14,6 +14,18 @@ enum EpiMode : int {
     EPI_STORE = 0,     // out = acc * scale (bf16 or f32)
     EPI_GELU_GU = 1,   // weights interleaved in 128-row gate / up halves per 256-row block: out = gelu(g) * u
     EPI_PLE_GATE = 2,  // out = gelu(acc) * aux[row * aux_ld + aux_off + col]
+    EPI_QKV = 3,       // fused projection [q | k | v] -> per-head RMSNorm (+ weights on q, k) and RoPE on
+                       // q, k, written to q [M, nh, hd], k / v [M, nkv, hd]; needs 256 % hd == 0
+};
+
+struct QkvEpilogue {
+    void *q = nullptr, *k = nullptr, *v = nullptr;
+    const float *wq = nullptr, *wk = nullptr;
+    const float* inv_freq = nullptr;  // part / 2 RoPE inverse frequencies (f32, as the reference computes them)
+    const int* pos = nullptr;         // position of row r, rotation part pi: pos[r * pos_stride + pi] (nullptr: r)
+    int pos_stride = 1;
+    int nh = 0, nkv = 0, hd = 0, part = 0;     // part: rotation width (hd, or hd / 2 for 2-D RoPE)
+    float eps = 1e-6f;
 };
 
 struct GemmEpilogue {
@@ -25,6 +37,7 @@ struct GemmEpilogue {
     long aux_ld = 0;
     int aux_off = 0;
     float scale = 1.f;
+    QkvEpilogue qkv;
 };
 
 // Number of SMs of the current device (cached per device).
@@ -38,6 +51,8 @@ int make_tmap_2d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint6
 int make_tmap_3d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t d0, uint64_t d1, uint64_t d2,
                  uint64_t s1, uint64_t s2, uint32_t b0, uint32_t b1, uint32_t b2);
 
+// Whether EPI_QKV applies to a head configuration (whole heads per 256-column tile).
+bool qkv_fusable(const QkvEpilogue& q);
 // C = A . W^T on tcgen05 (bf16 or tf32 inputs). N must be a multiple of 256, K of 64 (bf16) / 32 (tf32).
 int gemm_tc(GemmKind kind, const void* A, long lda, const void* W, long ldw, int M, int N, int K,
             const GemmEpilogue& epi, cudaStream_t s);

@@ -18,55 +18,86 @@
 
 namespace eg2 {
 
-// Load 16 consecutive-in-stride elements of a 512-wide row: element (lane * 4 + 128 * j + c).
-template <typename T>
-EG2_DEV void load_row(const T* r, int dim, float* v) {
-    for (int j = 0; j < dim / 128; j++)
+// Row kernels: one warp per row; lane l owns the VPL = dim / 32 contiguous columns
+// [l * VPL, (l + 1) * VPL), so every load and store is a 16-byte vector and a warp sweeps each row
+// as one contiguous 2 KB (f32) / 1 KB (bf16) span.
+template <int VPL>
+EG2_DEV void ld_row(const float* p, float (&v)[VPL]) {
 #pragma unroll
-        for (int c = 0; c < 4; c++) v[4 * j + c] = ldf(r, (long)(threadIdx.x & 31) * 4 + 128 * j + c);
+    for (int q = 0; q < VPL / 4; q++) {
+        const float4 a = reinterpret_cast<const float4*>(p)[q];
+        v[4 * q] = a.x, v[4 * q + 1] = a.y, v[4 * q + 2] = a.z, v[4 * q + 3] = a.w;
+    }
+}
+template <int VPL>
+EG2_DEV void ld_row(const bf16_t* p, float (&v)[VPL]) {
+#pragma unroll
+    for (int q = 0; q < VPL / 8; q++) {
+        const uint4 a = reinterpret_cast<const uint4*>(p)[q];
+        const uint32_t u[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            v[8 * q + 2 * i] = __uint_as_float(u[i] << 16);
+            v[8 * q + 2 * i + 1] = __uint_as_float(u[i] & 0xffff0000u);
+        }
+    }
+}
+template <int VPL>
+EG2_DEV void st_row(float* p, const float (&v)[VPL]) {
+#pragma unroll
+    for (int q = 0; q < VPL / 4; q++)
+        reinterpret_cast<float4*>(p)[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+}
+template <int VPL>
+EG2_DEV void st_row(bf16_t* p, const float (&v)[VPL]) {
+#pragma unroll
+    for (int q = 0; q < VPL / 8; q++)
+        reinterpret_cast<uint4*>(p)[q] =
+            make_uint4(bf16x2_bits(v[8 * q], v[8 * q + 1]), bf16x2_bits(v[8 * q + 2], v[8 * q + 3]),
+                       bf16x2_bits(v[8 * q + 4], v[8 * q + 5]), bf16x2_bits(v[8 * q + 6], v[8 * q + 7]));
 }
 
-constexpr int ROW_MAX_VALS = 24;  // dims up to 768
-
 // ---------------------------------------------------------------------------------------------
-template <typename TO>
+template <typename TO, int VPL>
 __global__ void rms_norm_kernel(const float* __restrict__ x, TO* __restrict__ out, const float* __restrict__ w, long rows,
-                                int dim, float eps, float pre) {
-    long row = (long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+                                float eps, float pre) {
+    const long row = (long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (row >= rows) return;
-    const int lane = threadIdx.x & 31;
-    const float* r = x + row * dim;
-    float v[ROW_MAX_VALS];
-    const int nj = dim / 128;
+    constexpr int dim = 32 * VPL;
+    const long base = row * dim + (threadIdx.x & 31) * VPL;
+    float v[VPL];
+    ld_row<VPL>(x + base, v);
     float ss = 0.f;
-    for (int j = 0; j < nj; j++) {
-        float4 a = *reinterpret_cast<const float4*>(r + lane * 4 + 128 * j);
-        v[4 * j + 0] = a.x * pre;
-        v[4 * j + 1] = a.y * pre;
-        v[4 * j + 2] = a.z * pre;
-        v[4 * j + 3] = a.w * pre;
 #pragma unroll
-        for (int c = 0; c < 4; c++) ss = fmaf(v[4 * j + c], v[4 * j + c], ss);
+    for (int i = 0; i < VPL; i++) {
+        v[i] *= pre;
+        ss = fmaf(v[i], v[i], ss);
     }
     ss = warp_sum(ss);
     const float inv = 1.0f / sqrtf(ss / (float)dim + eps);
-    TO* o = out + row * dim;
-    for (int j = 0; j < nj; j++)
+    if (w) {
+        float wv[VPL];
+        ld_row<VPL>(w + (threadIdx.x & 31) * VPL, wv);
 #pragma unroll
-        for (int c = 0; c < 4; c++) {
-            const int col = lane * 4 + 128 * j + c;
-            float n = v[4 * j + c] * inv;
-            if (w) n *= w[col];
-            stf(o, col, n);
-        }
+        for (int i = 0; i < VPL; i++) v[i] = v[i] * inv * wv[i];
+    } else {
+#pragma unroll
+        for (int i = 0; i < VPL; i++) v[i] *= inv;
+    }
+    st_row<VPL>(out + base, v);
 }
 
 template <typename TO>
 int rms_norm_rows(const float* x, TO* out, const float* w, long rows, int dim, float eps, float pre, cudaStream_t s) {
     if (rows <= 0) return 0;
-    if (dim % 128 || dim > 128 * (ROW_MAX_VALS / 4)) return -1;
     const int wpb = 8;
-    rms_norm_kernel<TO><<<(unsigned)((rows + wpb - 1) / wpb), 32 * wpb, 0, s>>>(x, out, w, rows, dim, eps, pre);
+    const unsigned grid = (unsigned)((rows + wpb - 1) / wpb);
+    if (dim == 512)
+        rms_norm_kernel<TO, 16><<<grid, 32 * wpb, 0, s>>>(x, out, w, rows, eps, pre);
+    else if (dim == 768)
+        rms_norm_kernel<TO, 24><<<grid, 32 * wpb, 0, s>>>(x, out, w, rows, eps, pre);
+    else
+        return -1;
     return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
 template int rms_norm_rows<float>(const float*, float*, const float*, long, int, float, float, cudaStream_t);
@@ -77,57 +108,53 @@ int rms_norm_inplace(float* x, const float* w, long rows, int dim, float eps, fl
 }
 
 // ---------------------------------------------------------------------------------------------
-template <typename TI, typename TT>
+template <typename TI, typename TT, int VPL>
 __global__ void add_norm_kernel(float* __restrict__ h, const TI* __restrict__ o, const float* __restrict__ w1,
-                                TT* __restrict__ t, const float* __restrict__ w2, long rows, int dim, float eps,
-                                float scalar) {
-    long row = (long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+                                TT* __restrict__ t, const float* __restrict__ w2, long rows, float eps, float scalar) {
+    const long row = (long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (row >= rows) return;
-    const int lane = threadIdx.x & 31;
-    const int nj = dim / 128;
-    float v[ROW_MAX_VALS];
-    load_row(o + row * dim, dim, v);
+    constexpr int dim = 32 * VPL;
+    const int c0 = (threadIdx.x & 31) * VPL;
+    const long base = row * dim + c0;
+    float v[VPL], hv[VPL], wv[VPL];
+    ld_row<VPL>(o + base, v);
+    ld_row<VPL>(h + base, hv);
+    ld_row<VPL>(w1 + c0, wv);
     float ss = 0.f;
-    for (int i = 0; i < 4 * nj; i++) ss = fmaf(v[i], v[i], ss);
+#pragma unroll
+    for (int i = 0; i < VPL; i++) ss = fmaf(v[i], v[i], ss);
     ss = warp_sum(ss);
     const float inv1 = 1.0f / sqrtf(ss / (float)dim + eps);
-    float* hr = h + row * dim;
     float ss2 = 0.f;
-    for (int j = 0; j < nj; j++) {
-        float4 hv = *reinterpret_cast<float4*>(hr + lane * 4 + 128 * j);
-        float hh[4] = {hv.x, hv.y, hv.z, hv.w};
 #pragma unroll
-        for (int c = 0; c < 4; c++) {
-            const int col = lane * 4 + 128 * j + c;
-            const float n = v[4 * j + c] * inv1 * w1[col];
-            hh[c] = (hh[c] + n) * scalar;
-            v[4 * j + c] = hh[c];
-            ss2 = fmaf(hh[c], hh[c], ss2);
-        }
-        *reinterpret_cast<float4*>(hr + lane * 4 + 128 * j) = make_float4(hh[0], hh[1], hh[2], hh[3]);
+    for (int i = 0; i < VPL; i++) {
+        hv[i] = (hv[i] + v[i] * inv1 * wv[i]) * scalar;
+        ss2 = fmaf(hv[i], hv[i], ss2);
     }
+    st_row<VPL>(h + base, hv);
     if (!t) return;
-    TT* tr = t + row * dim;
-    float inv2 = 1.f;
     if (w2) {
         ss2 = warp_sum(ss2);
-        inv2 = 1.0f / sqrtf(ss2 / (float)dim + eps);
-    }
-    for (int j = 0; j < nj; j++)
+        const float inv2 = 1.0f / sqrtf(ss2 / (float)dim + eps);
+        ld_row<VPL>(w2 + c0, wv);
 #pragma unroll
-        for (int c = 0; c < 4; c++) {
-            const int col = lane * 4 + 128 * j + c;
-            stf(tr, col, w2 ? v[4 * j + c] * inv2 * w2[col] : v[4 * j + c]);
-        }
+        for (int i = 0; i < VPL; i++) hv[i] = hv[i] * inv2 * wv[i];
+    }
+    st_row<VPL>(t + base, hv);
 }
 
 template <typename TI, typename TT>
 int add_norm(float* h, const TI* o, const float* w1, TT* t, const float* w2, long rows, int dim, float eps, float scalar,
              cudaStream_t s) {
     if (rows <= 0) return 0;
-    if (dim % 128 || dim > 128 * (ROW_MAX_VALS / 4)) return -1;
     const int wpb = 8;
-    add_norm_kernel<TI, TT><<<(unsigned)((rows + wpb - 1) / wpb), 32 * wpb, 0, s>>>(h, o, w1, t, w2, rows, dim, eps, scalar);
+    const unsigned grid = (unsigned)((rows + wpb - 1) / wpb);
+    if (dim == 512)
+        add_norm_kernel<TI, TT, 16><<<grid, 32 * wpb, 0, s>>>(h, o, w1, t, w2, rows, eps, scalar);
+    else if (dim == 768)
+        add_norm_kernel<TI, TT, 24><<<grid, 32 * wpb, 0, s>>>(h, o, w1, t, w2, rows, eps, scalar);
+    else
+        return -1;
     return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
 template int add_norm<float, float>(float*, const float*, const float*, float*, const float*, long, int, float, float, cudaStream_t);

@@ -323,8 +323,9 @@ struct RopeTab {
     double theta = 0;
     int hd = 0;
     long len = 0;
-    float* cs = nullptr;
+    float* cs = nullptr;  // [len, hd / 2]: one position per row (qkv_post: a warp reads one row)
     float* sn = nullptr;
+    float* inv = nullptr;  // [hd / 2] inverse frequencies (the fused GEMM epilogue computes its own angles)
 };
 
 // ---------------------------------------------------------------------------------------------
@@ -384,6 +385,7 @@ struct eg2_ctx {
     // vision workspace
     long vcap = 0;
     float *v_hidden = nullptr, *v_pooled = nullptr, *v_cs = nullptr, *v_sn = nullptr, *v_soft = nullptr;
+    float* v_inv = nullptr;  // [hd / 4] axial inverse frequencies
     void *v_x = nullptr, *v_t = nullptr, *v_qkv = nullptr, *v_q = nullptr, *v_k = nullptr, *v_v = nullptr, *v_a = nullptr,
          *v_o = nullptr, *v_gate = nullptr, *v_gu = nullptr;
     int *v_pos = nullptr, *v_seq_start = nullptr, *v_seq_len = nullptr;
@@ -609,6 +611,10 @@ static void ensure_rope(eg2_ctx* c, long max_len) {
         r.sn = (float*)dalloc(c, sn.size() * 4);
         CK(cudaMemcpy(r.cs, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice));
         CK(cudaMemcpy(r.sn, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice));
+        if (!r.inv) {
+            r.inv = (float*)dalloc(c, half * 4);
+            CK(cudaMemcpy(r.inv, inv.data(), half * 4, cudaMemcpyHostToDevice));
+        }
         r.len = len;
     }
 }
@@ -723,6 +729,24 @@ static void gemm(eg2_ctx* c, const void* x, long ldx, const void* W, int M, int 
     KL(gemm_tc(bf16_mode(c) ? GEMM_BF16 : GEMM_TF32, x, ldx, W, K, M, N, K, e, c->stream), "gemm_tc");
 }
 
+// The q/k/v projection with per-head RMSNorm and RoPE fused into the tensor-core GEMM's epilogue
+// (EPI_QKV). Returns false when the configuration does not fuse (f32 precision, or heads that do
+// not tile the 256-column output tile); the caller then runs GEMM + qkv_post.
+static bool qkv_projection(eg2_ctx* c, const void* x, int k, const void* W, long rows, void* q, void* kk, void* v,
+                           const float* wq, const float* wk, const float* inv_freq, const int* pos, int pos_stride, int nh, int nkv, int hd, int part, float eps) {
+    if (c->precision == EG2_F32 || getenv("EG2_NO_QKV_FUSION")) return false;
+    GemmEpilogue e;
+    e.mode = EPI_QKV;
+    QkvEpilogue& Q = e.qkv;
+    Q.q = q, Q.k = kk, Q.v = v, Q.wq = wq, Q.wk = wk, Q.inv_freq = inv_freq, Q.pos = pos, Q.pos_stride = pos_stride;
+    Q.nh = nh, Q.nkv = nkv, Q.hd = hd, Q.part = part, Q.eps = eps;
+    if (!qkv_fusable(Q)) return false;
+    KL(gemm_tc(bf16_mode(c) ? GEMM_BF16 : GEMM_TF32, x, k, W, k, (int)rows, (nh + 2 * nkv) * hd, k, e, c->stream),
+       "gemm qkv + norm/rope");
+    mark(c, "gemm qkv + norm/rope");
+    return true;
+}
+
 template <typename T>
 static void attention(eg2_ctx* c, const T* q, const T* k, const T* v, T* out, long rows, int nh, int nkv, int hd,
                       int window, const int* seq_start, const int* seq_len, const AttnTile* tiles, int n_tiles);
@@ -776,12 +800,15 @@ static void enqueue_text(eg2_ctx* c, long rows, const std::vector<TileSet>& tset
         const int hd = L.hd, nkv = L.nkv;
         const int nqkv = (nh + 2 * nkv) * hd;
         const RopeTab& rt = c->ropes[L.rope];
-        gemm(c, t, h, L.qkv, (int)rows, nqkv, h, w.qkv, nqkv, EPI_STORE, true);
-        mark(c, "gemm qkv");
-        KL((qkv_post<float, T>((const float*)w.qkv, (T*)w.q, (T*)w.k, (T*)w.v, L.q_norm, L.k_norm, rt.cs, rt.sn, hd / 2, w.pos,
-                           rows, nh, nkv, hd, hd, eps, c->stream)),
-           "qkv_post");
-        mark(c, "qkv_post");
+        if (!qkv_projection(c, t, h, L.qkv, rows, w.q, w.k, w.v, L.q_norm, L.k_norm, rt.inv, w.pos, 1, nh, nkv,
+                            hd, hd, eps)) {
+            gemm(c, t, h, L.qkv, (int)rows, nqkv, h, w.qkv, nqkv, EPI_STORE, true);
+            mark(c, "gemm qkv");
+            KL((qkv_post<float, T>((const float*)w.qkv, (T*)w.q, (T*)w.k, (T*)w.v, L.q_norm, L.k_norm, rt.cs, rt.sn, hd / 2,
+                               w.pos, rows, nh, nkv, hd, hd, eps, c->stream)),
+               "qkv_post");
+            mark(c, "qkv_post");
+        }
         const AttnTile* tiles = nullptr;
         int n_tiles = 0;
         for (const TileSet& s : tsets)
@@ -911,10 +938,13 @@ static void enqueue_vision(eg2_ctx* c, long n, int gh, int gw) {
     const int nqkv = (nh + 2 * nkv) * hd;
     for (int l = 0; l < vc.layers; l++) {
         const VLayerW& L = c->vlayers[l];
-        gemm(c, t, h, L.qkv, (int)n, nqkv, h, c->v_qkv, nqkv, EPI_STORE, true);
-        KL((qkv_post<float, T>((const float*)c->v_qkv, (T*)c->v_q, (T*)c->v_k, (T*)c->v_v, L.q_norm, L.k_norm, c->v_cs, c->v_sn,
-                           hd / 2, nullptr, n, nh, nkv, hd, hd / 2, eps, c->stream)),
-           "qkv_post");
+        if (!qkv_projection(c, t, h, L.qkv, n, c->v_q, c->v_k, c->v_v, L.q_norm, L.k_norm, c->v_inv, c->v_pos, 2,
+                            nh, nkv, hd, hd / 2, eps)) {
+            gemm(c, t, h, L.qkv, (int)n, nqkv, h, c->v_qkv, nqkv, EPI_STORE, true);
+            KL((qkv_post<float, T>((const float*)c->v_qkv, (T*)c->v_q, (T*)c->v_k, (T*)c->v_v, L.q_norm, L.k_norm, c->v_cs,
+                               c->v_sn, hd / 2, nullptr, n, nh, nkv, hd, hd / 2, eps, c->stream)),
+               "qkv_post");
+        }
         mark(c, "vision qkv");
         if (f32)
             KL(attention_simt<float>((const float*)c->v_q, (const float*)c->v_k, (const float*)c->v_v, (float*)c->v_a,
@@ -1198,6 +1228,7 @@ int eg2_vision_encode(eg2_ctx* c, const float* patches, const int32_t* pos_xy, i
         if (n > c->vcap) {
             CK(cudaStreamSynchronize(c->stream));
             void** bufs[] = {(void**)&c->v_hidden, (void**)&c->v_pooled, (void**)&c->v_cs, (void**)&c->v_sn, (void**)&c->v_soft,
+                             (void**)&c->v_inv,
                              &c->v_x, &c->v_t, &c->v_qkv, &c->v_q, &c->v_k, &c->v_v, &c->v_a, &c->v_o, &c->v_gate, &c->v_gu,
                              (void**)&c->v_pos, (void**)&c->v_seq_start, (void**)&c->v_seq_len};
             for (void** b : bufs) {
@@ -1210,6 +1241,7 @@ int eg2_vision_encode(eg2_ctx* c, const float* patches, const int32_t* pos_xy, i
             c->v_soft = (float*)dalloc(c, cap * c->tc.hidden * 4);
             c->v_cs = (float*)dalloc(c, cap * (hd / 2) * 4);
             c->v_sn = (float*)dalloc(c, cap * (hd / 2) * 4);
+            c->v_inv = (float*)dalloc(c, 4 * hd);
             c->v_x = dalloc(c, cap * pd * 4);
             c->v_t = dalloc(c, cap * std::max(h, pd) * as);
             c->v_qkv = dalloc(c, cap * (nh + 2 * nkv) * hd * 4);
@@ -1233,9 +1265,11 @@ int eg2_vision_encode(eg2_ctx* c, const float* patches, const int32_t* pos_xy, i
             for (int axis = 0; axis < 2; axis++)
                 for (int i = 0; i < q4; i++) {
                     const float f = (float)pos_xy[2 * t + axis] * inv[i];
-                    cs[(size_t)t * (hd / 2) + axis * q4 + i] = cosf(f);
-                    sn[(size_t)t * (hd / 2) + axis * q4 + i] = sinf(f);
+                    const int col = axis * q4 + i;
+                    cs[(size_t)t * (hd / 2) + col] = cosf(f);
+                    sn[(size_t)t * (hd / 2) + col] = sinf(f);
                 }
+        CK(cudaMemcpyAsync(c->v_inv, inv.data(), inv.size() * 4, cudaMemcpyHostToDevice, c->stream));
         std::vector<int> zeros(n, 0), lens_v(n, (int)n);
         CK(cudaMemcpyAsync(c->v_cs, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice, c->stream));
         CK(cudaMemcpyAsync(c->v_sn, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice, c->stream));
