@@ -3,14 +3,17 @@
 //
 // Replaces the reference's cuBLAS calls `Gpu::gemm_bf16` (src/gpu/mod.rs:600-630, cublasGemmEx
 // bf16 -> f32 accumulate) and `Gpu::matmul_nt` in TF32 mode (src/gpu/mod.rs:554-577), plus the
-// elementwise kernels that follow them: `gelu_mul_gu` (kernels.cu:239-246, fused as EPI_GELU_GU)
-// and `ple_gate` (kernels.cu:294-299, fused as EPI_PLE_GATE).
+// elementwise kernels that follow them: `gelu_mul_gu` (kernels.cu:239-246, fused as EPI_GELU_GU),
+// `ple_gate` (kernels.cu:294-299, fused as EPI_PLE_GATE) and `qkv_post` (kernels.cu:183-237,
+// fused as EPI_QKV for head widths that tile the 256 output columns).
 //
 // Structure (one CTA per SM, persistent over output tiles of 128 x BN):
-//   warp 0      TMA producer: A tile [128 x 64 bf16] and W tile [BN x 64] per stage, 128 B swizzle
-//   warp 1      TMEM allocation; lane 0 issues tcgen05.mma (M=128, N=BN, K=16) and commits
-//   warps 2..5  epilogue: tcgen05.ld of the accumulator, fused math, stores to global memory
-// Two TMEM accumulators (2 x BN columns) let the epilogue of tile i overlap the MMAs of tile i+1.
+//   warp 0       TMA producer: A tile [128 x 64 bf16] and W tile [BN x 64] per stage, 128 B swizzle
+//   warp 1       TMEM allocation; lane 0 issues tcgen05.mma (M=128, N=BN, K=16) and commits
+//   warps 2..9   two epilogue sets of 4 warps (one warp per TMEM lane quadrant). Set s owns TMEM
+//                accumulator s and the CTA's tiles of parity s, so two tiles' epilogues run at once
+//                while the MMAs of a third fill the free accumulator: the epilogues (norms, RoPE,
+//                GELU) are latency-bound and need the extra warps to overlap the main loop.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -30,7 +33,7 @@ struct InTraits<float> {
 };
 
 constexpr int GEMM_BM = 128;
-constexpr int GEMM_THREADS = 192;
+constexpr int GEMM_THREADS = 320;
 
 template <int BN>
 struct GemmCfg {
@@ -39,47 +42,63 @@ struct GemmCfg {
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
     static constexpr int STAGES = (BN == 256) ? 4 : 6;
     static constexpr int OFF_STAGE = STAGES * STAGE_BYTES + 256;  // after the barriers
-    static constexpr int STAGE_WARP = 32 * (128 + 16);            // 32 rows x 32 f32 + 16 B pad
-    static constexpr int OFF_W = OFF_STAGE + 4 * STAGE_WARP;      // EPI_QKV: q / k norm weights
+    static constexpr int STAGE_WARP = 32 * (64 + 16);             // 32 rows x 64 B + 16 B pad
+    static constexpr int OFF_W = OFF_STAGE + 8 * STAGE_WARP;      // EPI_QKV: norm weights, inv freqs
     static constexpr int SMEM_BYTES = 1024 + OFF_W + 3072;
     static constexpr uint32_t TMEM_COLS = 2 * BN;
 };
 
-// Warp-cooperative store of a 32-row x 32-column output chunk (lane i holds row row0 + i):
-// the chunk goes through a padded shared-memory tile, then each store instruction writes whole
-// 64 / 128-byte row segments of 8 / 4 rows (instead of 32 scattered 16-byte pieces). Rows >= M
-// are skipped. All 32 lanes must call it.
+// GELU (tanh form) for the tensor-core epilogues: 0.5 x (1 + tanh(u)) = x * sigmoid(2 u), with
+// sigmoid via ex2 and a fast reciprocal; within ~2e-7 relative of gelu_tanh_f (which the
+// float32 path keeps), far below the bf16 / TF32 rounding these results go through.
+EG2_DEV float gelu_fast(float x) {
+    const float u = 0.79788456f * (x + 0.044715f * x * x * x);
+    return __fdividef(x, 1.f + ex2_approx(-2.8853900817779268f * u));  // 2 log2(e) u
+}
+
+// Warp-cooperative store of a 32-row x 32-column chunk (lane i holds row row0 + i): each 64-byte
+// row segment goes through the warp's padded shared-memory tile, then every store instruction
+// writes whole 64-byte segments of 8 rows instead of 32 scattered 16-byte pieces. f32 chunks go
+// in two 16-column halves. Rows >= M are skipped. All 32 lanes must call it.
 template <typename TOut>
 EG2_DEV void warp_store32(TOut* out, long ldo, int row0, int M, long col, const float (&v)[32], uint8_t* stage) {
     const int lane = threadIdx.x & 31;
-    constexpr int ROWB = 32 * (int)sizeof(TOut), STRIDE = ROWB + 16, PIECES = ROWB / 16;
-    uint8_t* my = stage + lane * STRIDE;
-    if constexpr (sizeof(TOut) == 2) {
+    constexpr int STRIDE = 64 + 16;
+    constexpr int COLS = 64 / (int)sizeof(TOut);  // columns per 64-byte segment
 #pragma unroll
-        for (int q = 0; q < 4; q++)
-            *reinterpret_cast<uint4*>(my + q * 16) = make_uint4(bf16x2_bits(v[8 * q + 0], v[8 * q + 1]), bf16x2_bits(v[8 * q + 2], v[8 * q + 3]),
-                                                                bf16x2_bits(v[8 * q + 4], v[8 * q + 5]), bf16x2_bits(v[8 * q + 6], v[8 * q + 7]));
-    } else {
+    for (int h = 0; h < 32 / COLS; h++) {
+        uint8_t* my = stage + lane * STRIDE;
+        if constexpr (sizeof(TOut) == 2) {
 #pragma unroll
-        for (int q = 0; q < 8; q++)
-            *reinterpret_cast<float4*>(my + q * 16) = make_float4(v[4 * q + 0], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+            for (int q = 0; q < 4; q++)
+                *reinterpret_cast<uint4*>(my + q * 16) =
+                    make_uint4(bf16x2_bits(v[8 * q + 0], v[8 * q + 1]), bf16x2_bits(v[8 * q + 2], v[8 * q + 3]),
+                               bf16x2_bits(v[8 * q + 4], v[8 * q + 5]), bf16x2_bits(v[8 * q + 6], v[8 * q + 7]));
+        } else {
+#pragma unroll
+            for (int q = 0; q < 4; q++)
+                *reinterpret_cast<float4*>(my + q * 16) =
+                    make_float4(v[16 * h + 4 * q], v[16 * h + 4 * q + 1], v[16 * h + 4 * q + 2], v[16 * h + 4 * q + 3]);
+        }
+        __syncwarp();
+#pragma unroll
+        for (int p = lane; p < 32 * 4; p += 32) {
+            const int r = p >> 2, sg = p & 3;
+            if (row0 + r < M)
+                *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(out + (long)(row0 + r) * ldo + col + h * COLS) + sg * 16) =
+                    *reinterpret_cast<const uint4*>(stage + r * STRIDE + sg * 16);
+        }
+        __syncwarp();
     }
-    __syncwarp();
-#pragma unroll
-    for (int p = lane; p < 32 * PIECES; p += 32) {
-        const int r = p / PIECES, sg = p % PIECES;
-        if (row0 + r < M)
-            *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(out + (long)(row0 + r) * ldo + col) + sg * 16) =
-                *reinterpret_cast<const uint4*>(stage + r * STRIDE + sg * 16);
-    }
-    __syncwarp();
 }
 
 // EPI_QKV: the tile's BN columns are whole heads of one kind (q, k or v). Pass 1 reads the
 // accumulator for the per-head sums of squares; pass 2 reads it again, normalises (q / k times
 // their norm weights), applies RoPE to q / k (split-halves rule, pairs i and i + part / 2) and
-// stores the heads. Mirrors qkv_post_kernel (rowops.cu) operation for operation. All 32 lanes
-// run every tcgen05.ld; rows past M only skip the stores.
+// stores the heads. Operation for operation the arithmetic of qkv_post_kernel (rowops.cu), except
+// that the RoPE angle pos * inv_freq (computed in f32 like the reference's tables, src/ops.rs:303-306)
+// goes through sincos_reduced instead of a table. All 32 lanes run every tcgen05.ld; rows past M
+// only skip the stores.
 template <typename TOut, int BN>
 EG2_DEV void epilogue_qkv(const GemmEpilogue& epi, uint32_t tbase, int row0, int M, int n0, uint8_t* stage,
                           const float* wsm) {
@@ -97,7 +116,7 @@ EG2_DEV void epilogue_qkv(const GemmEpilogue& epi, uint32_t tbase, int row0, int
     } else {
         base = (TOut*)Q.v, nheads = Q.nkv, head0 = (n0 - qw - kw) / hd, w = nullptr, rot = false;
     }
-    float ss0 = 0.f, ss1 = 0.f, ss2 = 0.f, ss3 = 0.f;
+    float ss[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll 1
     for (int c = 0; c < BN / 32; c++) {
         uint32_t r[32];
@@ -107,25 +126,24 @@ EG2_DEV void epilogue_qkv(const GemmEpilogue& epi, uint32_t tbase, int row0, int
 #pragma unroll
         for (int j = 0; j < 32; j++) s = fmaf(__uint_as_float(r[j]), __uint_as_float(r[j]), s);
         const int hi = (c * 32) / hd;
-        if (hi == 0) ss0 += s;
-        else if (hi == 1) ss1 += s;
-        else if (hi == 2) ss2 += s;
-        else ss3 += s;
+#pragma unroll
+        for (int q = 0; q < 4; q++)
+            if (q == hi) ss[q] += s;
     }
-    const float inv0 = 1.0f / sqrtf(ss0 / (float)hd + Q.eps), inv1 = 1.0f / sqrtf(ss1 / (float)hd + Q.eps);
-    const float inv2 = 1.0f / sqrtf(ss2 / (float)hd + Q.eps), inv3 = 1.0f / sqrtf(ss3 / (float)hd + Q.eps);
+    float inv[4];
+#pragma unroll
+    for (int q = 0; q < 4; q++) inv[q] = 1.0f / sqrtf(ss[q] / (float)hd + Q.eps);
     const bool live = row < M;
-    // Frequency-major tables: entry (f, pos) at f * tstride + pos, so the 32 lanes (consecutive
-    // rows, mostly consecutive positions) of a warp read neighbouring addresses.
-    // RoPE angles: position * inv_freq in f32 exactly as the reference's tables (src/ops.rs:303-306),
-    // then sin / cos after a Cody-Waite reduction to [-pi, pi] on the MUFU unit (abs. error < 1e-6).
     const int half = Q.part / 2;
     const float* invs = wsm + 2 * hd;
     const long ldo = (long)nheads * hd;
 #pragma unroll 1
     for (int c = 0; c < BN / 32; c++) {
         const int col0 = c * 32, hi = col0 / hd, hc = col0 % hd;
-        const float inv = hi == 0 ? inv0 : hi == 1 ? inv1 : hi == 2 ? inv2 : inv3;
+        float iv = inv[0];
+#pragma unroll
+        for (int q = 1; q < 4; q++)
+            if (q == hi) iv = inv[q];
         const long col_base = (long)(head0 + hi) * hd;
         if (!rot) {
             uint32_t r[32];
@@ -133,44 +151,53 @@ EG2_DEV void epilogue_qkv(const GemmEpilogue& epi, uint32_t tbase, int row0, int
             tmem_ld_wait();
             float o[32];
 #pragma unroll
-            for (int t = 0; t < 32; t++) o[t] = __uint_as_float(r[t]) * inv;
+            for (int t = 0; t < 32; t++) o[t] = __uint_as_float(r[t]) * iv;
             warp_store32<TOut>(base, ldo, row0, M, col_base + hc, o, stage);
         } else if (half >= 32) {
             if ((hc % Q.part) >= half) continue;  // written together with its partner chunk
-            uint32_t a[32], b[32];
-            tmem_ld32(tbase + col0, a);
-            tmem_ld32(tbase + col0 + half, b);
-            tmem_ld_wait();
             const int pi = hc / Q.part, j0 = hc % Q.part;
             const float pf = live ? (float)(Q.pos ? Q.pos[(long)row * Q.pos_stride + pi] : row) : 0.f;
-            float o1[32], o2[32];
+            float x1[32], x2[32];
+            {
+                uint32_t a[32], b[32];
+                tmem_ld32(tbase + col0, a);
+                tmem_ld32(tbase + col0 + half, b);
+                tmem_ld_wait();
+#pragma unroll
+                for (int t = 0; t < 32; t++) {
+                    x1[t] = __uint_as_float(a[t]) * iv * w[hc + t];
+                    x2[t] = __uint_as_float(b[t]) * iv * w[hc + half + t];
+                }
+            }
 #pragma unroll
             for (int t = 0; t < 32; t++) {
-                const float x1 = __uint_as_float(a[t]) * inv * w[hc + t];
-                const float x2 = __uint_as_float(b[t]) * inv * w[hc + half + t];
                 float sj, cj;
                 sincos_reduced(pf * invs[j0 + t], sj, cj);
-                o1[t] = x1 * cj - x2 * sj;
-                o2[t] = x2 * cj + x1 * sj;
+                const float a1 = x1[t], a2 = x2[t];
+                x1[t] = a1 * cj - a2 * sj;
+                x2[t] = a2 * cj + a1 * sj;
             }
-            warp_store32<TOut>(base, ldo, row0, M, col_base + hc, o1, stage);
-            warp_store32<TOut>(base, ldo, row0, M, col_base + hc + half, o2, stage);
+            warp_store32<TOut>(base, ldo, row0, M, col_base + hc, x1, stage);
+            warp_store32<TOut>(base, ldo, row0, M, col_base + hc + half, x2, stage);
         } else {
             // part == 32: both halves of each rotated pair lie in this chunk.
-            uint32_t a[32];
-            tmem_ld32(tbase + col0, a);
-            tmem_ld_wait();
             const int pi = hc / Q.part;
             const float pf = live ? (float)(Q.pos ? Q.pos[(long)row * Q.pos_stride + pi] : row) : 0.f;
             float o[32];
+            {
+                uint32_t a[32];
+                tmem_ld32(tbase + col0, a);
+                tmem_ld_wait();
+#pragma unroll
+                for (int t = 0; t < 32; t++) o[t] = __uint_as_float(a[t]) * iv * w[hc + t];
+            }
 #pragma unroll
             for (int t = 0; t < 16; t++) {
-                const float x1 = __uint_as_float(a[t]) * inv * w[hc + t];
-                const float x2 = __uint_as_float(a[t + 16]) * inv * w[hc + 16 + t];
                 float sj, cj;
                 sincos_reduced(pf * invs[t], sj, cj);
-                o[t] = x1 * cj - x2 * sj;
-                o[t + 16] = x2 * cj + x1 * sj;
+                const float a1 = o[t], a2 = o[t + 16];
+                o[t] = a1 * cj - a2 * sj;
+                o[t + 16] = a2 * cj + a1 * sj;
             }
             warp_store32<TOut>(base, ldo, row0, M, col_base + hc, o, stage);
         }
@@ -212,6 +239,13 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         tma_prefetch_desc(&tmA);
         tma_prefetch_desc(&tmB);
     }
+    if constexpr (EPI == EPI_QKV) {
+        // q_norm / k_norm weights and the inverse frequencies, once per CTA.
+        float* wsm = reinterpret_cast<float*>(smem + Cfg::OFF_W);
+        const int hd = epi.qkv.hd, nf = epi.qkv.part / 2;
+        for (int i = threadIdx.x; i < 2 * hd + nf; i += GEMM_THREADS)
+            wsm[i] = i < hd ? epi.qkv.wq[i] : i < 2 * hd ? epi.qkv.wk[i - hd] : epi.qkv.inv_freq[i - 2 * hd];
+    }
     if (warp == 1) tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
     tc_fence_before();
     __syncthreads();
@@ -240,6 +274,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     } else if (warp == 1) {
         if (lane == 0) {
             constexpr uint32_t idesc = umma_idesc(GEMM_BM, BN, InTraits<TIn>::FMT);
+            // Descriptors are built once; a K step of 32 bytes adds 2 to the start-address field.
             const uint64_t da0 = umma_desc_sw128(smem_u32(smem), 16, 1024);
             int stage = 0;
             uint32_t phase = 0;
@@ -253,7 +288,6 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
                 for (int kb = 0; kb < kblocks; kb++) {
                     if (!mbar_wait(&full[stage], phase, EG2_DEV_TIMEOUT_GEMM, abort_flag)) goto done;
                     tc_fence_after();
-                    // One add per MMA on prebuilt descriptors (32-byte K steps = 2 address units).
                     const uint64_t ad = da0 + (uint64_t)(stage * (Cfg::STAGE_BYTES >> 4));
                     const uint64_t bd = ad + (uint64_t)(Cfg::A_BYTES >> 4);
                     mma_bf16_or_tf32<TIn>(d_tmem, ad, bd, idesc, kb != 0);
@@ -269,71 +303,68 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             }
         }
     } else {
-        const int e = warp & 3;  // TMEM lane quadrant this warp may access
-        float* wsm = reinterpret_cast<float*>(smem + Cfg::OFF_W);
-        if constexpr (EPI == EPI_QKV) {
-            // q_norm / k_norm weights once per CTA (the 4 epilogue warps share them).
-            const int hd = epi.qkv.hd;
-            const int nf = epi.qkv.part / 2;  // distinct inverse frequencies
-            for (int i = threadIdx.x - 64; i < 2 * hd + nf; i += 128)
-                wsm[i] = i < hd ? epi.qkv.wq[i] : i < 2 * hd ? epi.qkv.wk[i - hd] : epi.qkv.inv_freq[i - 2 * hd];
-            asm volatile("bar.sync 1, 128;" ::: "memory");
-        }
-        int local = 0;
-        for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, local++) {
-            const int acc = local & 1;
-            const uint32_t acc_phase = (local >> 1) & 1;
-            if (!mbar_wait(&tfull[acc], acc_phase, EG2_DEV_TIMEOUT_GEMM, abort_flag)) break;
+        const int e = warp & 3;           // TMEM lane quadrant this warp may access
+        const int set = (warp - 2) >> 2;  // epilogue set = accumulator it owns
+        const float* wsm = reinterpret_cast<const float*>(smem + Cfg::OFF_W);
+        uint8_t* stage = smem + Cfg::OFF_STAGE + (warp - 2) * Cfg::STAGE_WARP;
+        TOut* out = reinterpret_cast<TOut*>(epi.out);
+        int k = 0;  // tiles this set has taken: its k-th completion of tfull[set]
+        for (int tile = blockIdx.x + set * gridDim.x; tile < num_tiles; tile += 2 * gridDim.x, k++) {
+            if (!mbar_wait(&tfull[set], k & 1, EG2_DEV_TIMEOUT_GEMM, abort_flag)) break;
             tc_fence_after();
             const int m0 = (tile / tiles_n) * GEMM_BM, n0 = (tile % tiles_n) * BN;
             const int row0 = m0 + 32 * e, row = row0 + lane;
-            uint8_t* stage = smem + Cfg::OFF_STAGE + e * Cfg::STAGE_WARP;
-            const uint32_t tbase = tmem_base + ((uint32_t)(32 * e) << 16) + acc * BN;
+            const uint32_t tbase = tmem_base + ((uint32_t)(32 * e) << 16) + set * BN;
             if constexpr (EPI == EPI_QKV) {
                 epilogue_qkv<TOut, BN>(epi, tbase, row0, M, n0, stage, wsm);
             } else if constexpr (EPI == EPI_GELU_GU) {
                 // Tile columns [0, BN/2) are gate features, [BN/2, BN) the matching up features.
-                TOut* out = reinterpret_cast<TOut*>(epi.out);
 #pragma unroll 1
                 for (int c = 0; c < BN / 64; c++) {
-                    uint32_t g[32], u[32];
-                    tmem_ld32(tbase + c * 32, g);
-                    tmem_ld32(tbase + BN / 2 + c * 32, u);
-                    tmem_ld_wait();
                     float v[32];
+                    {
+                        uint32_t g[32], u[32];
+                        tmem_ld32(tbase + c * 32, g);
+                        tmem_ld32(tbase + BN / 2 + c * 32, u);
+                        tmem_ld_wait();
 #pragma unroll
-                    for (int j = 0; j < 32; j++) v[j] = gelu_tanh_f(__uint_as_float(g[j])) * __uint_as_float(u[j]);
+                        for (int j = 0; j < 32; j++) v[j] = gelu_fast(__uint_as_float(g[j])) * __uint_as_float(u[j]);
+                    }
                     warp_store32<TOut>(out, epi.ldo, row0, M, n0 / 2 + c * 32, v, stage);
                 }
             } else {
-                TOut* out = reinterpret_cast<TOut*>(epi.out);
 #pragma unroll 1
                 for (int c = 0; c < BN / 32; c++) {
-                    uint32_t r[32];
-                    tmem_ld32(tbase + c * 32, r);
-                    tmem_ld_wait();
                     float v[32];
+                    {
+                        uint32_t r[32];
+                        tmem_ld32(tbase + c * 32, r);
+                        tmem_ld_wait();
+#pragma unroll
+                        for (int j = 0; j < 32; j++) v[j] = __uint_as_float(r[j]);
+                    }
                     if constexpr (EPI == EPI_PLE_GATE) {
                         if (row < M) {
-                            const float4* pl = reinterpret_cast<const float4*>(epi.aux + (long)row * epi.aux_ld + epi.aux_off + n0 + c * 32);
+                            const float4* pl =
+                                reinterpret_cast<const float4*>(epi.aux + (long)row * epi.aux_ld + epi.aux_off + n0 + c * 32);
 #pragma unroll
                             for (int q = 0; q < 8; q++) {
                                 const float4 p4 = pl[q];
-                                v[4 * q + 0] = gelu_tanh_f(__uint_as_float(r[4 * q + 0])) * p4.x;
-                                v[4 * q + 1] = gelu_tanh_f(__uint_as_float(r[4 * q + 1])) * p4.y;
-                                v[4 * q + 2] = gelu_tanh_f(__uint_as_float(r[4 * q + 2])) * p4.z;
-                                v[4 * q + 3] = gelu_tanh_f(__uint_as_float(r[4 * q + 3])) * p4.w;
+                                v[4 * q + 0] = gelu_fast(v[4 * q + 0]) * p4.x;
+                                v[4 * q + 1] = gelu_fast(v[4 * q + 1]) * p4.y;
+                                v[4 * q + 2] = gelu_fast(v[4 * q + 2]) * p4.z;
+                                v[4 * q + 3] = gelu_fast(v[4 * q + 3]) * p4.w;
                             }
                         }
                     } else {
 #pragma unroll
-                        for (int j = 0; j < 32; j++) v[j] = __uint_as_float(r[j]) * epi.scale;
+                        for (int j = 0; j < 32; j++) v[j] *= epi.scale;
                     }
                     warp_store32<TOut>(out, epi.ldo, row0, M, n0 + c * 32, v, stage);
                 }
             }
             tc_fence_before();
-            mbar_arrive(&tempty[acc]);
+            mbar_arrive(&tempty[set]);
         }
     }
 done:
