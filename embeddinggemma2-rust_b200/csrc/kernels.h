@@ -78,8 +78,10 @@ int gelu_gu(const TI* gu, TO* out, long rows, int ff, cudaStream_t s);
 template <typename TI, typename TO>
 int ple_gate(const TI* g, TO* out, const float* ple, long rows, int p, int n_layers, int layer, cudaStream_t s);
 // dims_dev: device array of n_dims cut widths (the first is normally dim itself); out row stride out_stride.
-int pool_rows(const float* x, const int* seq_start, const int* seq_len, int n_seq, int dim, const int* dims_dev,
-              int n_dims, int out_stride, float* out, cudaStream_t s);
+// scratch: pool_scratch_doubles(n_seq, max_len, dim) doubles of partial sums.
+int pool_scratch_doubles(int n_seq, int max_len, int dim);
+int pool_rows(const float* x, const int* seq_start, const int* seq_len, int n_seq, int max_len, int dim,
+              const int* dims_dev, int n_dims, int out_stride, float* out, double* scratch, cudaStream_t s);
 int embed_gather(const bf16_t* table, long vocab, int h, const uint32_t* ids, long n, float scale, float* out,
                  int* bad, cudaStream_t s);
 template <typename TO>

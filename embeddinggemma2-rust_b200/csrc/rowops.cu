@@ -286,18 +286,42 @@ template int ple_gate<float, float>(const float*, float*, const float*, long, in
 // ---------------------------------------------------------------------------------------------
 // Mean over a sequence's rows (f64 sums), L2 normalisation (f64) and Matryoshka cuts: for each
 // sequence the output holds, back to back, the normalised first dims[d] components for each d.
-__global__ void pool_kernel(const float* __restrict__ x, const int* __restrict__ seq_start, const int* __restrict__ seq_len,
-                            int dim, const int* __restrict__ dims, int n_dims, int out_stride, float* __restrict__ out) {
+// Two stages so that every SM works on long sequences: pool_partial_kernel sums chunks of
+// POOL_CHUNK rows (block (s, ch), one float4 column group per thread) into partial[s][ch][dim];
+// pool_final_kernel adds a sequence's chunks in order (deterministic) and normalises.
+constexpr int POOL_CHUNK = 128;
+
+__global__ void pool_partial_kernel(const float* __restrict__ x, const int* __restrict__ seq_start,
+                                    const int* __restrict__ seq_len, int dim, int n_chunks, double* __restrict__ partial) {
+    const int s = blockIdx.x, ch = blockIdx.y;
+    const long r0 = seq_start[s];
+    const int len = seq_len[s];
+    const int a = ch * POOL_CHUNK, b = min(len, a + POOL_CHUNK);
+    for (int c4 = threadIdx.x; c4 < dim / 4; c4 += blockDim.x) {
+        double acc[4] = {0.0, 0.0, 0.0, 0.0};
+        const float* col = x + (r0 + a) * dim + 4 * c4;
+#pragma unroll 4
+        for (int r = a; r < b; r++, col += dim) {
+            const float4 v = *reinterpret_cast<const float4*>(col);
+            acc[0] += (double)v.x, acc[1] += (double)v.y, acc[2] += (double)v.z, acc[3] += (double)v.w;
+        }
+        double* dst = partial + ((long)s * n_chunks + ch) * dim + 4 * c4;
+        dst[0] = acc[0], dst[1] = acc[1], dst[2] = acc[2], dst[3] = acc[3];
+    }
+}
+
+__global__ void pool_final_kernel(const double* __restrict__ partial, const int* __restrict__ seq_len, int dim,
+                                  int n_chunks, const int* __restrict__ dims, int n_dims, int out_stride,
+                                  float* __restrict__ out) {
     extern __shared__ double dsh[];  // dim means + 32 partials
     double* mean = dsh;
     double* part = dsh + dim;
     const int sidx = blockIdx.x;
-    const long r0 = seq_start[sidx];
     const int len = seq_len[sidx];
+    const int used = (len + POOL_CHUNK - 1) / POOL_CHUNK;
     for (int c = threadIdx.x; c < dim; c += blockDim.x) {
         double acc = 0.0;
-        const float* col = x + r0 * dim + c;
-        for (int r = 0; r < len; r++) acc += (double)col[(long)r * dim];
+        for (int ch = 0; ch < used; ch++) acc += partial[((long)sidx * n_chunks + ch) * dim + c];
         mean[c] = (double)(float)(acc / (double)len);
     }
     __syncthreads();
@@ -320,10 +344,18 @@ __global__ void pool_kernel(const float* __restrict__ x, const int* __restrict__
     }
 }
 
-int pool_rows(const float* x, const int* seq_start, const int* seq_len, int n_seq, int dim, const int* dims_dev,
-                  int n_dims, int out_stride, float* out, cudaStream_t s) {
+int pool_scratch_doubles(int n_seq, int max_len, int dim) {
+    return n_seq * ((max_len + POOL_CHUNK - 1) / POOL_CHUNK) * dim;
+}
+
+int pool_rows(const float* x, const int* seq_start, const int* seq_len, int n_seq, int max_len, int dim,
+              const int* dims_dev, int n_dims, int out_stride, float* out, double* scratch, cudaStream_t s) {
     if (n_seq <= 0) return 0;
-    pool_kernel<<<n_seq, 256, (dim + 32) * sizeof(double), s>>>(x, seq_start, seq_len, dim, dims_dev, n_dims, out_stride, out);
+    if (dim % 4) return -1;
+    const int n_chunks = (max_len + POOL_CHUNK - 1) / POOL_CHUNK;
+    pool_partial_kernel<<<dim3(n_seq, n_chunks), 192, 0, s>>>(x, seq_start, seq_len, dim, n_chunks, scratch);
+    pool_final_kernel<<<n_seq, 256, (dim + 32) * sizeof(double), s>>>(scratch, seq_len, dim, n_chunks, dims_dev, n_dims,
+                                                                     out_stride, out);
     return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
 

@@ -357,6 +357,8 @@ struct Work {
     int* dims = nullptr;
     int seq_meta_cap = 0;
     int* seq_meta = nullptr;
+    long pool_scratch_cap = 0;
+    double* pool_scratch = nullptr;
 };
 
 }  // namespace eg2
@@ -1189,7 +1191,19 @@ static int embed_impl(eg2_ctx* c, const uint32_t* ids, const int32_t* lens, int 
                         c->bad_flag, c->stream),
            "embed_gather");
         run_text(c, rows, sets);
-        KL(pool_rows(w.out, seq_meta, seq_meta + n_seq, n_seq, c->tc.emb, w.dims, n_dims, total, w.pooled, c->stream), "pool");
+        int max_len = 0;
+        for (int s2 = 0; s2 < n_seq; s2++) max_len = std::max(max_len, (int)lens[s2]);
+        const long need = pool_scratch_doubles(n_seq, max_len, c->tc.emb);
+        if (need > w.pool_scratch_cap) {
+            CK(cudaStreamSynchronize(c->stream));
+            dfree(c, w.pool_scratch);
+            w.pool_scratch_cap = std::max(need, 1L << 20);
+            w.pool_scratch = (double*)dalloc(c, w.pool_scratch_cap * 8);
+        }
+        KL(pool_rows(w.out, seq_meta, seq_meta + n_seq, n_seq, max_len, c->tc.emb, w.dims, n_dims, total, w.pooled,
+                     w.pool_scratch, c->stream),
+           "pool");
+        g_launches.fetch_add(1, std::memory_order_relaxed);  // pool_rows is two launches
         mark(c, "pool");
         CK(cudaMemcpyAsync(out, w.pooled, (size_t)n_seq * total * 4,
                            device_ptrs ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost, c->stream));
