@@ -8,4 +8,5 @@
 #include "simt.cu"
 #include "rowops.cu"
 #include "attention_tc.cu"
+#include "noalloc.cu"
 #include "runtime.cu"

@@ -98,6 +98,9 @@ struct AttnTile {
 // Tensor-core flash attention, bf16 q/k/v/out, GQA-packed query tiles (attention_tc.cu).
 int attention_tc(const bf16_t* q, const bf16_t* k, const bf16_t* v, bf16_t* out, long rows, const AttnTile* tiles,
                  int n_tiles, int nh, int nkv, int hd, int window, cudaStream_t s);
+// attention_tc with its tile list built in a fixed device array instead of allocated memory (noalloc.cu).
+int attention_noalloc(const bf16_t* q, const bf16_t* k, const bf16_t* v, bf16_t* out, const int32_t* lens, int n_seq,
+                      int nh, int nkv, int hd, int window, cudaStream_t s);
 // Query tokens per tile of attention_tc for a head configuration.
 int attention_tc_tile_tokens(int nh, int nkv);
 // CUDA-core attention (f32 arithmetic; bf16 or f32 storage), one warp per (row, head).

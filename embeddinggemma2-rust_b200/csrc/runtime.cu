@@ -1405,6 +1405,16 @@ int eg2_attention(int kind, const void* q, const void* k, const void* v, void* o
     return stv ? EG2_ERR_TIMEOUT : EG2_OK;
 }
 
+int eg2_attention_noalloc(const void* q, const void* k, const void* v, void* out, const int32_t* lens, int n_seq, int nh,
+                          int nkv, int hd, int window, void* stream) {
+    const int rc = attention_noalloc((const bf16_t*)q, (const bf16_t*)k, (const bf16_t*)v, (bf16_t*)out, lens, n_seq, nh,
+                                     nkv, hd, window, (cudaStream_t)stream);
+    if (rc == -1) return EG2_ERR_INVALID;
+    if (rc) return EG2_ERR_CUDA;
+    g_launches.fetch_add(2, std::memory_order_relaxed);
+    return EG2_OK;
+}
+
 long long eg2_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
 
 int eg2_device_status(void) {

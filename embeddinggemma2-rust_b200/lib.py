@@ -66,6 +66,7 @@ def load(build_if_missing: bool = True) -> C.CDLL:
         "eg2_profile_read": (C.c_int, [_P, C.c_char_p, C.c_int]),
         "eg2_gemm": (C.c_int, [C.c_int, _P, C.c_int64, _P, C.c_int64, _P, C.c_int64, C.c_int, C.c_int, C.c_int, C.c_int, _P]),
         "eg2_attention": (C.c_int, [C.c_int, _P, _P, _P, _P, _I32P, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, _P]),
+        "eg2_attention_noalloc": (C.c_int, [_P, _P, _P, _P, _I32P, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, _P]),
         "eg2_launch_count": (C.c_longlong, []),
         "eg2_device_status": (C.c_int, []),
         "eg2_device_status_reset": (None, []),

@@ -111,6 +111,19 @@ int eg2_gemm(int kind, const void* A, int64_t lda, const void* W, int64_t ldw, v
 int eg2_attention(int kind, const void* q, const void* k, const void* v, void* out, const int32_t* lens, int n_seq,
                   int nh, int nkv, int hd, int window, void* stream);
 
+/* No counterpart in the reference. The tensor-core attention of eg2_attention (kind EG2_BF16,
+ * same arguments and results) without any device allocation, for callers that cannot call
+ * cudaMalloc: engines that hand all device memory to their own pool up front, code recording into
+ * a CUDA graph, latency-critical paths that cannot take cudaMalloc's implicit synchronisation.
+ * Its scratch (sequence lengths and the query-tile list) lives in one fixed 1 MiB device array per
+ * GPU, held until the process exits; calls with more than 65536 sequences or 65536 query tiles
+ * (~4 M rows at 64 tokens per tile) return EG2_ERR_INVALID. The first call on a device looks the
+ * array up (make that first call before any stream capture). All calls share the array: calls
+ * that overlap on the GPU (unordered streams or threads) race. The call is asynchronous on
+ * `stream` and reads `lens` from host memory before it returns. */
+int eg2_attention_noalloc(const void* q, const void* k, const void* v, void* out, const int32_t* lens, int n_seq,
+                          int nh, int nkv, int hd, int window, void* stream);
+
 /* Number of kernel launches this library has issued in the process (all contexts). */
 long long eg2_launch_count(void);
 
