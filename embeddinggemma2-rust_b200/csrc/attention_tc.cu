@@ -14,10 +14,12 @@
 //
 //   warp 0      TMA: Q once (head_dim / 64 swizzled [128 x 64] boxes), then per 64-key tile the
 //               K chunks (ring of 4 x [64 x 64]) and the V tile [64 keys x 256] (VB buffers)
-//   warp 1      TMEM owner; lane 0 issues S = Q K^T (M 128, N 64, K 16) into S[j % 2] and
-//               O += P V (M 128, N 256, K 16, V read MN-major) and commits
-//   warps 2..5  softmax: thread = row; reads S from TMEM, masks, online max / sum in the log2
-//               domain, writes P (bf16, swizzled K-major) to P[j % 2]; O is rescaled in TMEM only
+//   warp 1      TMEM owner; lane 0 issues S = Q K^T (M 128, N 64, K 16) and O += P V (M 128,
+//               N 256, K 16, P read from TMEM, V read MN-major) and commits. Head 256 keeps Q in
+//               TMEM too (one S buffer); head 512 reads Q from shared memory (two S buffers)
+//   warps 2..5  softmax: thread = row; (head 256: first copies its Q row into TMEM) reads S from
+//               TMEM, masks, online max / sum in the log2 domain, writes P as packed bf16 pairs
+//               into P[j % 2] in TMEM; O is rescaled in TMEM only
 //               when a row max grows by more than 2^8 (else the stale max is kept, which is exact);
 //               at the end O / l is stored as bf16.
 #include "common.cuh"
@@ -29,10 +31,15 @@ constexpr int ATT_THREADS = 224;  // warp 0 Q/K loads, 1 MMA, 2..5 softmax, 6 V 
 constexpr int ATT_V_WARP = 6;
 constexpr int ATT_BN = 64;       // keys per tile
 constexpr int ATT_DV = 256;      // output channels per CTA
-// K chunk ring depth (slots of [64 keys x 64 channels]): as deep as shared memory allows, since
-// the kernel is bound by the latency of the K loads when fewer than ~2 key tiles are in flight.
+// K chunk ring depth (slots of [64 keys x 64 channels]): as deep as shared memory allows.
 template <int DQK>
 constexpr int att_kst() { return DQK == 256 ? 8 : 4; }
+// K chunks per barrier group: one mbarrier wait and one commit per group. The single thread that
+// issues the MMAs can only keep a couple of them queued, so every wait / commit between two MMA
+// groups leaves the tensor pipe idle; head 256 therefore loads and releases K a whole tile (4
+// chunks) at a time, head 512 two chunks at a time.
+template <int DQK>
+constexpr int att_kgrp() { return DQK == 256 ? 4 : 2; }
 constexpr float ATT_RESCALE_LOG2 = 8.f;
 
 template <int DQK, int VB>
@@ -58,19 +65,26 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
                         const __grid_constant__ CUtensorMap tmV, AttParams prm) {
     using Cfg = AttCfg<DQK, VB>;
     constexpr int QCH = DQK / 64;
+    // Head 256: Q is copied into TMEM and the S = Q K^T MMAs read it from there (only K comes from
+    // shared memory, which is the bandwidth these MMAs are limited by); one S buffer then fits.
+    constexpr bool QT = DQK == 256;
+    constexpr int NS = QT ? 1 : 2;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::OFF_BAR);
     uint64_t* q_full = bars;
+    constexpr int KGRP = att_kgrp<DQK>();
+    constexpr int NKG = att_kst<DQK>() / KGRP;  // barrier groups in the K ring
     uint64_t* k_full = bars + 1;
-    uint64_t* k_empty = k_full + att_kst<DQK>();
-    uint64_t* v_full = k_empty + att_kst<DQK>();
+    uint64_t* k_empty = k_full + NKG;
+    uint64_t* v_full = k_empty + NKG;
     uint64_t* v_empty = v_full + VB;
     uint64_t* s_full = v_empty + VB;
     uint64_t* s_empty = s_full + 2;
     uint64_t* p_full = s_empty + 2;
     uint64_t* pv_done = p_full + 2;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pv_done + 2);
+    uint64_t* q_tmem = pv_done + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(q_tmem + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -86,7 +100,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
 
     if (threadIdx.x == 0) {
         mbar_init(q_full, 1);
-        for (int s = 0; s < att_kst<DQK>(); s++) {
+        for (int s = 0; s < NKG; s++) {
             mbar_init(&k_full[s], 1);
             mbar_init(&k_empty[s], 1);
         }
@@ -100,6 +114,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
             mbar_init(&p_full[s], 128);
             mbar_init(&pv_done[s], 1);
         }
+        mbar_init(q_tmem, 128);
         *abort_flag = 0;
         fence_mbarrier_init();
     }
@@ -108,9 +123,13 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    const uint32_t t_s = tmem;          // S[0] cols [0, 64), S[1] cols [64, 128)
-    const uint32_t t_p = tmem + 128;    // P[0] cols [128, 160), P[1] cols [160, 192) (bf16 pairs)
-    const uint32_t t_o = tmem + 256;    // O cols [256, 512)
+    // TMEM columns. Q in TMEM (head 256): S [0, 64) single-buffered, P [64, 128), Q [128, 256),
+    // O [256, 512). Q in shared memory (head 512): S[0..1] [0, 128), P [128, 192), O [256, 512).
+    // P holds packed bf16 pairs: 32 columns per 64-key tile, two tiles.
+    const uint32_t t_s = tmem;
+    const uint32_t t_p = tmem + (QT ? 64 : 128);
+    const uint32_t t_q = tmem + 128;
+    const uint32_t t_o = tmem + 256;
 
     if (n_kt == 0) goto done;
 
@@ -122,16 +141,17 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
             mbar_arrive_expect_tx(q_full, Cfg::Q_BYTES);
             for (int c = 0; c < QCH; c++)
                 tma_load_3d(smem + c * 128 * 128, &tmQ, q_full, c * 64, g * G, tile.row0 + tile.q0);
-            int ks = 0;
+            int kg = 0;
             uint32_t kph = 0;
             for (int j = 0; j < n_kt; j++) {
                 const int key0 = tile.row0 + k_lo + j * ATT_BN;
-                for (int c = 0; c < QCH; c++) {
-                    if (!mbar_wait(&k_empty[ks], kph ^ 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) goto done;
-                    mbar_arrive_expect_tx(&k_full[ks], Cfg::K_SLOT);
-                    tma_load_3d(smem + Cfg::OFF_K + ks * Cfg::K_SLOT, &tmK, &k_full[ks], c * 64, g, key0);
-                    if (++ks == att_kst<DQK>()) {
-                        ks = 0;
+                for (int c0 = 0; c0 < QCH; c0 += KGRP) {
+                    if (!mbar_wait(&k_empty[kg], kph ^ 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) goto done;
+                    mbar_arrive_expect_tx(&k_full[kg], KGRP * Cfg::K_SLOT);
+                    for (int cc = 0; cc < KGRP; cc++)
+                        tma_load_3d(smem + Cfg::OFF_K + (kg * KGRP + cc) * Cfg::K_SLOT, &tmK, &k_full[kg], (c0 + cc) * 64, g, key0);
+                    if (++kg == NKG) {
+                        kg = 0;
                         kph ^= 1;
                     }
                 }
@@ -164,26 +184,38 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
             const uint64_t dq0 = umma_desc_sw128(smem_u32(smem), 16, 1024);
             const uint64_t dk0 = umma_desc_sw128(smem_u32(smem + Cfg::OFF_K), 16, 1024);
             const uint64_t dv0 = umma_desc_sw128(smem_u32(smem + Cfg::OFF_V), ATT_BN * 128, 1024);
-            int ks = 0, vs = 0;
+            int kg = 0, vs = 0;
             uint32_t kph = 0, vph = 0;
-            if (!mbar_wait(q_full, 0, EG2_DEV_TIMEOUT_ATTN, abort_flag)) goto done;
+            if (!mbar_wait(QT ? q_tmem : q_full, 0, EG2_DEV_TIMEOUT_ATTN, abort_flag)) goto done;
             // S[j % 2] = Q K_j^T over head_dim in 64-channel chunks.
             auto issue_qk = [&](int j) -> bool {
-                const int sb = j & 1;
+                const int sb = j % NS;
                 const uint32_t ts = t_s + sb * ATT_BN;
-                if (!mbar_wait(&s_empty[sb], ((j >> 1) & 1) ^ 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) return false;
+                if (!mbar_wait(&s_empty[sb], ((j / NS) & 1) ^ 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) return false;
                 tc_fence_after();
-                for (int c = 0; c < QCH; c++) {
-                    if (!mbar_wait(&k_full[ks], kph, EG2_DEV_TIMEOUT_ATTN, abort_flag)) return false;
-                    tc_fence_after();
-                    const uint64_t da = dq0 + (uint64_t)(c * (128 * 128 >> 4));
-                    const uint64_t db = dk0 + (uint64_t)(ks * (Cfg::K_SLOT >> 4));
-                    mma_bf16(ts, da, db, idesc_s, c != 0);
+                for (int c0 = 0; c0 < QCH; c0 += KGRP) {
+                    // K arrives by TMA (async proxy, like the MMA's reads): the barrier wait is enough.
+                    if (!mbar_wait(&k_full[kg], kph, EG2_DEV_TIMEOUT_ATTN, abort_flag)) return false;
 #pragma unroll
-                    for (int kk = 1; kk < 4; kk++) mma_bf16(ts, da + 2 * kk, db + 2 * kk, idesc_s, 1);
-                    mma_commit(&k_empty[ks]);
-                    if (++ks == att_kst<DQK>()) {
-                        ks = 0;
+                    for (int cc = 0; cc < KGRP; cc++) {
+                        const int c = c0 + cc;
+                        const uint64_t db = dk0 + (uint64_t)((kg * KGRP + cc) * (Cfg::K_SLOT >> 4));
+                        if constexpr (QT) {
+                            // A = Q from TMEM: 16 channels = 8 packed columns per MMA.
+                            const uint32_t ta = t_q + c * 32;
+                            mma_bf16_ts(ts, ta, db, idesc_s, c != 0);
+#pragma unroll
+                            for (int kk = 1; kk < 4; kk++) mma_bf16_ts(ts, ta + 8 * kk, db + 2 * kk, idesc_s, 1);
+                        } else {
+                            const uint64_t da = dq0 + (uint64_t)(c * (128 * 128 >> 4));
+                            mma_bf16(ts, da, db, idesc_s, c != 0);
+#pragma unroll
+                            for (int kk = 1; kk < 4; kk++) mma_bf16(ts, da + 2 * kk, db + 2 * kk, idesc_s, 1);
+                        }
+                    }
+                    mma_commit(&k_empty[kg]);
+                    if (++kg == NKG) {
+                        kg = 0;
                         kph ^= 1;
                     }
                 }
@@ -220,9 +252,28 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         const uint32_t lane_off = (uint32_t)(32 * e) << 16;
         const float LOG2E = 1.4426950408889634f;
         float m_used = -INFINITY, l = 0.f;
+        if constexpr (QT) {
+            // Q row r into TMEM columns [t_q, t_q + 128): un-swizzle the row from the four 128-byte
+            // swizzled TMA boxes; bf16 pairs are already packed the way the A operand wants them.
+            if (!mbar_wait(q_full, 0, EG2_DEV_TIMEOUT_ATTN, abort_flag)) goto done;
+#pragma unroll 1
+            for (int c = 0; c < QCH; c++) {
+                uint32_t qv[32];
+                const uint8_t* rowp = smem + c * 128 * 128 + r * 128;
+#pragma unroll
+                for (int piece = 0; piece < 8; piece++) {
+                    const uint4 u = *reinterpret_cast<const uint4*>(rowp + ((piece ^ (r & 7)) << 4));
+                    qv[4 * piece] = u.x, qv[4 * piece + 1] = u.y, qv[4 * piece + 2] = u.z, qv[4 * piece + 3] = u.w;
+                }
+                tmem_st32(t_q + c * 32 + lane_off, qv);
+            }
+            tmem_st_wait();
+            tc_fence_before();
+            mbar_arrive(q_tmem);
+        }
         for (int j = 0; j < n_kt; j++) {
-            const int sb = j & 1;
-            if (!mbar_wait(&s_full[sb], (j >> 1) & 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) break;
+            const int sb = j % NS, pb = j & 1;
+            if (!mbar_wait(&s_full[sb], (j / NS) & 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) break;
             tc_fence_after();
             uint32_t s0[32], s1[32];
             tmem_ld32(t_s + sb * ATT_BN + lane_off, s0);
@@ -248,9 +299,14 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
 #pragma unroll
                 for (int c = 0; c < 64; c++) sv[c] = (c >= lo_c && c < hi_c) ? sv[c] : -INFINITY;
             }
-            float mt = sv[0];
+            // Row max as 8 independent chains (a single warp per SM sub-partition: no other warp hides
+            // the latency of a 64-long dependent chain).
+            float mx[8];
 #pragma unroll
-            for (int c = 1; c < 64; c++) mt = fmaxf(mt, sv[c]);
+            for (int c = 0; c < 8; c++) mx[c] = sv[c];
+#pragma unroll
+            for (int c = 8; c < 64; c++) mx[c & 7] = fmaxf(mx[c & 7], sv[c]);
+            const float mt = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
             // Reference max (raw logit units): keep the stale one unless the new max exceeds it by
             // 2^8 in probability, so O is rescaled only rarely (the result is exact either way).
             float factor = 1.f;
@@ -265,7 +321,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
                 }
             }
             // P buffer reuse: PV(j - 2) must be done. Rescaling O also needs PV(j - 1) done.
-            if (j >= 2 && !mbar_wait(&pv_done[sb], ((j - 2) >> 1) & 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) break;
+            if (j >= 2 && !mbar_wait(&pv_done[pb], ((j - 2) >> 1) & 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) break;
             const bool warp_need = __any_sync(0xffffffffu, need);
             if (warp_need && j >= 1) {
                 if (!mbar_wait(&pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) break;
@@ -297,10 +353,10 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
                 pk[q] = bf16x2_bits(p0, p1);
             }
             l += (lsum[0] + lsum[1]) + (lsum[2] + lsum[3]);
-            tmem_st32(t_p + sb * (ATT_BN / 2) + lane_off, pk);
+            tmem_st32(t_p + pb * (ATT_BN / 2) + lane_off, pk);
             tmem_st_wait();
             tc_fence_before();
-            mbar_arrive(&p_full[sb]);
+            mbar_arrive(&p_full[pb]);
         }
         // Epilogue: O / l for this row's 256 channels.
         if (!*abort_flag && mbar_wait(&pv_done[(n_kt - 1) & 1], ((n_kt - 1) >> 1) & 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) {

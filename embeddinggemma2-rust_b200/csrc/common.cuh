@@ -156,7 +156,7 @@ EG2_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, int code, volatile int* a
 }
 
 // ---------------------------------------------------------------------------------------------
-// TMA (tiled tensor loads into this CTA's shared memory; no cluster multicast anywhere)
+// TMA (tiled tensor loads into this CTA's own shared memory)
 // ---------------------------------------------------------------------------------------------
 EG2_DEV void tma_prefetch_desc(const CUtensorMap* m) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");
