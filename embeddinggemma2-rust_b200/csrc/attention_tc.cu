@@ -340,8 +340,10 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
             l *= factor;
             // p = 2^((s - m_used) log2 e): one FFMA + one MUFU op per element; masked entries are
             // -inf and give 0 (a row with no valid key yet has m_used = -inf: bias 0 keeps it 0).
-            // Summed in f32, stored as packed bf16 pairs into P[j % 2] in TMEM (lane = row, column c
-            // holds keys 2c and 2c + 1: the A-operand layout of the P V product).
+            // Stored as packed bf16 pairs into P[j % 2] in TMEM (lane = row, column c holds keys 2c
+            // and 2c + 1: the A-operand layout of the P V product). The row sum adds the ROUNDED
+            // values, so the weights that multiply V sum to exactly l: with few keys an unrounded sum
+            // would scale the whole output row by up to 2^-9.
             const float bias = (m_used == -INFINITY) ? 0.f : -m_used * LOG2E;
             float lsum[4] = {0.f, 0.f, 0.f, 0.f};
             uint32_t pk[32];
@@ -349,8 +351,8 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
             for (int q = 0; q < 32; q++) {
                 const float p0 = ex2_approx(fmaf(sv[2 * q], LOG2E, bias));
                 const float p1 = ex2_approx(fmaf(sv[2 * q + 1], LOG2E, bias));
-                lsum[q & 3] += p0 + p1;
                 pk[q] = bf16x2_bits(p0, p1);
+                lsum[q & 3] += __uint_as_float(pk[q] << 16) + __uint_as_float(pk[q] & 0xffff0000u);
             }
             l += (lsum[0] + lsum[1]) + (lsum[2] + lsum[3]);
             tmem_st32(t_p + pb * (ATT_BN / 2) + lane_off, pk);
