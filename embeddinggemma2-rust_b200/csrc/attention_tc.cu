@@ -321,7 +321,10 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
                 }
             }
             // P buffer reuse: PV(j - 2) must be done. Rescaling O also needs PV(j - 1) done.
-            if (j >= 2 && !mbar_wait(&pv_done[pb], ((j - 2) >> 1) & 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) break;
+            if (j >= 2) {
+                if (!mbar_wait(&pv_done[pb], ((j - 2) >> 1) & 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) break;
+                tc_fence_after();
+            }
             const bool warp_need = __any_sync(0xffffffffu, need);
             if (warp_need && j >= 1) {
                 if (!mbar_wait(&pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) break;
@@ -366,6 +369,301 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
             const float inv = (l > 0.f) ? 1.f / l : 0.f;
             const int head = g * G + r % G;
             bf16_t* orow = prm.out + ((long)(tile.row0 + tok) * prm.nh + head) * prm.hd + dsplit * ATT_DV;
+#pragma unroll 1
+            for (int c = 0; c < ATT_DV / 32; c++) {
+                uint32_t o[32];
+                tmem_ld32(t_o + c * 32 + lane_off, o);
+                tmem_ld_wait();
+                if (row_valid) {
+                    uint4* d = reinterpret_cast<uint4*>(orow + c * 32);
+#pragma unroll
+                    for (int q = 0; q < 4; q++)
+                        d[q] = make_uint4(pack_bf16x2(__uint_as_float(o[8 * q + 0]) * inv, __uint_as_float(o[8 * q + 1]) * inv),
+                                          pack_bf16x2(__uint_as_float(o[8 * q + 2]) * inv, __uint_as_float(o[8 * q + 3]) * inv),
+                                          pack_bf16x2(__uint_as_float(o[8 * q + 4]) * inv, __uint_as_float(o[8 * q + 5]) * inv),
+                                          pack_bf16x2(__uint_as_float(o[8 * q + 6]) * inv, __uint_as_float(o[8 * q + 7]) * inv));
+                }
+            }
+        }
+    }
+done:
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 512);
+    }
+}
+
+// ---------------------------------------------------------------------------------------------
+// Head 256 with 128-key tiles.
+//
+// S = Q K^T runs at N = 128 (the full tensor rate; N = 64 MMAs reach ~60%) and every barrier wait
+// or commit covers twice the keys. TMEM: S [0, 128) (one buffer), P[0] [128, 192), P[1] [192, 256)
+// (packed bf16 pairs), O [256, 512). S(j + 1) is issued as soon as the softmax has copied S(j) into
+// registers, so it overlaps softmax(j); P V(j) follows once P(j) is written. K and V stream
+// through ONE ring of five 32 KB units in the order the MMAs consume them: K(j + 1) (two halves
+// of 128 channels), then V(j) (two halves of 64 keys).
+//
+//   warp 0      TMA producer (Q once, then the K / V units)
+//   warp 1      TMEM owner; lane 0 issues QK(j + 1), then P V(j)
+//   warps 2..5  softmax, one thread per row of the 128-row tile; O / l epilogue
+// ---------------------------------------------------------------------------------------------
+constexpr int AW_THREADS = 192;
+constexpr int AW_BN = 128;
+constexpr int AW_UNITS = 5;
+constexpr int AW_UNIT = 32768;
+struct AwCfg {
+    static constexpr int Q_BYTES = 4 * 128 * 128;
+    static constexpr int OFF_R = Q_BYTES;
+    static constexpr int OFF_BAR = OFF_R + AW_UNITS * AW_UNIT;
+    static constexpr int N_BARS = 1 + 2 * AW_UNITS + 6;  // q, ring full/empty, s full/empty, p[2], pv[2]
+    static constexpr int SMEM = 1024 + OFF_BAR + N_BARS * 8 + 16;
+};
+static_assert(AwCfg::SMEM <= 227 * 1024, "attention w128: shared memory");
+
+__global__ void __launch_bounds__(AW_THREADS, 1)
+    attention_w128_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                          const __grid_constant__ CUtensorMap tmV, AttParams prm) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + AwCfg::OFF_BAR);
+    uint64_t* q_full = bars;
+    uint64_t* r_full = bars + 1;
+    uint64_t* r_empty = r_full + AW_UNITS;
+    uint64_t* s_full = r_empty + AW_UNITS;
+    uint64_t* s_empty = s_full + 1;
+    uint64_t* p_full = s_empty + 1;
+    uint64_t* pv_done = p_full + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + AwCfg::N_BARS);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int tile_idx = blockIdx.x / prm.nkv;
+    const int g = blockIdx.x % prm.nkv;
+    const AttnTile tile = prm.tiles[tile_idx];
+    const int G = prm.G, W = prm.window;
+    const int q_last = min(tile.q0 + prm.tq, tile.len) - 1;
+    const int k_lo = (W >= 0) ? max(0, tile.q0 - W) : 0;
+    const int k_hi = (W >= 0) ? min(tile.len, q_last + W + 1) : tile.len;
+    const int n_kt = tile.len > 0 ? (k_hi - k_lo + AW_BN - 1) / AW_BN : 0;
+
+    if (threadIdx.x == 0) {
+        mbar_init(q_full, 1);
+        for (int u = 0; u < AW_UNITS; u++) {
+            mbar_init(&r_full[u], 1);
+            mbar_init(&r_empty[u], 1);
+        }
+        mbar_init(s_full, 1);
+        mbar_init(s_empty, 128);
+        for (int b = 0; b < 2; b++) {
+            mbar_init(&p_full[b], 128);
+            mbar_init(&pv_done[b], 1);
+        }
+        *abort_flag = 0;
+        fence_mbarrier_init();
+    }
+    if (warp == 1) tmem_alloc(tmem_slot, 512);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const uint32_t t_s = tmem;        // S: 128 fp32 columns
+    const uint32_t t_p = tmem + 128;  // P buffer b at t_p + 64 b
+    const uint32_t t_o = tmem + 256;  // O: 256 fp32 columns
+
+    if (n_kt == 0) goto done;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            mbar_arrive_expect_tx(q_full, AwCfg::Q_BYTES);
+            for (int c = 0; c < 4; c++) tma_load_3d(smem + c * 128 * 128, &tmQ, q_full, c * 64, g * G, tile.row0 + tile.q0);
+            int u = 0;
+            uint32_t uph = 0;
+            // One 32 KB unit: K channels [128 h, 128 h + 128) of key tile jt (two [128 x 64] boxes), or
+            // V keys [64 h, 64 h + 64) of key tile jt, all 256 channels (four [64 x 64] boxes).
+            auto load_unit = [&](bool is_k, int jt, int h) -> bool {
+                if (!mbar_wait(&r_empty[u], uph ^ 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) return false;
+                uint8_t* dst = smem + AwCfg::OFF_R + u * AW_UNIT;
+                const int key0 = tile.row0 + k_lo + jt * AW_BN;
+                mbar_arrive_expect_tx(&r_full[u], AW_UNIT);
+                if (is_k) {
+                    tma_load_3d(dst, &tmK, &r_full[u], (2 * h) * 64, g, key0);
+                    tma_load_3d(dst + 16384, &tmK, &r_full[u], (2 * h + 1) * 64, g, key0);
+                } else {
+                    for (int c = 0; c < 4; c++) tma_load_3d(dst + c * 8192, &tmV, &r_full[u], c * 64, g, key0 + 64 * h);
+                }
+                if (++u == AW_UNITS) {
+                    u = 0;
+                    uph ^= 1;
+                }
+                return true;
+            };
+            if (!load_unit(true, 0, 0) || !load_unit(true, 0, 1)) goto done;
+            for (int j = 0; j < n_kt; j++) {
+                if (j + 1 < n_kt && (!load_unit(true, j + 1, 0) || !load_unit(true, j + 1, 1))) goto done;
+                if (!load_unit(false, j, 0) || !load_unit(false, j, 1)) goto done;
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            constexpr uint32_t idesc_s = umma_idesc(128, AW_BN, 1);
+            constexpr uint32_t idesc_o = umma_idesc(128, ATT_DV, 1, /*b_mn_major=*/true);
+            const uint64_t dq0 = umma_desc_sw128(smem_u32(smem), 16, 1024);
+            const uint64_t dk0 = umma_desc_sw128(smem_u32(smem + AwCfg::OFF_R), 16, 1024);
+            const uint64_t dv0 = umma_desc_sw128(smem_u32(smem + AwCfg::OFF_R), 8192, 1024);
+            int u = 0;
+            uint32_t uph = 0;
+            if (!mbar_wait(q_full, 0, EG2_DEV_TIMEOUT_ATTN, abort_flag)) goto done;
+            auto issue_qk = [&](int j) -> bool {
+                // S is free once softmax(j - 1) has copied it into registers.
+                if (!mbar_wait(s_empty, (j & 1) ^ 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) return false;
+                tc_fence_after();
+                const uint32_t ts = t_s;
+                for (int h = 0; h < 2; h++) {
+                    if (!mbar_wait(&r_full[u], uph, EG2_DEV_TIMEOUT_ATTN, abort_flag)) return false;
+                    const uint64_t db = dk0 + (uint64_t)(u * (AW_UNIT >> 4));
+#pragma unroll
+                    for (int cc = 0; cc < 2; cc++) {
+                        const uint64_t da = dq0 + (uint64_t)((2 * h + cc) * (16384 >> 4));
+                        const uint64_t dbc = db + (uint64_t)(cc * (16384 >> 4));
+#pragma unroll
+                        for (int kk = 0; kk < 4; kk++) mma_bf16(ts, da + 2 * kk, dbc + 2 * kk, idesc_s, (h | cc | kk) != 0);
+                    }
+                    mma_commit(&r_empty[u]);
+                    if (++u == AW_UNITS) {
+                        u = 0;
+                        uph ^= 1;
+                    }
+                }
+                mma_commit(s_full);
+                return true;
+            };
+            if (!issue_qk(0)) goto done;
+            for (int j = 0; j < n_kt; j++) {
+                if (j + 1 < n_kt && !issue_qk(j + 1)) goto done;
+                if (!mbar_wait(&p_full[j & 1], (j >> 1) & 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) goto done;
+                tc_fence_after();
+                const uint32_t tp = t_p + (j & 1) * (AW_BN / 2);
+                for (int h = 0; h < 2; h++) {
+                    if (!mbar_wait(&r_full[u], uph, EG2_DEV_TIMEOUT_ATTN, abort_flag)) goto done;
+                    const uint64_t dv = dv0 + (uint64_t)(u * (AW_UNIT >> 4));
+                    // 16 keys per MMA: 8 packed P columns, 16 V rows (2048 bytes).
+#pragma unroll
+                    for (int kk = 0; kk < 4; kk++)
+                        mma_bf16_ts(t_o, tp + h * 32 + kk * 8, dv + kk * (2048 >> 4), idesc_o, (j | h | kk) != 0);
+                    mma_commit(&r_empty[u]);
+                    if (++u == AW_UNITS) {
+                        u = 0;
+                        uph ^= 1;
+                    }
+                }
+                mma_commit(&pv_done[j & 1]);
+            }
+        }
+    } else {
+        const int e = warp & 3;
+        const int r = 32 * e + lane;
+        const int tok = tile.q0 + r / G;
+        const bool row_valid = tok < tile.len;
+        const uint32_t lane_off = (uint32_t)(32 * e) << 16;
+        const float LOG2E = 1.4426950408889634f;
+        float m_used = -INFINITY, l = 0.f;
+        for (int j = 0; j < n_kt; j++) {
+            const int b = j & 1;
+            if (!mbar_wait(s_full, j & 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) break;
+            tc_fence_after();
+            float sv[128];
+            {
+                uint32_t s0[32], s1[32], s2[32], s3[32];
+                tmem_ld32(t_s + lane_off, s0);
+                tmem_ld32(t_s + 32 + lane_off, s1);
+                tmem_ld32(t_s + 64 + lane_off, s2);
+                tmem_ld32(t_s + 96 + lane_off, s3);
+                tmem_ld_wait();
+                tc_fence_before();
+                mbar_arrive(s_empty);
+#pragma unroll
+                for (int c = 0; c < 32; c++) {
+                    sv[c] = __uint_as_float(s0[c]);
+                    sv[32 + c] = __uint_as_float(s1[c]);
+                    sv[64 + c] = __uint_as_float(s2[c]);
+                    sv[96 + c] = __uint_as_float(s3[c]);
+                }
+            }
+            const int kbase = k_lo + j * AW_BN;
+            int lo_c = 0, hi_c = min(AW_BN, tile.len - kbase);
+            if (W >= 0 && row_valid) {
+                lo_c = max(lo_c, tok - W - kbase);
+                hi_c = min(hi_c, tok + W + 1 - kbase);
+            }
+            if (!__all_sync(0xffffffffu, lo_c <= 0 && hi_c >= AW_BN)) {
+#pragma unroll
+                for (int c = 0; c < AW_BN; c++) sv[c] = (c >= lo_c && c < hi_c) ? sv[c] : -INFINITY;
+            }
+            float mx[8];
+#pragma unroll
+            for (int c = 0; c < 8; c++) mx[c] = sv[c];
+#pragma unroll
+            for (int c = 8; c < AW_BN; c++) mx[c & 7] = fmaxf(mx[c & 7], sv[c]);
+            const float mt = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+            float factor = 1.f;
+            bool need = false;
+            if (mt > m_used) {
+                if (m_used == -INFINITY) {
+                    m_used = mt;
+                } else if ((mt - m_used) * LOG2E > ATT_RESCALE_LOG2) {
+                    factor = ex2_approx((m_used - mt) * LOG2E);
+                    m_used = mt;
+                    need = true;
+                }
+            }
+            if (__any_sync(0xffffffffu, need) && j >= 1) {
+                // O must hold every P V up to tile j - 1 before it is rescaled.
+                if (!mbar_wait(&pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) break;
+                tc_fence_after();
+#pragma unroll 1
+                for (int c = 0; c < ATT_DV / 32; c++) {
+                    uint32_t o[32];
+                    tmem_ld32(t_o + c * 32 + lane_off, o);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int q = 0; q < 32; q++) o[q] = __float_as_uint(__uint_as_float(o[q]) * factor);
+                    tmem_st32(t_o + c * 32 + lane_off, o);
+                }
+                tmem_st_wait();
+            }
+            l *= factor;
+            // P buffer b was last read by P V(j - 2).
+            if (j >= 2) {
+                if (!mbar_wait(&pv_done[b], ((j - 2) >> 1) & 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) break;
+                tc_fence_after();
+            }
+            const float bias = (m_used == -INFINITY) ? 0.f : -m_used * LOG2E;
+            float lsum[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int half = 0; half < 2; half++) {
+                uint32_t pk[32];
+#pragma unroll
+                for (int q = 0; q < 32; q++) {
+                    const float p0 = ex2_approx(fmaf(sv[64 * half + 2 * q], LOG2E, bias));
+                    const float p1 = ex2_approx(fmaf(sv[64 * half + 2 * q + 1], LOG2E, bias));
+                    pk[q] = bf16x2_bits(p0, p1);
+                    lsum[q & 3] += __uint_as_float(pk[q] << 16) + __uint_as_float(pk[q] & 0xffff0000u);
+                }
+                tmem_st32(t_p + b * (AW_BN / 2) + 32 * half + lane_off, pk);
+            }
+            l += (lsum[0] + lsum[1]) + (lsum[2] + lsum[3]);
+            tmem_st_wait();
+            tc_fence_before();
+            mbar_arrive(&p_full[b]);
+        }
+        if (!*abort_flag &&
+            mbar_wait(&pv_done[(n_kt - 1) & 1], ((n_kt - 1) >> 1) & 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) {
+            tc_fence_after();
+            const float inv = (l > 0.f) ? 1.f / l : 0.f;
+            const int head = g * G + r % G;
+            bf16_t* orow = prm.out + ((long)(tile.row0 + tok) * prm.nh + head) * prm.hd;
 #pragma unroll 1
             for (int c = 0; c < ATT_DV / 32; c++) {
                 uint32_t o[32];
@@ -438,8 +736,22 @@ int attention_tc(const bf16_t* q, const bf16_t* k, const bf16_t* v, bf16_t* out,
     prm.G = G;
     prm.tq = tq;
     prm.nsplit = hd / ATT_DV;
-    // V buffers: as many as shared memory holds next to Q and the K ring (224 KB in both cases).
-    if (hd == 256) return launch_att<256, 3>(mq, mk, mv, prm, n_tiles, s);
+    if (hd == 256) {
+        // 128-key tiles: K boxes of 128 keys.
+        CUtensorMap mk128;
+        if (make_tmap_3d(&mk128, dt, k, hd, nkv, rows, (uint64_t)hd * 2, (uint64_t)nkv * hd * 2, 64, 1, AW_BN)) return -1;
+        static bool attr = false;
+        if (!attr) {
+            if (cudaFuncSetAttribute(attention_w128_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, AwCfg::SMEM) !=
+                cudaSuccess)
+                return -3;
+            attr = true;
+        }
+        const long grid = (long)n_tiles * nkv;
+        attention_w128_kernel<<<(unsigned)grid, AW_THREADS, AwCfg::SMEM, s>>>(mq, mk128, mv, prm);
+        return cudaGetLastError() == cudaSuccess ? 0 : -3;
+    }
+    // V buffers: as many as shared memory holds next to Q and the K ring (224 KB).
     return launch_att<512, 2>(mq, mk, mv, prm, n_tiles, s);
 }
 

@@ -156,10 +156,73 @@ EG2_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, int code, volatile int* a
 }
 
 // ---------------------------------------------------------------------------------------------
+// Thread-block clusters: distributed shared memory between the CTAs of a cluster
+// ---------------------------------------------------------------------------------------------
+EG2_DEV uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+// All threads of every CTA of the cluster; orders earlier shared-memory writes (and mbarrier
+// initialisation) before later accesses from the other CTAs.
+EG2_DEV void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// The shared::cluster address of the variable at `local` (this CTA's shared memory) in CTA `rank`.
+EG2_DEV uint32_t mapa_shared(uint32_t local, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local), "r"(rank));
+    return r;
+}
+EG2_DEV void st_cluster_f32(uint32_t addr, float v) {
+    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+}
+// Arrive on an mbarrier of another CTA of the cluster, releasing this thread's earlier writes.
+EG2_DEV void mbar_arrive_cluster(uint32_t remote_bar) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(remote_bar) : "memory");
+}
+EG2_DEV bool mbar_try_wait_acq_cluster(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Bounded wait (as mbar_wait) with cluster-scope acquire: writes that another CTA made before its
+// releasing arrive are visible afterwards.
+EG2_DEV bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, int code, volatile int* abort) {
+    if (mbar_try_wait_acq_cluster(bar, parity)) return true;
+    uint64_t t0 = globaltimer_ns();
+    for (uint32_t it = 0;; ++it) {
+        if (mbar_try_wait_acq_cluster(bar, parity)) return true;
+        if ((it & 255u) == 255u) {
+            if (abort && *abort) return false;
+            if (*(volatile int*)&eg2_dev_status != 0) {
+                if (abort) *abort = 1;
+                return false;
+            }
+            if (globaltimer_ns() - t0 > EG2_WAIT_LIMIT_NS) {
+                eg2_record_error(code);
+                if (abort) *abort = 1;
+                return false;
+            }
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------------------------
 // TMA (tiled tensor loads into this CTA's own shared memory)
 // ---------------------------------------------------------------------------------------------
 EG2_DEV void tma_prefetch_desc(const CUtensorMap* m) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");
+}
+// Bulk prefetch of `bytes` (multiple of 16, 16-byte aligned address) of global memory into L2.
+EG2_DEV void prefetch_l2_bulk(const void* p, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(p)), "r"(bytes) : "memory");
 }
 EG2_DEV void tma_load_2d(void* dst, const CUtensorMap* m, uint64_t* bar, int x, int y) {
     asm volatile(

@@ -14,6 +14,10 @@
 //                accumulator s and the CTA's tiles of parity s, so two tiles' epilogues run at once
 //                while the MMAs of a third fill the free accumulator: the epilogues (norms, RoPE,
 //                GELU) are latency-bound and need the extra warps to overlap the main loop.
+//
+// EPI_ADD_NORM launches clusters of two CTAs: CTA rank r computes output columns [256 r, 256 r +
+// 256) of the cluster's row blocks, and the per-row sums of squares of the two halves are swapped
+// through distributed shared memory (a remote store plus a remote mbarrier arrive per value).
 #include "common.cuh"
 #include "kernels.h"
 
@@ -44,7 +48,10 @@ struct GemmCfg {
     static constexpr int OFF_STAGE = STAGES * STAGE_BYTES + 256;  // after the barriers
     static constexpr int STAGE_WARP = 32 * (64 + 16);             // 32 rows x 64 B + 16 B pad
     static constexpr int OFF_W = OFF_STAGE + 8 * STAGE_WARP;      // EPI_QKV: norm weights, inv freqs
-    static constexpr int SMEM_BYTES = 1024 + OFF_W + 3072;
+    // EPI_QKV: norm weights + inverse frequencies (<= 3 KB). EPI_ADD_NORM: w1 / w2 halves (2 KB),
+    // exchange slots [set][slot][128 rows] (2 KB), exchange barriers [set][slot] at +4096.
+    static constexpr int W_BYTES = 4096 + 64;
+    static constexpr int SMEM_BYTES = 1024 + OFF_W + W_BYTES;
     static constexpr uint32_t TMEM_COLS = 2 * BN;
 };
 
@@ -204,6 +211,43 @@ EG2_DEV void epilogue_qkv(const GemmEpilogue& epi, uint32_t tbase, int row0, int
     }
 }
 
+// Lane i loads the 16-byte segments p = i + 32 q (q = 0..7) of a 32-row x 32-column f32 chunk:
+// row p / 8, columns 4 (p % 8) .. + 3; every load instruction covers four whole 128-byte row
+// segments. Rows >= M read as zeros. warp_load32_finish hands lane i the 32 values of row i
+// through the warp's staging tile (two 16-column halves, as warp_store32).
+EG2_DEV void warp_load32_issue(const float* src, long ld, int row0, int M, long col, uint4 (&b)[8]) {
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int q = 0; q < 8; q++) {
+        const int r = (lane >> 3) + 4 * q;
+        b[q] = (row0 + r < M) ? *(reinterpret_cast<const uint4*>(src + (long)(row0 + r) * ld + col) + (lane & 7))
+                              : make_uint4(0u, 0u, 0u, 0u);
+    }
+}
+EG2_DEV void warp_load32_finish(const uint4 (&b)[8], float (&v)[32], uint8_t* stage) {
+    const int lane = threadIdx.x & 31;
+    constexpr int STRIDE = 64 + 16;
+    const int sg = lane & 7;
+#pragma unroll
+    for (int h = 0; h < 2; h++) {
+        if ((sg >> 2) == h) {
+#pragma unroll
+            for (int q = 0; q < 8; q++)
+                *reinterpret_cast<uint4*>(stage + ((lane >> 3) + 4 * q) * STRIDE + (sg & 3) * 16) = b[q];
+        }
+        __syncwarp();
+#pragma unroll
+        for (int s4 = 0; s4 < 4; s4++) {
+            const float4 x = *reinterpret_cast<const float4*>(stage + lane * STRIDE + s4 * 16);
+            v[16 * h + 4 * s4 + 0] = x.x;
+            v[16 * h + 4 * s4 + 1] = x.y;
+            v[16 * h + 4 * s4 + 2] = x.z;
+            v[16 * h + 4 * s4 + 3] = x.w;
+        }
+        __syncwarp();
+    }
+}
+
 template <typename TIn, int BN, int EPI, typename TOut>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int N, int K,
@@ -222,8 +266,16 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int tiles_m = (M + GEMM_BM - 1) / GEMM_BM, tiles_n = N / BN;
-    const int num_tiles = tiles_m * tiles_n;
     const int kblocks = K / BK;
+    // This CTA's tiles: linear ids t_first + i * t_step < t_count. EPI_ADD_NORM: the cluster's row
+    // blocks, columns fixed by the CTA's rank in the cluster.
+    constexpr bool AN = EPI == EPI_ADD_NORM;
+    const uint32_t crank = AN ? cluster_ctarank() : 0u;
+    const int t_first = AN ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+    const int t_step = AN ? (int)(gridDim.x >> 1) : (int)gridDim.x;
+    const int t_count = AN ? tiles_m : tiles_m * tiles_n;
+    auto tile_m0 = [&](int t) { return (AN ? t : t / tiles_n) * GEMM_BM; };
+    auto tile_n0 = [&](int t) { return AN ? (int)crank * BN : (t % tiles_n) * BN; };
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; s++) {
@@ -233,6 +285,10 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         for (int a = 0; a < 2; a++) {
             mbar_init(&tfull[a], 1);
             mbar_init(&tempty[a], 128);
+        }
+        if constexpr (AN) {
+            uint64_t* xb = reinterpret_cast<uint64_t*>(smem + Cfg::OFF_W + 4096);
+            for (int x = 0; x < 4; x++) mbar_init(&xb[x], 128);
         }
         *abort_flag = 0;
         fence_mbarrier_init();
@@ -246,18 +302,33 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         for (int i = threadIdx.x; i < 2 * hd + nf; i += GEMM_THREADS)
             wsm[i] = i < hd ? epi.qkv.wq[i] : i < 2 * hd ? epi.qkv.wk[i - hd] : epi.qkv.inv_freq[i - 2 * hd];
     }
+    if constexpr (AN) {
+        // This CTA's halves of the two norm weights.
+        float* wsm = reinterpret_cast<float*>(smem + Cfg::OFF_W);
+        const int n0 = (int)crank * BN;
+        for (int i = threadIdx.x; i < 2 * BN; i += GEMM_THREADS)
+            wsm[i] = i < BN ? epi.an.w1[n0 + i] : (epi.an.w2 ? epi.an.w2[n0 + i - BN] : 0.f);
+    }
     if (warp == 1) tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    // The peer CTA's exchange barriers must be initialised before anyone arrives on them.
+    if constexpr (AN) cluster_sync();
 
     if (warp == 0) {
         if (lane == 0) {
             int stage = 0;
             uint32_t phase = 0;
-            for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
-                const int m0 = (tile / tiles_n) * GEMM_BM, n0 = (tile % tiles_n) * BN;
+            for (int tile = t_first; tile < t_count; tile += t_step) {
+                const int m0 = tile_m0(tile), n0 = tile_n0(tile);
+                if constexpr (AN) {
+                    // The epilogue reads this tile's residual rows 128 bytes at a time; pulling each
+                    // row's 1 KB into L2 in one piece now keeps those reads off scattered DRAM pages.
+                    const int nr = min(GEMM_BM, M - m0);
+                    for (int r = 0; r < nr; r++) prefetch_l2_bulk(epi.an.h + (long)(m0 + r) * 512 + n0, BN * 4);
+                }
                 for (int kb = 0; kb < kblocks; kb++) {
                     if (!mbar_wait(&empty[stage], phase ^ 1, EG2_DEV_TIMEOUT_GEMM, abort_flag)) goto done;
                     uint8_t* sa = smem + stage * Cfg::STAGE_BYTES;
@@ -279,7 +350,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             int stage = 0;
             uint32_t phase = 0;
             int local = 0;
-            for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, local++) {
+            for (int tile = t_first; tile < t_count; tile += t_step, local++) {
                 const int acc = local & 1;
                 const uint32_t acc_phase = (local >> 1) & 1;
                 if (!mbar_wait(&tempty[acc], acc_phase ^ 1, EG2_DEV_TIMEOUT_GEMM, abort_flag)) goto done;
@@ -309,13 +380,99 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         uint8_t* stage = smem + Cfg::OFF_STAGE + (warp - 2) * Cfg::STAGE_WARP;
         TOut* out = reinterpret_cast<TOut*>(epi.out);
         int k = 0;  // tiles this set has taken: its k-th completion of tfull[set]
-        for (int tile = blockIdx.x + set * gridDim.x; tile < num_tiles; tile += 2 * gridDim.x, k++) {
+        for (int tile = t_first + set * t_step; tile < t_count; tile += 2 * t_step, k++) {
             if (!mbar_wait(&tfull[set], k & 1, EG2_DEV_TIMEOUT_GEMM, abort_flag)) break;
             tc_fence_after();
-            const int m0 = (tile / tiles_n) * GEMM_BM, n0 = (tile % tiles_n) * BN;
+            const int m0 = tile_m0(tile), n0 = tile_n0(tile);
             const int row0 = m0 + 32 * e, row = row0 + lane;
             const uint32_t tbase = tmem_base + ((uint32_t)(32 * e) << 16) + set * BN;
-            if constexpr (EPI == EPI_QKV) {
+            if constexpr (EPI == EPI_ADD_NORM) {
+                const AddNormEpilogue& A = epi.an;
+                float* xv = reinterpret_cast<float*>(smem + Cfg::OFF_W) + 2 * BN;  // [set][slot][128]
+                uint64_t* xb = reinterpret_cast<uint64_t*>(smem + Cfg::OFF_W + 4096);
+                const int rl = 32 * e + lane;
+                const uint32_t peer = crank ^ 1u;
+                // Sends this row's partial sum to the peer CTA (same slot there) and returns the total.
+                // Both CTAs add the same two numbers, so both use the same norm.
+                bool ok = true;
+                auto exchange = [&](float part, int slot) -> float {
+                    const int x = set * 2 + slot;
+                    float* mine = xv + x * 128 + rl;
+                    st_cluster_f32(mapa_shared(smem_u32(mine), peer), part);
+                    mbar_arrive_cluster(mapa_shared(smem_u32(&xb[x]), peer));
+                    if (!mbar_wait_cluster(&xb[x], k & 1, EG2_DEV_TIMEOUT_GEMM, abort_flag)) {
+                        ok = false;
+                        return 0.f;
+                    }
+                    return part + *reinterpret_cast<volatile float*>(mine);
+                };
+                const float* w1s = wsm;
+                const float* w2s = wsm + BN;
+                // Residual chunk 0 is loaded first, so its latency overlaps pass 1 and the exchange.
+                // (The producer has already pulled this tile's residual rows into L2.)
+                uint4 hb[8];
+                warp_load32_issue(A.h, 512, row0, M, n0, hb);
+                float ss = 0.f;
+#pragma unroll 1
+                for (int c = 0; c < BN / 32; c += 2) {
+                    uint32_t r0[32], r1[32];
+                    tmem_ld32(tbase + c * 32, r0);
+                    tmem_ld32(tbase + c * 32 + 32, r1);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int j = 0; j < 32; j++) {
+                        ss = fmaf(__uint_as_float(r0[j]), __uint_as_float(r0[j]), ss);
+                        ss = fmaf(__uint_as_float(r1[j]), __uint_as_float(r1[j]), ss);
+                    }
+                }
+                const float inv1 = 1.0f / sqrtf(exchange(ss, 0) / 512.f + A.eps);
+                if (!ok) break;
+                float ss2 = 0.f;
+#pragma unroll 1
+                for (int c = 0; c < BN / 32; c++) {
+                    float hv[32];
+                    {
+                        uint4 cur[8];
+#pragma unroll
+                        for (int q = 0; q < 8; q++) cur[q] = hb[q];
+                        if (c + 1 < BN / 32) warp_load32_issue(A.h, 512, row0, M, n0 + (c + 1) * 32, hb);
+                        warp_load32_finish(cur, hv, stage);
+                    }
+                    uint32_t r[32];
+                    tmem_ld32(tbase + c * 32, r);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int j = 0; j < 32; j++) {
+                        hv[j] = (hv[j] + __uint_as_float(r[j]) * inv1 * w1s[c * 32 + j]) * A.scalar;
+                        ss2 = fmaf(hv[j], hv[j], ss2);
+                    }
+                    warp_store32<float>(A.h, 512, row0, M, n0 + c * 32, hv, stage);
+                    if (A.w2) {
+#pragma unroll
+                        for (int j = 0; j < 32; j++) r[j] = __float_as_uint(hv[j]);
+                        tmem_st32(tbase + c * 32, r);  // kept for the second norm
+                    } else {
+                        warp_store32<TOut>(out, epi.ldo, row0, M, n0 + c * 32, hv, stage);
+                    }
+                }
+                // The second exchange runs even without w2: it is also the handshake that keeps the
+                // peer from writing this set's slot 0 for the next tile before it has been read here.
+                if (A.w2) tmem_st_wait();
+                const float inv2 = 1.0f / sqrtf(exchange(ss2, 1) / 512.f + A.eps);
+                if (!ok) break;
+                if (A.w2) {
+#pragma unroll 1
+                    for (int c = 0; c < BN / 32; c++) {
+                        uint32_t r[32];
+                        tmem_ld32(tbase + c * 32, r);
+                        tmem_ld_wait();
+                        float v[32];
+#pragma unroll
+                        for (int j = 0; j < 32; j++) v[j] = __uint_as_float(r[j]) * inv2 * w2s[c * 32 + j];
+                        warp_store32<TOut>(out, epi.ldo, row0, M, n0 + c * 32, v, stage);
+                    }
+                }
+            } else if constexpr (EPI == EPI_QKV) {
                 epilogue_qkv<TOut, BN>(epi, tbase, row0, M, n0, stage, wsm);
             } else if constexpr (EPI == EPI_GELU_GU) {
                 // Tile columns [0, BN/2) are gate features, [BN/2, BN) the matching up features.
@@ -374,6 +531,8 @@ done:
         tc_fence_after();
         tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
     }
+    // No CTA leaves while its peer may still write into its shared memory.
+    if constexpr (AN) cluster_sync();
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -395,6 +554,41 @@ static int launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N,
     const int grid = tiles < num_sms() ? tiles : num_sms();
     kern<<<grid, GEMM_THREADS, Cfg::SMEM_BYTES, s>>>(ta, tb, M, N, K, epi);
     return cudaGetLastError() == cudaSuccess ? 0 : -3;
+}
+
+// EPI_ADD_NORM: clusters of two CTAs, as many as can be resident at once (the loop over row blocks
+// is persistent, so every launched cluster must run concurrently with the others).
+static int launch_add_norm(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int K, const GemmEpilogue& epi,
+                           cudaStream_t s) {
+    using Cfg = GemmCfg<256>;
+    auto kern = gemm_tc_kernel<bf16_t, 256, EPI_ADD_NORM, bf16_t>;
+    static int max_clusters[64] = {0};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -3;
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.blockDim = dim3(GEMM_THREADS, 1, 1);
+    cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
+    cfg.stream = s;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (!max_clusters[dev]) {
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES) != cudaSuccess)
+            return -3;
+        cfg.gridDim = dim3(2 * num_sms(), 1, 1);
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) return -3;
+        max_clusters[dev] = n;
+    }
+    const int tiles_m = (M + GEMM_BM - 1) / GEMM_BM;
+    const int clusters = tiles_m < max_clusters[dev] ? tiles_m : max_clusters[dev];
+    cfg.gridDim = dim3(2 * clusters, 1, 1);
+    if (N != 512) return -1;
+    return cudaLaunchKernelEx(&cfg, kern, ta, tb, M, N, K, epi) == cudaSuccess ? 0 : -3;
 }
 
 bool qkv_fusable(const QkvEpilogue& q) {
@@ -428,9 +622,13 @@ int gemm_tc(GemmKind kind, const void* A, long lda, const void* W, long ldw, int
                 return launch_tc<bf16_t, BN, EPI_PLE_GATE, bf16_t>(ta, tb, M, N, K, epi, s);
             case EPI_QKV:
                 return launch_tc<bf16_t, BN, EPI_QKV, bf16_t>(ta, tb, M, N, K, epi, s);
+            case EPI_ADD_NORM:
+                if (N != 512 || !epi.an.h || !epi.an.w1 || !epi.out) return -1;
+                return launch_add_norm(ta, tb, M, N, K, epi, s);
         }
     } else {
         if (epi.mode == EPI_QKV) return launch_tc<float, BN, EPI_QKV, float>(ta, tb, M, N, K, epi, s);
+        if (epi.mode == EPI_ADD_NORM) return -1;  // bf16 only
         switch (epi.mode) {
             case EPI_STORE:
                 return launch_tc<float, BN, EPI_STORE, float>(ta, tb, M, N, K, epi, s);

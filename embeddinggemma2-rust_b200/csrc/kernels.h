@@ -16,6 +16,20 @@ enum EpiMode : int {
     EPI_PLE_GATE = 2,  // out = gelu(acc) * aux[row * aux_ld + aux_off + col]
     EPI_QKV = 3,       // fused projection [q | k | v] -> per-head RMSNorm (+ weights on q, k) and RoPE on
                        // q, k, written to q [M, nh, hd], k / v [M, nkv, hd]; needs 256 % hd == 0
+    EPI_ADD_NORM = 4,  // N = 512, bf16 inputs: residual update and norms of add_norm() on the accumulator
+                       // (see AddNormEpilogue); `out` receives t (bf16, ldo), the accumulator is not stored
+};
+
+// EPI_ADD_NORM, with o the GEMM result row (512 wide):
+//   h = (h + o / rms(o) * w1) * scalar;  out = w2 ? h / rms(h) * w2 : h   (rms(x) = sqrt(mean(x^2) + eps))
+// Runs as clusters of two CTAs, one per 256-column half of a 128-row block; the two halves of each
+// row's sum of squares are exchanged through distributed shared memory.
+struct AddNormEpilogue {
+    float* h = nullptr;          // [M, 512] f32 residual stream, updated in place
+    const float* w1 = nullptr;   // [512]
+    const float* w2 = nullptr;   // [512] or nullptr
+    float eps = 1e-6f;
+    float scalar = 1.f;
 };
 
 struct QkvEpilogue {
@@ -38,6 +52,7 @@ struct GemmEpilogue {
     int aux_off = 0;
     float scale = 1.f;
     QkvEpilogue qkv;
+    AddNormEpilogue an;
 };
 
 // Number of SMs of the current device (cached per device).

@@ -749,6 +749,35 @@ static bool qkv_projection(eg2_ctx* c, const void* x, int k, const void* W, long
     return true;
 }
 
+// o = x . W^T (N = hidden) followed by the residual update and norms of add_norm():
+//   hidden = (hidden + rms_norm(o) * w1) * scalar;  t = w2 ? rms_norm(hidden) * w2 : hidden.
+// bf16 with hidden 512 runs it as one GEMM with the EPI_ADD_NORM epilogue (o never leaves the
+// tensor memory); otherwise GEMM into w.o (f32) + the add_norm kernel.
+template <typename T>
+static void gemm_add_norm(eg2_ctx* c, const void* x, long ldx, const void* W, long rows, int K, const float* w1,
+                          const float* w2, float scalar, const char* label) {
+    Work& w = c->w;
+    const int h = c->tc.hidden;
+    if (bf16_mode(c) && h == 512 && !getenv("EG2_NO_ADD_NORM_FUSION")) {
+        GemmEpilogue e;
+        e.mode = EPI_ADD_NORM;
+        e.out = w.t;
+        e.ldo = h;
+        e.an.h = w.hidden;
+        e.an.w1 = w1;
+        e.an.w2 = w2;
+        e.an.eps = c->tc.eps;
+        e.an.scalar = scalar;
+        KL(gemm_tc(GEMM_BF16, x, ldx, W, K, (int)rows, h, K, e, c->stream), label);
+        mark(c, label);
+        return;
+    }
+    gemm(c, x, ldx, W, (int)rows, h, K, w.o, h, EPI_STORE, true);
+    mark(c, label);
+    KL((add_norm<float, T>(w.hidden, (const float*)w.o, w1, (T*)w.t, w2, rows, h, c->tc.eps, scalar, c->stream)), "add_norm");
+    mark(c, "add_norm");
+}
+
 template <typename T>
 static void attention(eg2_ctx* c, const T* q, const T* k, const T* v, T* out, long rows, int nh, int nkv, int hd,
                       int window, const int* seq_start, const int* seq_len, const AttnTile* tiles, int n_tiles);
@@ -821,25 +850,15 @@ static void enqueue_text(eg2_ctx* c, long rows, const std::vector<TileSet>& tset
         attention<T>(c, (const T*)w.q, (const T*)w.k, (const T*)w.v, (T*)w.a, rows, nh, nkv, hd,
                      L.sliding ? tc.window : -1, w.seq_start, w.seq_len, tiles, n_tiles);
         mark(c, hd == 256 ? "attention d256" : "attention d512");
-        gemm(c, w.a, nh * hd, L.o, (int)rows, h, nh * hd, w.o, h, EPI_STORE, true);
-        mark(c, "gemm o");
-        KL((add_norm<float, T>(w.hidden, (const float*)w.o, L.post_attn_ln, t, L.pre_ff_ln, rows, h, eps, 1.f, c->stream)), "add_norm");
-        mark(c, "add_norm");
+        gemm_add_norm<T>(c, w.a, nh * hd, L.o, rows, nh * hd, L.post_attn_ln, L.pre_ff_ln, 1.f, "gemm o (+ add_norm)");
         gemm(c, t, h, L.gu, (int)rows, 2 * ff, h, w.gate, ff, EPI_GELU_GU, f32, 1.f, nullptr, 0, 0, w.gu);
         mark(c, "gemm gate|up + gelu");
-        gemm(c, w.gate, ff, L.down, (int)rows, h, ff, w.o, h, EPI_STORE, true);
-        mark(c, "gemm down");
         // t = hidden (as the per-layer-input gate's input, bf16 in bf16 mode).
-        KL((add_norm<float, T>(w.hidden, (const float*)w.o, L.post_ff_ln, t, nullptr, rows, h, eps, 1.f, c->stream)), "add_norm");
-        mark(c, "add_norm");
+        gemm_add_norm<T>(c, w.gate, ff, L.down, rows, ff, L.post_ff_ln, nullptr, 1.f, "gemm down (+ add_norm)");
         gemm(c, t, h, L.pg, (int)rows, p, h, w.pg, p, EPI_PLE_GATE, f32, 1.f, w.ple, (long)nl * p, i * p);
         mark(c, "gemm ple_gate");
-        gemm(c, w.pg, p, L.pp, (int)rows, h, p, w.o, h, EPI_STORE, true);
-        mark(c, "gemm ple_proj");
         const float* next_w = (i + 1 < nl) ? c->layers[i + 1].input_ln : c->final_norm;
-        KL((add_norm<float, T>(w.hidden, (const float*)w.o, L.ple_post_norm, t, next_w, rows, h, eps, L.layer_scalar, c->stream)),
-           "add_norm");
-        mark(c, "add_norm");
+        gemm_add_norm<T>(c, w.pg, p, L.pp, rows, p, L.ple_post_norm, next_w, L.layer_scalar, "gemm ple_proj (+ add_norm)");
     }
     gemm(c, t, h, c->emb_proj, (int)rows, tc.emb, h, w.out, tc.emb, EPI_STORE, true);
     mark(c, "gemm embed_proj");

@@ -120,3 +120,19 @@ def test_repeated_calls_are_deterministic(dev_bf16):
     a = tb.embed_ids(seqs)[768].copy()
     b = tb.embed_ids(seqs)[768].copy()
     np.testing.assert_array_equal(a, b)
+
+
+def test_add_norm_fusion_matches_kernel_path(cases, request, monkeypatch):
+    """The o / down / ple_proj GEMMs with the residual update and norms in their epilogue (2-CTA
+    clusters exchanging row sums of squares) against the GEMM + add_norm kernel path."""
+    dev = request.getfixturevalue("dev_bf16")
+    tb = B.TextBackend(dev)
+    seqs = cases["mixed"][0] + cases["short"][0]
+    fused = tb.embed_ids(seqs)
+    monkeypatch.setenv("EG2_NO_ADD_NORM_FUSION", "1")
+    plain = tb.embed_ids(seqs)
+    for d in (768, 128):
+        diff = np.abs(fused[d] - plain[d]).max()
+        cos = (fused[d] * plain[d]).sum(1) / (np.linalg.norm(fused[d], axis=1) * np.linalg.norm(plain[d], axis=1))
+        print(f"fused vs kernel path @{d}: max|d| {diff:.2e} min cos {cos.min():.8f}")
+        assert diff <= 2e-3 and cos.min() >= 0.99995
