@@ -396,184 +396,205 @@ done:
 }
 
 // ---------------------------------------------------------------------------------------------
-// Head 256 with 128-key tiles.
+// Head 256: CTA pairs (cta_group::2) over 128-key tiles.
 //
-// S = Q K^T runs at N = 128 (the full tensor rate; N = 64 MMAs reach ~60%) and every barrier wait
-// or commit covers twice the keys. TMEM: S [0, 128) (one buffer), P[0] [128, 192), P[1] [192, 256)
-// (packed bf16 pairs), O [256, 512). S(j + 1) is issued as soon as the softmax has copied S(j) into
-// registers, so it overlaps softmax(j); P V(j) follows once P(j) is written. K and V stream
-// through ONE ring of five 32 KB units in the order the MMAs consume them: K(j + 1) (two halves
-// of 128 channels), then V(j) (two halves of 64 keys).
+// A 2-CTA cluster takes two adjacent query tiles of one sequence and K/V head (128 MMA rows each)
+// and runs every MMA as one M = 256 tcgen05.mma issued by the even CTA: S = Q K^T at N = 128 keys
+// (each CTA holds 64 of them) and O += P V at N = 256 channels (each CTA holds V for 128 of them).
+// Each CTA therefore loads and feeds the tensor cores half of every K / V tile, which halves the
+// shared-memory traffic per FLOP of a single-CTA kernel (there: 320 KB per 128-key tile against
+// 128 B/cycle of shared memory for 2,048 tensor cycles; here 192 KB). Keys span the union of both
+// tiles' windows; each row masks its own.
 //
-//   warp 0      TMA producer (Q once, then the K / V units)
-//   warp 1      TMEM owner; lane 0 issues QK(j + 1), then P V(j)
-//   warps 2..5  softmax, one thread per row of the 128-row tile; O / l epilogue
+// TMEM per CTA: S [0, 128), P[0] [128, 192), P[1] [192, 256) (packed bf16), O [256, 512). Per CTA
+// shared memory: Q (64 KB) and a ring of five 32 KB units, consumed in order K(j + 1), V(j); a K unit
+// is 64 keys x 256 channels, a V unit 128 keys x 128 channels. The even CTA's barriers collect both
+// CTAs' TMA bytes (q_full, r_full) and both CTAs' softmax arrivals (s_empty, p_full: 256); MMA
+// completion is committed to the barriers of both CTAs (r_empty, s_full, pv_done).
+//
+//   warp 0      TMA producer (this CTA's Q and its half of every unit)
+//   warp 1      TMEM allocation (both CTAs); in the even CTA lane 0 issues the S = Q K^T MMAs
+//   warps 2..5  softmax, one thread per row of this CTA's 128 rows; O / l epilogue
+//   warp 6      in the even CTA lane 0 issues the O += P V MMAs
+// Two issuing threads: tcgen05.mma issue blocks once a couple of MMAs are queued, so one thread
+// leaves the tensor pipe idle during each of its waits and commits; with S and P V on different
+// threads (disjoint TMEM, per-thread commit tracking) one feeds the pipe while the other waits.
 // ---------------------------------------------------------------------------------------------
-constexpr int AW_THREADS = 192;
-constexpr int AW_BN = 128;
-constexpr int AW_UNITS = 5;
-constexpr int AW_UNIT = 32768;
-struct AwCfg {
+constexpr int AP_THREADS = 224;
+constexpr int AP_BN = 128;
+constexpr int AP_UNITS = 5;
+constexpr int AP_UNIT = 32768;
+struct ApCfg {
     static constexpr int Q_BYTES = 4 * 128 * 128;
     static constexpr int OFF_R = Q_BYTES;
-    static constexpr int OFF_BAR = OFF_R + AW_UNITS * AW_UNIT;
-    static constexpr int N_BARS = 1 + 2 * AW_UNITS + 6;  // q, ring full/empty, s full/empty, p[2], pv[2]
+    static constexpr int OFF_BAR = OFF_R + AP_UNITS * AP_UNIT;
+    static constexpr int N_BARS = 1 + 2 * AP_UNITS + 2 + 4 + 2;  // q, ring, s full/empty, p[2], pv[2], drain[2]
     static constexpr int SMEM = 1024 + OFF_BAR + N_BARS * 8 + 16;
 };
-static_assert(AwCfg::SMEM <= 227 * 1024, "attention w128: shared memory");
+static_assert(ApCfg::SMEM <= 227 * 1024, "attention pair: shared memory");
 
-__global__ void __launch_bounds__(AW_THREADS, 1)
-    attention_w128_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+__global__ void __launch_bounds__(AP_THREADS, 1)
+    attention_pair_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                           const __grid_constant__ CUtensorMap tmV, AttParams prm) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + AwCfg::OFF_BAR);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + ApCfg::OFF_BAR);
     uint64_t* q_full = bars;
     uint64_t* r_full = bars + 1;
-    uint64_t* r_empty = r_full + AW_UNITS;
-    uint64_t* s_full = r_empty + AW_UNITS;
+    uint64_t* r_empty = r_full + AP_UNITS;
+    uint64_t* s_full = r_empty + AP_UNITS;
     uint64_t* s_empty = s_full + 1;
     uint64_t* p_full = s_empty + 1;
     uint64_t* pv_done = p_full + 2;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + AwCfg::N_BARS);
+    uint64_t* drain = pv_done + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + ApCfg::N_BARS);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int tile_idx = blockIdx.x / prm.nkv;
-    const int g = blockIdx.x % prm.nkv;
+    const uint32_t rank = cluster_ctarank();
+    const bool even = rank == 0;
+    const int cid = (int)(blockIdx.x >> 1);
+    const int tile_idx = cid / prm.nkv;
+    const int g = cid % prm.nkv;
     const AttnTile tile = prm.tiles[tile_idx];
-    const int G = prm.G, W = prm.window;
-    const int q_last = min(tile.q0 + prm.tq, tile.len) - 1;
+    const int G = prm.G, W = prm.window, tqc = prm.tq;
+    const int q0r = tile.q0 + (int)rank * tqc;  // this CTA's first query token
+    const int q_last = min(tile.q0 + 2 * tqc, tile.len) - 1;
     const int k_lo = (W >= 0) ? max(0, tile.q0 - W) : 0;
     const int k_hi = (W >= 0) ? min(tile.len, q_last + W + 1) : tile.len;
-    const int n_kt = tile.len > 0 ? (k_hi - k_lo + AW_BN - 1) / AW_BN : 0;
+    const int n_kt = tile.len > 0 ? (k_hi - k_lo + AP_BN - 1) / AP_BN : 0;
 
     if (threadIdx.x == 0) {
         mbar_init(q_full, 1);
-        for (int u = 0; u < AW_UNITS; u++) {
+        for (int u = 0; u < AP_UNITS; u++) {
             mbar_init(&r_full[u], 1);
             mbar_init(&r_empty[u], 1);
         }
         mbar_init(s_full, 1);
-        mbar_init(s_empty, 128);
+        mbar_init(s_empty, 256);
         for (int b = 0; b < 2; b++) {
-            mbar_init(&p_full[b], 128);
+            mbar_init(&p_full[b], 256);
             mbar_init(&pv_done[b], 1);
         }
+        mbar_init(&drain[0], 1);
+        mbar_init(&drain[1], 1);
         *abort_flag = 0;
         fence_mbarrier_init();
     }
-    if (warp == 1) tmem_alloc(tmem_slot, 512);
+    if (warp == 1) tmem_alloc_pair(tmem_slot, 512);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
+    // Both CTAs' barriers are initialised (and TMEM allocated) before either CTA touches the other's.
+    cluster_sync();
     const uint32_t tmem = *tmem_slot;
-    const uint32_t t_s = tmem;        // S: 128 fp32 columns
-    const uint32_t t_p = tmem + 128;  // P buffer b at t_p + 64 b
-    const uint32_t t_o = tmem + 256;  // O: 256 fp32 columns
+    const uint32_t t_s = tmem;
+    const uint32_t t_p = tmem + 128;
+    const uint32_t t_o = tmem + 256;
+    auto on_even = [&](uint64_t* b) { return mapa_shared(smem_u32(b), 0); };
 
     if (n_kt == 0) goto done;
 
     if (warp == 0) {
         if (lane == 0) {
-            mbar_arrive_expect_tx(q_full, AwCfg::Q_BYTES);
-            for (int c = 0; c < 4; c++) tma_load_3d(smem + c * 128 * 128, &tmQ, q_full, c * 64, g * G, tile.row0 + tile.q0);
+            if (even) mbar_arrive_expect_tx(q_full, 2 * ApCfg::Q_BYTES);
+            const uint32_t qbar = on_even(q_full);
+            for (int c = 0; c < 4; c++)
+                tma_load_3d_pair(smem + c * 128 * 128, &tmQ, qbar, c * 64, g * G, tile.row0 + q0r);
             int u = 0;
             uint32_t uph = 0;
-            // One 32 KB unit: K channels [128 h, 128 h + 128) of key tile jt (two [128 x 64] boxes), or
-            // V keys [64 h, 64 h + 64) of key tile jt, all 256 channels (four [64 x 64] boxes).
-            auto load_unit = [&](bool is_k, int jt, int h) -> bool {
+            // K unit of key tile jt: this CTA's 64 keys, 4 boxes of [64 keys x 64 channels]. V unit: all
+            // 128 keys for this CTA's 128 channels, 2 boxes of [128 keys x 64 channels].
+            auto load_unit = [&](bool is_k, int jt) -> bool {
                 if (!mbar_wait(&r_empty[u], uph ^ 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) return false;
-                uint8_t* dst = smem + AwCfg::OFF_R + u * AW_UNIT;
-                const int key0 = tile.row0 + k_lo + jt * AW_BN;
-                mbar_arrive_expect_tx(&r_full[u], AW_UNIT);
+                if (even) mbar_arrive_expect_tx(&r_full[u], 2 * AP_UNIT);
+                const uint32_t bar = on_even(&r_full[u]);
+                uint8_t* dst = smem + ApCfg::OFF_R + u * AP_UNIT;
+                const int key0 = tile.row0 + k_lo + jt * AP_BN;
                 if (is_k) {
-                    tma_load_3d(dst, &tmK, &r_full[u], (2 * h) * 64, g, key0);
-                    tma_load_3d(dst + 16384, &tmK, &r_full[u], (2 * h + 1) * 64, g, key0);
+                    for (int c = 0; c < 4; c++) tma_load_3d_pair(dst + c * 8192, &tmK, bar, c * 64, g, key0 + 64 * (int)rank);
                 } else {
-                    for (int c = 0; c < 4; c++) tma_load_3d(dst + c * 8192, &tmV, &r_full[u], c * 64, g, key0 + 64 * h);
+                    for (int c = 0; c < 2; c++) tma_load_3d_pair(dst + c * 16384, &tmV, bar, (2 * (int)rank + c) * 64, g, key0);
                 }
-                if (++u == AW_UNITS) {
+                if (++u == AP_UNITS) {
                     u = 0;
                     uph ^= 1;
                 }
                 return true;
             };
-            if (!load_unit(true, 0, 0) || !load_unit(true, 0, 1)) goto done;
+            if (!load_unit(true, 0)) goto done;
             for (int j = 0; j < n_kt; j++) {
-                if (j + 1 < n_kt && (!load_unit(true, j + 1, 0) || !load_unit(true, j + 1, 1))) goto done;
-                if (!load_unit(false, j, 0) || !load_unit(false, j, 1)) goto done;
+                if (j + 1 < n_kt && !load_unit(true, j + 1)) goto done;
+                if (!load_unit(false, j)) goto done;
             }
         }
-    } else if (warp == 1) {
-        if (lane == 0) {
-            constexpr uint32_t idesc_s = umma_idesc(128, AW_BN, 1);
-            constexpr uint32_t idesc_o = umma_idesc(128, ATT_DV, 1, /*b_mn_major=*/true);
-            const uint64_t dq0 = umma_desc_sw128(smem_u32(smem), 16, 1024);
-            const uint64_t dk0 = umma_desc_sw128(smem_u32(smem + AwCfg::OFF_R), 16, 1024);
-            const uint64_t dv0 = umma_desc_sw128(smem_u32(smem + AwCfg::OFF_R), 8192, 1024);
-            int u = 0;
-            uint32_t uph = 0;
-            if (!mbar_wait(q_full, 0, EG2_DEV_TIMEOUT_ATTN, abort_flag)) goto done;
-            auto issue_qk = [&](int j) -> bool {
-                // S is free once softmax(j - 1) has copied it into registers.
-                if (!mbar_wait(s_empty, (j & 1) ^ 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) return false;
-                tc_fence_after();
-                const uint32_t ts = t_s;
-                for (int h = 0; h < 2; h++) {
-                    if (!mbar_wait(&r_full[u], uph, EG2_DEV_TIMEOUT_ATTN, abort_flag)) return false;
-                    const uint64_t db = dk0 + (uint64_t)(u * (AW_UNIT >> 4));
+    } else if (warp == 1 || warp == 6) {
+        if (even && lane == 0) {
+            // Ring unit of K(j) / V(j): the producer's order is K(0), then per tile j K(j + 1) (if
+            // any) and V(j).
+            auto unit_k = [&](int j) { return j == 0 ? 0 : 2 * j - 1; };
+            auto unit_v = [&](int j) { return j + 1 < n_kt ? 2 * j + 2 : 2 * j + 1; };
+            if (warp == 1) {
+                constexpr uint32_t idesc_s = umma_idesc(256, AP_BN, 1);
+                const uint64_t dq0 = umma_desc_sw128(smem_u32(smem), 16, 1024);
+                const uint64_t dk0 = umma_desc_sw128(smem_u32(smem + ApCfg::OFF_R), 16, 1024);
+                if (!mbar_wait(q_full, 0, EG2_DEV_TIMEOUT_ATTN, abort_flag)) goto done;
+                for (int j = 0; j < n_kt; j++) {
+                    // S is free once both CTAs' softmax(j - 1) have copied it into registers.
+                    if (!mbar_wait(s_empty, (j & 1) ^ 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) goto done;
+                    tc_fence_after();
+                    const int iu = unit_k(j), u = iu % AP_UNITS;
+                    if (!mbar_wait(&r_full[u], (iu / AP_UNITS) & 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) goto done;
+                    const uint64_t db = dk0 + (uint64_t)(u * (AP_UNIT >> 4));
 #pragma unroll
-                    for (int cc = 0; cc < 2; cc++) {
-                        const uint64_t da = dq0 + (uint64_t)((2 * h + cc) * (16384 >> 4));
-                        const uint64_t dbc = db + (uint64_t)(cc * (16384 >> 4));
+                    for (int c = 0; c < 4; c++) {
 #pragma unroll
-                        for (int kk = 0; kk < 4; kk++) mma_bf16(ts, da + 2 * kk, dbc + 2 * kk, idesc_s, (h | cc | kk) != 0);
+                        for (int kk = 0; kk < 4; kk++)
+                            mma_bf16_pair(t_s, dq0 + (uint64_t)(c * (16384 >> 4) + 2 * kk),
+                                          db + (uint64_t)(c * (8192 >> 4) + 2 * kk), idesc_s, (c | kk) != 0);
                     }
-                    mma_commit(&r_empty[u]);
-                    if (++u == AW_UNITS) {
-                        u = 0;
-                        uph ^= 1;
-                    }
+                    mma_commit_pair_both(&r_empty[u]);
+                    mma_commit_pair_both(s_full);
                 }
-                mma_commit(s_full);
-                return true;
-            };
-            if (!issue_qk(0)) goto done;
-            for (int j = 0; j < n_kt; j++) {
-                if (j + 1 < n_kt && !issue_qk(j + 1)) goto done;
-                if (!mbar_wait(&p_full[j & 1], (j >> 1) & 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) goto done;
-                tc_fence_after();
-                const uint32_t tp = t_p + (j & 1) * (AW_BN / 2);
-                for (int h = 0; h < 2; h++) {
-                    if (!mbar_wait(&r_full[u], uph, EG2_DEV_TIMEOUT_ATTN, abort_flag)) goto done;
-                    const uint64_t dv = dv0 + (uint64_t)(u * (AW_UNIT >> 4));
-                    // 16 keys per MMA: 8 packed P columns, 16 V rows (2048 bytes).
+            } else {
+                constexpr uint32_t idesc_o = umma_idesc(256, ATT_DV, 1, /*b_mn_major=*/true);
+                const uint64_t dv0 = umma_desc_sw128(smem_u32(smem + ApCfg::OFF_R), 16384, 1024);
+                for (int j = 0; j < n_kt; j++) {
+                    const int b = j & 1;
+                    if (!mbar_wait(&p_full[b], (j >> 1) & 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) goto done;
+                    tc_fence_after();
+                    const int iu = unit_v(j), u = iu % AP_UNITS;
+                    if (!mbar_wait(&r_full[u], (iu / AP_UNITS) & 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) goto done;
+                    const uint64_t dv = dv0 + (uint64_t)(u * (AP_UNIT >> 4));
+                    // 16 keys per MMA: 8 packed P columns, 16 V rows (2048 bytes per 64-channel chunk).
 #pragma unroll
-                    for (int kk = 0; kk < 4; kk++)
-                        mma_bf16_ts(t_o, tp + h * 32 + kk * 8, dv + kk * (2048 >> 4), idesc_o, (j | h | kk) != 0);
-                    mma_commit(&r_empty[u]);
-                    if (++u == AW_UNITS) {
-                        u = 0;
-                        uph ^= 1;
-                    }
+                    for (int kk = 0; kk < AP_BN / 16; kk++)
+                        mma_bf16_pair_ts(t_o, t_p + b * (AP_BN / 2) + kk * 8, dv + (uint64_t)(kk * (2048 >> 4)), idesc_o,
+                                         (j | kk) != 0);
+                    mma_commit_pair_both(&r_empty[u]);
+                    mma_commit_pair_both(&pv_done[b]);
                 }
-                mma_commit(&pv_done[j & 1]);
             }
         }
     } else {
         const int e = warp & 3;
         const int r = 32 * e + lane;
-        const int tok = tile.q0 + r / G;
+        const int tok = q0r + r / G;
         const bool row_valid = tok < tile.len;
         const uint32_t lane_off = (uint32_t)(32 * e) << 16;
         const float LOG2E = 1.4426950408889634f;
+        // Arrivals for the MMA issuer go to the even CTA's barriers. What they guard is TMEM (S read,
+        // P written), ordered by tcgen05.wait + tcgen05.fence::before_thread_sync.
+        auto arrive_even = [&](uint64_t* bar) {
+            if (even) mbar_arrive(bar);
+            else mbar_arrive_remote(on_even(bar));
+        };
         float m_used = -INFINITY, l = 0.f;
         for (int j = 0; j < n_kt; j++) {
             const int b = j & 1;
             if (!mbar_wait(s_full, j & 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) break;
             tc_fence_after();
-            float sv[128];
+            float sv[AP_BN];
             {
                 uint32_t s0[32], s1[32], s2[32], s3[32];
                 tmem_ld32(t_s + lane_off, s0);
@@ -582,7 +603,7 @@ __global__ void __launch_bounds__(AW_THREADS, 1)
                 tmem_ld32(t_s + 96 + lane_off, s3);
                 tmem_ld_wait();
                 tc_fence_before();
-                mbar_arrive(s_empty);
+                arrive_even(s_empty);
 #pragma unroll
                 for (int c = 0; c < 32; c++) {
                     sv[c] = __uint_as_float(s0[c]);
@@ -591,21 +612,21 @@ __global__ void __launch_bounds__(AW_THREADS, 1)
                     sv[96 + c] = __uint_as_float(s3[c]);
                 }
             }
-            const int kbase = k_lo + j * AW_BN;
-            int lo_c = 0, hi_c = min(AW_BN, tile.len - kbase);
+            const int kbase = k_lo + j * AP_BN;
+            int lo_c = 0, hi_c = min(AP_BN, tile.len - kbase);
             if (W >= 0 && row_valid) {
                 lo_c = max(lo_c, tok - W - kbase);
                 hi_c = min(hi_c, tok + W + 1 - kbase);
             }
-            if (!__all_sync(0xffffffffu, lo_c <= 0 && hi_c >= AW_BN)) {
+            if (!__all_sync(0xffffffffu, lo_c <= 0 && hi_c >= AP_BN)) {
 #pragma unroll
-                for (int c = 0; c < AW_BN; c++) sv[c] = (c >= lo_c && c < hi_c) ? sv[c] : -INFINITY;
+                for (int c = 0; c < AP_BN; c++) sv[c] = (c >= lo_c && c < hi_c) ? sv[c] : -INFINITY;
             }
             float mx[8];
 #pragma unroll
             for (int c = 0; c < 8; c++) mx[c] = sv[c];
 #pragma unroll
-            for (int c = 8; c < AW_BN; c++) mx[c & 7] = fmaxf(mx[c & 7], sv[c]);
+            for (int c = 8; c < AP_BN; c++) mx[c & 7] = fmaxf(mx[c & 7], sv[c]);
             const float mt = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
             float factor = 1.f;
             bool need = false;
@@ -639,6 +660,7 @@ __global__ void __launch_bounds__(AW_THREADS, 1)
                 if (!mbar_wait(&pv_done[b], ((j - 2) >> 1) & 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) break;
                 tc_fence_after();
             }
+            // Row sum over the bf16-ROUNDED probabilities that multiply V (weights sum to exactly l).
             const float bias = (m_used == -INFINITY) ? 0.f : -m_used * LOG2E;
             float lsum[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
@@ -651,12 +673,12 @@ __global__ void __launch_bounds__(AW_THREADS, 1)
                     pk[q] = bf16x2_bits(p0, p1);
                     lsum[q & 3] += __uint_as_float(pk[q] << 16) + __uint_as_float(pk[q] & 0xffff0000u);
                 }
-                tmem_st32(t_p + b * (AW_BN / 2) + 32 * half + lane_off, pk);
+                tmem_st32(t_p + b * (AP_BN / 2) + 32 * half + lane_off, pk);
             }
             l += (lsum[0] + lsum[1]) + (lsum[2] + lsum[3]);
             tmem_st_wait();
             tc_fence_before();
-            mbar_arrive(&p_full[b]);
+            arrive_even(&p_full[b]);
         }
         if (!*abort_flag &&
             mbar_wait(&pv_done[(n_kt - 1) & 1], ((n_kt - 1) >> 1) & 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) {
@@ -682,19 +704,28 @@ __global__ void __launch_bounds__(AW_THREADS, 1)
         }
     }
 done:
+    // Every MMA the even CTA issued (into both CTAs' TMEM) has completed before either CTA frees it:
+    // each issuing thread waits for its own.
+    if (even && (warp == 1 || warp == 6) && lane == 0) {
+        uint64_t* d = &drain[warp == 1 ? 0 : 1];
+        mma_commit_pair(smem_u32(d));
+        mbar_wait(d, 0, EG2_DEV_TIMEOUT_ATTN, nullptr);
+    }
     tc_fence_before();
     __syncthreads();
+    cluster_sync();
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tmem, 512);
+        tmem_dealloc_pair(tmem, 512);
     }
 }
 
-int attention_tc_tile_tokens(int nh, int nkv) {
+int attention_tc_tile_tokens(int nh, int nkv, int hd) {
     if (nkv <= 0 || nh % nkv) return 0;
     const int G = nh / nkv;
     if (128 % G) return 0;
-    return 128 / G;
+    // Head 256 runs CTA pairs: one tile covers both CTAs' 128 rows.
+    return (hd == 256 ? 256 : 128) / G;
 }
 
 template <int DQK, int VB>
@@ -716,15 +747,15 @@ static int launch_att(const CUtensorMap& tq, const CUtensorMap& tk, const CUtens
 int attention_tc(const bf16_t* q, const bf16_t* k, const bf16_t* v, bf16_t* out, long rows, const AttnTile* tiles,
                  int n_tiles, int nh, int nkv, int hd, int window, cudaStream_t s) {
     if (rows <= 0 || n_tiles <= 0) return 0;
-    const int tq = attention_tc_tile_tokens(nh, nkv);
-    if (!tq || (hd != 256 && hd != 512)) return -1;
+    if ((hd != 256 && hd != 512) || !attention_tc_tile_tokens(nh, nkv, hd)) return -1;
     const int G = nh / nkv;
+    const int tq = 128 / G;  // query tokens per CTA (128 MMA rows)
     CUtensorMap mq, mk, mv;
     const CUtensorMapDataType dt = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
     // q [rows, nh, hd]: box (64 ch, G heads, tq tokens) -> 128 rows of 128 B.
     if (make_tmap_3d(&mq, dt, q, hd, nh, rows, (uint64_t)hd * 2, (uint64_t)nh * hd * 2, 64, G, tq) ||
         make_tmap_3d(&mk, dt, k, hd, nkv, rows, (uint64_t)hd * 2, (uint64_t)nkv * hd * 2, 64, 1, ATT_BN) ||
-        make_tmap_3d(&mv, dt, v, hd, nkv, rows, (uint64_t)hd * 2, (uint64_t)nkv * hd * 2, 64, 1, ATT_BN))
+        make_tmap_3d(&mv, dt, v, hd, nkv, rows, (uint64_t)hd * 2, (uint64_t)nkv * hd * 2, 64, 1, hd == 256 ? AP_BN : ATT_BN))
         return -1;
     AttParams prm;
     prm.tiles = tiles;
@@ -737,19 +768,27 @@ int attention_tc(const bf16_t* q, const bf16_t* k, const bf16_t* v, bf16_t* out,
     prm.tq = tq;
     prm.nsplit = hd / ATT_DV;
     if (hd == 256) {
-        // 128-key tiles: K boxes of 128 keys.
-        CUtensorMap mk128;
-        if (make_tmap_3d(&mk128, dt, k, hd, nkv, rows, (uint64_t)hd * 2, (uint64_t)nkv * hd * 2, 64, 1, AW_BN)) return -1;
+        // CTA pairs: clusters of 2, one per (pair tile, K/V head).
         static bool attr = false;
         if (!attr) {
-            if (cudaFuncSetAttribute(attention_w128_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, AwCfg::SMEM) !=
+            if (cudaFuncSetAttribute(attention_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, ApCfg::SMEM) !=
                 cudaSuccess)
                 return -3;
             attr = true;
         }
-        const long grid = (long)n_tiles * nkv;
-        attention_w128_kernel<<<(unsigned)grid, AW_THREADS, AwCfg::SMEM, s>>>(mq, mk128, mv, prm);
-        return cudaGetLastError() == cudaSuccess ? 0 : -3;
+        cudaLaunchConfig_t cfg = {};
+        cudaLaunchAttribute la[1];
+        la[0].id = cudaLaunchAttributeClusterDimension;
+        la[0].val.clusterDim.x = 2;
+        la[0].val.clusterDim.y = 1;
+        la[0].val.clusterDim.z = 1;
+        cfg.gridDim = dim3((unsigned)(2L * n_tiles * nkv), 1, 1);
+        cfg.blockDim = dim3(AP_THREADS, 1, 1);
+        cfg.dynamicSmemBytes = ApCfg::SMEM;
+        cfg.stream = s;
+        cfg.attrs = la;
+        cfg.numAttrs = 1;
+        return cudaLaunchKernelEx(&cfg, attention_pair_kernel, mq, mk, mv, prm) == cudaSuccess ? 0 : -3;
     }
     // V buffers: as many as shared memory holds next to Q and the K ring (224 KB).
     return launch_att<512, 2>(mq, mk, mv, prm, n_tiles, s);

@@ -174,46 +174,20 @@ EG2_DEV uint32_t mapa_shared(uint32_t local, uint32_t rank) {
     asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local), "r"(rank));
     return r;
 }
-EG2_DEV void st_cluster_f32(uint32_t addr, float v) {
-    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+// Arrive on an mbarrier of another CTA of the cluster (default release.cta semantics: enough when
+// the data it guards is ordered otherwise, e.g. TMEM through tcgen05 fences; a cluster-scope release
+// here costs ~1,000 cycles per arrive).
+EG2_DEV void mbar_arrive_remote(uint32_t remote_bar) {
+    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(remote_bar) : "memory");
 }
-// Arrive on an mbarrier of another CTA of the cluster, releasing this thread's earlier writes.
-EG2_DEV void mbar_arrive_cluster(uint32_t remote_bar) {
-    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(remote_bar) : "memory");
+// Store a 32-bit value into another CTA's shared memory and count its 4 bytes as completed
+// transactions on that CTA's mbarrier `remote_bar` (both shared::cluster addresses of the same CTA).
+// A thread that sees the barrier's phase complete also sees the value.
+EG2_DEV void st_async_f32(uint32_t remote_addr, float v, uint32_t remote_bar) {
+    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.f32 [%0], %1, [%2];" ::"r"(remote_addr), "f"(v),
+                 "r"(remote_bar)
+                 : "memory");
 }
-EG2_DEV bool mbar_try_wait_acq_cluster(uint64_t* bar, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
-// Bounded wait (as mbar_wait) with cluster-scope acquire: writes that another CTA made before its
-// releasing arrive are visible afterwards.
-EG2_DEV bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, int code, volatile int* abort) {
-    if (mbar_try_wait_acq_cluster(bar, parity)) return true;
-    uint64_t t0 = globaltimer_ns();
-    for (uint32_t it = 0;; ++it) {
-        if (mbar_try_wait_acq_cluster(bar, parity)) return true;
-        if ((it & 255u) == 255u) {
-            if (abort && *abort) return false;
-            if (*(volatile int*)&eg2_dev_status != 0) {
-                if (abort) *abort = 1;
-                return false;
-            }
-            if (globaltimer_ns() - t0 > EG2_WAIT_LIMIT_NS) {
-                eg2_record_error(code);
-                if (abort) *abort = 1;
-                return false;
-            }
-        }
-    }
-}
-
 // ---------------------------------------------------------------------------------------------
 // TMA (tiled tensor loads into this CTA's own shared memory)
 // ---------------------------------------------------------------------------------------------
@@ -285,6 +259,52 @@ template <>
 EG2_DEV void mma_bf16_or_tf32<float>(uint32_t d, uint64_t a, uint64_t b, uint32_t i, uint32_t acc) {
     mma_tf32(d, a, b, i, acc);
 }
+// ---- CTA pairs (cta_group::2): one MMA over both CTAs of a 2-CTA cluster ----------------------
+// M = 256: A rows 0..127 come from the issuing (even) CTA's shared memory / TMEM, rows 128..255 from
+// its peer's at the same address; B is split along N (first half in the even CTA, second half in the
+// odd one); D rows 0..127 land in the even CTA's TMEM, 128..255 in the odd CTA's, same columns.
+// TMEM is allocated by the same warp of both CTAs.
+EG2_DEV void tmem_alloc_pair(uint32_t* dst_smem, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)), "r"(ncols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::);
+}
+EG2_DEV void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols));
+}
+EG2_DEV void mma_bf16_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+EG2_DEV void mma_bf16_pair_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+// Arrive on the mbarrier at shared::cluster address `bar` (either CTA of the pair) once every pair
+// MMA issued so far by this thread has completed.
+EG2_DEV void mma_commit_pair(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+// Same, arriving on the mbarrier at this shared-memory offset in both CTAs of the pair.
+EG2_DEV void mma_commit_pair_both(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+                     smem_u32(bar)),
+                 "h"((uint16_t)3)
+                 : "memory");
+}
+// TMA tile load into this CTA's shared memory whose completion (bytes) is signalled on the mbarrier
+// at shared::cluster address `bar`, which may belong to the peer CTA of the pair.
+EG2_DEV void tma_load_3d_pair(void* dst, const CUtensorMap* m, uint32_t bar, int x, int y, int z) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(
+            smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(m)), "r"(bar), "r"(x), "r"(y), "r"(z)
+        : "memory");
+}
+
 // Arrive on `bar` once every MMA issued so far by this thread has completed.
 EG2_DEV void mma_commit(uint64_t* bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))

@@ -288,7 +288,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         }
         if constexpr (AN) {
             uint64_t* xb = reinterpret_cast<uint64_t*>(smem + Cfg::OFF_W + 4096);
-            for (int x = 0; x < 4; x++) mbar_init(&xb[x], 128);
+            for (int x = 0; x < 4; x++) mbar_init(&xb[x], 1);  // one local arrival (expect_tx) per exchange
         }
         *abort_flag = 0;
         fence_mbarrier_init();
@@ -392,15 +392,17 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
                 uint64_t* xb = reinterpret_cast<uint64_t*>(smem + Cfg::OFF_W + 4096);
                 const int rl = 32 * e + lane;
                 const uint32_t peer = crank ^ 1u;
-                // Sends this row's partial sum to the peer CTA (same slot there) and returns the total.
-                // Both CTAs add the same two numbers, so both use the same norm.
+                // Sends this row's partial sum to the peer CTA (same slot there, st.async counting 4
+                // bytes on the peer's barrier) and returns the total once the peer's 128 values (512
+                // bytes, expected by this set's first thread) have landed here. Both CTAs add the same
+                // two numbers, so both use the same norm.
                 bool ok = true;
                 auto exchange = [&](float part, int slot) -> float {
                     const int x = set * 2 + slot;
                     float* mine = xv + x * 128 + rl;
-                    st_cluster_f32(mapa_shared(smem_u32(mine), peer), part);
-                    mbar_arrive_cluster(mapa_shared(smem_u32(&xb[x]), peer));
-                    if (!mbar_wait_cluster(&xb[x], k & 1, EG2_DEV_TIMEOUT_GEMM, abort_flag)) {
+                    if (rl == 0) mbar_arrive_expect_tx(&xb[x], 128 * 4);
+                    st_async_f32(mapa_shared(smem_u32(mine), peer), part, mapa_shared(smem_u32(&xb[x]), peer));
+                    if (!mbar_wait(&xb[x], k & 1, EG2_DEV_TIMEOUT_GEMM, abort_flag)) {
                         ok = false;
                         return 0.f;
                     }

@@ -117,7 +117,7 @@ int attention_tc(const bf16_t* q, const bf16_t* k, const bf16_t* v, bf16_t* out,
 int attention_noalloc(const bf16_t* q, const bf16_t* k, const bf16_t* v, bf16_t* out, const int32_t* lens, int n_seq,
                       int nh, int nkv, int hd, int window, cudaStream_t s);
 // Query tokens per tile of attention_tc for a head configuration.
-int attention_tc_tile_tokens(int nh, int nkv);
+int attention_tc_tile_tokens(int nh, int nkv, int hd);
 // CUDA-core attention (f32 arithmetic; bf16 or f32 storage), one warp per (row, head).
 template <typename T>
 int attention_simt(const T* q, const T* k, const T* v, T* out, const int* seq_start, const int* seq_len, long rows,

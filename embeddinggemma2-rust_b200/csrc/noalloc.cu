@@ -93,7 +93,7 @@ static NoAllocScratch* scratch_address() {
 
 int attention_noalloc(const bf16_t* q, const bf16_t* k, const bf16_t* v, bf16_t* out, const int32_t* lens, int n_seq,
                       int nh, int nkv, int hd, int window, cudaStream_t s) {
-    const int tq = attention_tc_tile_tokens(nh, nkv);
+    const int tq = attention_tc_tile_tokens(nh, nkv, hd);
     if (!q || !k || !v || !out || !lens || n_seq <= 0 || tq <= 0) return -1;
     if (n_seq > EG2_NOALLOC_MAX_SEQ) return -1;
     long rows = 0, n_tiles = 0;

@@ -798,10 +798,10 @@ void attention<bf16_t>(eg2_ctx* c, const bf16_t* q, const bf16_t* k, const bf16_
 
 // ---------------------------------------------------------------------------------------------
 // Text backbone over w.hidden (rows x hidden f32, already holding the input embeddings).
-// Per-layer tile lists: tiles_by_cfg[k] covers layers whose (nkv) matches tile_nkv[k].
+// Per-layer tile lists: one list per (nkv, head_dim) among the layers.
 // ---------------------------------------------------------------------------------------------
 struct TileSet {
-    int nkv;
+    int nkv, hd;
     long offset;  // into w.tiles
     int count;
 };
@@ -843,7 +843,7 @@ static void enqueue_text(eg2_ctx* c, long rows, const std::vector<TileSet>& tset
         const AttnTile* tiles = nullptr;
         int n_tiles = 0;
         for (const TileSet& s : tsets)
-            if (s.nkv == nkv) {
+            if (s.nkv == nkv && s.hd == hd) {
                 tiles = w.tiles + s.offset;
                 n_tiles = s.count;
             }
@@ -878,17 +878,20 @@ static std::vector<TileSet> prepare_pass(eg2_ctx* c, const int32_t* lens, int n_
         }
         max_len = std::max<long>(max_len, lens[s]);
     }
-    std::vector<int> kinds;
-    for (auto& L : c->layers)
-        if (std::find(kinds.begin(), kinds.end(), L.nkv) == kinds.end()) kinds.push_back(L.nkv);
+    std::vector<std::pair<int, int>> kinds;  // (nkv, head_dim) of the layers
+    for (auto& L : c->layers) {
+        const std::pair<int, int> kd(L.nkv, L.hd);
+        if (std::find(kinds.begin(), kinds.end(), kd) == kinds.end()) kinds.push_back(kd);
+    }
     std::vector<TileSet> sets;
     std::vector<AttnTile> tiles;
     if (bf16_mode(c) && c->use_tc_attention) {
-        for (int nkv : kinds) {
+        for (const auto& kd : kinds) {
             TileSet ts;
-            ts.nkv = nkv;
+            ts.nkv = kd.first;
+            ts.hd = kd.second;
             ts.offset = (long)tiles.size();
-            const int tq = attention_tc_tile_tokens(tc.nh, nkv);
+            const int tq = attention_tc_tile_tokens(tc.nh, kd.first, kd.second);
             long row0 = 0;
             for (int s = 0; s < n_seq; s++) {
                 for (int q0 = 0; q0 < lens[s]; q0 += tq) tiles.push_back(AttnTile{(int)row0, lens[s], q0});
@@ -1384,7 +1387,7 @@ int eg2_attention(int kind, const void* q, const void* k, const void* v, void* o
     std::vector<int> st(rows), ln(rows);
     std::vector<AttnTile> tiles;
     long r = 0;
-    const int tq = kind == EG2_BF16 ? attention_tc_tile_tokens(nh, nkv) : 0;
+    const int tq = kind == EG2_BF16 ? attention_tc_tile_tokens(nh, nkv, hd) : 0;
     if (kind == EG2_BF16 && tq <= 0) return EG2_ERR_INVALID;
     for (int i = 0; i < n_seq; i++) {
         for (int j = 0; j < lens[i]; j++) {
