@@ -15,9 +15,10 @@
 //                while the MMAs of a third fill the free accumulator: the epilogues (norms, RoPE,
 //                GELU) are latency-bound and need the extra warps to overlap the main loop.
 //
-// EPI_ADD_NORM launches clusters of two CTAs: CTA rank r computes output columns [256 r, 256 r +
-// 256) of the cluster's row blocks, and the per-row sums of squares of the two halves are swapped
-// through distributed shared memory (a remote store plus a remote mbarrier arrive per value).
+// EPI_ADD_NORM and EPI_GROUP_NORM launch clusters of two CTAs: CTA rank r computes columns
+// [256 r, 256 r + 256) of each 512-column group, and the per-row sums of squares of the two halves are
+// swapped through distributed shared memory (st.async into the peer's slot, completing bytes on the
+// peer's mbarrier).
 #include "common.cuh"
 #include "kernels.h"
 
@@ -267,15 +268,17 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int tiles_m = (M + GEMM_BM - 1) / GEMM_BM, tiles_n = N / BN;
     const int kblocks = K / BK;
-    // This CTA's tiles: linear ids t_first + i * t_step < t_count. EPI_ADD_NORM: the cluster's row
-    // blocks, columns fixed by the CTA's rank in the cluster.
+    // This CTA's tiles: linear ids t_first + i * t_step < t_count. Cluster modes: the cluster's
+    // (row block, 512-column group) pairs, the 256-column half fixed by the CTA's rank.
     constexpr bool AN = EPI == EPI_ADD_NORM;
-    const uint32_t crank = AN ? cluster_ctarank() : 0u;
-    const int t_first = AN ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
-    const int t_step = AN ? (int)(gridDim.x >> 1) : (int)gridDim.x;
-    const int t_count = AN ? tiles_m : tiles_m * tiles_n;
-    auto tile_m0 = [&](int t) { return (AN ? t : t / tiles_n) * GEMM_BM; };
-    auto tile_n0 = [&](int t) { return AN ? (int)crank * BN : (t % tiles_n) * BN; };
+    constexpr bool CL = AN || EPI == EPI_GROUP_NORM;
+    const int groups = N / 512;
+    const uint32_t crank = CL ? cluster_ctarank() : 0u;
+    const int t_first = CL ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+    const int t_step = CL ? (int)(gridDim.x >> 1) : (int)gridDim.x;
+    const int t_count = CL ? tiles_m * groups : tiles_m * tiles_n;
+    auto tile_m0 = [&](int t) { return (CL ? t / groups : t / tiles_n) * GEMM_BM; };
+    auto tile_n0 = [&](int t) { return CL ? (t % groups) * 512 + (int)crank * BN : (t % tiles_n) * BN; };
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; s++) {
@@ -286,7 +289,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             mbar_init(&tfull[a], 1);
             mbar_init(&tempty[a], 128);
         }
-        if constexpr (AN) {
+        if constexpr (CL) {
             uint64_t* xb = reinterpret_cast<uint64_t*>(smem + Cfg::OFF_W + 4096);
             for (int x = 0; x < 4; x++) mbar_init(&xb[x], 1);  // one local arrival (expect_tx) per exchange
         }
@@ -302,8 +305,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         for (int i = threadIdx.x; i < 2 * hd + nf; i += GEMM_THREADS)
             wsm[i] = i < hd ? epi.qkv.wq[i] : i < 2 * hd ? epi.qkv.wk[i - hd] : epi.qkv.inv_freq[i - 2 * hd];
     }
-    if constexpr (AN) {
-        // This CTA's halves of the two norm weights.
+    if constexpr (CL) {
+        // This CTA's halves of the norm weights (the same for every 512-column group).
         float* wsm = reinterpret_cast<float*>(smem + Cfg::OFF_W);
         const int n0 = (int)crank * BN;
         for (int i = threadIdx.x; i < 2 * BN; i += GEMM_THREADS)
@@ -315,7 +318,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
     // The peer CTA's exchange barriers must be initialised before anyone arrives on them.
-    if constexpr (AN) cluster_sync();
+    if constexpr (CL) cluster_sync();
 
     if (warp == 0) {
         if (lane == 0) {
@@ -386,28 +389,59 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             const int m0 = tile_m0(tile), n0 = tile_n0(tile);
             const int row0 = m0 + 32 * e, row = row0 + lane;
             const uint32_t tbase = tmem_base + ((uint32_t)(32 * e) << 16) + set * BN;
-            if constexpr (EPI == EPI_ADD_NORM) {
-                const AddNormEpilogue& A = epi.an;
+            // Cluster modes: sends this row's partial sum to the peer CTA (same slot there, st.async
+            // counting 4 bytes on the peer's barrier) and returns the total once the peer's 128 values
+            // (512 bytes, expected by this set's first thread) have landed here. Both CTAs add the same
+            // two numbers, so both use the same norm.
+            bool ok = true;
+            auto exchange = [&](float part, int slot, uint32_t parity) -> float {
                 float* xv = reinterpret_cast<float*>(smem + Cfg::OFF_W) + 2 * BN;  // [set][slot][128]
                 uint64_t* xb = reinterpret_cast<uint64_t*>(smem + Cfg::OFF_W + 4096);
                 const int rl = 32 * e + lane;
                 const uint32_t peer = crank ^ 1u;
-                // Sends this row's partial sum to the peer CTA (same slot there, st.async counting 4
-                // bytes on the peer's barrier) and returns the total once the peer's 128 values (512
-                // bytes, expected by this set's first thread) have landed here. Both CTAs add the same
-                // two numbers, so both use the same norm.
-                bool ok = true;
-                auto exchange = [&](float part, int slot) -> float {
-                    const int x = set * 2 + slot;
-                    float* mine = xv + x * 128 + rl;
-                    if (rl == 0) mbar_arrive_expect_tx(&xb[x], 128 * 4);
-                    st_async_f32(mapa_shared(smem_u32(mine), peer), part, mapa_shared(smem_u32(&xb[x]), peer));
-                    if (!mbar_wait(&xb[x], k & 1, EG2_DEV_TIMEOUT_GEMM, abort_flag)) {
-                        ok = false;
-                        return 0.f;
+                const int x = set * 2 + slot;
+                float* mine = xv + x * 128 + rl;
+                if (rl == 0) mbar_arrive_expect_tx(&xb[x], 128 * 4);
+                st_async_f32(mapa_shared(smem_u32(mine), peer), part, mapa_shared(smem_u32(&xb[x]), peer));
+                if (!mbar_wait(&xb[x], parity, EG2_DEV_TIMEOUT_GEMM, abort_flag)) {
+                    ok = false;
+                    return 0.f;
+                }
+                return part + *reinterpret_cast<volatile float*>(mine);
+            };
+            if constexpr (EPI == EPI_GROUP_NORM) {
+                // One exchange per tile; the slot alternates with the tile's parity, which is also the
+                // handshake: the peer writes this set's slot for tile k + 2 only after it has this CTA's
+                // value for tile k + 1, sent after this tile's value was read here.
+                const float* w1s = wsm;
+                float ss = 0.f;
+#pragma unroll 1
+                for (int c = 0; c < BN / 32; c += 2) {
+                    uint32_t r0[32], r1[32];
+                    tmem_ld32(tbase + c * 32, r0);
+                    tmem_ld32(tbase + c * 32 + 32, r1);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int j = 0; j < 32; j++) {
+                        const float a = __uint_as_float(r0[j]) * epi.scale, b = __uint_as_float(r1[j]) * epi.scale;
+                        ss = fmaf(a, a, ss);
+                        ss = fmaf(b, b, ss);
                     }
-                    return part + *reinterpret_cast<volatile float*>(mine);
-                };
+                }
+                const float inv = 1.0f / sqrtf(exchange(ss, k & 1, (k >> 1) & 1) / 512.f + epi.an.eps);
+                if (!ok) break;
+#pragma unroll 1
+                for (int c = 0; c < BN / 32; c++) {
+                    uint32_t r[32];
+                    tmem_ld32(tbase + c * 32, r);
+                    tmem_ld_wait();
+                    float v[32];
+#pragma unroll
+                    for (int j = 0; j < 32; j++) v[j] = __uint_as_float(r[j]) * epi.scale * inv * w1s[c * 32 + j];
+                    warp_store32<TOut>(out, epi.ldo, row0, M, n0 + c * 32, v, stage);
+                }
+            } else if constexpr (EPI == EPI_ADD_NORM) {
+                const AddNormEpilogue& A = epi.an;
                 const float* w1s = wsm;
                 const float* w2s = wsm + BN;
                 // Residual chunk 0 is loaded first, so its latency overlaps pass 1 and the exchange.
@@ -427,7 +461,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
                         ss = fmaf(__uint_as_float(r1[j]), __uint_as_float(r1[j]), ss);
                     }
                 }
-                const float inv1 = 1.0f / sqrtf(exchange(ss, 0) / 512.f + A.eps);
+                const float inv1 = 1.0f / sqrtf(exchange(ss, 0, k & 1) / 512.f + A.eps);
                 if (!ok) break;
                 float ss2 = 0.f;
 #pragma unroll 1
@@ -460,7 +494,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
                 // The second exchange runs even without w2: it is also the handshake that keeps the
                 // peer from writing this set's slot 0 for the next tile before it has been read here.
                 if (A.w2) tmem_st_wait();
-                const float inv2 = 1.0f / sqrtf(exchange(ss2, 1) / 512.f + A.eps);
+                const float inv2 = 1.0f / sqrtf(exchange(ss2, 1, k & 1) / 512.f + A.eps);
                 if (!ok) break;
                 if (A.w2) {
 #pragma unroll 1
@@ -534,7 +568,7 @@ done:
         tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
     }
     // No CTA leaves while its peer may still write into its shared memory.
-    if constexpr (AN) cluster_sync();
+    if constexpr (CL) cluster_sync();
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -558,12 +592,13 @@ static int launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N,
     return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
 
-// EPI_ADD_NORM: clusters of two CTAs, as many as can be resident at once (the loop over row blocks
-// is persistent, so every launched cluster must run concurrently with the others).
-static int launch_add_norm(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int K, const GemmEpilogue& epi,
-                           cudaStream_t s) {
+// Cluster modes: clusters of two CTAs, as many as can be resident at once (the loop over tiles is
+// persistent, so every launched cluster must run concurrently with the others).
+template <int EPI, typename TOut>
+static int launch_cluster(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int K, const GemmEpilogue& epi,
+                          cudaStream_t s) {
     using Cfg = GemmCfg<256>;
-    auto kern = gemm_tc_kernel<bf16_t, 256, EPI_ADD_NORM, bf16_t>;
+    auto kern = gemm_tc_kernel<bf16_t, 256, EPI, TOut>;
     static int max_clusters[64] = {0};
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -3;
@@ -586,10 +621,10 @@ static int launch_add_norm(const CUtensorMap& ta, const CUtensorMap& tb, int M, 
         if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) return -3;
         max_clusters[dev] = n;
     }
-    const int tiles_m = (M + GEMM_BM - 1) / GEMM_BM;
-    const int clusters = tiles_m < max_clusters[dev] ? tiles_m : max_clusters[dev];
+    if (N % 512) return -1;
+    const long tiles = (long)((M + GEMM_BM - 1) / GEMM_BM) * (N / 512);
+    const int clusters = tiles < max_clusters[dev] ? (int)tiles : max_clusters[dev];
     cfg.gridDim = dim3(2 * clusters, 1, 1);
-    if (N != 512) return -1;
     return cudaLaunchKernelEx(&cfg, kern, ta, tb, M, N, K, epi) == cudaSuccess ? 0 : -3;
 }
 
@@ -626,11 +661,14 @@ int gemm_tc(GemmKind kind, const void* A, long lda, const void* W, long ldw, int
                 return launch_tc<bf16_t, BN, EPI_QKV, bf16_t>(ta, tb, M, N, K, epi, s);
             case EPI_ADD_NORM:
                 if (N != 512 || !epi.an.h || !epi.an.w1 || !epi.out) return -1;
-                return launch_add_norm(ta, tb, M, N, K, epi, s);
+                return launch_cluster<EPI_ADD_NORM, bf16_t>(ta, tb, M, N, K, epi, s);
+            case EPI_GROUP_NORM:
+                if (N % 512 || !epi.an.w1 || !epi.out) return -1;
+                return launch_cluster<EPI_GROUP_NORM, float>(ta, tb, M, N, K, epi, s);
         }
     } else {
         if (epi.mode == EPI_QKV) return launch_tc<float, BN, EPI_QKV, float>(ta, tb, M, N, K, epi, s);
-        if (epi.mode == EPI_ADD_NORM) return -1;  // bf16 only
+        if (epi.mode == EPI_ADD_NORM || epi.mode == EPI_GROUP_NORM) return -1;  // bf16 only
         switch (epi.mode) {
             case EPI_STORE:
                 return launch_tc<float, BN, EPI_STORE, float>(ta, tb, M, N, K, epi, s);

@@ -18,6 +18,8 @@ enum EpiMode : int {
                        // q, k, written to q [M, nh, hd], k / v [M, nkv, hd]; needs 256 % hd == 0
     EPI_ADD_NORM = 4,  // N = 512, bf16 inputs: residual update and norms of add_norm() on the accumulator
                        // (see AddNormEpilogue); `out` receives t (bf16, ldo), the accumulator is not stored
+    EPI_GROUP_NORM = 5,  // N = 512 g, bf16 inputs: each 512-column group of acc * scale is RMS-normalised
+                         // (an.eps) and multiplied by an.w1[col % 512]; `out` f32 [M, ldo]
 };
 
 // EPI_ADD_NORM, with o the GEMM result row (512 wide):

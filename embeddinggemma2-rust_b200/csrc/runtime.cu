@@ -821,11 +821,24 @@ static void enqueue_text(eg2_ctx* c, long rows, const std::vector<TileSet>& tset
         KL(cast_rows<bf16_t>(w.hidden, (bf16_t*)w.t, rows * h, 1.f, 0.f, c->stream), "cast");
         x_in = w.t;
     }
-    gemm(c, x_in, h, c->ple_proj, (int)rows, nl * p, h, w.ple, (long)nl * p, EPI_STORE, true, powf((float)h, -0.5f));
-    mark(c, "gemm ple_model");
-    KL(rms_norm_inplace(w.ple, c->ple_norm, rows * nl, p, eps, 1.f, c->stream), "rms_norm ple");
+    if (!f32 && bf16_mode(c) && p == 512) {
+        // One GEMM: the per-(token, layer) RMSNorm runs in its epilogue (EPI_GROUP_NORM).
+        GemmEpilogue e;
+        e.mode = EPI_GROUP_NORM;
+        e.out = w.ple;
+        e.ldo = (long)nl * p;
+        e.scale = powf((float)h, -0.5f);
+        e.an.w1 = c->ple_norm;
+        e.an.eps = eps;
+        KL(gemm_tc(GEMM_BF16, x_in, h, c->ple_proj, h, (int)rows, nl * p, h, e, c->stream), "gemm ple_model + norm");
+        mark(c, "gemm ple_model (+ norm)");
+    } else {
+        gemm(c, x_in, h, c->ple_proj, (int)rows, nl * p, h, w.ple, (long)nl * p, EPI_STORE, true, powf((float)h, -0.5f));
+        mark(c, "gemm ple_model");
+        KL(rms_norm_inplace(w.ple, c->ple_norm, rows * nl, p, eps, 1.f, c->stream), "rms_norm ple");
+    }
     KL(rms_norm_rows<T>(w.hidden, t, c->layers[0].input_ln, rows, h, eps, 1.f, c->stream), "rms_norm");
-    mark(c, "norms (ple, first)");
+    mark(c, (!f32 && bf16_mode(c) && p == 512) ? "norm (first)" : "norms (ple, first)");
     for (int i = 0; i < nl; i++) {
         const LayerW& L = c->layers[i];
         const int hd = L.hd, nkv = L.nkv;
