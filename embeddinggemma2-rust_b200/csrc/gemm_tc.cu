@@ -49,9 +49,12 @@ struct GemmCfg {
     static constexpr int OFF_STAGE = STAGES * STAGE_BYTES + 256;  // after the barriers
     static constexpr int STAGE_WARP = 32 * (64 + 16);             // 32 rows x 64 B + 16 B pad
     static constexpr int OFF_W = OFF_STAGE + 8 * STAGE_WARP;      // EPI_QKV: norm weights, inv freqs
-    // EPI_QKV: norm weights + inverse frequencies (<= 3 KB). EPI_ADD_NORM: w1 / w2 halves (2 KB),
-    // exchange slots [set][slot][128 rows] (2 KB), exchange barriers [set][slot] at +4096.
-    static constexpr int W_BYTES = 4096 + 64;
+    // EPI_QKV: norm weights + inverse frequencies (<= 3 KB). Cluster modes: this CTA's halves of the
+    // norm weights (EPI_QKV_PAIR: wq, wk and 128 inverse frequencies, 2.5 KB), exchange slots
+    // [set][slot][128 rows] at +X_OFF (2 KB), exchange barriers [set][slot] at +XB_OFF.
+    static constexpr int X_OFF = 2560;
+    static constexpr int XB_OFF = X_OFF + 2048;
+    static constexpr int W_BYTES = XB_OFF + 64;
     static constexpr int SMEM_BYTES = 1024 + OFF_W + W_BYTES;
     static constexpr uint32_t TMEM_COLS = 2 * BN;
 };
@@ -271,7 +274,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     // This CTA's tiles: linear ids t_first + i * t_step < t_count. Cluster modes: the cluster's
     // (row block, 512-column group) pairs, the 256-column half fixed by the CTA's rank.
     constexpr bool AN = EPI == EPI_ADD_NORM;
-    constexpr bool CL = AN || EPI == EPI_GROUP_NORM;
+    constexpr bool CL = AN || EPI == EPI_GROUP_NORM || EPI == EPI_QKV_PAIR;
     const int groups = N / 512;
     const uint32_t crank = CL ? cluster_ctarank() : 0u;
     const int t_first = CL ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
@@ -290,7 +293,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             mbar_init(&tempty[a], 128);
         }
         if constexpr (CL) {
-            uint64_t* xb = reinterpret_cast<uint64_t*>(smem + Cfg::OFF_W + 4096);
+            uint64_t* xb = reinterpret_cast<uint64_t*>(smem + Cfg::OFF_W + Cfg::XB_OFF);
             for (int x = 0; x < 4; x++) mbar_init(&xb[x], 1);  // one local arrival (expect_tx) per exchange
         }
         *abort_flag = 0;
@@ -305,7 +308,17 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         for (int i = threadIdx.x; i < 2 * hd + nf; i += GEMM_THREADS)
             wsm[i] = i < hd ? epi.qkv.wq[i] : i < 2 * hd ? epi.qkv.wk[i - hd] : epi.qkv.inv_freq[i - 2 * hd];
     }
-    if constexpr (CL) {
+    if constexpr (EPI == EPI_QKV_PAIR) {
+        // q_norm / k_norm weights for this CTA's 256 head channels (tile column t holds channel
+        // 128 r + t, or 256 + 128 r + t - 128), then the inverse frequencies of its 128 rotated pairs.
+        float* wsm = reinterpret_cast<float*>(smem + Cfg::OFF_W);
+        const int r = (int)crank;
+        for (int i = threadIdx.x; i < 2 * BN + 128; i += GEMM_THREADS) {
+            const int t = i & (BN - 1);
+            const int ch = t < 128 ? 128 * r + t : 256 + 128 * r + (t - 128);
+            wsm[i] = i < BN ? epi.qkv.wq[ch] : i < 2 * BN ? epi.qkv.wk[ch] : epi.qkv.inv_freq[128 * r + (i - 2 * BN)];
+        }
+    } else if constexpr (CL) {
         // This CTA's halves of the norm weights (the same for every 512-column group).
         float* wsm = reinterpret_cast<float*>(smem + Cfg::OFF_W);
         const int n0 = (int)crank * BN;
@@ -395,8 +408,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             // two numbers, so both use the same norm.
             bool ok = true;
             auto exchange = [&](float part, int slot, uint32_t parity) -> float {
-                float* xv = reinterpret_cast<float*>(smem + Cfg::OFF_W) + 2 * BN;  // [set][slot][128]
-                uint64_t* xb = reinterpret_cast<uint64_t*>(smem + Cfg::OFF_W + 4096);
+                float* xv = reinterpret_cast<float*>(smem + Cfg::OFF_W + Cfg::X_OFF);  // [set][slot][128]
+                uint64_t* xb = reinterpret_cast<uint64_t*>(smem + Cfg::OFF_W + Cfg::XB_OFF);
                 const int rl = 32 * e + lane;
                 const uint32_t peer = crank ^ 1u;
                 const int x = set * 2 + slot;
@@ -409,7 +422,70 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
                 }
                 return part + *reinterpret_cast<volatile float*>(mine);
             };
-            if constexpr (EPI == EPI_GROUP_NORM) {
+            if constexpr (EPI == EPI_QKV_PAIR) {
+                // One head per 512-column group; as EPI_QKV (rowops.cu qkv_post_kernel arithmetic) with
+                // the head's sum of squares completed by the exchange (slots alternate by tile parity).
+                const QkvEpilogue& Q = epi.qkv;
+                const int hidx = n0 / 512;
+                TOut* base;
+                int nheads, head;
+                const float* w;
+                bool rot;
+                if (hidx < Q.nh) {
+                    base = (TOut*)Q.q, nheads = Q.nh, head = hidx, w = wsm, rot = true;
+                } else if (hidx < Q.nh + Q.nkv) {
+                    base = (TOut*)Q.k, nheads = Q.nkv, head = hidx - Q.nh, w = wsm + BN, rot = true;
+                } else {
+                    base = (TOut*)Q.v, nheads = Q.nkv, head = hidx - Q.nh - Q.nkv, w = nullptr, rot = false;
+                }
+                float ss = 0.f;
+#pragma unroll 1
+                for (int c = 0; c < BN / 32; c += 2) {
+                    uint32_t r0[32], r1[32];
+                    tmem_ld32(tbase + c * 32, r0);
+                    tmem_ld32(tbase + c * 32 + 32, r1);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int j = 0; j < 32; j++) {
+                        ss = fmaf(__uint_as_float(r0[j]), __uint_as_float(r0[j]), ss);
+                        ss = fmaf(__uint_as_float(r1[j]), __uint_as_float(r1[j]), ss);
+                    }
+                }
+                const float inv = 1.0f / sqrtf(exchange(ss, k & 1, (k >> 1) & 1) / 512.f + Q.eps);
+                if (!ok) break;
+                const float* invs = wsm + 2 * BN;
+                const long ldo = (long)nheads * 512;
+                const long col1 = (long)head * 512 + 128 * crank, col2 = col1 + 256;
+                const bool live = row < M;
+                const float pf = live ? (float)(Q.pos ? Q.pos[(long)row * Q.pos_stride] : row) : 0.f;
+#pragma unroll 1
+                for (int c = 0; c < 4; c++) {
+                    float x1[32], x2[32];
+                    {
+                        uint32_t a[32], b[32];
+                        tmem_ld32(tbase + c * 32, a);
+                        tmem_ld32(tbase + 128 + c * 32, b);
+                        tmem_ld_wait();
+#pragma unroll
+                        for (int t = 0; t < 32; t++) {
+                            x1[t] = __uint_as_float(a[t]) * inv;
+                            x2[t] = __uint_as_float(b[t]) * inv;
+                        }
+                    }
+                    if (rot) {
+#pragma unroll
+                        for (int t = 0; t < 32; t++) {
+                            const float a1 = x1[t] * w[c * 32 + t], a2 = x2[t] * w[128 + c * 32 + t];
+                            float sj, cj;
+                            sincos_reduced(pf * invs[c * 32 + t], sj, cj);
+                            x1[t] = a1 * cj - a2 * sj;
+                            x2[t] = a2 * cj + a1 * sj;
+                        }
+                    }
+                    warp_store32<TOut>(base, ldo, row0, M, col1 + c * 32, x1, stage);
+                    warp_store32<TOut>(base, ldo, row0, M, col2 + c * 32, x2, stage);
+                }
+            } else if constexpr (EPI == EPI_GROUP_NORM) {
                 // One exchange per tile; the slot alternates with the tile's parity, which is also the
                 // handshake: the peer writes this set's slot for tile k + 2 only after it has this CTA's
                 // value for tile k + 1, sent after this tile's value was read here.
@@ -628,6 +704,10 @@ static int launch_cluster(const CUtensorMap& ta, const CUtensorMap& tb, int M, i
     return cudaLaunchKernelEx(&cfg, kern, ta, tb, M, N, K, epi) == cudaSuccess ? 0 : -3;
 }
 
+bool qkv_pair_fusable(const QkvEpilogue& q) {
+    return q.hd == 512 && q.part == 512 && q.nh > 0 && q.nkv > 0 && q.wq && q.wk && q.inv_freq;
+}
+
 bool qkv_fusable(const QkvEpilogue& q) {
     const int hd = q.hd, half = q.part / 2;
     if (hd <= 0 || hd % 32 || 256 % hd || q.part <= 0 || hd % q.part) return false;
@@ -665,10 +745,13 @@ int gemm_tc(GemmKind kind, const void* A, long lda, const void* W, long ldw, int
             case EPI_GROUP_NORM:
                 if (N % 512 || !epi.an.w1 || !epi.out) return -1;
                 return launch_cluster<EPI_GROUP_NORM, float>(ta, tb, M, N, K, epi, s);
+            case EPI_QKV_PAIR:
+                if (!qkv_pair_fusable(epi.qkv) || N != (epi.qkv.nh + 2 * epi.qkv.nkv) * 512) return -1;
+                return launch_cluster<EPI_QKV_PAIR, bf16_t>(ta, tb, M, N, K, epi, s);
         }
     } else {
         if (epi.mode == EPI_QKV) return launch_tc<float, BN, EPI_QKV, float>(ta, tb, M, N, K, epi, s);
-        if (epi.mode == EPI_ADD_NORM || epi.mode == EPI_GROUP_NORM) return -1;  // bf16 only
+        if (epi.mode == EPI_ADD_NORM || epi.mode == EPI_GROUP_NORM || epi.mode == EPI_QKV_PAIR) return -1;  // bf16 only
         switch (epi.mode) {
             case EPI_STORE:
                 return launch_tc<float, BN, EPI_STORE, float>(ta, tb, M, N, K, epi, s);

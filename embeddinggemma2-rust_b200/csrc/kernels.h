@@ -20,7 +20,19 @@ enum EpiMode : int {
                        // (see AddNormEpilogue); `out` receives t (bf16, ldo), the accumulator is not stored
     EPI_GROUP_NORM = 5,  // N = 512 g, bf16 inputs: each 512-column group of acc * scale is RMS-normalised
                          // (an.eps) and multiplied by an.w1[col % 512]; `out` f32 [M, ldo]
+    EPI_QKV_PAIR = 6,    // EPI_QKV for head_dim 512 (RoPE over the whole head): one 512-column group per
+                         // head, the two 256-column halves on a 2-CTA cluster. The weight rows of each head
+                         // must be in the pair layout (qkv_pair_row): half r holds head channels
+                         // [128 r, 128 r + 128) and [256 + 128 r, 256 + 128 r + 128), so every rotated pair
+                         // (i, i + 256) is inside one half
 };
+
+// Pair layout of a 512-channel head: weight row n' (0..511) of the permuted head holds original
+// channel qkv_pair_row(n').
+inline int qkv_pair_row(int np) {
+    const int r = (np >> 7) & 1, hi = np >> 8;  // [0,128) -> 0, [128,256) -> 256, [256,384) -> 128, [384,512) -> 384
+    return (np & 127) + 128 * hi + 256 * r;
+}
 
 // EPI_ADD_NORM, with o the GEMM result row (512 wide):
 //   h = (h + o / rms(o) * w1) * scalar;  out = w2 ? h / rms(h) * w2 : h   (rms(x) = sqrt(mean(x^2) + eps))
@@ -70,6 +82,7 @@ int make_tmap_3d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint6
 
 // Whether EPI_QKV applies to a head configuration (whole heads per 256-column tile).
 bool qkv_fusable(const QkvEpilogue& q);
+bool qkv_pair_fusable(const QkvEpilogue& q);
 // C = A . W^T on tcgen05 (bf16 or tf32 inputs). N must be a multiple of 256, K of 64 (bf16) / 32 (tf32).
 int gemm_tc(GemmKind kind, const void* A, long lda, const void* W, long ldw, int M, int N, int K,
             const GemmEpilogue& epi, cudaStream_t s);

@@ -336,6 +336,7 @@ struct LayerW {
     float *input_ln, *post_attn_ln, *pre_ff_ln, *post_ff_ln, *q_norm, *k_norm, *ple_post_norm;
     float layer_scalar = 1.f;
     int hd = 0, nkv = 0, sliding = 0, rope = 0;
+    bool qkv_pair = false;  // qkv rows in the pair layout of EPI_QKV_PAIR (bf16, 512-wide heads)
 };
 
 struct VLayerW {
@@ -461,6 +462,15 @@ static void upload_rows(eg2_ctx* c, const SafeTensors& st, const std::string& na
     CK(cudaMemcpy((uint8_t*)dst + dst_row0 * cols * es, tmp.data(), n * es, cudaMemcpyHostToDevice));
 }
 
+// The weight rows of `nheads` 512-channel heads in the pair layout of EPI_QKV_PAIR (kernels.h
+// qkv_pair_row): four blocks of 128 rows per head.
+static void upload_rows_pair(eg2_ctx* c, const SafeTensors& st, const std::string& name, std::initializer_list<long> shape,
+                             void* dst, long dst_row0, long nheads) {
+    for (long hh = 0; hh < nheads; hh++)
+        for (int np = 0; np < 512; np += 128)
+            upload_rows(c, st, name, shape, dst, dst_row0 + hh * 512 + np, hh * 512 + qkv_pair_row(np), 128);
+}
+
 static float* upload_vec(eg2_ctx* c, const SafeTensors& st, const std::string& name, long n) {
     std::vector<float> v = st.f32(name, {n});
     float* d = (float*)dalloc(c, n * 4);
@@ -496,9 +506,17 @@ static void load_text(eg2_ctx* c, const SafeTensors& st) {
         std::string P(pre);
         const long nqkv = (nh + 2 * nkv) * hd;
         L.qkv = dalloc(c, nqkv * h * act_size(c));
-        upload_rows(c, st, P + "self_attn.q_proj.weight", {nh * hd, h}, L.qkv, 0, 0, nh * hd);
-        upload_rows(c, st, P + "self_attn.k_proj.weight", {nkv * hd, h}, L.qkv, nh * hd, 0, nkv * hd);
-        upload_rows(c, st, P + "self_attn.v_proj.weight", {nkv * hd, h}, L.qkv, (nh + nkv) * hd, 0, nkv * hd);
+        // bf16 with 512-wide heads: rows in the pair layout of the fused QKV epilogue (EPI_QKV_PAIR).
+        L.qkv_pair = bf16_mode(c) && hd == 512 && !getenv("EG2_NO_QKV_FUSION");
+        if (L.qkv_pair) {
+            upload_rows_pair(c, st, P + "self_attn.q_proj.weight", {nh * hd, h}, L.qkv, 0, nh);
+            upload_rows_pair(c, st, P + "self_attn.k_proj.weight", {nkv * hd, h}, L.qkv, nh * hd, nkv);
+            upload_rows_pair(c, st, P + "self_attn.v_proj.weight", {nkv * hd, h}, L.qkv, (nh + nkv) * hd, nkv);
+        } else {
+            upload_rows(c, st, P + "self_attn.q_proj.weight", {nh * hd, h}, L.qkv, 0, 0, nh * hd);
+            upload_rows(c, st, P + "self_attn.k_proj.weight", {nkv * hd, h}, L.qkv, nh * hd, 0, nkv * hd);
+            upload_rows(c, st, P + "self_attn.v_proj.weight", {nkv * hd, h}, L.qkv, (nh + nkv) * hd, 0, nkv * hd);
+        }
         L.o = dalloc(c, h * nh * hd * act_size(c));
         upload_rows(c, st, P + "self_attn.o_proj.weight", {h, nh * hd}, L.o, 0, 0, h);
         L.gu = upload_gate_up(c, st, P + "mlp.gate_proj.weight", P + "mlp.up_proj.weight", ff, h);
@@ -735,13 +753,22 @@ static void gemm(eg2_ctx* c, const void* x, long ldx, const void* W, int M, int 
 // (EPI_QKV). Returns false when the configuration does not fuse (f32 precision, or heads that do
 // not tile the 256-column output tile); the caller then runs GEMM + qkv_post.
 static bool qkv_projection(eg2_ctx* c, const void* x, int k, const void* W, long rows, void* q, void* kk, void* v,
-                           const float* wq, const float* wk, const float* inv_freq, const int* pos, int pos_stride, int nh, int nkv, int hd, int part, float eps) {
-    if (c->precision == EG2_F32 || getenv("EG2_NO_QKV_FUSION")) return false;
+                           const float* wq, const float* wk, const float* inv_freq, const int* pos, int pos_stride, int nh, int nkv, int hd, int part, float eps,
+                           bool pair_layout = false) {
     GemmEpilogue e;
-    e.mode = EPI_QKV;
     QkvEpilogue& Q = e.qkv;
     Q.q = q, Q.k = kk, Q.v = v, Q.wq = wq, Q.wk = wk, Q.inv_freq = inv_freq, Q.pos = pos, Q.pos_stride = pos_stride;
     Q.nh = nh, Q.nkv = nkv, Q.hd = hd, Q.part = part, Q.eps = eps;
+    if (pair_layout) {
+        // The weights were loaded in the pair layout: only the fused epilogue undoes it.
+        if (!qkv_pair_fusable(Q)) fail(EG2_ERR_INVALID, "qkv pair layout without a fusable configuration");
+        e.mode = EPI_QKV_PAIR;
+        KL(gemm_tc(GEMM_BF16, x, k, W, k, (int)rows, (nh + 2 * nkv) * hd, k, e, c->stream), "gemm qkv (head 512) + norm/rope");
+        mark(c, "gemm qkv (head 512) + norm/rope");
+        return true;
+    }
+    if (c->precision == EG2_F32 || getenv("EG2_NO_QKV_FUSION")) return false;
+    e.mode = EPI_QKV;
     if (!qkv_fusable(Q)) return false;
     KL(gemm_tc(bf16_mode(c) ? GEMM_BF16 : GEMM_TF32, x, k, W, k, (int)rows, (nh + 2 * nkv) * hd, k, e, c->stream),
        "gemm qkv + norm/rope");
@@ -845,7 +872,7 @@ static void enqueue_text(eg2_ctx* c, long rows, const std::vector<TileSet>& tset
         const int nqkv = (nh + 2 * nkv) * hd;
         const RopeTab& rt = c->ropes[L.rope];
         if (!qkv_projection(c, t, h, L.qkv, rows, w.q, w.k, w.v, L.q_norm, L.k_norm, rt.inv, w.pos, 1, nh, nkv,
-                            hd, hd, eps)) {
+                            hd, hd, eps, L.qkv_pair)) {
             gemm(c, t, h, L.qkv, (int)rows, nqkv, h, w.qkv, nqkv, EPI_STORE, true);
             mark(c, "gemm qkv");
             KL((qkv_post<float, T>((const float*)w.qkv, (T*)w.q, (T*)w.k, (T*)w.v, L.q_norm, L.k_norm, rt.cs, rt.sn, hd / 2,
