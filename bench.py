@@ -141,6 +141,68 @@ def make_checkpoint(dirpath: Path):
     pkg("weights").make_random_checkpoint(dirpath, seed=0, vision=False)
 
 
+MIXED_DOCS, MIXED_LO, MIXED_HI, MIXED_SEED = 64, 128, 2208, 7
+LONG_LEN = 11774
+
+
+def run_mixed(tb, cfg, stream, rank, world, args, barrier, max_over_ranks):
+    """C3: 64 documents with lengths uniform in [128, 2208] (seeded), split over the ranks longest-first
+    by estimated cost (shard.assign), each rank one packed pass per step; docs/s of the job = 64 x
+    steps / max over ranks of the device time (strong scaling: the total work is fixed)."""
+    import torch
+
+    rng = np.random.default_rng(MIXED_SEED)
+    all_lens = rng.integers(MIXED_LO, MIXED_HI + 1, size=MIXED_DOCS)
+    all_ids = [rng.integers(0, cfg.text.vocab_size, size=int(n)).astype(np.uint32) for n in all_lens]
+    mine = pkg("shard").assign(all_lens, world)[rank]
+    lens = [int(all_lens[i]) for i in mine]
+    ids = np.concatenate([all_ids[i] for i in mine]) if mine else np.zeros(1, np.uint32)
+    ids_dev = torch.from_numpy(ids.view(np.int32)).cuda()
+    out_dev = torch.empty((max(1, len(lens)), sum(DIMS)), dtype=torch.float32, device="cuda")
+
+    def step():
+        if lens:
+            tb.embed_ids_device(ids_dev.data_ptr(), lens, DIMS, out_dev.data_ptr(), stream.cuda_stream)
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1))
+    return {"value": round(MIXED_DOCS * args.steps / (ms / 1000.0), 2), "unit": "docs/s", "docs": MIXED_DOCS,
+            "tokens": int(all_lens.sum()), "lengths": f"uniform integers in [{MIXED_LO}, {MIXED_HI}], seed {MIXED_SEED}",
+            "scaling": "strong (64 documents split over the GPUs longest-first by estimated cost)",
+            "ms_per_step": round(ms / args.steps, 3)}
+
+
+def run_long(tb, cfg, stream):
+    """C4: one sequence of 11,774 seeded uniform ids on one GPU (the reference's long case)."""
+    import torch
+
+    ids = np.random.default_rng(LONG_LEN).integers(0, cfg.text.vocab_size, size=LONG_LEN).astype(np.uint32)
+    ids_dev = torch.from_numpy(ids.view(np.int32)).cuda()
+    out_dev = torch.empty((1, sum(DIMS)), dtype=torch.float32, device="cuda")
+    for _ in range(2):
+        tb.embed_ids_device(ids_dev.data_ptr(), [LONG_LEN], DIMS, out_dev.data_ptr(), stream.cuda_stream)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 5
+    e0.record(stream)
+    for _ in range(reps):
+        tb.embed_ids_device(ids_dev.data_ptr(), [LONG_LEN], DIMS, out_dev.data_ptr(), stream.cuda_stream)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    return {"ms_per_doc": round(ms, 3), "tokens": LONG_LEN, "tokens_per_s": round(LONG_LEN / (ms / 1000.0), 1),
+            "gpus": 1}
+
+
 # ---------------------------------------------------------------------------------------------
 def cpu_baseline_run(model_dir: Path, docs: int, seed: int):
     """The oracle (C restatement of the reference CPU f32 path) on `docs` documents of SEQ_LEN."""
@@ -286,6 +348,13 @@ def main():
     barrier()
     e2e_value = world * n_docs * e2e_steps / t_e2e
 
+    # ---- C3: 64 documents of mixed length, sharded over the ranks (strong scaling) ----
+    dev.set_stream(stream.cuda_stream)
+    mixed = run_mixed(tb, cfg, stream, rank, world, args, barrier, max_over_ranks)
+    # ---- C4: one 11,774-token document (rank 0 only; the other ranks wait at the next barrier) ----
+    long_case = run_long(tb, cfg, stream) if rank == 0 else None
+    barrier()
+
     # ---- per-op device time shares (CUDA events around each op, one profiled step) ----
     dev.set_stream(stream.cuda_stream)
     dev.profile(True)
@@ -354,6 +423,8 @@ def main():
             "gpu_launches": int(launches),
             "clocks": clocks,
             "cpu_baseline": cpu,
+            "mixed_c3": mixed,
+            "long_c4": long_case,
         }
         print(json.dumps(line))
     dev.close()

@@ -15,7 +15,7 @@ from pathlib import Path
 HERE = Path(__file__).resolve().parent
 CSRC = HERE / "csrc"
 OUT = HERE / "_lib" / "libeg2_b200.so"
-SOURCES = ["eg2_lib.cu", "common.cuh", "kernels.h", "json.h", "gemm_tc.cu", "simt.cu", "rowops.cu", "attention_tc.cu", "noalloc.cu", "runtime.cu"]
+SOURCES = ["eg2_lib.cu", "common.cuh", "kernels.h", "json.h", "gemm_tc.cu", "simt.cu", "rowops.cu", "attention_tc.cu", "noalloc.cu", "probe.cu", "runtime.cu"]
 
 
 def nvcc() -> str:

@@ -22,6 +22,7 @@ enum Eg2DevError : int {
     EG2_DEV_TIMEOUT_GEMM = 1,
     EG2_DEV_TIMEOUT_ATTN = 2,
     EG2_DEV_BAD_ARGS = 3,
+    EG2_DEV_TIMEOUT_PROBE = 4,  // the failure-detection probe's wait ran out (as designed)
 };
 
 // Upper bound of any single wait: 2 s. A healthy pipeline waits microseconds.
@@ -133,8 +134,8 @@ EG2_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 // Bounded wait for the phase with the given parity to complete. Returns false (and records
-// `code`) if it does not complete within EG2_WAIT_LIMIT_NS, or if `abort` is already set.
-EG2_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, int code, volatile int* abort) {
+// `code`) if it does not complete within `limit_ns`, or if `abort` is already set.
+EG2_DEV bool mbar_wait_limit(uint64_t* bar, uint32_t parity, int code, volatile int* abort, uint64_t limit_ns) {
     if (mbar_try_wait(bar, parity)) return true;
     uint64_t t0 = globaltimer_ns();
     for (uint32_t it = 0;; ++it) {
@@ -146,13 +147,16 @@ EG2_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, int code, volatile int* a
                 if (abort) *abort = 1;
                 return false;
             }
-            if (globaltimer_ns() - t0 > EG2_WAIT_LIMIT_NS) {
+            if (globaltimer_ns() - t0 > limit_ns) {
                 eg2_record_error(code);
                 if (abort) *abort = 1;
                 return false;
             }
         }
     }
+}
+EG2_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, int code, volatile int* abort) {
+    return mbar_wait_limit(bar, parity, code, abort, EG2_WAIT_LIMIT_NS);
 }
 
 // ---------------------------------------------------------------------------------------------

@@ -9,4 +9,5 @@
 #include "rowops.cu"
 #include "attention_tc.cu"
 #include "noalloc.cu"
+#include "probe.cu"
 #include "runtime.cu"

@@ -133,6 +133,8 @@ int attention_noalloc(const bf16_t* q, const bf16_t* k, const bf16_t* v, bf16_t*
                       int nh, int nkv, int hd, int window, cudaStream_t s);
 // Query tokens per tile of attention_tc for a head configuration.
 int attention_tc_tile_tokens(int nh, int nkv, int hd);
+// Failure-detection probe: a bounded wait on a barrier nothing arrives on (probe.cu).
+int wait_timeout_probe(unsigned long long limit_ns, cudaStream_t s);
 // CUDA-core attention (f32 arithmetic; bf16 or f32 storage), one warp per (row, head).
 template <typename T>
 int attention_simt(const T* q, const T* k, const T* v, T* out, const int* seq_start, const int* seq_len, long rows,

@@ -1489,4 +1489,16 @@ void eg2_device_status_reset(void) {
     cudaMemcpyToSymbol(eg2_dev_status, &zero, sizeof(int));
 }
 
+int eg2_wait_timeout_probe(int device, unsigned int limit_us, int* device_status) {
+    if (!device_status || limit_us == 0 || limit_us > 2000000u) return EG2_ERR_INVALID;
+    if (cudaSetDevice(device) != cudaSuccess) return EG2_ERR_CUDA;
+    eg2_device_status_reset();
+    if (wait_timeout_probe((unsigned long long)limit_us * 1000ull, nullptr)) return EG2_ERR_CUDA;
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    if (cudaDeviceSynchronize() != cudaSuccess) return EG2_ERR_CUDA;
+    *device_status = eg2_device_status();
+    eg2_device_status_reset();
+    return EG2_OK;
+}
+
 }  // extern "C"

@@ -70,6 +70,7 @@ def load(build_if_missing: bool = True) -> C.CDLL:
         "eg2_launch_count": (C.c_longlong, []),
         "eg2_device_status": (C.c_int, []),
         "eg2_device_status_reset": (None, []),
+        "eg2_wait_timeout_probe": (C.c_int, [C.c_int, C.c_uint, C.POINTER(C.c_int)]),
     }
     for name, (res, args) in sig.items():
         f = getattr(lib, name)

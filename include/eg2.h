@@ -131,6 +131,14 @@ long long eg2_launch_count(void);
 int eg2_device_status(void);
 void eg2_device_status_reset(void);
 
+/* Failure-detection probe. No counterpart in the reference (its kernels have no bounded waits):
+ * launches one CTA on `device` that waits on an mbarrier nothing arrives on, bounded by `limit_us`
+ * (1 .. 2,000,000) microseconds of wall time -- the same bounded wait every pipeline barrier of the
+ * library uses. The wait runs out and records status 4 in the device status word; the call
+ * synchronises, stores that status in *device_status, clears it and returns EG2_OK when the context
+ * is still usable. Every other entry point reports such a recorded status as EG2_ERR_TIMEOUT. */
+int eg2_wait_timeout_probe(int device, unsigned int limit_us, int* device_status);
+
 #ifdef __cplusplus
 }
 #endif
