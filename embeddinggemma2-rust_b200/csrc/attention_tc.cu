@@ -48,33 +48,43 @@ struct AttParams {
 //
 //   warp 0      TMA producer (this CTA's Q and its half of every unit)
 //   warp 1      TMEM allocation (both CTAs); in the even CTA lane 0 issues the S = Q K^T MMAs
-//   warps 2..5  softmax, one thread per row of this CTA's 128 rows; O / l epilogue
-//   warp 6      in the even CTA lane 0 issues the O += P V MMAs
+//   softmax     head 256: warps 2..9, two threads per row (64 of the 128 columns each; the pair
+//               swaps its row maxima through shared memory with a bounded mbarrier handshake, so
+//               both take the same stale-max decisions, and adds the row sums at the end); head 512:
+//               warps 2..5, one thread per row. O / l epilogue
+//   last warp   in the even CTA lane 0 issues the O += P V MMAs
 // Two issuing threads: tcgen05.mma issue blocks once a couple of MMAs are queued, so one thread
 // leaves the tensor pipe idle during each of its waits and commits; with S and P V on different
 // threads (disjoint TMEM, per-thread commit tracking) one feeds the pipe while the other waits.
 // ---------------------------------------------------------------------------------------------
-constexpr int AP_THREADS = 224;
 constexpr int AP_BN = 128;
 constexpr int AP_UNIT = 32768;
 template <int DQK>
 struct ApCfg {
+    static constexpr bool SPLIT = DQK == 256;        // two softmax threads per row
+    static constexpr int NSW = SPLIT ? 8 : 4;        // softmax warps
+    static constexpr int PV_WARP = 2 + NSW;
+    static constexpr int THREADS = 32 * (PV_WARP + 1);
     static constexpr int QCH = DQK / 64;             // Q chunks of [128 rows x 64 channels]
     static constexpr int KU = DQK / 256;             // K units per key tile
     static constexpr int Q_BYTES = QCH * 128 * 128;
-    static constexpr int UNITS = DQK == 256 ? 5 : 3;
+    static constexpr int UNITS = DQK == 256 ? 4 : 3;
     static constexpr int OFF_R = Q_BYTES;
     static constexpr int OFF_BAR = OFF_R + UNITS * AP_UNIT;
-    static constexpr int N_BARS = 1 + 2 * UNITS + 2 + 4 + 2;  // q, ring, s full/empty, p[2], pv[2], drain[2]
-    static constexpr int SMEM = 1024 + OFF_BAR + N_BARS * 8 + 16;
+    // q, ring full/empty, s full/empty, p[2], pv[2], drain[2]; split softmax: pair handshakes [4 quadrants][2]
+    static constexpr int N_BARS = 1 + 2 * UNITS + 2 + 4 + 2 + (SPLIT ? 8 : 0);
+    static constexpr int OFF_X = OFF_BAR + N_BARS * 8 + 16;  // split softmax: maxima [2 slots][2 halves][128], sums [2][128]
+    static constexpr int SMEM = 1024 + OFF_X + (SPLIT ? 3 * 1024 : 0);
 };
 static_assert(ApCfg<256>::SMEM <= 227 * 1024 && ApCfg<512>::SMEM <= 227 * 1024, "attention pair: shared memory");
 
 template <int DQK>
-__global__ void __launch_bounds__(AP_THREADS, 1)
+__global__ void __launch_bounds__(ApCfg<DQK>::THREADS, 1)
     attention_pair_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                           const __grid_constant__ CUtensorMap tmV, AttParams prm) {
     using Cfg = ApCfg<DQK>;
+    constexpr bool SPLIT = Cfg::SPLIT;
+    constexpr int SM_ARRIVALS = 2 * 32 * Cfg::NSW;  // softmax threads of both CTAs
     constexpr int AP_UNITS = Cfg::UNITS;
     constexpr int KU = Cfg::KU;
     extern __shared__ uint8_t smem_raw[];
@@ -88,6 +98,7 @@ __global__ void __launch_bounds__(AP_THREADS, 1)
     uint64_t* p_full = s_empty + 1;
     uint64_t* pv_done = p_full + 2;
     uint64_t* drain = pv_done + 2;
+    uint64_t* xpair = drain + 2;  // split softmax: [quadrant][slot], 64 arrivals (the row's two warps)
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + Cfg::N_BARS);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -113,11 +124,13 @@ __global__ void __launch_bounds__(AP_THREADS, 1)
             mbar_init(&r_empty[u], 1);
         }
         mbar_init(s_full, 1);
-        mbar_init(s_empty, 256);
+        mbar_init(s_empty, SM_ARRIVALS);
         for (int b = 0; b < 2; b++) {
-            mbar_init(&p_full[b], 256);
+            mbar_init(&p_full[b], SM_ARRIVALS);
             mbar_init(&pv_done[b], 1);
         }
+        if constexpr (SPLIT)
+            for (int x = 0; x < 8; x++) mbar_init(&xpair[x], 64);
         mbar_init(&drain[0], 1);
         mbar_init(&drain[1], 1);
         *abort_flag = 0;
@@ -176,7 +189,7 @@ __global__ void __launch_bounds__(AP_THREADS, 1)
                 if (!load_unit(-1, j)) goto done;
             }
         }
-    } else if (warp == 1 || warp == 6) {
+    } else if (warp == 1 || warp == Cfg::PV_WARP) {
         if (even && lane == 0) {
             // Ring position of K(j) unit ku / V(j): the producer's order is K(0), then per tile j
             // K(j + 1) (if any) and V(j).
@@ -226,13 +239,19 @@ __global__ void __launch_bounds__(AP_THREADS, 1)
                 }
             }
         }
-    } else {
+    } else if (warp >= 2 && warp < 2 + Cfg::NSW) {
+        const int sw = warp - 2;
         const int e = warp & 3;
+        const int ch = SPLIT ? (sw >> 2) : 0;    // column half of S / P / O this thread owns
+        constexpr int NC = SPLIT ? 64 : 128;     // S columns per thread
+        constexpr int OC = SPLIT ? 128 : 256;    // O columns per thread
         const int r = 32 * e + lane;
         const int tok = q0r + r / G;
         const bool row_valid = tok < tile.len;
         const uint32_t lane_off = (uint32_t)(32 * e) << 16;
         const float LOG2E = 1.4426950408889634f;
+        float* xmax = reinterpret_cast<float*>(smem + Cfg::OFF_X);  // [slot][half][128]
+        float* xsum = xmax + 2 * 2 * 128;                            // [half][128]
         // Arrivals for the MMA issuer go to the even CTA's barriers. What they guard is TMEM (S read,
         // P written), ordered by tcgen05.wait + tcgen05.fence::before_thread_sync.
         auto arrive_even = [&](uint64_t* bar) {
@@ -244,40 +263,45 @@ __global__ void __launch_bounds__(AP_THREADS, 1)
             const int b = j & 1;
             if (!mbar_wait(s_full, j & 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) break;
             tc_fence_after();
-            float sv[AP_BN];
+            float sv[NC];
             {
-                uint32_t s0[32], s1[32], s2[32], s3[32];
-                tmem_ld32(t_s + lane_off, s0);
-                tmem_ld32(t_s + 32 + lane_off, s1);
-                tmem_ld32(t_s + 64 + lane_off, s2);
-                tmem_ld32(t_s + 96 + lane_off, s3);
-                tmem_ld_wait();
+#pragma unroll
+                for (int c = 0; c < NC / 32; c++) {
+                    uint32_t s0[32];
+                    tmem_ld32(t_s + ch * 64 + 32 * c + lane_off, s0);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int q = 0; q < 32; q++) sv[32 * c + q] = __uint_as_float(s0[q]);
+                }
                 tc_fence_before();
                 arrive_even(s_empty);
-#pragma unroll
-                for (int c = 0; c < 32; c++) {
-                    sv[c] = __uint_as_float(s0[c]);
-                    sv[32 + c] = __uint_as_float(s1[c]);
-                    sv[64 + c] = __uint_as_float(s2[c]);
-                    sv[96 + c] = __uint_as_float(s3[c]);
-                }
             }
-            const int kbase = k_lo + j * AP_BN;
-            int lo_c = 0, hi_c = min(AP_BN, tile.len - kbase);
+            // Valid key columns of this row in this tile, relative to this thread's first column.
+            const int kbase = k_lo + j * AP_BN + ch * 64;
+            int lo_c = 0, hi_c = min(NC, tile.len - kbase);
             if (W >= 0 && row_valid) {
                 lo_c = max(lo_c, tok - W - kbase);
                 hi_c = min(hi_c, tok + W + 1 - kbase);
             }
-            if (!__all_sync(0xffffffffu, lo_c <= 0 && hi_c >= AP_BN)) {
+            if (!__all_sync(0xffffffffu, lo_c <= 0 && hi_c >= NC)) {
 #pragma unroll
-                for (int c = 0; c < AP_BN; c++) sv[c] = (c >= lo_c && c < hi_c) ? sv[c] : -INFINITY;
+                for (int c = 0; c < NC; c++) sv[c] = (c >= lo_c && c < hi_c) ? sv[c] : -INFINITY;
             }
             float mx[8];
 #pragma unroll
             for (int c = 0; c < 8; c++) mx[c] = sv[c];
 #pragma unroll
-            for (int c = 8; c < AP_BN; c++) mx[c & 7] = fmaxf(mx[c & 7], sv[c]);
-            const float mt = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+            for (int c = 8; c < NC; c++) mx[c & 7] = fmaxf(mx[c & 7], sv[c]);
+            float mt = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+            if constexpr (SPLIT) {
+                // The row's other half: slots alternate by tile, so a slot is rewritten only after
+                // the partner has passed the next handshake (and read this one).
+                float* slot = xmax + (j & 1) * 256;
+                slot[ch * 128 + r] = mt;
+                mbar_arrive(&xpair[e * 2 + (j & 1)]);
+                if (!mbar_wait(&xpair[e * 2 + (j & 1)], (j >> 1) & 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) break;
+                mt = fmaxf(mt, *reinterpret_cast<volatile float*>(slot + (ch ^ 1) * 128 + r));
+            }
             float factor = 1.f;
             bool need = false;
             if (mt > m_used) {
@@ -294,13 +318,13 @@ __global__ void __launch_bounds__(AP_THREADS, 1)
                 if (!mbar_wait(&pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) break;
                 tc_fence_after();
 #pragma unroll 1
-                for (int c = 0; c < ATT_DV / 32; c++) {
+                for (int c = 0; c < OC / 32; c++) {
                     uint32_t o[32];
-                    tmem_ld32(t_o + c * 32 + lane_off, o);
+                    tmem_ld32(t_o + ch * 128 + c * 32 + lane_off, o);
                     tmem_ld_wait();
 #pragma unroll
                     for (int q = 0; q < 32; q++) o[q] = __float_as_uint(__uint_as_float(o[q]) * factor);
-                    tmem_st32(t_o + c * 32 + lane_off, o);
+                    tmem_st32(t_o + ch * 128 + c * 32 + lane_off, o);
                 }
                 tmem_st_wait();
             }
@@ -314,7 +338,7 @@ __global__ void __launch_bounds__(AP_THREADS, 1)
             const float bias = (m_used == -INFINITY) ? 0.f : -m_used * LOG2E;
             float lsum[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-            for (int half = 0; half < 2; half++) {
+            for (int half = 0; half < NC / 64; half++) {
                 uint32_t pk[32];
 #pragma unroll
                 for (int q = 0; q < 32; q++) {
@@ -323,7 +347,7 @@ __global__ void __launch_bounds__(AP_THREADS, 1)
                     pk[q] = bf16x2_bits(p0, p1);
                     lsum[q & 3] += __uint_as_float(pk[q] << 16) + __uint_as_float(pk[q] & 0xffff0000u);
                 }
-                tmem_st32(t_p + b * (AP_BN / 2) + 32 * half + lane_off, pk);
+                tmem_st32(t_p + b * (AP_BN / 2) + 32 * (ch + half) + lane_off, pk);
             }
             l += (lsum[0] + lsum[1]) + (lsum[2] + lsum[3]);
             tmem_st_wait();
@@ -332,23 +356,35 @@ __global__ void __launch_bounds__(AP_THREADS, 1)
         }
         if (!*abort_flag &&
             mbar_wait(&pv_done[(n_kt - 1) & 1], ((n_kt - 1) >> 1) & 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) {
-            tc_fence_after();
-            const float inv = (l > 0.f) ? 1.f / l : 0.f;
-            const int head = g * G + r % G;
-            bf16_t* orow = prm.out + ((long)(tile.row0 + tok) * prm.nh + head) * prm.hd + dsplit * ATT_DV;
+            bool ok = true;
+            if constexpr (SPLIT) {
+                // Both halves' row sums (the same stale max scaled both); the handshake slot after the
+                // last tile's is free for this one use.
+                xsum[ch * 128 + r] = l;
+                uint64_t* xb = &xpair[e * 2 + (n_kt & 1)];
+                mbar_arrive(xb);
+                ok = mbar_wait(xb, (n_kt >> 1) & 1, EG2_DEV_TIMEOUT_ATTN, abort_flag);
+                if (ok) l += *reinterpret_cast<volatile float*>(xsum + (ch ^ 1) * 128 + r);
+            }
+            if (ok) {
+                tc_fence_after();
+                const float inv = (l > 0.f) ? 1.f / l : 0.f;
+                const int head = g * G + r % G;
+                bf16_t* orow = prm.out + ((long)(tile.row0 + tok) * prm.nh + head) * prm.hd + dsplit * ATT_DV + ch * 128;
 #pragma unroll 1
-            for (int c = 0; c < ATT_DV / 32; c++) {
-                uint32_t o[32];
-                tmem_ld32(t_o + c * 32 + lane_off, o);
-                tmem_ld_wait();
-                if (row_valid) {
-                    uint4* d = reinterpret_cast<uint4*>(orow + c * 32);
+                for (int c = 0; c < OC / 32; c++) {
+                    uint32_t o[32];
+                    tmem_ld32(t_o + ch * 128 + c * 32 + lane_off, o);
+                    tmem_ld_wait();
+                    if (row_valid) {
+                        uint4* d = reinterpret_cast<uint4*>(orow + c * 32);
 #pragma unroll
-                    for (int q = 0; q < 4; q++)
-                        d[q] = make_uint4(pack_bf16x2(__uint_as_float(o[8 * q + 0]) * inv, __uint_as_float(o[8 * q + 1]) * inv),
-                                          pack_bf16x2(__uint_as_float(o[8 * q + 2]) * inv, __uint_as_float(o[8 * q + 3]) * inv),
-                                          pack_bf16x2(__uint_as_float(o[8 * q + 4]) * inv, __uint_as_float(o[8 * q + 5]) * inv),
-                                          pack_bf16x2(__uint_as_float(o[8 * q + 6]) * inv, __uint_as_float(o[8 * q + 7]) * inv));
+                        for (int q = 0; q < 4; q++)
+                            d[q] = make_uint4(pack_bf16x2(__uint_as_float(o[8 * q + 0]) * inv, __uint_as_float(o[8 * q + 1]) * inv),
+                                              pack_bf16x2(__uint_as_float(o[8 * q + 2]) * inv, __uint_as_float(o[8 * q + 3]) * inv),
+                                              pack_bf16x2(__uint_as_float(o[8 * q + 4]) * inv, __uint_as_float(o[8 * q + 5]) * inv),
+                                              pack_bf16x2(__uint_as_float(o[8 * q + 6]) * inv, __uint_as_float(o[8 * q + 7]) * inv));
+                    }
                 }
             }
         }
@@ -356,7 +392,7 @@ __global__ void __launch_bounds__(AP_THREADS, 1)
 done:
     // Every MMA the even CTA issued (into both CTAs' TMEM) has completed before either CTA frees it:
     // each issuing thread waits for its own.
-    if (even && (warp == 1 || warp == 6) && lane == 0) {
+    if (even && (warp == 1 || warp == Cfg::PV_WARP) && lane == 0) {
         uint64_t* d = &drain[warp == 1 ? 0 : 1];
         mma_commit_pair(smem_u32(d));
         mbar_wait(d, 0, EG2_DEV_TIMEOUT_ATTN, nullptr);
@@ -396,7 +432,7 @@ static int launch_pair(const CUtensorMap& mq, const CUtensorMap& mk, const CUten
     la[0].val.clusterDim.y = 1;
     la[0].val.clusterDim.z = 1;
     cfg.gridDim = dim3((unsigned)(2L * n_tiles * prm.nkv * prm.nsplit), 1, 1);
-    cfg.blockDim = dim3(AP_THREADS, 1, 1);
+    cfg.blockDim = dim3(Cfg::THREADS, 1, 1);
     cfg.dynamicSmemBytes = Cfg::SMEM;
     cfg.stream = s;
     cfg.attrs = la;
