@@ -395,6 +395,17 @@ struct eg2_ctx {
     eg2::AttnTile* v_tiles = nullptr;
     long v_tiles_cap = 0;
     int* bad_flag = nullptr;
+    // CUDA graphs of short embedding passes (<= 128 rows), one per (row bucket, pooled dims); a graph
+    // holds device addresses, so any device (re)allocation (buf_gen) invalidates it.
+    struct TextGraph {
+        int bucket = 0, n_dims = 0, total = 0;
+        uint64_t gen = 0;
+        long launches = 0;
+        cudaGraphExec_t exec = nullptr;
+    };
+    std::vector<TextGraph> graphs;
+    uint64_t buf_gen = 0;
+    cudaStream_t capture_stream = nullptr;
     // profiling
     bool profiling = false;
     std::vector<std::pair<std::string, cudaEvent_t>> marks;
@@ -416,6 +427,7 @@ static void* dalloc(eg2_ctx* c, size_t bytes) {
         fail(e == cudaErrorMemoryAllocation ? EG2_ERR_OOM : EG2_ERR_CUDA, "cudaMalloc(%zu): %s", bytes, cudaGetErrorString(e));
     }
     c->allocs.push_back(p);
+    c->buf_gen++;
     return p;
 }
 static void dfree(eg2_ctx* c, void* p) {
@@ -423,6 +435,7 @@ static void dfree(eg2_ctx* c, void* p) {
     auto it = std::find(c->allocs.begin(), c->allocs.end(), p);
     if (it != c->allocs.end()) c->allocs.erase(it);
     cudaFree(p);
+    c->buf_gen++;
 }
 
 static bool bf16_mode(const eg2_ctx* c) { return c->precision == EG2_BF16; }
@@ -904,8 +917,10 @@ static void enqueue_text(eg2_ctx* c, long rows, const std::vector<TileSet>& tset
     mark(c, "gemm embed_proj");
 }
 
-// Row metadata and attention tile lists for sequences packed back to back.
-static std::vector<TileSet> prepare_pass(eg2_ctx* c, const int32_t* lens, int n_seq, long rows) {
+// Row metadata and attention tile lists for sequences packed back to back. tile_slots > 0 pads each
+// tile list to that many entries with empty tiles (length 0: the attention CTAs exit at once), so a
+// captured graph's grid sizes stay valid for any sequence split of the same row count.
+static std::vector<TileSet> prepare_pass(eg2_ctx* c, const int32_t* lens, int n_seq, long rows, int tile_slots = 0) {
     const TextCfg& tc = c->tc;
     std::vector<int> pos(rows), st(rows), ln(rows);
     long r = 0;
@@ -936,6 +951,10 @@ static std::vector<TileSet> prepare_pass(eg2_ctx* c, const int32_t* lens, int n_
             for (int s = 0; s < n_seq; s++) {
                 for (int q0 = 0; q0 < lens[s]; q0 += tq) tiles.push_back(AttnTile{(int)row0, lens[s], q0});
                 row0 += lens[s];
+            }
+            if (tile_slots > 0) {
+                if ((long)tiles.size() - ts.offset > tile_slots) fail(EG2_ERR_INVALID, "tile list exceeds its slots");
+                while ((long)tiles.size() - ts.offset < tile_slots) tiles.push_back(AttnTile{0, 0, 0});
             }
             ts.count = (int)(tiles.size() - ts.offset);
             sets.push_back(ts);
@@ -1046,6 +1065,9 @@ using namespace eg2;
 
 eg2_ctx::~eg2_ctx() {
     if (stream) cudaStreamSynchronize(stream);
+    for (auto& g : graphs)
+        if (g.exec) cudaGraphExecDestroy(g.exec);
+    if (capture_stream) cudaStreamDestroy(capture_stream);
     for (void* p : allocs) cudaFree(p);
     for (auto& m : marks) cudaEventDestroy(m.second);
     for (auto e : event_pool) cudaEventDestroy(e);
@@ -1199,6 +1221,112 @@ int eg2_forward_packed_device(eg2_ctx* c, const float* embeds, const int32_t* le
     return forward_impl(c, embeds, lens, n_seq, out, stream, true);
 }
 
+// Short passes (<= 128 rows, bf16): rows are padded to a bucket of 16 / 32 / 64 / 128 with one extra
+// sequence of token 0, the attention tile lists and the pooled-sequence list to bucket + 1 entries
+// (empty ones have length 0), so every launch of the pass has the same parameters for any split of
+// the bucket into sequences. The pass (gather, 24 layers, pool) is captured once per (bucket, dims)
+// into a CUDA graph and replayed with new metadata: ~175 launches become one (the reference captures
+// graphs per row bucket for the same reason, src/gpu/text.rs:475-516).
+static void embed_graph(eg2_ctx* c, const uint32_t* ids, const int32_t* lens, int n_seq, long rows, const int32_t* dims,
+                        int n_dims, int total, float* out, bool device_ptrs) {
+    const int B = rows <= 16 ? 16 : rows <= 32 ? 32 : rows <= 64 ? 64 : 128;
+    const int S = B + 1;  // pooled-sequence slots
+    std::vector<int32_t> lp(lens, lens + n_seq);
+    if (B > rows) lp.push_back((int32_t)(B - rows));
+    auto sets = prepare_pass(c, lp.data(), (int)lp.size(), B, S);
+    Work& w = c->w;
+    if ((long)S * total > w.pooled_cap || !w.dims) {
+        CK(cudaStreamSynchronize(c->stream));
+        dfree(c, w.pooled);
+        w.pooled_cap = std::max((long)S * total, 4096L);
+        w.pooled = (float*)dalloc(c, w.pooled_cap * 4);
+        if (!w.dims) w.dims = (int*)dalloc(c, 64);
+    }
+    if (S > w.seq_meta_cap) {
+        CK(cudaStreamSynchronize(c->stream));
+        dfree(c, w.seq_meta);
+        w.seq_meta_cap = std::max(S, 1024);
+        w.seq_meta = (int*)dalloc(c, 2L * w.seq_meta_cap * 4);
+    }
+    const long need = pool_scratch_doubles(S, B, c->tc.emb);
+    if (need > w.pool_scratch_cap) {
+        CK(cudaStreamSynchronize(c->stream));
+        dfree(c, w.pool_scratch);
+        w.pool_scratch_cap = std::max(need, 1L << 20);
+        w.pool_scratch = (double*)dalloc(c, w.pool_scratch_cap * 8);
+    }
+    // Metadata (the graph reads it from these fixed buffers): starts / lengths of S slots, dims, ids.
+    std::vector<int> meta(2 * (size_t)S, 0);
+    long r = 0;
+    for (size_t s2 = 0; s2 < lp.size(); s2++) {
+        meta[s2] = (int)r;
+        meta[S + s2] = lp[s2];
+        r += lp[s2];
+    }
+    int* seq_meta = w.seq_meta;
+    CK(cudaMemcpyAsync(seq_meta, meta.data(), meta.size() * 4, cudaMemcpyHostToDevice, c->stream));
+    CK(cudaMemcpyAsync(w.dims, dims, n_dims * 4, cudaMemcpyHostToDevice, c->stream));
+    CK(cudaMemsetAsync(c->bad_flag, 0, 4, c->stream));
+    CK(cudaMemsetAsync(w.ids, 0, (size_t)B * 4, c->stream));
+    CK(cudaMemcpyAsync(w.ids, ids, rows * 4, device_ptrs ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, c->stream));
+    auto body = [&]() {
+        KL(embed_gather(c->embed_table, c->tc.vocab, c->tc.hidden, w.ids, B, sqrtf((float)c->tc.hidden), w.hidden,
+                        c->bad_flag, c->stream),
+           "embed_gather");
+        run_text(c, B, sets);
+        KL(pool_rows(w.out, seq_meta, seq_meta + S, S, B, c->tc.emb, w.dims, n_dims, total, w.pooled, w.pool_scratch,
+                     c->stream),
+           "pool");
+        g_launches.fetch_add(1, std::memory_order_relaxed);  // pool_rows is two launches
+    };
+    eg2_ctx::TextGraph* g = nullptr;
+    for (auto& x : c->graphs)
+        if (x.bucket == B && x.n_dims == n_dims && x.total == total) g = &x;
+    if (g && g->gen == c->buf_gen) {
+        CK(cudaGraphLaunch(g->exec, c->stream));
+        g_launches.fetch_add(g->launches, std::memory_order_relaxed);
+    } else {
+        // Run the pass (this call's result, and it sets every kernel's attributes), then capture it on
+        // a stream of the context's own; the capture itself runs nothing.
+        body();
+        if (!c->capture_stream) CK(cudaStreamCreateWithFlags(&c->capture_stream, cudaStreamNonBlocking));
+        cudaStream_t saved = c->stream;
+        c->stream = c->capture_stream;
+        const long l0 = g_launches.load(std::memory_order_relaxed);
+        cudaGraph_t graph = nullptr;
+        CK(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
+        try {
+            body();
+        } catch (...) {
+            cudaStreamEndCapture(c->stream, &graph);
+            if (graph) cudaGraphDestroy(graph);
+            c->stream = saved;
+            throw;
+        }
+        CK(cudaStreamEndCapture(c->stream, &graph));
+        c->stream = saved;
+        const long n_launch = g_launches.load(std::memory_order_relaxed) - l0;
+        g_launches.fetch_sub(n_launch, std::memory_order_relaxed);  // captured, not run
+        cudaGraphExec_t exec = nullptr;
+        const cudaError_t e = cudaGraphInstantiate(&exec, graph, 0);
+        cudaGraphDestroy(graph);
+        CK(e);
+        if (!g) {
+            c->graphs.push_back(eg2_ctx::TextGraph());
+            g = &c->graphs.back();
+        } else if (g->exec) {
+            cudaGraphExecDestroy(g->exec);
+        }
+        g->bucket = B, g->n_dims = n_dims, g->total = total, g->gen = c->buf_gen, g->launches = n_launch, g->exec = exec;
+    }
+    CK(cudaMemcpyAsync(out, w.pooled, (size_t)n_seq * total * 4, device_ptrs ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost,
+                       c->stream));
+    int bad = 0;
+    CK(cudaMemcpyAsync(&bad, c->bad_flag, 4, cudaMemcpyDeviceToHost, c->stream));
+    check_device_status(c);
+    if (bad) fail(EG2_ERR_INVALID, "token id out of range");
+}
+
 static int embed_impl(eg2_ctx* c, const uint32_t* ids, const int32_t* lens, int n_seq, const int32_t* dims, int n_dims,
                       float* out, void* stream, bool device_ptrs) {
     return guarded(c, [&] {
@@ -1220,6 +1348,10 @@ static int embed_impl(eg2_ctx* c, const uint32_t* ids, const int32_t* lens, int 
         if (!device_ptrs)
             for (long i = 0; i < rows; i++)
                 if ((int64_t)ids[i] >= c->tc.vocab) fail(EG2_ERR_INVALID, "token id %u out of range", ids[i]);
+        if (bf16_mode(c) && c->use_tc_attention && !c->profiling && rows <= 128 && !getenv("EG2_NO_GRAPHS")) {
+            embed_graph(c, ids, lens, n_seq, rows, dims, n_dims, total, out, device_ptrs);
+            return;
+        }
         auto sets = prepare_pass(c, lens, n_seq, rows);
         Work& w = c->w;
         if ((long)n_seq * total > w.pooled_cap || !w.dims) {

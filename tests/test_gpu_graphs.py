@@ -1,0 +1,61 @@
+"""Short passes (<= 128 rows) replay a captured CUDA graph per row bucket (the reference's graph
+buckets, src/gpu/text.rs:475-516): results must equal the launch-by-launch path for any sequence split,
+on first capture and on replays, and across buckets."""
+import ctypes as C
+import os
+import time
+
+import numpy as np
+import pytest
+
+from conftest import pkg
+
+B = pkg("backend")
+L = pkg("lib")
+
+pytestmark = pytest.mark.gpu
+DIMS = (768, 512, 256, 128)
+
+
+def embed_host(dev, seqs):
+    lib = L.load()
+    ids = np.concatenate(seqs).astype(np.uint32)
+    lens = [len(s) for s in seqs]
+    out = np.zeros((len(seqs), sum(DIMS)), np.float32)
+    dev.check(lib.eg2_embed_packed(dev.handle, C.c_void_p(ids.ctypes.data), L.i32_array(lens), len(lens),
+                                   L.i32_array(DIMS), len(DIMS), C.c_void_p(out.ctypes.data)))
+    return out
+
+
+@pytest.mark.parametrize("lens", [[17], [3, 1, 9], [40, 24], [64, 60, 3], [128], [100, 1, 1, 26], [1] * 70])
+def test_graph_replay_matches_direct_path(lens, request, monkeypatch):
+    dev = request.getfixturevalue("dev_bf16")
+    rng = np.random.default_rng(sum(lens) * 7 + len(lens))
+    seqs = [rng.integers(0, 262144, size=n).astype(np.uint32) for n in lens]
+    first = embed_host(dev, seqs)    # captures (or replays) the bucket's graph
+    again = embed_host(dev, seqs)    # replays it
+    monkeypatch.setenv("EG2_NO_GRAPHS", "1")
+    direct = embed_host(dev, seqs)
+    assert np.abs(first - direct).max() <= 1e-6
+    assert np.abs(again - direct).max() <= 1e-6
+
+
+def test_graph_latency(request, monkeypatch):
+    dev = request.getfixturevalue("dev_bf16")
+    rng = np.random.default_rng(5)
+    seqs = [rng.integers(0, 262144, size=17).astype(np.uint32)]
+    for _ in range(3):
+        embed_host(dev, seqs)
+    t0 = time.perf_counter()
+    for _ in range(20):
+        embed_host(dev, seqs)
+    graph_ms = (time.perf_counter() - t0) / 20 * 1e3
+    monkeypatch.setenv("EG2_NO_GRAPHS", "1")
+    for _ in range(3):
+        embed_host(dev, seqs)
+    t0 = time.perf_counter()
+    for _ in range(20):
+        embed_host(dev, seqs)
+    direct_ms = (time.perf_counter() - t0) / 20 * 1e3
+    print(f"17-token query, host ids in / embeddings out: graph {graph_ms:.3f} ms, launch by launch {direct_ms:.3f} ms")
+    assert graph_ms < direct_ms
