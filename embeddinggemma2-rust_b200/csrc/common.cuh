@@ -292,6 +292,13 @@ EG2_DEV void mma_bf16_pair_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, 
 EG2_DEV void mma_commit_pair(uint32_t bar) {
     asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
 }
+EG2_DEV void tma_load_2d_pair(void* dst, const CUtensorMap* m, uint32_t bar, int x, int y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+            smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(m)), "r"(bar), "r"(x), "r"(y)
+        : "memory");
+}
 // Same, arriving on the mbarrier at this shared-memory offset in both CTAs of the pair.
 EG2_DEV void mma_commit_pair_both(uint64_t* bar) {
     asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(

@@ -40,12 +40,16 @@ struct InTraits<float> {
 constexpr int GEMM_BM = 128;
 constexpr int GEMM_THREADS = 320;
 
-template <int BN>
+// PAIR: 2-CTA clusters computing 256 x BN tiles with tcgen05.mma.cta_group::2 (M = 256): each CTA
+// loads its own 128 rows of A and half (BN / 2 rows) of B, so per SM a K block moves 32 KB into and
+// 32 KB out of shared memory instead of 48 + 48 KB -- the single-CTA tile needs ~190 B/cycle of shared
+// memory at the full tensor rate, more than shared memory delivers.
+template <int BN, bool PAIR = false>
 struct GemmCfg {
     static constexpr int A_BYTES = GEMM_BM * 128;
-    static constexpr int B_BYTES = BN * 128;
+    static constexpr int B_BYTES = (PAIR ? BN / 2 : BN) * 128;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-    static constexpr int STAGES = (BN == 256) ? 4 : 6;
+    static constexpr int STAGES = PAIR ? 6 : (BN == 256) ? 4 : 6;
     static constexpr int OFF_STAGE = STAGES * STAGE_BYTES + 256;  // after the barriers
     static constexpr int STAGE_WARP = 32 * (64 + 16);             // 32 rows x 64 B + 16 B pad
     static constexpr int OFF_W = OFF_STAGE + 8 * STAGE_WARP;      // EPI_QKV: norm weights, inv freqs
@@ -110,11 +114,84 @@ EG2_DEV void warp_store32(TOut* out, long ldo, int row0, int M, long col, const 
 // that the RoPE angle pos * inv_freq (computed in f32 like the reference's tables, src/ops.rs:303-306)
 // goes through sincos_reduced instead of a table. All 32 lanes run every tcgen05.ld; rows past M
 // only skip the stores.
+// EPI_QKV with one 256-wide head per tile and RoPE over the whole head (pairs i, i + 128): the same
+// arithmetic as the general form below with the head geometry known at compile time, the position
+// read once per tile (before pass 1, so its latency hides behind the TMEM reads) and two TMEM loads
+// in flight per wait.
+template <typename TOut>
+EG2_DEV void epilogue_qkv256(const QkvEpilogue& Q, uint32_t tbase, int row0, int M, int n0, uint8_t* stage,
+                             const float* wsm) {
+    const int row = row0 + (int)(threadIdx.x & 31);
+    const int qw = Q.nh * 256, kw = Q.nkv * 256;
+    TOut* base;
+    int nheads, head;
+    const float* w;
+    bool rot;
+    if (n0 < qw) {
+        base = (TOut*)Q.q, nheads = Q.nh, head = n0 >> 8, w = wsm, rot = true;
+    } else if (n0 < qw + kw) {
+        base = (TOut*)Q.k, nheads = Q.nkv, head = (n0 - qw) >> 8, w = wsm + 256, rot = true;
+    } else {
+        base = (TOut*)Q.v, nheads = Q.nkv, head = (n0 - qw - kw) >> 8, w = nullptr, rot = false;
+    }
+    const bool live = row < M;
+    const float pf = (rot && live) ? (float)(Q.pos ? Q.pos[(long)row * Q.pos_stride] : row) : 0.f;
+    float ss = 0.f;
+#pragma unroll 1
+    for (int c = 0; c < 8; c += 2) {
+        uint32_t r0[32], r1[32];
+        tmem_ld32(tbase + c * 32, r0);
+        tmem_ld32(tbase + c * 32 + 32, r1);
+        tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 32; j++) {
+            ss = fmaf(__uint_as_float(r0[j]), __uint_as_float(r0[j]), ss);
+            ss = fmaf(__uint_as_float(r1[j]), __uint_as_float(r1[j]), ss);
+        }
+    }
+    const float inv = 1.0f / sqrtf(ss / 256.f + Q.eps);
+    const float* invs = wsm + 512;
+    const long ldo = (long)nheads * 256, col1 = (long)head * 256;
+#pragma unroll 1
+    for (int c = 0; c < 4; c++) {
+        float x1[32], x2[32];
+        {
+            uint32_t a[32], b[32];
+            tmem_ld32(tbase + c * 32, a);
+            tmem_ld32(tbase + 128 + c * 32, b);
+            tmem_ld_wait();
+#pragma unroll
+            for (int t = 0; t < 32; t++) {
+                x1[t] = __uint_as_float(a[t]) * inv;
+                x2[t] = __uint_as_float(b[t]) * inv;
+            }
+        }
+        if (rot) {
+#pragma unroll
+            for (int t = 0; t < 32; t++) {
+                const float a1 = x1[t] * w[c * 32 + t], a2 = x2[t] * w[128 + c * 32 + t];
+                float sj, cj;
+                sincos_reduced(pf * invs[c * 32 + t], sj, cj);
+                x1[t] = a1 * cj - a2 * sj;
+                x2[t] = a2 * cj + a1 * sj;
+            }
+        }
+        warp_store32<TOut>(base, ldo, row0, M, col1 + c * 32, x1, stage);
+        warp_store32<TOut>(base, ldo, row0, M, col1 + 128 + c * 32, x2, stage);
+    }
+}
+
 template <typename TOut, int BN>
 EG2_DEV void epilogue_qkv(const GemmEpilogue& epi, uint32_t tbase, int row0, int M, int n0, uint8_t* stage,
                           const float* wsm) {
     const int row = row0 + (int)(threadIdx.x & 31);
     const QkvEpilogue& Q = epi.qkv;
+    if constexpr (BN == 256) {
+        if (Q.hd == 256 && Q.part == 256) {
+            epilogue_qkv256<TOut>(Q, tbase, row0, M, n0, stage, wsm);
+            return;
+        }
+    }
     const int hd = Q.hd, qw = Q.nh * hd, kw = Q.nkv * hd;
     TOut* base;
     int nheads, head0;
@@ -252,11 +329,11 @@ EG2_DEV void warp_load32_finish(const uint4 (&b)[8], float (&v)[32], uint8_t* st
     }
 }
 
-template <typename TIn, int BN, int EPI, typename TOut>
+template <typename TIn, int BN, int EPI, typename TOut, bool PAIR = false>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int N, int K,
                    GemmEpilogue epi) {
-    using Cfg = GemmCfg<BN>;
+    using Cfg = GemmCfg<BN, PAIR>;
     constexpr int BK = InTraits<TIn>::BK;
     constexpr int STAGES = Cfg::STAGES;
     extern __shared__ uint8_t smem_raw[];
@@ -265,7 +342,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     uint64_t* empty = full + STAGES;
     uint64_t* tfull = empty + STAGES;
     uint64_t* tempty = tfull + 2;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+    uint64_t* drain = tempty + 2;  // PAIR: the MMA issuer's final wait for its own MMAs
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -273,14 +351,21 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     const int kblocks = K / BK;
     // This CTA's tiles: linear ids t_first + i * t_step < t_count. Cluster modes: the cluster's
     // (row block, 512-column group) pairs, the 256-column half fixed by the CTA's rank.
+    // PAIR: the cluster's 256-row x BN tiles, this CTA's 128 rows fixed by its rank.
     constexpr bool AN = EPI == EPI_ADD_NORM;
     constexpr bool CL = AN || EPI == EPI_GROUP_NORM || EPI == EPI_QKV_PAIR;
+    static_assert(!(CL && PAIR), "cluster epilogues and CTA-pair MMAs are separate kernels");
+    static_assert(!PAIR || sizeof(TIn) == 2, "CTA-pair MMAs are bf16 only");
     const int groups = N / 512;
-    const uint32_t crank = CL ? cluster_ctarank() : 0u;
-    const int t_first = CL ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
-    const int t_step = CL ? (int)(gridDim.x >> 1) : (int)gridDim.x;
-    const int t_count = CL ? tiles_m * groups : tiles_m * tiles_n;
-    auto tile_m0 = [&](int t) { return (CL ? t / groups : t / tiles_n) * GEMM_BM; };
+    const uint32_t crank = (CL || PAIR) ? cluster_ctarank() : 0u;
+    const bool lead = crank == 0;
+    const int tiles_mp = (tiles_m + 1) / 2;
+    const int t_first = (CL || PAIR) ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+    const int t_step = (CL || PAIR) ? (int)(gridDim.x >> 1) : (int)gridDim.x;
+    const int t_count = CL ? tiles_m * groups : PAIR ? tiles_mp * tiles_n : tiles_m * tiles_n;
+    auto tile_m0 = [&](int t) {
+        return PAIR ? (t / tiles_n) * 2 * GEMM_BM + (int)crank * GEMM_BM : (CL ? t / groups : t / tiles_n) * GEMM_BM;
+    };
     auto tile_n0 = [&](int t) { return CL ? (t % groups) * 512 + (int)crank * BN : (t % tiles_n) * BN; };
 
     if (threadIdx.x == 0) {
@@ -290,8 +375,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         }
         for (int a = 0; a < 2; a++) {
             mbar_init(&tfull[a], 1);
-            mbar_init(&tempty[a], 128);
+            mbar_init(&tempty[a], PAIR ? 256 : 128);  // PAIR: both CTAs' epilogue sets free the accumulator
         }
+        mbar_init(drain, 1);
         if constexpr (CL) {
             uint64_t* xb = reinterpret_cast<uint64_t*>(smem + Cfg::OFF_W + Cfg::XB_OFF);
             for (int x = 0; x < 4; x++) mbar_init(&xb[x], 1);  // one local arrival (expect_tx) per exchange
@@ -325,13 +411,18 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         for (int i = threadIdx.x; i < 2 * BN; i += GEMM_THREADS)
             wsm[i] = i < BN ? epi.an.w1[n0 + i] : (epi.an.w2 ? epi.an.w2[n0 + i - BN] : 0.f);
     }
-    if (warp == 1) tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
+    if (warp == 1) {
+        if constexpr (PAIR)
+            tmem_alloc_pair(tmem_slot, Cfg::TMEM_COLS);
+        else
+            tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
+    }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
-    // The peer CTA's exchange barriers must be initialised before anyone arrives on them.
-    if constexpr (CL) cluster_sync();
+    // The peer CTA's barriers must be initialised before anyone arrives on them.
+    if constexpr (CL || PAIR) cluster_sync();
 
     if (warp == 0) {
         if (lane == 0) {
@@ -348,9 +439,17 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
                 for (int kb = 0; kb < kblocks; kb++) {
                     if (!mbar_wait(&empty[stage], phase ^ 1, EG2_DEV_TIMEOUT_GEMM, abort_flag)) goto done;
                     uint8_t* sa = smem + stage * Cfg::STAGE_BYTES;
-                    mbar_arrive_expect_tx(&full[stage], Cfg::STAGE_BYTES);
-                    tma_load_2d(sa, &tmA, &full[stage], kb * BK, m0);
-                    tma_load_2d(sa + Cfg::A_BYTES, &tmB, &full[stage], kb * BK, n0);
+                    if constexpr (PAIR) {
+                        // Both CTAs' bytes complete on the even CTA's barrier.
+                        if (lead) mbar_arrive_expect_tx(&full[stage], 2 * Cfg::STAGE_BYTES);
+                        const uint32_t bar = mapa_shared(smem_u32(&full[stage]), 0);
+                        tma_load_2d_pair(sa, &tmA, bar, kb * BK, m0);
+                        tma_load_2d_pair(sa + Cfg::A_BYTES, &tmB, bar, kb * BK, n0 + (int)crank * (BN / 2));
+                    } else {
+                        mbar_arrive_expect_tx(&full[stage], Cfg::STAGE_BYTES);
+                        tma_load_2d(sa, &tmA, &full[stage], kb * BK, m0);
+                        tma_load_2d(sa + Cfg::A_BYTES, &tmB, &full[stage], kb * BK, n0);
+                    }
                     if (++stage == STAGES) {
                         stage = 0;
                         phase ^= 1;
@@ -359,7 +458,36 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             }
         }
     } else if (warp == 1) {
-        if (lane == 0) {
+        if (lane == 0 && PAIR && lead) {
+            // CTA-pair MMAs: M = 256 (A rows 0..127 here, 128..255 in the peer), B halves in both CTAs.
+            constexpr uint32_t idesc = umma_idesc(2 * GEMM_BM, BN, InTraits<TIn>::FMT);
+            const uint64_t da0 = umma_desc_sw128(smem_u32(smem), 16, 1024);
+            int stage = 0;
+            uint32_t phase = 0;
+            int local = 0;
+            for (int tile = t_first; tile < t_count; tile += t_step, local++) {
+                const int acc = local & 1;
+                const uint32_t acc_phase = (local >> 1) & 1;
+                if (!mbar_wait(&tempty[acc], acc_phase ^ 1, EG2_DEV_TIMEOUT_GEMM, abort_flag)) goto done;
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + acc * BN;
+                for (int kb = 0; kb < kblocks; kb++) {
+                    if (!mbar_wait(&full[stage], phase, EG2_DEV_TIMEOUT_GEMM, abort_flag)) goto done;
+                    tc_fence_after();
+                    const uint64_t ad = da0 + (uint64_t)(stage * (Cfg::STAGE_BYTES >> 4));
+                    const uint64_t bd = ad + (uint64_t)(Cfg::A_BYTES >> 4);
+                    mma_bf16_pair(d_tmem, ad, bd, idesc, kb != 0);
+#pragma unroll
+                    for (int kk = 1; kk < 4; kk++) mma_bf16_pair(d_tmem, ad + 2 * kk, bd + 2 * kk, idesc, 1);
+                    mma_commit_pair_both(&empty[stage]);
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1;
+                    }
+                }
+                mma_commit_pair_both(&tfull[acc]);
+            }
+        } else if (lane == 0 && !PAIR) {
             constexpr uint32_t idesc = umma_idesc(GEMM_BM, BN, InTraits<TIn>::FMT);
             // Descriptors are built once; a K step of 32 bytes adds 2 to the start-address field.
             const uint64_t da0 = umma_desc_sw128(smem_u32(smem), 16, 1024);
@@ -633,18 +761,36 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
                 }
             }
             tc_fence_before();
-            mbar_arrive(&tempty[set]);
+            if (!PAIR || lead)
+                mbar_arrive(&tempty[set]);
+            else
+                mbar_arrive_remote(mapa_shared(smem_u32(&tempty[set]), 0));
         }
     }
 done:
+    if constexpr (PAIR) {
+        // Every pair MMA (written into both CTAs' TMEM) has completed before either CTA frees it.
+        if (lead && warp == 1 && lane == 0) {
+            mma_commit_pair(smem_u32(drain));
+            mbar_wait(drain, 0, EG2_DEV_TIMEOUT_GEMM, nullptr);
+        }
+    }
     tc_fence_before();
     __syncthreads();
-    if (warp == 1) {
-        tc_fence_after();
-        tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+    if constexpr (PAIR) {
+        cluster_sync();
+        if (warp == 1) {
+            tc_fence_after();
+            tmem_dealloc_pair(tmem_base, Cfg::TMEM_COLS);
+        }
+    } else {
+        if (warp == 1) {
+            tc_fence_after();
+            tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+        }
+        // No CTA leaves while its peer may still write into its shared memory.
+        if constexpr (CL) cluster_sync();
     }
-    // No CTA leaves while its peer may still write into its shared memory.
-    if constexpr (CL) cluster_sync();
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -668,13 +814,14 @@ static int launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N,
     return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
 
-// Cluster modes: clusters of two CTAs, as many as can be resident at once (the loop over tiles is
-// persistent, so every launched cluster must run concurrently with the others).
-template <int EPI, typename TOut>
+// Clusters of two CTAs (the cluster epilogues, and CTA-pair MMAs), as many as can be resident at
+// once (the loop over tiles is persistent, so every launched cluster must run concurrently with
+// the others).
+template <int EPI, typename TOut, bool PAIR = false>
 static int launch_cluster(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int K, const GemmEpilogue& epi,
                           cudaStream_t s) {
-    using Cfg = GemmCfg<256>;
-    auto kern = gemm_tc_kernel<bf16_t, 256, EPI, TOut>;
+    using Cfg = GemmCfg<256, PAIR>;
+    auto kern = gemm_tc_kernel<bf16_t, 256, EPI, TOut, PAIR>;
     static int max_clusters[64] = {0};
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -3;
@@ -697,11 +844,22 @@ static int launch_cluster(const CUtensorMap& ta, const CUtensorMap& tb, int M, i
         if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) return -3;
         max_clusters[dev] = n;
     }
-    if (N % 512) return -1;
-    const long tiles = (long)((M + GEMM_BM - 1) / GEMM_BM) * (N / 512);
+    const int tiles_m = (M + GEMM_BM - 1) / GEMM_BM;
+    if (N % (PAIR ? 256 : 512)) return -1;
+    const long tiles = PAIR ? (long)((tiles_m + 1) / 2) * (N / 256) : (long)tiles_m * (N / 512);
     const int clusters = tiles < max_clusters[dev] ? (int)tiles : max_clusters[dev];
     cfg.gridDim = dim3(2 * clusters, 1, 1);
     return cudaLaunchKernelEx(&cfg, kern, ta, tb, M, N, K, epi) == cudaSuccess ? 0 : -3;
+}
+
+// CTA-pair MMAs for the plain epilogues; EG2_GEMM_NO_PAIR=1 selects the single-CTA kernels instead
+// (same results up to summation order: both accumulate K in the same 64-element blocks).
+static bool gemm_pair_enabled() {
+    static const bool on = [] {
+        const char* e = getenv("EG2_GEMM_NO_PAIR");
+        return !(e && e[0] == '1');
+    }();
+    return on;
 }
 
 bool qkv_pair_fusable(const QkvEpilogue& q) {
@@ -726,8 +884,26 @@ int gemm_tc(GemmKind kind, const void* A, long lda, const void* W, long ldw, int
     if (epi.mode == EPI_QKV && !qkv_fusable(epi.qkv)) return -1;
     CUtensorMap ta, tb;
     const CUtensorMapDataType dt = tf32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
-    if (make_tmap_2d(&ta, dt, A, K, M, lda * esize, BK, GEMM_BM) || make_tmap_2d(&tb, dt, W, K, N, ldw * esize, BK, BN))
+    if (make_tmap_2d(&ta, dt, A, K, M, lda * esize, BK, GEMM_BM)) return -1;
+    // bf16 store / GELU / PLE-gate / QKV epilogues run on CTA pairs (each CTA loads half of the
+    // weight tile, BN / 2 rows); the cluster epilogues and TF32 on single-CTA MMAs.
+    const bool pair = !tf32 && (epi.mode == EPI_STORE || epi.mode == EPI_GELU_GU || epi.mode == EPI_PLE_GATE ||
+                                epi.mode == EPI_QKV) && gemm_pair_enabled();
+    if (make_tmap_2d(&tb, dt, W, K, N, ldw * esize, BK, pair ? BN / 2 : BN)) return -1;
+    if (pair) {
+        switch (epi.mode) {
+            case EPI_STORE:
+                return epi.out_f32 ? launch_cluster<EPI_STORE, float, true>(ta, tb, M, N, K, epi, s)
+                                   : launch_cluster<EPI_STORE, bf16_t, true>(ta, tb, M, N, K, epi, s);
+            case EPI_GELU_GU:
+                return launch_cluster<EPI_GELU_GU, bf16_t, true>(ta, tb, M, N, K, epi, s);
+            case EPI_PLE_GATE:
+                return launch_cluster<EPI_PLE_GATE, bf16_t, true>(ta, tb, M, N, K, epi, s);
+            case EPI_QKV:
+                return launch_cluster<EPI_QKV, bf16_t, true>(ta, tb, M, N, K, epi, s);
+        }
         return -1;
+    }
     if (!tf32) {
         switch (epi.mode) {
             case EPI_STORE:

@@ -74,6 +74,18 @@ def test_bf16_gemm_large_m(n, k):
     assert np.abs(got - want).max() < 2e-4 * max(1.0, float(np.abs(want).max()))
 
 
+@pytest.mark.parametrize("m", [1, 128, 129, 255, 256, 257, 383, 1000])
+def test_bf16_gemm_pair_tile_edges(m):
+    """bf16 GEMMs run on CTA pairs (256-row tiles, 128 rows per CTA): row counts that leave the
+    odd CTA of the last pair empty, partly filled or full."""
+    x, w = data(m, 2048, 512, seed=3)
+    want = O.sgemm_nt(W.bf16_round(x), W.bf16_round(w))
+    got = run_gemm(L.EG2_BF16, x, w)
+    assert np.abs(got - want).max() < 2e-4 * max(1.0, float(np.abs(want).max()))
+    got_b = run_gemm(L.EG2_BF16, x, w, out_f32=False)
+    np.testing.assert_array_equal(W.bf16_round(got), got_b)
+
+
 def test_bf16_output_is_rounded_f32_accumulator():
     x, w = data(300, 1024, 512)
     f = run_gemm(L.EG2_BF16, x, w, out_f32=True)
