@@ -158,6 +158,15 @@ EG2_DEV bool mbar_wait_limit(uint64_t* bar, uint32_t parity, int code, volatile 
 EG2_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, int code, volatile int* abort) {
     return mbar_wait_limit(bar, parity, code, abort, EG2_WAIT_LIMIT_NS);
 }
+// Exit path: waits (at most limit_ns, whatever the error state) for a copy this CTA issued to land,
+// so no TMA write reaches shared memory after the CTA has ended.
+EG2_DEV void mbar_drain(uint64_t* bar, uint32_t parity, uint64_t limit_ns) {
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t it = 0;; ++it) {
+        if (mbar_try_wait(bar, parity)) return;
+        if ((it & 255u) == 255u && globaltimer_ns() - t0 > limit_ns) return;
+    }
+}
 
 // ---------------------------------------------------------------------------------------------
 // Thread-block clusters: distributed shared memory between the CTAs of a cluster
@@ -199,6 +208,24 @@ EG2_DEV void tma_prefetch_desc(const CUtensorMap* m) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");
 }
 // Bulk prefetch of `bytes` (multiple of 16, 16-byte aligned address) of global memory into L2.
+// TMA store of a tile from this CTA's shared memory (box and swizzle from the tensor map); rows and
+// columns outside the tensor are not written. Completion is tracked by bulk async-groups of the
+// issuing thread: commit after issuing, then wait_group[.read] on the same thread.
+EG2_DEV void tma_store_2d(const CUtensorMap* m, const void* src, int x, int y) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                     reinterpret_cast<uint64_t>(m)),
+                 "r"(smem_u32(src)), "r"(x), "r"(y)
+                 : "memory");
+}
+EG2_DEV void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// All but the newest N groups have finished reading their shared-memory sources.
+template <int N>
+EG2_DEV void bulk_wait_read() {
+    asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+// Every group of this thread has completed (writes performed).
+EG2_DEV void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
 EG2_DEV void prefetch_l2_bulk(const void* p, uint32_t bytes) {
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(p)), "r"(bytes) : "memory");
 }
@@ -341,6 +368,21 @@ EG2_DEV void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
         "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),
         "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
         "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31]));
+}
+// 32 lanes x 16 consecutive 32-bit columns.
+EG2_DEV void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+}
+EG2_DEV void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+            taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+        "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]));
 }
 EG2_DEV void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 EG2_DEV void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }

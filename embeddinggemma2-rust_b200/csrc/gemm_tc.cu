@@ -44,15 +44,21 @@ constexpr int GEMM_THREADS = 320;
 // loads its own 128 rows of A and half (BN / 2 rows) of B, so per SM a K block moves 32 KB into and
 // 32 KB out of shared memory instead of 48 + 48 KB -- the single-CTA tile needs ~190 B/cycle of shared
 // memory at the full tensor rate, more than shared memory delivers.
-template <int BN, bool PAIR = false>
+// TIO: the epilogue's global I/O goes through TMA, each epilogue warp owning four 2 KB
+// shared-memory slots (64-byte swizzle) -- EPI_ADD_NORM for its residual reads and h / t writes,
+// EPI_QKV and EPI_PLE_GATE for their outputs (these keep the 2.5 KB staging tile of the register
+// path after the slots, for the PLE inputs). The main loop gives up stages for them.
+template <int BN, bool PAIR = false, bool TIO = false>
 struct GemmCfg {
     static constexpr int A_BYTES = GEMM_BM * 128;
     static constexpr int B_BYTES = (PAIR ? BN / 2 : BN) * 128;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-    static constexpr int STAGES = PAIR ? 6 : (BN == 256) ? 4 : 6;
-    static constexpr int OFF_STAGE = STAGES * STAGE_BYTES + 256;  // after the barriers
-    static constexpr int STAGE_WARP = 32 * (64 + 16);             // 32 rows x 64 B + 16 B pad
-    static constexpr int OFF_W = OFF_STAGE + 8 * STAGE_WARP;      // EPI_QKV: norm weights, inv freqs
+    static constexpr int STAGES = TIO ? (PAIR ? 4 : 3) : PAIR ? 6 : (BN == 256) ? 4 : 6;
+    // Barriers follow the stages; TIO slots must start on a 1 KB boundary.
+    static constexpr int OFF_STAGE = STAGES * STAGE_BYTES + (TIO ? 1024 : 256);
+    static constexpr int STAGE_WARP = TIO ? (PAIR ? 11264 : 8192) : 32 * (64 + 16);  // 32 rows x 64 B + 16 B pad
+    static constexpr int OFF_LOAD = TIO ? 8192 : 0;  // register-path staging within a warp's area
+    static constexpr int OFF_W = OFF_STAGE + 8 * STAGE_WARP;        // EPI_QKV: norm weights, inv freqs
     // EPI_QKV: norm weights + inverse frequencies (<= 3 KB). Cluster modes: this CTA's halves of the
     // norm weights (EPI_QKV_PAIR: wq, wk and 128 inverse frequencies, 2.5 KB), exchange slots
     // [set][slot][128 rows] at +X_OFF (2 KB), exchange barriers [set][slot] at +XB_OFF.
@@ -114,25 +120,58 @@ EG2_DEV void warp_store32(TOut* out, long ldo, int row0, int M, long col, const 
 // that the RoPE angle pos * inv_freq (computed in f32 like the reference's tables, src/ops.rs:303-306)
 // goes through sincos_reduced instead of a table. All 32 lanes run every tcgen05.ld; rows past M
 // only skip the stores.
+// Tensor maps of the epilogue's TMA I/O (TIO). EPI_ADD_NORM: [0] residual h (f32, 16 x 32 boxes),
+// [1] t (bf16, 32 x 32); EPI_QKV: [0..2] q, k, v; EPI_PLE_GATE: [0] the output (bf16, 32 x 32). All
+// with the 64-byte swizzle.
+struct alignas(64) EpiMaps {
+    CUtensorMap m[3];
+};
+
+// TIO store of a 32-row x 32-column bf16 chunk (lane i holds row i) at (x, y) of map m, through
+// slot n % 4 of the warp's four 2 KB slots (64-byte swizzle: row r's 16-byte unit j at
+// r * 64 + 16 * (j ^ ((r >> 1) & 3)), conflict-free for lane = row). The slot's previous store (the
+// 4th newest bulk group of lane 0) must have been read out first. Rows past the tensor are not
+// written. All 32 lanes call it with the same n.
+EG2_DEV void tio_store32(const CUtensorMap* m, uint8_t* slots, int n, const float (&v)[32], int x, int y) {
+    const int lane = threadIdx.x & 31;
+    uint8_t* buf = slots + (n & 3) * 2048;
+    if (lane == 0) bulk_wait_read<3>();
+    __syncwarp();
+    const uint32_t sw = (uint32_t)((lane >> 1) & 3);
+    uint8_t* row = buf + lane * 64;
+#pragma unroll
+    for (int j = 0; j < 4; j++)
+        *reinterpret_cast<uint4*>(row + ((j ^ sw) << 4)) =
+            make_uint4(bf16x2_bits(v[8 * j], v[8 * j + 1]), bf16x2_bits(v[8 * j + 2], v[8 * j + 3]),
+                       bf16x2_bits(v[8 * j + 4], v[8 * j + 5]), bf16x2_bits(v[8 * j + 6], v[8 * j + 7]));
+    fence_proxy_async();
+    __syncwarp();
+    if (lane == 0) {
+        tma_store_2d(m, buf, x, y);
+        bulk_commit();
+    }
+}
+
 // EPI_QKV with one 256-wide head per tile and RoPE over the whole head (pairs i, i + 128): the same
 // arithmetic as the general form below with the head geometry known at compile time, the position
 // read once per tile (before pass 1, so its latency hides behind the TMEM reads) and two TMEM loads
 // in flight per wait.
-template <typename TOut>
+template <typename TOut, bool TIO>
 EG2_DEV void epilogue_qkv256(const QkvEpilogue& Q, uint32_t tbase, int row0, int M, int n0, uint8_t* stage,
-                             const float* wsm) {
+                             const float* wsm, const EpiMaps& em, int& nst) {
     const int row = row0 + (int)(threadIdx.x & 31);
     const int qw = Q.nh * 256, kw = Q.nkv * 256;
     TOut* base;
     int nheads, head;
     const float* w;
     bool rot;
+    int which;
     if (n0 < qw) {
-        base = (TOut*)Q.q, nheads = Q.nh, head = n0 >> 8, w = wsm, rot = true;
+        base = (TOut*)Q.q, nheads = Q.nh, head = n0 >> 8, w = wsm, rot = true, which = 0;
     } else if (n0 < qw + kw) {
-        base = (TOut*)Q.k, nheads = Q.nkv, head = (n0 - qw) >> 8, w = wsm + 256, rot = true;
+        base = (TOut*)Q.k, nheads = Q.nkv, head = (n0 - qw) >> 8, w = wsm + 256, rot = true, which = 1;
     } else {
-        base = (TOut*)Q.v, nheads = Q.nkv, head = (n0 - qw - kw) >> 8, w = nullptr, rot = false;
+        base = (TOut*)Q.v, nheads = Q.nkv, head = (n0 - qw - kw) >> 8, w = nullptr, rot = false, which = 2;
     }
     const bool live = row < M;
     const float pf = (rot && live) ? (float)(Q.pos ? Q.pos[(long)row * Q.pos_stride] : row) : 0.f;
@@ -176,22 +215,28 @@ EG2_DEV void epilogue_qkv256(const QkvEpilogue& Q, uint32_t tbase, int row0, int
                 x2[t] = a2 * cj + a1 * sj;
             }
         }
-        warp_store32<TOut>(base, ldo, row0, M, col1 + c * 32, x1, stage);
-        warp_store32<TOut>(base, ldo, row0, M, col1 + 128 + c * 32, x2, stage);
+        if constexpr (TIO) {
+            tio_store32(&em.m[which], stage, nst++, x1, (int)col1 + c * 32, row0);
+            tio_store32(&em.m[which], stage, nst++, x2, (int)col1 + 128 + c * 32, row0);
+        } else {
+            warp_store32<TOut>(base, ldo, row0, M, col1 + c * 32, x1, stage);
+            warp_store32<TOut>(base, ldo, row0, M, col1 + 128 + c * 32, x2, stage);
+        }
     }
 }
 
-template <typename TOut, int BN>
+template <typename TOut, int BN, bool TIO>
 EG2_DEV void epilogue_qkv(const GemmEpilogue& epi, uint32_t tbase, int row0, int M, int n0, uint8_t* stage,
-                          const float* wsm) {
+                          const float* wsm, const EpiMaps& em, int& nst) {
     const int row = row0 + (int)(threadIdx.x & 31);
     const QkvEpilogue& Q = epi.qkv;
     if constexpr (BN == 256) {
         if (Q.hd == 256 && Q.part == 256) {
-            epilogue_qkv256<TOut>(Q, tbase, row0, M, n0, stage, wsm);
+            epilogue_qkv256<TOut, TIO>(Q, tbase, row0, M, n0, stage, wsm, em, nst);
             return;
         }
     }
+    if constexpr (TIO) return;  // TIO is only launched for the 256-wide form (checked on the host)
     const int hd = Q.hd, qw = Q.nh * hd, kw = Q.nkv * hd;
     TOut* base;
     int nheads, head0;
@@ -329,11 +374,14 @@ EG2_DEV void warp_load32_finish(const uint4 (&b)[8], float (&v)[32], uint8_t* st
     }
 }
 
-template <typename TIn, int BN, int EPI, typename TOut, bool PAIR = false>
+// em: the tensor maps of the epilogue's TMA I/O (TIO only).
+template <typename TIn, int BN, int EPI, typename TOut, bool PAIR = false, bool TIO = false>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
-    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int N, int K,
-                   GemmEpilogue epi) {
-    using Cfg = GemmCfg<BN, PAIR>;
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const __grid_constant__ EpiMaps em, int M, int N, int K, GemmEpilogue epi) {
+    static_assert(!TIO || (BN == 256 && (EPI == EPI_ADD_NORM || (PAIR && (EPI == EPI_QKV || EPI == EPI_PLE_GATE)))),
+                  "TMA epilogue I/O: add-norm, and the pair QKV / PLE-gate epilogues");
+    using Cfg = GemmCfg<BN, PAIR, TIO>;
     constexpr int BK = InTraits<TIn>::BK;
     constexpr int STAGES = Cfg::STAGES;
     extern __shared__ uint8_t smem_raw[];
@@ -345,6 +393,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     uint64_t* drain = tempty + 2;  // PAIR: the MMA issuer's final wait for its own MMAs
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    uint64_t* hbar = drain + 2;  // TIO: [epilogue warp][slot] residual-load barriers
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int tiles_m = (M + GEMM_BM - 1) / GEMM_BM, tiles_n = N / BN;
@@ -378,6 +427,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             mbar_init(&tempty[a], PAIR ? 256 : 128);  // PAIR: both CTAs' epilogue sets free the accumulator
         }
         mbar_init(drain, 1);
+        if constexpr (TIO) {
+            for (int x = 0; x < 32; x++) mbar_init(&hbar[x], 1);
+        }
         if constexpr (CL) {
             uint64_t* xb = reinterpret_cast<uint64_t*>(smem + Cfg::OFF_W + Cfg::XB_OFF);
             for (int x = 0; x < 4; x++) mbar_init(&xb[x], 1);  // one local arrival (expect_tx) per exchange
@@ -386,6 +438,11 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         fence_mbarrier_init();
         tma_prefetch_desc(&tmA);
         tma_prefetch_desc(&tmB);
+        if constexpr (TIO) {
+            tma_prefetch_desc(&em.m[0]);
+            if constexpr (EPI != EPI_PLE_GATE) tma_prefetch_desc(&em.m[1]);
+            if constexpr (EPI == EPI_QKV) tma_prefetch_desc(&em.m[2]);
+        }
     }
     if constexpr (EPI == EPI_QKV) {
         // q_norm / k_norm weights and the inverse frequencies, once per CTA.
@@ -435,6 +492,12 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
                     // row's 1 KB into L2 in one piece now keeps those reads off scattered DRAM pages.
                     const int nr = min(GEMM_BM, M - m0);
                     for (int r = 0; r < nr; r++) prefetch_l2_bulk(epi.an.h + (long)(m0 + r) * 512 + n0, BN * 4);
+                }
+                if constexpr (EPI == EPI_PLE_GATE) {
+                    // Same for the tile's slice of the per-layer inputs (1 KB per row).
+                    const int nr = min(GEMM_BM, M - m0);
+                    for (int r = 0; r < nr; r++)
+                        prefetch_l2_bulk(epi.aux + (long)(m0 + r) * epi.aux_ld + epi.aux_off + n0, BN * 4);
                 }
                 for (int kb = 0; kb < kblocks; kb++) {
                     if (!mbar_wait(&empty[stage], phase ^ 1, EG2_DEV_TIMEOUT_GEMM, abort_flag)) goto done;
@@ -523,8 +586,26 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         const float* wsm = reinterpret_cast<const float*>(smem + Cfg::OFF_W);
         uint8_t* stage = smem + Cfg::OFF_STAGE + (warp - 2) * Cfg::STAGE_WARP;
         TOut* out = reinterpret_cast<TOut*>(epi.out);
-        int k = 0;  // tiles this set has taken: its k-th completion of tfull[set]
+        // TIO: residual chunk g (16 columns; 16 per tile) goes to slot g % 4 of this warp, its load
+        // completing phase (g / 4) % 2 of hb[g % 4]. Loads issued / chunks consumed so far:
+        uint64_t* hb = hbar + (warp - 2) * 4;
+        int ld_issued = 0, ld_used = 0;
+        int nst = 0;  // TIO output stores issued by this warp (slot nst % 4)
+        int k = 0;    // tiles this set has taken: its k-th completion of tfull[set]
         for (int tile = t_first + set * t_step; tile < t_count; tile += 2 * t_step, k++) {
+            if constexpr (TIO && EPI == EPI_ADD_NORM) {
+                // Chunks 0-2 of this tile's residual, before the accumulator is ready; the slots'
+                // last TMA stores (the previous tile's t) must have been read out first.
+                if (lane == 0) {
+                    bulk_wait_read<0>();
+                    const int hr = tile_m0(tile) + 32 * e, hc = tile_n0(tile);
+                    for (int c = 0; c < 3; c++) {
+                        mbar_arrive_expect_tx(&hb[c], 2048);
+                        tma_load_2d(stage + c * 2048, &em.m[0], &hb[c], hc + 16 * c, hr);
+                    }
+                }
+                ld_issued += 3;
+            }
             if (!mbar_wait(&tfull[set], k & 1, EG2_DEV_TIMEOUT_GEMM, abort_flag)) break;
             tc_fence_after();
             const int m0 = tile_m0(tile), n0 = tile_n0(tile);
@@ -644,6 +725,113 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
                     for (int j = 0; j < 32; j++) v[j] = __uint_as_float(r[j]) * epi.scale * inv * w1s[c * 32 + j];
                     warp_store32<TOut>(out, epi.ldo, row0, M, n0 + c * 32, v, stage);
                 }
+            } else if constexpr (EPI == EPI_ADD_NORM && TIO) {
+                // Residual in 16-column chunks through this warp's four 2 KB slots (64-byte swizzle:
+                // row r's 16-byte unit j at r * 64 + 16 * (j ^ ((r >> 1) & 3)), conflict-free for
+                // lane = row). Chunk c is read, updated in place and stored back by TMA; the load of
+                // chunk c + 3 goes into the slot of chunk c - 1 once that store has been read out.
+                // h_new stays in TMEM; t (bf16, 32 columns = one slot per chunk) is written from it
+                // after the second exchange (t = h_new when there is no second norm).
+                const AddNormEpilogue& A = epi.an;
+                const float* w1s = wsm;
+                const float* w2s = wsm + BN;
+                const uint32_t sw = (uint32_t)((lane >> 1) & 3);
+                float ss = 0.f;
+#pragma unroll 1
+                for (int c = 0; c < BN / 32; c += 2) {
+                    uint32_t r0[32], r1[32];
+                    tmem_ld32(tbase + c * 32, r0);
+                    tmem_ld32(tbase + c * 32 + 32, r1);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int j = 0; j < 32; j++) {
+                        ss = fmaf(__uint_as_float(r0[j]), __uint_as_float(r0[j]), ss);
+                        ss = fmaf(__uint_as_float(r1[j]), __uint_as_float(r1[j]), ss);
+                    }
+                }
+                const float inv1 = 1.0f / sqrtf(exchange(ss, 0, k & 1) / 512.f + A.eps);
+                if (!ok) break;
+                float ss2 = 0.f;
+#pragma unroll 1
+                for (int c = 0; c < BN / 16; c++) {
+                    uint8_t* buf = stage + (c & 3) * 2048 + lane * 64;
+                    if (!mbar_wait(&hb[c & 3], (c >> 2) & 1, EG2_DEV_TIMEOUT_GEMM, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    ld_used++;
+                    float hv[16];
+#pragma unroll
+                    for (int j = 0; j < 4; j++) {
+                        const float4 x = *reinterpret_cast<const float4*>(buf + ((j ^ sw) << 4));
+                        hv[4 * j] = x.x, hv[4 * j + 1] = x.y, hv[4 * j + 2] = x.z, hv[4 * j + 3] = x.w;
+                    }
+                    if (c + 3 < BN / 16) {
+                        if (lane == 0) {
+                            bulk_wait_read<0>();  // the store of chunk c - 1 (same slot) is read out
+                            const int s3 = (c + 3) & 3;
+                            mbar_arrive_expect_tx(&hb[s3], 2048);
+                            tma_load_2d(stage + s3 * 2048, &em.m[0], &hb[s3], n0 + 16 * (c + 3), row0);
+                        }
+                        ld_issued++;
+                    }
+                    uint32_t r[16];
+                    tmem_ld16(tbase + c * 16, r);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int j = 0; j < 16; j++) {
+                        hv[j] = (hv[j] + __uint_as_float(r[j]) * inv1 * w1s[c * 16 + j]) * A.scalar;
+                        ss2 = fmaf(hv[j], hv[j], ss2);
+                        r[j] = __float_as_uint(hv[j]);
+                    }
+                    tmem_st16(tbase + c * 16, r);  // kept for t
+#pragma unroll
+                    for (int j = 0; j < 4; j++)
+                        *reinterpret_cast<float4*>(buf + ((j ^ sw) << 4)) =
+                            make_float4(hv[4 * j], hv[4 * j + 1], hv[4 * j + 2], hv[4 * j + 3]);
+                    fence_proxy_async();
+                    __syncwarp();
+                    if (lane == 0) {
+                        tma_store_2d(&em.m[0], stage + (c & 3) * 2048, n0 + 16 * c, row0);
+                        bulk_commit();
+                    }
+                }
+                if (!ok) break;
+                // The second exchange runs even without w2: it is also the handshake that keeps the
+                // peer from writing this set's slot 0 for the next tile before it has been read here.
+                tmem_st_wait();
+                const float inv2 = 1.0f / sqrtf(exchange(ss2, 1, k & 1) / 512.f + A.eps);
+                if (!ok) break;
+#pragma unroll 1
+                for (int c = 0; c < BN / 32; c++) {
+                    uint32_t r[32];
+                    tmem_ld32(tbase + c * 32, r);
+                    tmem_ld_wait();
+                    uint32_t pk[16];
+                    if (A.w2) {
+#pragma unroll
+                        for (int j = 0; j < 16; j++)
+                            pk[j] = bf16x2_bits(__uint_as_float(r[2 * j]) * inv2 * w2s[c * 32 + 2 * j],
+                                              __uint_as_float(r[2 * j + 1]) * inv2 * w2s[c * 32 + 2 * j + 1]);
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 16; j++) pk[j] = bf16x2_bits(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1]));
+                    }
+                    // Slot c % 4 was last the source of the 4th-newest store.
+                    if (lane == 0) bulk_wait_read<3>();
+                    __syncwarp();
+                    uint8_t* buf = stage + (c & 3) * 2048 + lane * 64;
+#pragma unroll
+                    for (int j = 0; j < 4; j++)
+                        *reinterpret_cast<uint4*>(buf + ((j ^ sw) << 4)) =
+                            make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
+                    fence_proxy_async();
+                    __syncwarp();
+                    if (lane == 0) {
+                        tma_store_2d(&em.m[1], stage + (c & 3) * 2048, n0 + 32 * c, row0);
+                        bulk_commit();
+                    }
+                }
             } else if constexpr (EPI == EPI_ADD_NORM) {
                 const AddNormEpilogue& A = epi.an;
                 const float* w1s = wsm;
@@ -713,7 +901,33 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
                     }
                 }
             } else if constexpr (EPI == EPI_QKV) {
-                epilogue_qkv<TOut, BN>(epi, tbase, row0, M, n0, stage, wsm);
+                epilogue_qkv<TOut, BN, TIO>(epi, tbase, row0, M, n0, stage, wsm, em, nst);
+            } else if constexpr (EPI == EPI_PLE_GATE) {
+                // GELU(gate) x ple[:, layer]: the per-layer inputs are read as coalesced 32 x 32 chunks
+                // (4 whole 128-byte row segments per load instruction), one chunk ahead of their use.
+                const float* pl = epi.aux + epi.aux_off;
+                uint4 pa[8], pb[8];
+                auto chunk = [&](int c, const uint4(&cur)[8]) {
+                    float v[32];
+                    warp_load32_finish(cur, v, stage + Cfg::OFF_LOAD);
+                    uint32_t r[32];
+                    tmem_ld32(tbase + c * 32, r);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int j = 0; j < 32; j++) v[j] = gelu_fast(__uint_as_float(r[j])) * v[j];
+                    if constexpr (TIO)
+                        tio_store32(&em.m[0], stage, nst++, v, n0 + c * 32, row0);
+                    else
+                        warp_store32<TOut>(out, epi.ldo, row0, M, n0 + c * 32, v, stage);
+                };
+                warp_load32_issue(pl, epi.aux_ld, row0, M, n0, pa);
+#pragma unroll 1
+                for (int c = 0; c < BN / 32; c += 2) {
+                    warp_load32_issue(pl, epi.aux_ld, row0, M, n0 + (c + 1) * 32, pb);
+                    chunk(c, pa);
+                    if (c + 2 < BN / 32) warp_load32_issue(pl, epi.aux_ld, row0, M, n0 + (c + 2) * 32, pa);
+                    chunk(c + 1, pb);
+                }
             } else if constexpr (EPI == EPI_GELU_GU) {
                 // Tile columns [0, BN/2) are gate features, [BN/2, BN) the matching up features.
 #pragma unroll 1
@@ -740,23 +954,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
 #pragma unroll
                         for (int j = 0; j < 32; j++) v[j] = __uint_as_float(r[j]);
                     }
-                    if constexpr (EPI == EPI_PLE_GATE) {
-                        if (row < M) {
-                            const float4* pl =
-                                reinterpret_cast<const float4*>(epi.aux + (long)row * epi.aux_ld + epi.aux_off + n0 + c * 32);
 #pragma unroll
-                            for (int q = 0; q < 8; q++) {
-                                const float4 p4 = pl[q];
-                                v[4 * q + 0] = gelu_fast(v[4 * q + 0]) * p4.x;
-                                v[4 * q + 1] = gelu_fast(v[4 * q + 1]) * p4.y;
-                                v[4 * q + 2] = gelu_fast(v[4 * q + 2]) * p4.z;
-                                v[4 * q + 3] = gelu_fast(v[4 * q + 3]) * p4.w;
-                            }
-                        }
-                    } else {
-#pragma unroll
-                        for (int j = 0; j < 32; j++) v[j] *= epi.scale;
-                    }
+                    for (int j = 0; j < 32; j++) v[j] *= epi.scale;
                     warp_store32<TOut>(out, epi.ldo, row0, M, n0 + c * 32, v, stage);
                 }
             }
@@ -765,6 +964,15 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
                 mbar_arrive(&tempty[set]);
             else
                 mbar_arrive_remote(mapa_shared(smem_u32(&tempty[set]), 0));
+        }
+        if constexpr (TIO) {
+            // Every TMA store has completed and every residual load issued has landed (bounded, for
+            // the error path) before the CTA's shared memory goes away.
+            if (lane == 0) {
+                bulk_wait_all();
+                for (int g = ld_used; g < ld_issued; g++) mbar_drain(&hb[g & 3], (g >> 2) & 1, 20000000ull);
+            }
+            __syncwarp();
         }
     }
 done:
@@ -810,18 +1018,19 @@ static int launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N,
     }
     const int tiles = ((M + GEMM_BM - 1) / GEMM_BM) * (N / BN);
     const int grid = tiles < num_sms() ? tiles : num_sms();
-    kern<<<grid, GEMM_THREADS, Cfg::SMEM_BYTES, s>>>(ta, tb, M, N, K, epi);
+    const EpiMaps none = {};  // no TMA epilogue I/O here
+    kern<<<grid, GEMM_THREADS, Cfg::SMEM_BYTES, s>>>(ta, tb, none, M, N, K, epi);
     return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
 
 // Clusters of two CTAs (the cluster epilogues, and CTA-pair MMAs), as many as can be resident at
 // once (the loop over tiles is persistent, so every launched cluster must run concurrently with
 // the others).
-template <int EPI, typename TOut, bool PAIR = false>
-static int launch_cluster(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int K, const GemmEpilogue& epi,
-                          cudaStream_t s) {
-    using Cfg = GemmCfg<256, PAIR>;
-    auto kern = gemm_tc_kernel<bf16_t, 256, EPI, TOut, PAIR>;
+template <int EPI, typename TOut, bool PAIR = false, bool TIO = false>
+static int launch_cluster(const CUtensorMap& ta, const CUtensorMap& tb, const EpiMaps& em, int M, int N, int K,
+                          const GemmEpilogue& epi, cudaStream_t s) {
+    using Cfg = GemmCfg<256, PAIR, TIO>;
+    auto kern = gemm_tc_kernel<bf16_t, 256, EPI, TOut, PAIR, TIO>;
     static int max_clusters[64] = {0};
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -3;
@@ -849,7 +1058,7 @@ static int launch_cluster(const CUtensorMap& ta, const CUtensorMap& tb, int M, i
     const long tiles = PAIR ? (long)((tiles_m + 1) / 2) * (N / 256) : (long)tiles_m * (N / 512);
     const int clusters = tiles < max_clusters[dev] ? (int)tiles : max_clusters[dev];
     cfg.gridDim = dim3(2 * clusters, 1, 1);
-    return cudaLaunchKernelEx(&cfg, kern, ta, tb, M, N, K, epi) == cudaSuccess ? 0 : -3;
+    return cudaLaunchKernelEx(&cfg, kern, ta, tb, em, M, N, K, epi) == cudaSuccess ? 0 : -3;
 }
 
 // CTA-pair MMAs for the plain epilogues; EG2_GEMM_NO_PAIR=1 selects the single-CTA kernels instead
@@ -890,17 +1099,37 @@ int gemm_tc(GemmKind kind, const void* A, long lda, const void* W, long ldw, int
     const bool pair = !tf32 && (epi.mode == EPI_STORE || epi.mode == EPI_GELU_GU || epi.mode == EPI_PLE_GATE ||
                                 epi.mode == EPI_QKV) && gemm_pair_enabled();
     if (make_tmap_2d(&tb, dt, W, K, N, ldw * esize, BK, pair ? BN / 2 : BN)) return -1;
+    const EpiMaps none = {};
+    // bf16 output tensor [M, cols] (row stride ld elements) as 32 x 32 TMA store boxes.
+    auto out_map = [&](CUtensorMap* m, const void* base, long cols, long ld) {
+        return make_tmap_2d(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, base, cols, M, ld * 2, 32, 32,
+                            CU_TENSOR_MAP_SWIZZLE_64B);
+    };
     if (pair) {
         switch (epi.mode) {
             case EPI_STORE:
-                return epi.out_f32 ? launch_cluster<EPI_STORE, float, true>(ta, tb, M, N, K, epi, s)
-                                   : launch_cluster<EPI_STORE, bf16_t, true>(ta, tb, M, N, K, epi, s);
+                return epi.out_f32 ? launch_cluster<EPI_STORE, float, true>(ta, tb, none, M, N, K, epi, s)
+                                   : launch_cluster<EPI_STORE, bf16_t, true>(ta, tb, none, M, N, K, epi, s);
             case EPI_GELU_GU:
-                return launch_cluster<EPI_GELU_GU, bf16_t, true>(ta, tb, M, N, K, epi, s);
-            case EPI_PLE_GATE:
-                return launch_cluster<EPI_PLE_GATE, bf16_t, true>(ta, tb, M, N, K, epi, s);
-            case EPI_QKV:
-                return launch_cluster<EPI_QKV, bf16_t, true>(ta, tb, M, N, K, epi, s);
+                return launch_cluster<EPI_GELU_GU, bf16_t, true>(ta, tb, none, M, N, K, epi, s);
+            case EPI_PLE_GATE: {
+                // Outputs by TMA store (the epilogue is bound by its global I/O).
+                EpiMaps em = {};
+                if (epi.ldo % 8 || out_map(&em.m[0], epi.out, N, epi.ldo)) return -1;
+                return launch_cluster<EPI_PLE_GATE, bf16_t, true, true>(ta, tb, em, M, N, K, epi, s);
+            }
+            case EPI_QKV: {
+                const QkvEpilogue& q = epi.qkv;
+                if (q.hd == 256 && q.part == 256) {
+                    EpiMaps em = {};
+                    if (out_map(&em.m[0], q.q, (long)q.nh * 256, (long)q.nh * 256) ||
+                        out_map(&em.m[1], q.k, (long)q.nkv * 256, (long)q.nkv * 256) ||
+                        out_map(&em.m[2], q.v, (long)q.nkv * 256, (long)q.nkv * 256))
+                        return -1;
+                    return launch_cluster<EPI_QKV, bf16_t, true, true>(ta, tb, em, M, N, K, epi, s);
+                }
+                return launch_cluster<EPI_QKV, bf16_t, true>(ta, tb, none, M, N, K, epi, s);
+            }
         }
         return -1;
     }
@@ -916,14 +1145,26 @@ int gemm_tc(GemmKind kind, const void* A, long lda, const void* W, long ldw, int
             case EPI_QKV:
                 return launch_tc<bf16_t, BN, EPI_QKV, bf16_t>(ta, tb, M, N, K, epi, s);
             case EPI_ADD_NORM:
-                if (N != 512 || !epi.an.h || !epi.an.w1 || !epi.out) return -1;
-                return launch_cluster<EPI_ADD_NORM, bf16_t>(ta, tb, M, N, K, epi, s);
+            {
+                if (N != 512 || !epi.an.h || !epi.an.w1 || !epi.out || epi.ldo % 8) return -1;
+                // Up to K = 1024 (O, PLE projections) the epilogue's residual I/O goes through TMA and
+                // the main loop keeps 3 stages; the down projection (K = 2048) needs the 4th stage
+                // more and keeps the register path.
+                if (K > 1024) return launch_cluster<EPI_ADD_NORM, bf16_t>(ta, tb, none, M, N, K, epi, s);
+                // Residual h: f32 [M, 512], 16 x 32 boxes; t: bf16 [M, 512] (row stride ldo), 32 x 32.
+                EpiMaps em = {};
+                if (make_tmap_2d(&em.m[0], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, epi.an.h, 512, M, 512 * 4, 16, 32,
+                                 CU_TENSOR_MAP_SWIZZLE_64B) ||
+                    out_map(&em.m[1], epi.out, 512, epi.ldo))
+                    return -1;
+                return launch_cluster<EPI_ADD_NORM, bf16_t, false, true>(ta, tb, em, M, N, K, epi, s);
+            }
             case EPI_GROUP_NORM:
                 if (N % 512 || !epi.an.w1 || !epi.out) return -1;
-                return launch_cluster<EPI_GROUP_NORM, float>(ta, tb, M, N, K, epi, s);
+                return launch_cluster<EPI_GROUP_NORM, float>(ta, tb, none, M, N, K, epi, s);
             case EPI_QKV_PAIR:
                 if (!qkv_pair_fusable(epi.qkv) || N != (epi.qkv.nh + 2 * epi.qkv.nkv) * 512) return -1;
-                return launch_cluster<EPI_QKV_PAIR, bf16_t>(ta, tb, M, N, K, epi, s);
+                return launch_cluster<EPI_QKV_PAIR, bf16_t>(ta, tb, none, M, N, K, epi, s);
         }
     } else {
         if (epi.mode == EPI_QKV) return launch_tc<float, BN, EPI_QKV, float>(ta, tb, M, N, K, epi, s);

@@ -75,7 +75,8 @@ int num_sms();
 // 2-D K-major tensor map with 128-byte swizzle: `inner` elements per row (the K extent),
 // `outer` rows, `row_bytes` between rows; box = box_inner x box_outer.
 int make_tmap_2d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t inner, uint64_t outer,
-                 uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer);
+                 uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer,
+                 CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B);
 // 3-D variant: dims (d0, d1, d2) with byte strides s1 (dim 1) and s2 (dim 2); box (b0, b1, b2).
 int make_tmap_3d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t d0, uint64_t d1, uint64_t d2,
                  uint64_t s1, uint64_t s2, uint32_t b0, uint32_t b1, uint32_t b2);

@@ -51,15 +51,15 @@ static EncodeTiledFn encode_tiled() {
 }
 
 int make_tmap_2d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t inner, uint64_t outer,
-                 uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer) {
+                 uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swizzle) {
     EncodeTiledFn fn = encode_tiled();
     if (!fn) return -3;
     cuuint64_t dims[2] = {inner, outer};
     cuuint64_t strides[1] = {row_bytes};
     cuuint32_t box[2] = {box_inner, box_outer};
     cuuint32_t es[2] = {1, 1};
-    CUresult r = fn(m, dt, 2, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    CUresult r = fn(m, dt, 2, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS ? 0 : -1;
 }
 
