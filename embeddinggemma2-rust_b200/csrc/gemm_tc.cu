@@ -45,9 +45,9 @@ constexpr int GEMM_THREADS = 320;
 // 32 KB out of shared memory instead of 48 + 48 KB -- the single-CTA tile needs ~190 B/cycle of shared
 // memory at the full tensor rate, more than shared memory delivers.
 // TIO: the epilogue's global I/O goes through TMA, each epilogue warp owning four 2 KB
-// shared-memory slots (64-byte swizzle) -- EPI_ADD_NORM for its residual reads and h / t writes,
-// EPI_QKV and EPI_PLE_GATE for their outputs (these keep the 2.5 KB staging tile of the register
-// path after the slots, for the PLE inputs). The main loop gives up stages for them.
+// shared-memory slots (instead of the 2.5 KB staging tile of the register path) -- EPI_ADD_NORM
+// for its residual reads and h / t writes, EPI_PLE_GATE for its PLE inputs and outputs, EPI_QKV
+// and EPI_GELU_GU for their outputs. The main loop gives up stages for them.
 template <int BN, bool PAIR = false, bool TIO = false>
 struct GemmCfg {
     static constexpr int A_BYTES = GEMM_BM * 128;
@@ -56,8 +56,7 @@ struct GemmCfg {
     static constexpr int STAGES = TIO ? (PAIR ? 4 : 3) : PAIR ? 6 : (BN == 256) ? 4 : 6;
     // Barriers follow the stages; TIO slots must start on a 1 KB boundary.
     static constexpr int OFF_STAGE = STAGES * STAGE_BYTES + (TIO ? 1024 : 256);
-    static constexpr int STAGE_WARP = TIO ? (PAIR ? 11264 : 8192) : 32 * (64 + 16);  // 32 rows x 64 B + 16 B pad
-    static constexpr int OFF_LOAD = TIO ? 8192 : 0;  // register-path staging within a warp's area
+    static constexpr int STAGE_WARP = TIO ? 8192 : 32 * (64 + 16);  // 32 rows x 64 B + 16 B pad
     static constexpr int OFF_W = OFF_STAGE + 8 * STAGE_WARP;        // EPI_QKV: norm weights, inv freqs
     // EPI_QKV: norm weights + inverse frequencies (<= 3 KB). Cluster modes: this CTA's halves of the
     // norm weights (EPI_QKV_PAIR: wq, wk and 128 inverse frequencies, 2.5 KB), exchange slots
@@ -379,8 +378,9 @@ template <typename TIn, int BN, int EPI, typename TOut, bool PAIR = false, bool 
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ EpiMaps em, int M, int N, int K, GemmEpilogue epi) {
-    static_assert(!TIO || (BN == 256 && (EPI == EPI_ADD_NORM || (PAIR && (EPI == EPI_QKV || EPI == EPI_PLE_GATE)))),
-                  "TMA epilogue I/O: add-norm, and the pair QKV / PLE-gate epilogues");
+    static_assert(!TIO || (BN == 256 && (EPI == EPI_ADD_NORM ||
+                                         (PAIR && (EPI == EPI_QKV || EPI == EPI_PLE_GATE || EPI == EPI_GELU_GU)))),
+                  "TMA epilogue I/O: add-norm, and the pair QKV / PLE-gate / GELU epilogues");
     using Cfg = GemmCfg<BN, PAIR, TIO>;
     constexpr int BK = InTraits<TIn>::BK;
     constexpr int STAGES = Cfg::STAGES;
@@ -593,15 +593,15 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         int nst = 0;  // TIO output stores issued by this warp (slot nst % 4)
         int k = 0;    // tiles this set has taken: its k-th completion of tfull[set]
         for (int tile = t_first + set * t_step; tile < t_count; tile += 2 * t_step, k++) {
-            if constexpr (TIO && EPI == EPI_ADD_NORM) {
-                // Chunks 0-2 of this tile's residual, before the accumulator is ready; the slots'
-                // last TMA stores (the previous tile's t) must have been read out first.
+            if constexpr (TIO && (EPI == EPI_ADD_NORM || EPI == EPI_PLE_GATE)) {
+                // Chunks 0-2 of this tile's residual (PLE inputs), before the accumulator is ready;
+                // the slots' last TMA stores (the previous tile's outputs) must have been read out.
                 if (lane == 0) {
                     bulk_wait_read<0>();
                     const int hr = tile_m0(tile) + 32 * e, hc = tile_n0(tile);
                     for (int c = 0; c < 3; c++) {
                         mbar_arrive_expect_tx(&hb[c], 2048);
-                        tma_load_2d(stage + c * 2048, &em.m[0], &hb[c], hc + 16 * c, hr);
+                        tma_load_2d(stage + c * 2048, &em.m[EPI == EPI_ADD_NORM ? 0 : 1], &hb[c], hc + 16 * c, hr);
                     }
                 }
                 ld_issued += 3;
@@ -902,6 +902,56 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
                 }
             } else if constexpr (EPI == EPI_QKV) {
                 epilogue_qkv<TOut, BN, TIO>(epi, tbase, row0, M, n0, stage, wsm, em, nst);
+            } else if constexpr (EPI == EPI_PLE_GATE && TIO) {
+                // GELU(gate) x ple[:, layer] in 16-column chunks: the inputs arrive by TMA in slot
+                // c % 4 (f32, 64-byte swizzle), the bf16 result replaces them there (32-byte swizzle:
+                // row r's 16-byte unit j at r * 32 + 16 * (j ^ ((r >> 2) & 1))) and leaves by TMA store;
+                // the load of chunk c + 3 reuses the slot of chunk c - 1 once its store is read out.
+                const uint32_t sw = (uint32_t)((lane >> 1) & 3), sw32 = (uint32_t)((lane >> 2) & 1);
+#pragma unroll 1
+                for (int c = 0; c < BN / 16; c++) {
+                    uint8_t* slot = stage + (c & 3) * 2048;
+                    if (!mbar_wait(&hb[c & 3], (c >> 2) & 1, EG2_DEV_TIMEOUT_GEMM, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    ld_used++;
+                    float v[16];
+#pragma unroll
+                    for (int j = 0; j < 4; j++) {
+                        const float4 x = *reinterpret_cast<const float4*>(slot + lane * 64 + ((j ^ sw) << 4));
+                        v[4 * j] = x.x, v[4 * j + 1] = x.y, v[4 * j + 2] = x.z, v[4 * j + 3] = x.w;
+                    }
+                    if (c + 3 < BN / 16) {
+                        if (lane == 0) {
+                            bulk_wait_read<0>();  // the store of chunk c - 1 (same slot) is read out
+                            const int s3 = (c + 3) & 3;
+                            mbar_arrive_expect_tx(&hb[s3], 2048);
+                            tma_load_2d(stage + s3 * 2048, &em.m[1], &hb[s3], n0 + 16 * (c + 3), row0);
+                        }
+                        ld_issued++;
+                    }
+                    uint32_t r[16];
+                    tmem_ld16(tbase + c * 16, r);
+                    tmem_ld_wait();
+                    uint32_t pk[8];
+#pragma unroll
+                    for (int j = 0; j < 8; j++)
+                        pk[j] = bf16x2_bits(gelu_fast(__uint_as_float(r[2 * j])) * v[2 * j],
+                                            gelu_fast(__uint_as_float(r[2 * j + 1])) * v[2 * j + 1]);
+                    __syncwarp();  // every lane has read its inputs from the slot
+#pragma unroll
+                    for (int j = 0; j < 2; j++)
+                        *reinterpret_cast<uint4*>(slot + lane * 32 + ((j ^ sw32) << 4)) =
+                            make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
+                    fence_proxy_async();
+                    __syncwarp();
+                    if (lane == 0) {
+                        tma_store_2d(&em.m[0], slot, n0 + 16 * c, row0);
+                        bulk_commit();
+                    }
+                }
+                if (!ok) break;
             } else if constexpr (EPI == EPI_PLE_GATE) {
                 // GELU(gate) x ple[:, layer]: the per-layer inputs are read as coalesced 32 x 32 chunks
                 // (4 whole 128-byte row segments per load instruction), one chunk ahead of their use.
@@ -909,16 +959,13 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
                 uint4 pa[8], pb[8];
                 auto chunk = [&](int c, const uint4(&cur)[8]) {
                     float v[32];
-                    warp_load32_finish(cur, v, stage + Cfg::OFF_LOAD);
+                    warp_load32_finish(cur, v, stage);
                     uint32_t r[32];
                     tmem_ld32(tbase + c * 32, r);
                     tmem_ld_wait();
 #pragma unroll
                     for (int j = 0; j < 32; j++) v[j] = gelu_fast(__uint_as_float(r[j])) * v[j];
-                    if constexpr (TIO)
-                        tio_store32(&em.m[0], stage, nst++, v, n0 + c * 32, row0);
-                    else
-                        warp_store32<TOut>(out, epi.ldo, row0, M, n0 + c * 32, v, stage);
+                    warp_store32<TOut>(out, epi.ldo, row0, M, n0 + c * 32, v, stage);
                 };
                 warp_load32_issue(pl, epi.aux_ld, row0, M, n0, pa);
 #pragma unroll 1
@@ -941,7 +988,10 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
 #pragma unroll
                         for (int j = 0; j < 32; j++) v[j] = gelu_fast(__uint_as_float(g[j])) * __uint_as_float(u[j]);
                     }
-                    warp_store32<TOut>(out, epi.ldo, row0, M, n0 / 2 + c * 32, v, stage);
+                    if constexpr (TIO)
+                        tio_store32(&em.m[0], stage, nst++, v, n0 / 2 + c * 32, row0);
+                    else
+                        warp_store32<TOut>(out, epi.ldo, row0, M, n0 / 2 + c * 32, v, stage);
                 }
             } else {
 #pragma unroll 1
@@ -1110,12 +1160,21 @@ int gemm_tc(GemmKind kind, const void* A, long lda, const void* W, long ldw, int
             case EPI_STORE:
                 return epi.out_f32 ? launch_cluster<EPI_STORE, float, true>(ta, tb, none, M, N, K, epi, s)
                                    : launch_cluster<EPI_STORE, bf16_t, true>(ta, tb, none, M, N, K, epi, s);
-            case EPI_GELU_GU:
-                return launch_cluster<EPI_GELU_GU, bf16_t, true>(ta, tb, none, M, N, K, epi, s);
-            case EPI_PLE_GATE: {
-                // Outputs by TMA store (the epilogue is bound by its global I/O).
+            case EPI_GELU_GU: {
                 EpiMaps em = {};
-                if (epi.ldo % 8 || out_map(&em.m[0], epi.out, N, epi.ldo)) return -1;
+                if (epi.ldo % 8 || out_map(&em.m[0], epi.out, N / 2, epi.ldo)) return -1;
+                return launch_cluster<EPI_GELU_GU, bf16_t, true, true>(ta, tb, em, M, N, K, epi, s);
+            }
+            case EPI_PLE_GATE: {
+                // Inputs and outputs through TMA (the epilogue is bound by its global I/O): [0] the
+                // bf16 output in 16 x 32 boxes, [1] this layer's slice of the PLE tensor (f32).
+                EpiMaps em = {};
+                if (epi.ldo % 8 || epi.aux_ld % 4 || epi.aux_off % 4 ||
+                    make_tmap_2d(&em.m[0], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, epi.out, N, M, epi.ldo * 2, 16, 32,
+                                 CU_TENSOR_MAP_SWIZZLE_32B) ||
+                    make_tmap_2d(&em.m[1], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, epi.aux + epi.aux_off, N, M, epi.aux_ld * 4,
+                                 16, 32, CU_TENSOR_MAP_SWIZZLE_64B))
+                    return -1;
                 return launch_cluster<EPI_PLE_GATE, bf16_t, true, true>(ta, tb, em, M, N, K, epi, s);
             }
             case EPI_QKV: {
