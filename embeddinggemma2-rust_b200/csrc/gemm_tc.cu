@@ -486,19 +486,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             int stage = 0;
             uint32_t phase = 0;
             for (int tile = t_first; tile < t_count; tile += t_step) {
+                // (No L2 prefetch of the epilogue's inputs here: 128 bulk prefetches per tile from this
+                // thread delayed the main loop's loads more than they saved -- measured on B200.)
                 const int m0 = tile_m0(tile), n0 = tile_n0(tile);
-                if constexpr (AN) {
-                    // The epilogue reads this tile's residual rows 128 bytes at a time; pulling each
-                    // row's 1 KB into L2 in one piece now keeps those reads off scattered DRAM pages.
-                    const int nr = min(GEMM_BM, M - m0);
-                    for (int r = 0; r < nr; r++) prefetch_l2_bulk(epi.an.h + (long)(m0 + r) * 512 + n0, BN * 4);
-                }
-                if constexpr (EPI == EPI_PLE_GATE) {
-                    // Same for the tile's slice of the per-layer inputs (1 KB per row).
-                    const int nr = min(GEMM_BM, M - m0);
-                    for (int r = 0; r < nr; r++)
-                        prefetch_l2_bulk(epi.aux + (long)(m0 + r) * epi.aux_ld + epi.aux_off + n0, BN * 4);
-                }
                 for (int kb = 0; kb < kblocks; kb++) {
                     if (!mbar_wait(&empty[stage], phase ^ 1, EG2_DEV_TIMEOUT_GEMM, abort_flag)) goto done;
                     uint8_t* sa = smem + stage * Cfg::STAGE_BYTES;
@@ -837,7 +827,6 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
                 const float* w1s = wsm;
                 const float* w2s = wsm + BN;
                 // Residual chunk 0 is loaded first, so its latency overlaps pass 1 and the exchange.
-                // (The producer has already pulled this tile's residual rows into L2.)
                 uint4 hb[8];
                 warp_load32_issue(A.h, 512, row0, M, n0, hb);
                 float ss = 0.f;
