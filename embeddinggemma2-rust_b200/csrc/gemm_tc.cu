@@ -715,7 +715,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
                     for (int j = 0; j < 32; j++) v[j] = __uint_as_float(r[j]) * epi.scale * inv * w1s[c * 32 + j];
                     warp_store32<TOut>(out, epi.ldo, row0, M, n0 + c * 32, v, stage);
                 }
-            } else if constexpr (EPI == EPI_ADD_NORM && TIO) {
+            } else if constexpr (EPI == EPI_ADD_NORM) {
+                static_assert(TIO, "the add-norm epilogue runs with TMA I/O");
                 // Residual in 16-column chunks through this warp's four 2 KB slots (64-byte swizzle:
                 // row r's 16-byte unit j at r * 64 + 16 * (j ^ ((r >> 1) & 3)), conflict-free for
                 // lane = row). Chunk c is read, updated in place and stored back by TMA; the load of
@@ -820,73 +821,6 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
                     if (lane == 0) {
                         tma_store_2d(&em.m[1], stage + (c & 3) * 2048, n0 + 32 * c, row0);
                         bulk_commit();
-                    }
-                }
-            } else if constexpr (EPI == EPI_ADD_NORM) {
-                const AddNormEpilogue& A = epi.an;
-                const float* w1s = wsm;
-                const float* w2s = wsm + BN;
-                // Residual chunk 0 is loaded first, so its latency overlaps pass 1 and the exchange.
-                uint4 hb[8];
-                warp_load32_issue(A.h, 512, row0, M, n0, hb);
-                float ss = 0.f;
-#pragma unroll 1
-                for (int c = 0; c < BN / 32; c += 2) {
-                    uint32_t r0[32], r1[32];
-                    tmem_ld32(tbase + c * 32, r0);
-                    tmem_ld32(tbase + c * 32 + 32, r1);
-                    tmem_ld_wait();
-#pragma unroll
-                    for (int j = 0; j < 32; j++) {
-                        ss = fmaf(__uint_as_float(r0[j]), __uint_as_float(r0[j]), ss);
-                        ss = fmaf(__uint_as_float(r1[j]), __uint_as_float(r1[j]), ss);
-                    }
-                }
-                const float inv1 = 1.0f / sqrtf(exchange(ss, 0, k & 1) / 512.f + A.eps);
-                if (!ok) break;
-                float ss2 = 0.f;
-#pragma unroll 1
-                for (int c = 0; c < BN / 32; c++) {
-                    float hv[32];
-                    {
-                        uint4 cur[8];
-#pragma unroll
-                        for (int q = 0; q < 8; q++) cur[q] = hb[q];
-                        if (c + 1 < BN / 32) warp_load32_issue(A.h, 512, row0, M, n0 + (c + 1) * 32, hb);
-                        warp_load32_finish(cur, hv, stage);
-                    }
-                    uint32_t r[32];
-                    tmem_ld32(tbase + c * 32, r);
-                    tmem_ld_wait();
-#pragma unroll
-                    for (int j = 0; j < 32; j++) {
-                        hv[j] = (hv[j] + __uint_as_float(r[j]) * inv1 * w1s[c * 32 + j]) * A.scalar;
-                        ss2 = fmaf(hv[j], hv[j], ss2);
-                    }
-                    warp_store32<float>(A.h, 512, row0, M, n0 + c * 32, hv, stage);
-                    if (A.w2) {
-#pragma unroll
-                        for (int j = 0; j < 32; j++) r[j] = __float_as_uint(hv[j]);
-                        tmem_st32(tbase + c * 32, r);  // kept for the second norm
-                    } else {
-                        warp_store32<TOut>(out, epi.ldo, row0, M, n0 + c * 32, hv, stage);
-                    }
-                }
-                // The second exchange runs even without w2: it is also the handshake that keeps the
-                // peer from writing this set's slot 0 for the next tile before it has been read here.
-                if (A.w2) tmem_st_wait();
-                const float inv2 = 1.0f / sqrtf(exchange(ss2, 1, k & 1) / 512.f + A.eps);
-                if (!ok) break;
-                if (A.w2) {
-#pragma unroll 1
-                    for (int c = 0; c < BN / 32; c++) {
-                        uint32_t r[32];
-                        tmem_ld32(tbase + c * 32, r);
-                        tmem_ld_wait();
-                        float v[32];
-#pragma unroll
-                        for (int j = 0; j < 32; j++) v[j] = __uint_as_float(r[j]) * inv2 * w2s[c * 32 + j];
-                        warp_store32<TOut>(out, epi.ldo, row0, M, n0 + c * 32, v, stage);
                     }
                 }
             } else if constexpr (EPI == EPI_QKV) {
@@ -1195,10 +1129,8 @@ int gemm_tc(GemmKind kind, const void* A, long lda, const void* W, long ldw, int
             case EPI_ADD_NORM:
             {
                 if (N != 512 || !epi.an.h || !epi.an.w1 || !epi.out || epi.ldo % 8) return -1;
-                // Up to K = 1024 (O, PLE projections) the epilogue's residual I/O goes through TMA and
-                // the main loop keeps 3 stages; the down projection (K = 2048) needs the 4th stage
-                // more and keeps the register path.
-                if (K > 1024) return launch_cluster<EPI_ADD_NORM, bf16_t>(ta, tb, none, M, N, K, epi, s);
+                // The epilogue's residual I/O goes through TMA (the main loop keeps 3 stages); measured
+                // faster than the register path with 4 stages for the O, down and PLE projections.
                 // Residual h: f32 [M, 512], 16 x 32 boxes; t: bf16 [M, 512] (row stride ldo), 32 x 32.
                 EpiMaps em = {};
                 if (make_tmap_2d(&em.m[0], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, epi.an.h, 512, M, 512 * 4, 16, 32,

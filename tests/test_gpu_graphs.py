@@ -59,3 +59,17 @@ def test_graph_latency(request, monkeypatch):
     direct_ms = (time.perf_counter() - t0) / 20 * 1e3
     print(f"17-token query, host ids in / embeddings out: graph {graph_ms:.3f} ms, launch by launch {direct_ms:.3f} ms")
     assert graph_ms < direct_ms
+
+
+@pytest.mark.parametrize("filler", [45, 13, 200])
+def test_result_independent_of_packing(filler, request, monkeypatch):
+    """A document's embedding is the same bits alone and packed behind another sequence at an offset
+    where its rows share tiles (and warps) with the other sequence's rows."""
+    dev = request.getfixturevalue("dev_bf16")
+    monkeypatch.setenv("EG2_NO_GRAPHS", "1")
+    rng = np.random.default_rng(filler)
+    doc = rng.integers(0, 262144, size=300).astype(np.uint32)
+    other = rng.integers(0, 262144, size=filler).astype(np.uint32)
+    alone = embed_host(dev, [doc])
+    packed = embed_host(dev, [other, doc])
+    np.testing.assert_array_equal(alone[0], packed[1])
