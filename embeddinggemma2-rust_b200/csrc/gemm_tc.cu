@@ -378,9 +378,9 @@ template <typename TIn, int BN, int EPI, typename TOut, bool PAIR = false, bool 
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ EpiMaps em, int M, int N, int K, GemmEpilogue epi) {
-    static_assert(!TIO || (BN == 256 && (EPI == EPI_ADD_NORM ||
+    static_assert(!TIO || (BN == 256 && (EPI == EPI_ADD_NORM || EPI == EPI_GROUP_NORM || EPI == EPI_QKV_PAIR ||
                                          (PAIR && (EPI == EPI_QKV || EPI == EPI_PLE_GATE || EPI == EPI_GELU_GU)))),
-                  "TMA epilogue I/O: add-norm, and the pair QKV / PLE-gate / GELU epilogues");
+                  "TMA epilogue I/O: the cluster epilogues, and the pair QKV / PLE-gate / GELU epilogues");
     using Cfg = GemmCfg<BN, PAIR, TIO>;
     constexpr int BK = InTraits<TIn>::BK;
     constexpr int STAGES = Cfg::STAGES;
@@ -438,10 +438,10 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         fence_mbarrier_init();
         tma_prefetch_desc(&tmA);
         tma_prefetch_desc(&tmB);
-        if constexpr (TIO) {
+        if constexpr (TIO) {  // the maps this epilogue uses
             tma_prefetch_desc(&em.m[0]);
-            if constexpr (EPI != EPI_PLE_GATE) tma_prefetch_desc(&em.m[1]);
-            if constexpr (EPI == EPI_QKV) tma_prefetch_desc(&em.m[2]);
+            if constexpr (EPI != EPI_GELU_GU && EPI != EPI_GROUP_NORM) tma_prefetch_desc(&em.m[1]);
+            if constexpr (EPI == EPI_QKV || EPI == EPI_QKV_PAIR) tma_prefetch_desc(&em.m[2]);
         }
     }
     if constexpr (EPI == EPI_QKV) {
@@ -681,8 +681,14 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
                             x2[t] = a2 * cj + a1 * sj;
                         }
                     }
-                    warp_store32<TOut>(base, ldo, row0, M, col1 + c * 32, x1, stage);
-                    warp_store32<TOut>(base, ldo, row0, M, col2 + c * 32, x2, stage);
+                    if constexpr (TIO) {
+                        const int which = hidx < Q.nh ? 0 : hidx < Q.nh + Q.nkv ? 1 : 2;
+                        tio_store32(&em.m[which], stage, nst++, x1, (int)col1 + c * 32, row0);
+                        tio_store32(&em.m[which], stage, nst++, x2, (int)col2 + c * 32, row0);
+                    } else {
+                        warp_store32<TOut>(base, ldo, row0, M, col1 + c * 32, x1, stage);
+                        warp_store32<TOut>(base, ldo, row0, M, col2 + c * 32, x2, stage);
+                    }
                 }
             } else if constexpr (EPI == EPI_GROUP_NORM) {
                 // One exchange per tile; the slot alternates with the tile's parity, which is also the
@@ -705,15 +711,43 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
                 }
                 const float inv = 1.0f / sqrtf(exchange(ss, k & 1, (k >> 1) & 1) / 512.f + epi.an.eps);
                 if (!ok) break;
+                if constexpr (TIO) {
+                    // f32 output in 16-column chunks through the slots (64-byte swizzle), by TMA store.
+                    const uint32_t sw = (uint32_t)((lane >> 1) & 3);
 #pragma unroll 1
-                for (int c = 0; c < BN / 32; c++) {
-                    uint32_t r[32];
-                    tmem_ld32(tbase + c * 32, r);
-                    tmem_ld_wait();
-                    float v[32];
+                    for (int c = 0; c < BN / 16; c++) {
+                        uint32_t r[16];
+                        tmem_ld16(tbase + c * 16, r);
+                        tmem_ld_wait();
+                        float v[16];
 #pragma unroll
-                    for (int j = 0; j < 32; j++) v[j] = __uint_as_float(r[j]) * epi.scale * inv * w1s[c * 32 + j];
-                    warp_store32<TOut>(out, epi.ldo, row0, M, n0 + c * 32, v, stage);
+                        for (int j = 0; j < 16; j++) v[j] = __uint_as_float(r[j]) * epi.scale * inv * w1s[c * 16 + j];
+                        uint8_t* slot = stage + (nst & 3) * 2048;
+                        if (lane == 0) bulk_wait_read<3>();  // the slot's previous store is read out
+                        __syncwarp();
+#pragma unroll
+                        for (int j = 0; j < 4; j++)
+                            *reinterpret_cast<float4*>(slot + lane * 64 + ((j ^ sw) << 4)) =
+                                make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+                        fence_proxy_async();
+                        __syncwarp();
+                        if (lane == 0) {
+                            tma_store_2d(&em.m[0], slot, n0 + 16 * c, row0);
+                            bulk_commit();
+                        }
+                        nst++;
+                    }
+                } else {
+#pragma unroll 1
+                    for (int c = 0; c < BN / 32; c++) {
+                        uint32_t r[32];
+                        tmem_ld32(tbase + c * 32, r);
+                        tmem_ld_wait();
+                        float v[32];
+#pragma unroll
+                        for (int j = 0; j < 32; j++) v[j] = __uint_as_float(r[j]) * epi.scale * inv * w1s[c * 32 + j];
+                        warp_store32<TOut>(out, epi.ldo, row0, M, n0 + c * 32, v, stage);
+                    }
                 }
             } else if constexpr (EPI == EPI_ADD_NORM) {
                 static_assert(TIO, "the add-norm epilogue runs with TMA I/O");
@@ -1139,12 +1173,26 @@ int gemm_tc(GemmKind kind, const void* A, long lda, const void* W, long ldw, int
                     return -1;
                 return launch_cluster<EPI_ADD_NORM, bf16_t, false, true>(ta, tb, em, M, N, K, epi, s);
             }
-            case EPI_GROUP_NORM:
-                if (N % 512 || !epi.an.w1 || !epi.out) return -1;
-                return launch_cluster<EPI_GROUP_NORM, float>(ta, tb, none, M, N, K, epi, s);
-            case EPI_QKV_PAIR:
-                if (!qkv_pair_fusable(epi.qkv) || N != (epi.qkv.nh + 2 * epi.qkv.nkv) * 512) return -1;
-                return launch_cluster<EPI_QKV_PAIR, bf16_t>(ta, tb, none, M, N, K, epi, s);
+            case EPI_GROUP_NORM: {
+                if (N % 512 || !epi.an.w1 || !epi.out || epi.ldo % 4) return -1;
+                // f32 output by TMA store, 16 x 32 boxes.
+                EpiMaps em = {};
+                if (make_tmap_2d(&em.m[0], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, epi.out, N, M, epi.ldo * 4, 16, 32,
+                                 CU_TENSOR_MAP_SWIZZLE_64B))
+                    return -1;
+                return launch_cluster<EPI_GROUP_NORM, float, false, true>(ta, tb, em, M, N, K, epi, s);
+            }
+            case EPI_QKV_PAIR: {
+                const QkvEpilogue& q = epi.qkv;
+                if (!qkv_pair_fusable(q) || N != (q.nh + 2 * q.nkv) * 512) return -1;
+                // q / k / v by TMA store, 32 x 32 boxes.
+                EpiMaps em = {};
+                if (out_map(&em.m[0], q.q, (long)q.nh * 512, (long)q.nh * 512) ||
+                    out_map(&em.m[1], q.k, (long)q.nkv * 512, (long)q.nkv * 512) ||
+                    out_map(&em.m[2], q.v, (long)q.nkv * 512, (long)q.nkv * 512))
+                    return -1;
+                return launch_cluster<EPI_QKV_PAIR, bf16_t, false, true>(ta, tb, em, M, N, K, epi, s);
+            }
         }
     } else {
         if (epi.mode == EPI_QKV) return launch_tc<float, BN, EPI_QKV, float>(ta, tb, M, N, K, epi, s);
