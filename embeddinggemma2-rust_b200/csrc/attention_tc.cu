@@ -24,7 +24,7 @@ constexpr float ATT_RESCALE_LOG2 = 8.f;
 struct AttParams {
     const AttnTile* tiles;
     bf16_t* out;
-    int nh, nkv, hd, window, G, tq, nsplit;
+    int nh, nkv, hd, window, G, tq, nsplit, n_tiles;
 };
 
 // ---------------------------------------------------------------------------------------------
@@ -71,13 +71,21 @@ struct ApCfg {
     static constexpr int UNITS = DQK == 256 ? 4 : 3;
     static constexpr int OFF_R = Q_BYTES;
     static constexpr int OFF_BAR = OFF_R + UNITS * AP_UNIT;
-    // q, ring full/empty, s full/empty, p[2], pv[2], drain[2]; split softmax: pair handshakes [4 quadrants][2]
-    static constexpr int N_BARS = 1 + 2 * UNITS + 2 + 4 + 2 + (SPLIT ? 8 : 0);
+    // q, ring full/empty, s full/empty, p[2], pv[2], drain[2], q_empty, o_empty; split softmax: pair
+    // handshakes [4 quadrants][2]
+    static constexpr int N_BARS = 1 + 2 * UNITS + 2 + 4 + 2 + 2 + (SPLIT ? 8 : 0);
     static constexpr int OFF_X = OFF_BAR + N_BARS * 8 + 16;  // split softmax: maxima [2 slots][2 halves][128], sums [2][128]
     static constexpr int SMEM = 1024 + OFF_X + (SPLIT ? 3 * 1024 : 0);
 };
 static_assert(ApCfg<256>::SMEM <= 227 * 1024 && ApCfg<512>::SMEM <= 227 * 1024, "attention pair: shared memory");
 
+// Persistent: each cluster walks work units u = cluster, cluster + clusters, ... (a unit is one
+// (pair tile, K/V head, 256-channel half of O)), keeping its barriers, K/V ring and TMEM. Across a
+// unit boundary the next unit's Q load (once every S MMA of the previous unit has completed:
+// q_empty) and its first S = Q K^T run under the previous unit's last P V and O epilogue; its first
+// P V waits until the softmax threads have read O out (o_empty). Barrier phases follow running
+// counts: T = key tiles so far (s_full / s_empty, p_full / pv_done), X = split-softmax handshakes,
+// U = units with keys so far (q_full, q_empty, o_empty); units without keys are skipped by every role.
 template <int DQK>
 __global__ void __launch_bounds__(ApCfg<DQK>::THREADS, 1)
     attention_pair_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -98,24 +106,37 @@ __global__ void __launch_bounds__(ApCfg<DQK>::THREADS, 1)
     uint64_t* p_full = s_empty + 1;
     uint64_t* pv_done = p_full + 2;
     uint64_t* drain = pv_done + 2;
-    uint64_t* xpair = drain + 2;  // split softmax: [quadrant][slot], 64 arrivals (the row's two warps)
+    uint64_t* q_empty = drain + 2;
+    uint64_t* o_empty = q_empty + 1;
+    uint64_t* xpair = o_empty + 1;  // split softmax: [quadrant][slot], 64 arrivals (the row's two warps)
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + Cfg::N_BARS);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t rank = cluster_ctarank();
     const bool even = rank == 0;
-    const int cid = (int)(blockIdx.x >> 1);
-    const int tile_idx = cid / (prm.nkv * prm.nsplit);
-    const int rem = cid % (prm.nkv * prm.nsplit);
-    const int g = rem / prm.nsplit, dsplit = rem % prm.nsplit;  // K/V head, 256-channel half of O
-    const AttnTile tile = prm.tiles[tile_idx];
+    const int n_units = prm.n_tiles * prm.nkv * prm.nsplit;
+    const int u_first = (int)(blockIdx.x >> 1), u_step = (int)(gridDim.x >> 1);
     const int G = prm.G, W = prm.window, tqc = prm.tq;
-    const int q0r = tile.q0 + (int)rank * tqc;  // this CTA's first query token
-    const int q_last = min(tile.q0 + 2 * tqc, tile.len) - 1;
-    const int k_lo = (W >= 0) ? max(0, tile.q0 - W) : 0;
-    const int k_hi = (W >= 0) ? min(tile.len, q_last + W + 1) : tile.len;
-    const int n_kt = tile.len > 0 ? (k_hi - k_lo + AP_BN - 1) / AP_BN : 0;
+    // Unit geometry: K/V head g, O half dsplit, the pair tile, this CTA's first query token, key range.
+    struct Unit {
+        AttnTile tile;
+        int g, dsplit, q0r, k_lo, n_kt;
+    };
+    auto unit_at = [&](int cid) {
+        Unit x;
+        const int tile_idx = cid / (prm.nkv * prm.nsplit);
+        const int rem = cid % (prm.nkv * prm.nsplit);
+        x.g = rem / prm.nsplit;
+        x.dsplit = rem % prm.nsplit;
+        x.tile = prm.tiles[tile_idx];
+        x.q0r = x.tile.q0 + (int)rank * tqc;
+        const int q_last = min(x.tile.q0 + 2 * tqc, x.tile.len) - 1;
+        x.k_lo = (W >= 0) ? max(0, x.tile.q0 - W) : 0;
+        const int k_hi = (W >= 0) ? min(x.tile.len, q_last + W + 1) : x.tile.len;
+        x.n_kt = x.tile.len > 0 ? (k_hi - x.k_lo + AP_BN - 1) / AP_BN : 0;
+        return x;
+    };
 
     if (threadIdx.x == 0) {
         mbar_init(q_full, 1);
@@ -129,6 +150,8 @@ __global__ void __launch_bounds__(ApCfg<DQK>::THREADS, 1)
             mbar_init(&p_full[b], SM_ARRIVALS);
             mbar_init(&pv_done[b], 1);
         }
+        mbar_init(q_empty, 1);
+        mbar_init(o_empty, SM_ARRIVALS);
         if constexpr (SPLIT)
             for (int x = 0; x < 8; x++) mbar_init(&xpair[x], 64);
         mbar_init(&drain[0], 1);
@@ -148,94 +171,120 @@ __global__ void __launch_bounds__(ApCfg<DQK>::THREADS, 1)
     const uint32_t t_o = tmem + 256;
     auto on_even = [&](uint64_t* b) { return mapa_shared(smem_u32(b), 0); };
 
-    if (n_kt == 0) goto done;
-
     if (warp == 0) {
         if (lane == 0) {
-            if (even) mbar_arrive_expect_tx(q_full, 2 * Cfg::Q_BYTES);
-            const uint32_t qbar = on_even(q_full);
-            for (int c = 0; c < Cfg::QCH; c++)
-                tma_load_3d_pair(smem + c * 128 * 128, &tmQ, qbar, c * 64, g * G, tile.row0 + q0r);
             int u = 0;
             uint32_t uph = 0;
-            // K unit ku of key tile jt: this CTA's 64 keys, channels [256 ku, 256 ku + 256), 4 boxes of
-            // [64 keys x 64 channels]. V unit: all 128 keys for this CTA's 128 channels of the O half,
-            // 2 boxes of [128 keys x 64 channels].
-            auto load_unit = [&](int ku, int jt) -> bool {
-                if (!mbar_wait(&r_empty[u], uph ^ 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) return false;
-                if (even) mbar_arrive_expect_tx(&r_full[u], 2 * AP_UNIT);
-                const uint32_t bar = on_even(&r_full[u]);
-                uint8_t* dst = smem + Cfg::OFF_R + u * AP_UNIT;
-                const int key0 = tile.row0 + k_lo + jt * AP_BN;
-                if (ku >= 0) {
-                    for (int c = 0; c < 4; c++)
-                        tma_load_3d_pair(dst + c * 8192, &tmK, bar, ku * 256 + c * 64, g, key0 + 64 * (int)rank);
-                } else {
-                    for (int c = 0; c < 2; c++)
-                        tma_load_3d_pair(dst + c * 16384, &tmV, bar, dsplit * ATT_DV + (2 * (int)rank + c) * 64, g, key0);
+            int U = 0;
+            for (int cid = u_first; cid < n_units; cid += u_step) {
+                const Unit x = unit_at(cid);
+                if (x.n_kt == 0) continue;
+                // K unit ku of key tile jt: this CTA's 64 keys, channels [256 ku, 256 ku + 256), 4 boxes
+                // of [64 keys x 64 channels]. V unit: all 128 keys for this CTA's 128 channels of the O
+                // half, 2 boxes of [128 keys x 64 channels].
+                auto load_unit = [&](int ku, int jt) -> bool {
+                    if (!mbar_wait(&r_empty[u], uph ^ 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) return false;
+                    if (even) mbar_arrive_expect_tx(&r_full[u], 2 * AP_UNIT);
+                    const uint32_t bar = on_even(&r_full[u]);
+                    uint8_t* dst = smem + Cfg::OFF_R + u * AP_UNIT;
+                    const int key0 = x.tile.row0 + x.k_lo + jt * AP_BN;
+                    if (ku >= 0) {
+                        for (int c = 0; c < 4; c++)
+                            tma_load_3d_pair(dst + c * 8192, &tmK, bar, ku * 256 + c * 64, x.g, key0 + 64 * (int)rank);
+                    } else {
+                        for (int c = 0; c < 2; c++)
+                            tma_load_3d_pair(dst + c * 16384, &tmV, bar, x.dsplit * ATT_DV + (2 * (int)rank + c) * 64, x.g,
+                                             key0);
+                    }
+                    if (++u == AP_UNITS) {
+                        u = 0;
+                        uph ^= 1;
+                    }
+                    return true;
+                };
+                for (int ku = 0; ku < KU; ku++)
+                    if (!load_unit(ku, 0)) goto done;
+                // Q: once every S MMA of the previous unit has completed.
+                if (U > 0 && !mbar_wait(q_empty, (U - 1) & 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) goto done;
+                if (even) mbar_arrive_expect_tx(q_full, 2 * Cfg::Q_BYTES);
+                const uint32_t qbar = on_even(q_full);
+                for (int c = 0; c < Cfg::QCH; c++)
+                    tma_load_3d_pair(smem + c * 128 * 128, &tmQ, qbar, c * 64, x.g * G, x.tile.row0 + x.q0r);
+                for (int j = 0; j < x.n_kt; j++) {
+                    if (j + 1 < x.n_kt)
+                        for (int ku = 0; ku < KU; ku++)
+                            if (!load_unit(ku, j + 1)) goto done;
+                    if (!load_unit(-1, j)) goto done;
                 }
-                if (++u == AP_UNITS) {
-                    u = 0;
-                    uph ^= 1;
-                }
-                return true;
-            };
-            for (int ku = 0; ku < KU; ku++)
-                if (!load_unit(ku, 0)) goto done;
-            for (int j = 0; j < n_kt; j++) {
-                if (j + 1 < n_kt)
-                    for (int ku = 0; ku < KU; ku++)
-                        if (!load_unit(ku, j + 1)) goto done;
-                if (!load_unit(-1, j)) goto done;
+                U++;
             }
         }
     } else if (warp == 1 || warp == Cfg::PV_WARP) {
         if (even && lane == 0) {
-            // Ring position of K(j) unit ku / V(j): the producer's order is K(0), then per tile j
-            // K(j + 1) (if any) and V(j).
-            auto unit_k = [&](int j, int ku) { return j == 0 ? ku : KU + (j - 1) * (KU + 1) + ku; };
-            auto unit_v = [&](int j) { return KU + j * (KU + 1) + (j + 1 < n_kt ? KU : 0); };
+            // Ring position (within a unit, from its first unit) of K(j) unit ku / V(j): the producer's
+            // order is K(0), then per tile j K(j + 1) (if any) and V(j); a unit takes n_kt (KU + 1).
+            int base = 0, T = 0, U = 0;
             if (warp == 1) {
                 constexpr uint32_t idesc_s = umma_idesc(256, AP_BN, 1);
                 const uint64_t dq0 = umma_desc_sw128(smem_u32(smem), 16, 1024);
                 const uint64_t dk0 = umma_desc_sw128(smem_u32(smem + Cfg::OFF_R), 16, 1024);
-                if (!mbar_wait(q_full, 0, EG2_DEV_TIMEOUT_ATTN, abort_flag)) goto done;
-                for (int j = 0; j < n_kt; j++) {
-                    // S is free once both CTAs' softmax(j - 1) have copied it into registers.
-                    if (!mbar_wait(s_empty, (j & 1) ^ 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) goto done;
-                    tc_fence_after();
-                    for (int ku = 0; ku < KU; ku++) {
-                        const int iu = unit_k(j, ku), u = iu % AP_UNITS;
-                        if (!mbar_wait(&r_full[u], (iu / AP_UNITS) & 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) goto done;
-                        const uint64_t db = dk0 + (uint64_t)(u * (AP_UNIT >> 4));
+                for (int cid = u_first; cid < n_units; cid += u_step) {
+                    const Unit x = unit_at(cid);
+                    const int n_kt = x.n_kt;
+                    if (n_kt == 0) continue;
+                    auto unit_k = [&](int j, int ku) { return base + (j == 0 ? ku : KU + (j - 1) * (KU + 1) + ku); };
+                    if (!mbar_wait(q_full, U & 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) goto done;
+                    for (int j = 0; j < n_kt; j++, T++) {
+                        // S is free once both CTAs' softmax(T - 1) have copied it into registers.
+                        if (!mbar_wait(s_empty, (T & 1) ^ 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) goto done;
+                        tc_fence_after();
+                        for (int ku = 0; ku < KU; ku++) {
+                            const int iu = unit_k(j, ku), u = iu % AP_UNITS;
+                            if (!mbar_wait(&r_full[u], (iu / AP_UNITS) & 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) goto done;
+                            const uint64_t db = dk0 + (uint64_t)(u * (AP_UNIT >> 4));
 #pragma unroll
-                        for (int c = 0; c < 4; c++) {
+                            for (int c = 0; c < 4; c++) {
 #pragma unroll
-                            for (int kk = 0; kk < 4; kk++)
-                                mma_bf16_pair(t_s, dq0 + (uint64_t)((4 * ku + c) * (16384 >> 4) + 2 * kk),
-                                              db + (uint64_t)(c * (8192 >> 4) + 2 * kk), idesc_s, (ku | c | kk) != 0);
+                                for (int kk = 0; kk < 4; kk++)
+                                    mma_bf16_pair(t_s, dq0 + (uint64_t)((4 * ku + c) * (16384 >> 4) + 2 * kk),
+                                                  db + (uint64_t)(c * (8192 >> 4) + 2 * kk), idesc_s, (ku | c | kk) != 0);
+                            }
+                            mma_commit_pair_both(&r_empty[u]);
                         }
-                        mma_commit_pair_both(&r_empty[u]);
+                        mma_commit_pair_both(s_full);
                     }
-                    mma_commit_pair_both(s_full);
+                    mma_commit_pair_both(q_empty);  // Q may be replaced once these MMAs are done
+                    base += n_kt * (KU + 1);
+                    U++;
                 }
             } else {
                 constexpr uint32_t idesc_o = umma_idesc(256, ATT_DV, 1, /*b_mn_major=*/true);
                 const uint64_t dv0 = umma_desc_sw128(smem_u32(smem + Cfg::OFF_R), 16384, 1024);
-                for (int j = 0; j < n_kt; j++) {
-                    const int b = j & 1;
-                    if (!mbar_wait(&p_full[b], (j >> 1) & 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) goto done;
-                    tc_fence_after();
-                    const int iu = unit_v(j), u = iu % AP_UNITS;
-                    if (!mbar_wait(&r_full[u], (iu / AP_UNITS) & 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) goto done;
-                    const uint64_t dv = dv0 + (uint64_t)(u * (AP_UNIT >> 4));
-                    // 16 keys per MMA: 8 packed P columns, 16 V rows (2048 bytes per 64-channel chunk).
+                for (int cid = u_first; cid < n_units; cid += u_step) {
+                    const Unit x = unit_at(cid);
+                    const int n_kt = x.n_kt;
+                    if (n_kt == 0) continue;
+                    auto unit_v = [&](int j) { return base + KU + j * (KU + 1) + (j + 1 < n_kt ? KU : 0); };
+                    for (int j = 0; j < n_kt; j++, T++) {
+                        const int b = T & 1;
+                        if (!mbar_wait(&p_full[b], (T >> 1) & 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) goto done;
+                        // The first P V of a unit overwrites O: the previous unit's O must have been read.
+                        if (j == 0 && U > 0 && !mbar_wait(o_empty, (U - 1) & 1, EG2_DEV_TIMEOUT_ATTN, abort_flag))
+                            goto done;
+                        tc_fence_after();
+                        const int iu = unit_v(j), u = iu % AP_UNITS;
+                        if (!mbar_wait(&r_full[u], (iu / AP_UNITS) & 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) goto done;
+                        const uint64_t dv = dv0 + (uint64_t)(u * (AP_UNIT >> 4));
+                        // 16 keys per MMA: 8 packed P columns, 16 V rows (2048 bytes per 64-channel chunk).
 #pragma unroll
-                    for (int kk = 0; kk < AP_BN / 16; kk++)
-                        mma_bf16_pair_ts(t_o, t_p + b * (AP_BN / 2) + kk * 8, dv + (uint64_t)(kk * (2048 >> 4)), idesc_o,
-                                         (j | kk) != 0);
-                    mma_commit_pair_both(&r_empty[u]);
-                    mma_commit_pair_both(&pv_done[b]);
+                        for (int kk = 0; kk < AP_BN / 16; kk++)
+                            mma_bf16_pair_ts(t_o, t_p + b * (AP_BN / 2) + kk * 8, dv + (uint64_t)(kk * (2048 >> 4)),
+                                             idesc_o, (j | kk) != 0);
+                        mma_commit_pair_both(&r_empty[u]);
+                        mma_commit_pair_both(&pv_done[b]);
+                    }
+                    base += n_kt * (KU + 1);
+                    U++;
                 }
             }
         }
@@ -246,147 +295,167 @@ __global__ void __launch_bounds__(ApCfg<DQK>::THREADS, 1)
         constexpr int NC = SPLIT ? 64 : 128;     // S columns per thread
         constexpr int OC = SPLIT ? 128 : 256;    // O columns per thread
         const int r = 32 * e + lane;
-        const int tok = q0r + r / G;
-        const bool row_valid = tok < tile.len;
         const uint32_t lane_off = (uint32_t)(32 * e) << 16;
         const float LOG2E = 1.4426950408889634f;
         float* xmax = reinterpret_cast<float*>(smem + Cfg::OFF_X);  // [slot][half][128]
         float* xsum = xmax + 2 * 2 * 128;                            // [half][128]
         // Arrivals for the MMA issuer go to the even CTA's barriers. What they guard is TMEM (S read,
-        // P written), ordered by tcgen05.wait + tcgen05.fence::before_thread_sync.
+        // P written, O read), ordered by tcgen05.wait + tcgen05.fence::before_thread_sync.
         auto arrive_even = [&](uint64_t* bar) {
             if (even) mbar_arrive(bar);
             else mbar_arrive_remote(on_even(bar));
         };
-        float m_used = -INFINITY, l = 0.f;
-        for (int j = 0; j < n_kt; j++) {
-            const int b = j & 1;
-            if (!mbar_wait(s_full, j & 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) break;
-            tc_fence_after();
-            float sv[NC];
-            {
-#pragma unroll
-                for (int c = 0; c < NC / 32; c++) {
-                    uint32_t s0[32];
-                    tmem_ld32(t_s + ch * 64 + 32 * c + lane_off, s0);
-                    tmem_ld_wait();
-#pragma unroll
-                    for (int q = 0; q < 32; q++) sv[32 * c + q] = __uint_as_float(s0[q]);
-                }
-                tc_fence_before();
-                arrive_even(s_empty);
-            }
-            // Valid key columns of this row in this tile, relative to this thread's first column.
-            const int kbase = k_lo + j * AP_BN + ch * 64;
-            int lo_c = 0, hi_c = min(NC, tile.len - kbase);
-            if (W >= 0 && row_valid) {
-                lo_c = max(lo_c, tok - W - kbase);
-                hi_c = min(hi_c, tok + W + 1 - kbase);
-            }
-            if (!__all_sync(0xffffffffu, lo_c <= 0 && hi_c >= NC)) {
-#pragma unroll
-                for (int c = 0; c < NC; c++) sv[c] = (c >= lo_c && c < hi_c) ? sv[c] : -INFINITY;
-            }
-            float mx[8];
-#pragma unroll
-            for (int c = 0; c < 8; c++) mx[c] = sv[c];
-#pragma unroll
-            for (int c = 8; c < NC; c++) mx[c & 7] = fmaxf(mx[c & 7], sv[c]);
-            float mt = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
-            if constexpr (SPLIT) {
-                // The row's other half: slots alternate by tile, so a slot is rewritten only after
-                // the partner has passed the next handshake (and read this one).
-                float* slot = xmax + (j & 1) * 256;
-                slot[ch * 128 + r] = mt;
-                mbar_arrive(&xpair[e * 2 + (j & 1)]);
-                if (!mbar_wait(&xpair[e * 2 + (j & 1)], (j >> 1) & 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) break;
-                mt = fmaxf(mt, *reinterpret_cast<volatile float*>(slot + (ch ^ 1) * 128 + r));
-            }
-            float factor = 1.f;
-            bool need = false;
-            if (mt > m_used) {
-                if (m_used == -INFINITY) {
-                    m_used = mt;
-                } else if ((mt - m_used) * LOG2E > ATT_RESCALE_LOG2) {
-                    factor = ex2_approx((m_used - mt) * LOG2E);
-                    m_used = mt;
-                    need = true;
-                }
-            }
-            if (__any_sync(0xffffffffu, need) && j >= 1) {
-                // O must hold every P V up to tile j - 1 before it is rescaled.
-                if (!mbar_wait(&pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) break;
-                tc_fence_after();
-#pragma unroll 1
-                for (int c = 0; c < OC / 32; c++) {
-                    uint32_t o[32];
-                    tmem_ld32(t_o + ch * 128 + c * 32 + lane_off, o);
-                    tmem_ld_wait();
-#pragma unroll
-                    for (int q = 0; q < 32; q++) o[q] = __float_as_uint(__uint_as_float(o[q]) * factor);
-                    tmem_st32(t_o + ch * 128 + c * 32 + lane_off, o);
-                }
-                tmem_st_wait();
-            }
-            l *= factor;
-            // P buffer b was last read by P V(j - 2).
-            if (j >= 2) {
-                if (!mbar_wait(&pv_done[b], ((j - 2) >> 1) & 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) break;
-                tc_fence_after();
-            }
-            // Row sum over the bf16-ROUNDED probabilities that multiply V (weights sum to exactly l).
-            const float bias = (m_used == -INFINITY) ? 0.f : -m_used * LOG2E;
-            float lsum[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-            for (int half = 0; half < NC / 64; half++) {
-                uint32_t pk[32];
-#pragma unroll
-                for (int q = 0; q < 32; q++) {
-                    const float p0 = ex2_approx(fmaf(sv[64 * half + 2 * q], LOG2E, bias));
-                    const float p1 = ex2_approx(fmaf(sv[64 * half + 2 * q + 1], LOG2E, bias));
-                    pk[q] = bf16x2_bits(p0, p1);
-                    lsum[q & 3] += __uint_as_float(pk[q] << 16) + __uint_as_float(pk[q] & 0xffff0000u);
-                }
-                tmem_st32(t_p + b * (AP_BN / 2) + 32 * (ch + half) + lane_off, pk);
-            }
-            l += (lsum[0] + lsum[1]) + (lsum[2] + lsum[3]);
-            tmem_st_wait();
-            tc_fence_before();
-            arrive_even(&p_full[b]);
-        }
-        if (!*abort_flag &&
-            mbar_wait(&pv_done[(n_kt - 1) & 1], ((n_kt - 1) >> 1) & 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) {
+        int T = 0, X = 0;
+        for (int cid = u_first; cid < n_units; cid += u_step) {
+            const Unit x = unit_at(cid);
+            const int n_kt = x.n_kt;
+            if (n_kt == 0) continue;
+            const AttnTile& tile = x.tile;
+            const int tok = x.q0r + r / G;
+            const bool row_valid = tok < tile.len;
             bool ok = true;
-            if constexpr (SPLIT) {
-                // Both halves' row sums (the same stale max scaled both); the handshake slot after the
-                // last tile's is free for this one use.
-                xsum[ch * 128 + r] = l;
-                uint64_t* xb = &xpair[e * 2 + (n_kt & 1)];
-                mbar_arrive(xb);
-                ok = mbar_wait(xb, (n_kt >> 1) & 1, EG2_DEV_TIMEOUT_ATTN, abort_flag);
-                if (ok) l += *reinterpret_cast<volatile float*>(xsum + (ch ^ 1) * 128 + r);
-            }
-            if (ok) {
+            float m_used = -INFINITY, l = 0.f;
+            for (int j = 0; j < n_kt; j++, T++) {
+                const int b = T & 1;
+                if (!mbar_wait(s_full, T & 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) {
+                    ok = false;
+                    break;
+                }
                 tc_fence_after();
-                const float inv = (l > 0.f) ? 1.f / l : 0.f;
-                const int head = g * G + r % G;
-                bf16_t* orow = prm.out + ((long)(tile.row0 + tok) * prm.nh + head) * prm.hd + dsplit * ATT_DV + ch * 128;
-#pragma unroll 1
-                for (int c = 0; c < OC / 32; c++) {
-                    uint32_t o[32];
-                    tmem_ld32(t_o + ch * 128 + c * 32 + lane_off, o);
-                    tmem_ld_wait();
-                    if (row_valid) {
-                        uint4* d = reinterpret_cast<uint4*>(orow + c * 32);
+                float sv[NC];
+                {
 #pragma unroll
-                        for (int q = 0; q < 4; q++)
-                            d[q] = make_uint4(pack_bf16x2(__uint_as_float(o[8 * q + 0]) * inv, __uint_as_float(o[8 * q + 1]) * inv),
-                                              pack_bf16x2(__uint_as_float(o[8 * q + 2]) * inv, __uint_as_float(o[8 * q + 3]) * inv),
-                                              pack_bf16x2(__uint_as_float(o[8 * q + 4]) * inv, __uint_as_float(o[8 * q + 5]) * inv),
-                                              pack_bf16x2(__uint_as_float(o[8 * q + 6]) * inv, __uint_as_float(o[8 * q + 7]) * inv));
+                    for (int c = 0; c < NC / 32; c++) {
+                        uint32_t s0[32];
+                        tmem_ld32(t_s + ch * 64 + 32 * c + lane_off, s0);
+                        tmem_ld_wait();
+#pragma unroll
+                        for (int q = 0; q < 32; q++) sv[32 * c + q] = __uint_as_float(s0[q]);
+                    }
+                    tc_fence_before();
+                    arrive_even(s_empty);
+                }
+                // Valid key columns of this row in this tile, relative to this thread's first column.
+                const int kbase = x.k_lo + j * AP_BN + ch * 64;
+                int lo_c = 0, hi_c = min(NC, tile.len - kbase);
+                if (W >= 0 && row_valid) {
+                    lo_c = max(lo_c, tok - W - kbase);
+                    hi_c = min(hi_c, tok + W + 1 - kbase);
+                }
+                if (!__all_sync(0xffffffffu, lo_c <= 0 && hi_c >= NC)) {
+#pragma unroll
+                    for (int c = 0; c < NC; c++) sv[c] = (c >= lo_c && c < hi_c) ? sv[c] : -INFINITY;
+                }
+                float mx[8];
+#pragma unroll
+                for (int c = 0; c < 8; c++) mx[c] = sv[c];
+#pragma unroll
+                for (int c = 8; c < NC; c++) mx[c & 7] = fmaxf(mx[c & 7], sv[c]);
+                float mt = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+                if constexpr (SPLIT) {
+                    // The row's other half: slots alternate by handshake, so a slot is rewritten only
+                    // after the partner has passed the next handshake (and read this one).
+                    float* slot = xmax + (X & 1) * 256;
+                    slot[ch * 128 + r] = mt;
+                    mbar_arrive(&xpair[e * 2 + (X & 1)]);
+                    if (!mbar_wait(&xpair[e * 2 + (X & 1)], (X >> 1) & 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    mt = fmaxf(mt, *reinterpret_cast<volatile float*>(slot + (ch ^ 1) * 128 + r));
+                    X++;
+                }
+                float factor = 1.f;
+                bool need = false;
+                if (mt > m_used) {
+                    if (m_used == -INFINITY) {
+                        m_used = mt;
+                    } else if ((mt - m_used) * LOG2E > ATT_RESCALE_LOG2) {
+                        factor = ex2_approx((m_used - mt) * LOG2E);
+                        m_used = mt;
+                        need = true;
                     }
                 }
+                if (__any_sync(0xffffffffu, need) && j >= 1) {
+                    // O must hold every P V up to tile T - 1 before it is rescaled.
+                    if (!mbar_wait(&pv_done[(T - 1) & 1], ((T - 1) >> 1) & 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+#pragma unroll 1
+                    for (int c = 0; c < OC / 32; c++) {
+                        uint32_t o[32];
+                        tmem_ld32(t_o + ch * 128 + c * 32 + lane_off, o);
+                        tmem_ld_wait();
+#pragma unroll
+                        for (int q = 0; q < 32; q++) o[q] = __float_as_uint(__uint_as_float(o[q]) * factor);
+                        tmem_st32(t_o + ch * 128 + c * 32 + lane_off, o);
+                    }
+                    tmem_st_wait();
+                }
+                l *= factor;
+                // P buffer b was last read by P V(T - 2) (possibly of the previous unit).
+                if (T >= 2) {
+                    if (!mbar_wait(&pv_done[b], ((T - 2) >> 1) & 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                }
+                // Row sum over the bf16-ROUNDED probabilities that multiply V (weights sum to exactly l).
+                const float bias = (m_used == -INFINITY) ? 0.f : -m_used * LOG2E;
+                float lsum[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+                for (int half = 0; half < NC / 64; half++) {
+                    uint32_t pk[32];
+#pragma unroll
+                    for (int q = 0; q < 32; q++) {
+                        const float p0 = ex2_approx(fmaf(sv[64 * half + 2 * q], LOG2E, bias));
+                        const float p1 = ex2_approx(fmaf(sv[64 * half + 2 * q + 1], LOG2E, bias));
+                        pk[q] = bf16x2_bits(p0, p1);
+                        lsum[q & 3] += __uint_as_float(pk[q] << 16) + __uint_as_float(pk[q] & 0xffff0000u);
+                    }
+                    tmem_st32(t_p + b * (AP_BN / 2) + 32 * (ch + half) + lane_off, pk);
+                }
+                l += (lsum[0] + lsum[1]) + (lsum[2] + lsum[3]);
+                tmem_st_wait();
+                tc_fence_before();
+                arrive_even(&p_full[b]);
             }
+            if (!ok || *abort_flag) break;
+            if (!mbar_wait(&pv_done[(T - 1) & 1], ((T - 1) >> 1) & 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) break;
+            if constexpr (SPLIT) {
+                // Both halves' row sums (the same stale max scaled both), through the next handshake.
+                xsum[ch * 128 + r] = l;
+                uint64_t* xb = &xpair[e * 2 + (X & 1)];
+                mbar_arrive(xb);
+                if (!mbar_wait(xb, (X >> 1) & 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) break;
+                l += *reinterpret_cast<volatile float*>(xsum + (ch ^ 1) * 128 + r);
+                X++;
+            }
+            tc_fence_after();
+            const float inv = (l > 0.f) ? 1.f / l : 0.f;
+            const int head = x.g * G + r % G;
+            bf16_t* orow = prm.out + ((long)(tile.row0 + tok) * prm.nh + head) * prm.hd + x.dsplit * ATT_DV + ch * 128;
+#pragma unroll 1
+            for (int c = 0; c < OC / 32; c++) {
+                uint32_t o[32];
+                tmem_ld32(t_o + ch * 128 + c * 32 + lane_off, o);
+                tmem_ld_wait();
+                if (row_valid) {
+                    uint4* d = reinterpret_cast<uint4*>(orow + c * 32);
+#pragma unroll
+                    for (int q = 0; q < 4; q++)
+                        d[q] = make_uint4(pack_bf16x2(__uint_as_float(o[8 * q + 0]) * inv, __uint_as_float(o[8 * q + 1]) * inv),
+                                          pack_bf16x2(__uint_as_float(o[8 * q + 2]) * inv, __uint_as_float(o[8 * q + 3]) * inv),
+                                          pack_bf16x2(__uint_as_float(o[8 * q + 4]) * inv, __uint_as_float(o[8 * q + 5]) * inv),
+                                          pack_bf16x2(__uint_as_float(o[8 * q + 6]) * inv, __uint_as_float(o[8 * q + 7]) * inv));
+                }
+            }
+            // O has been read: the next unit's first P V may overwrite it.
+            tc_fence_before();
+            arrive_even(o_empty);
         }
     }
 done:
@@ -415,28 +484,36 @@ int attention_tc_tile_tokens(int nh, int nkv, int hd) {
     return 256 / G;
 }
 
+// As many clusters as can be resident at once (at most one per work unit); each walks its units.
 template <int DQK>
 static int launch_pair(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const AttParams& prm,
-                       int n_tiles, cudaStream_t s) {
+                       cudaStream_t s) {
     using Cfg = ApCfg<DQK>;
     auto kern = attention_pair_kernel<DQK>;
-    static bool attr = false;
-    if (!attr) {
-        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM) != cudaSuccess) return -3;
-        attr = true;
-    }
+    static int max_clusters[64] = {0};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -3;
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute la[1];
     la[0].id = cudaLaunchAttributeClusterDimension;
     la[0].val.clusterDim.x = 2;
     la[0].val.clusterDim.y = 1;
     la[0].val.clusterDim.z = 1;
-    cfg.gridDim = dim3((unsigned)(2L * n_tiles * prm.nkv * prm.nsplit), 1, 1);
     cfg.blockDim = dim3(Cfg::THREADS, 1, 1);
     cfg.dynamicSmemBytes = Cfg::SMEM;
     cfg.stream = s;
     cfg.attrs = la;
     cfg.numAttrs = 1;
+    if (!max_clusters[dev]) {
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM) != cudaSuccess) return -3;
+        cfg.gridDim = dim3(2 * num_sms(), 1, 1);
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) return -3;
+        max_clusters[dev] = n;
+    }
+    const long units = (long)prm.n_tiles * prm.nkv * prm.nsplit;
+    const int clusters = units < max_clusters[dev] ? (int)units : max_clusters[dev];
+    cfg.gridDim = dim3((unsigned)(2 * clusters), 1, 1);
     return cudaLaunchKernelEx(&cfg, kern, mq, mk, mv, prm) == cudaSuccess ? 0 : -3;
 }
 
@@ -463,8 +540,9 @@ int attention_tc(const bf16_t* q, const bf16_t* k, const bf16_t* v, bf16_t* out,
     prm.G = G;
     prm.tq = tq;
     prm.nsplit = hd / ATT_DV;
-    // CTA pairs: clusters of 2, one per (pair tile, K/V head, 256-channel half of O).
-    return hd == 256 ? launch_pair<256>(mq, mk, mv, prm, n_tiles, s) : launch_pair<512>(mq, mk, mv, prm, n_tiles, s);
+    prm.n_tiles = n_tiles;
+    // CTA pairs: clusters of 2 walking the (pair tile, K/V head, 256-channel half of O) units.
+    return hd == 256 ? launch_pair<256>(mq, mk, mv, prm, s) : launch_pair<512>(mq, mk, mv, prm, s);
 }
 
 
