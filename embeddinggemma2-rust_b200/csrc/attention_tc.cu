@@ -306,6 +306,50 @@ __global__ void __launch_bounds__(ApCfg<DQK>::THREADS, 1)
             else mbar_arrive_remote(on_even(bar));
         };
         int T = 0, X = 0;
+        bool ok = true;
+        // The O epilogue of a unit runs after the next unit's first P has been written (so that P does
+        // not wait behind it); pend / pu / pl / pT: the unit waiting for it, its row sum, its last tile.
+        bool pend = false;
+        Unit pu;
+        float pl = 0.f;
+        int pT = 0;
+        auto finish = [&]() -> bool {
+            if (!mbar_wait(&pv_done[pT & 1], (pT >> 1) & 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) return false;
+            float lt = pl;
+            if constexpr (SPLIT) {
+                // Both halves' row sums (the same stale max scaled both), through the next handshake.
+                xsum[ch * 128 + r] = lt;
+                uint64_t* xb = &xpair[e * 2 + (X & 1)];
+                mbar_arrive(xb);
+                if (!mbar_wait(xb, (X >> 1) & 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) return false;
+                lt += *reinterpret_cast<volatile float*>(xsum + (ch ^ 1) * 128 + r);
+                X++;
+            }
+            tc_fence_after();
+            const float inv = (lt > 0.f) ? 1.f / lt : 0.f;
+            const int ptok = pu.q0r + r / G;
+            const int head = pu.g * G + r % G;
+            bf16_t* orow = prm.out + ((long)(pu.tile.row0 + ptok) * prm.nh + head) * prm.hd + pu.dsplit * ATT_DV + ch * 128;
+#pragma unroll 1
+            for (int c = 0; c < OC / 32; c++) {
+                uint32_t o[32];
+                tmem_ld32(t_o + ch * 128 + c * 32 + lane_off, o);
+                tmem_ld_wait();
+                if (ptok < pu.tile.len) {
+                    uint4* d = reinterpret_cast<uint4*>(orow + c * 32);
+#pragma unroll
+                    for (int q = 0; q < 4; q++)
+                        d[q] = make_uint4(pack_bf16x2(__uint_as_float(o[8 * q + 0]) * inv, __uint_as_float(o[8 * q + 1]) * inv),
+                                          pack_bf16x2(__uint_as_float(o[8 * q + 2]) * inv, __uint_as_float(o[8 * q + 3]) * inv),
+                                          pack_bf16x2(__uint_as_float(o[8 * q + 4]) * inv, __uint_as_float(o[8 * q + 5]) * inv),
+                                          pack_bf16x2(__uint_as_float(o[8 * q + 6]) * inv, __uint_as_float(o[8 * q + 7]) * inv));
+                }
+            }
+            // O has been read: the next unit's first P V may overwrite it.
+            tc_fence_before();
+            arrive_even(o_empty);
+            return true;
+        };
         for (int cid = u_first; cid < n_units; cid += u_step) {
             const Unit x = unit_at(cid);
             const int n_kt = x.n_kt;
@@ -313,7 +357,6 @@ __global__ void __launch_bounds__(ApCfg<DQK>::THREADS, 1)
             const AttnTile& tile = x.tile;
             const int tok = x.q0r + r / G;
             const bool row_valid = tok < tile.len;
-            bool ok = true;
             float m_used = -INFINITY, l = 0.f;
             for (int j = 0; j < n_kt; j++, T++) {
                 const int b = T & 1;
@@ -422,41 +465,21 @@ __global__ void __launch_bounds__(ApCfg<DQK>::THREADS, 1)
                 tmem_st_wait();
                 tc_fence_before();
                 arrive_even(&p_full[b]);
-            }
-            if (!ok || *abort_flag) break;
-            if (!mbar_wait(&pv_done[(T - 1) & 1], ((T - 1) >> 1) & 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) break;
-            if constexpr (SPLIT) {
-                // Both halves' row sums (the same stale max scaled both), through the next handshake.
-                xsum[ch * 128 + r] = l;
-                uint64_t* xb = &xpair[e * 2 + (X & 1)];
-                mbar_arrive(xb);
-                if (!mbar_wait(xb, (X >> 1) & 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) break;
-                l += *reinterpret_cast<volatile float*>(xsum + (ch ^ 1) * 128 + r);
-                X++;
-            }
-            tc_fence_after();
-            const float inv = (l > 0.f) ? 1.f / l : 0.f;
-            const int head = x.g * G + r % G;
-            bf16_t* orow = prm.out + ((long)(tile.row0 + tok) * prm.nh + head) * prm.hd + x.dsplit * ATT_DV + ch * 128;
-#pragma unroll 1
-            for (int c = 0; c < OC / 32; c++) {
-                uint32_t o[32];
-                tmem_ld32(t_o + ch * 128 + c * 32 + lane_off, o);
-                tmem_ld_wait();
-                if (row_valid) {
-                    uint4* d = reinterpret_cast<uint4*>(orow + c * 32);
-#pragma unroll
-                    for (int q = 0; q < 4; q++)
-                        d[q] = make_uint4(pack_bf16x2(__uint_as_float(o[8 * q + 0]) * inv, __uint_as_float(o[8 * q + 1]) * inv),
-                                          pack_bf16x2(__uint_as_float(o[8 * q + 2]) * inv, __uint_as_float(o[8 * q + 3]) * inv),
-                                          pack_bf16x2(__uint_as_float(o[8 * q + 4]) * inv, __uint_as_float(o[8 * q + 5]) * inv),
-                                          pack_bf16x2(__uint_as_float(o[8 * q + 6]) * inv, __uint_as_float(o[8 * q + 7]) * inv));
+                if (j == 0 && pend) {
+                    pend = false;
+                    if (!finish()) {
+                        ok = false;
+                        break;
+                    }
                 }
             }
-            // O has been read: the next unit's first P V may overwrite it.
-            tc_fence_before();
-            arrive_even(o_empty);
+            if (!ok || *abort_flag) break;
+            pend = true;
+            pu = x;
+            pl = l;
+            pT = T - 1;
         }
+        if (pend && ok && !*abort_flag) finish();
     }
 done:
     // Every MMA the even CTA issued (into both CTAs' TMEM) has completed before either CTA frees it:
