@@ -39,12 +39,17 @@ struct AttParams {
 // tiles' windows; each row masks its own. Head 512: O is produced 256 channels at a time, so two
 // clusters share each pair of query tiles (one per channel half), each computing the full S.
 //
-// TMEM per CTA: S [0, 128), P[0] [128, 192), P[1] [192, 256) (packed bf16), O [256, 512). Per CTA
-// shared memory: Q (64 / 128 KB) and a ring of 32 KB units (5 / 3), consumed in order K(j + 1),
-// V(j); a K unit is 64 keys x 256 channels (head 512: two per tile), a V unit 128 keys x 128
-// channels. The even CTA's barriers collect both CTAs' TMA bytes (q_full, r_full) and both CTAs'
-// softmax arrivals (s_empty, p_full: 256); MMA completion is committed to the barriers of both
-// CTAs (r_empty, s_full, pv_done).
+// TMEM per CTA, O at [256, 512). Head 512 (SDB): two S buffers [0, 128) and [128, 256); tile T's S
+// goes to buffer T % 2 and its P (packed bf16, 64 columns) over the first half of that S once the
+// softmax has read it, so S(T + 1) is computed while the softmax works on T and S(T) waits only for
+// P V(T - 2), the last reader of its buffer (the tensor work per tile, 3,072 cycles, exceeds the
+// softmax's). Head 256: one S [0, 128) and P[0] [128, 192), P[1] [192, 256); S(T) waits until the
+// softmax has read S(T - 1) (s_empty) -- its softmax takes about as long as its 2,048 cycles of
+// tensor work, and chaining P V(T - 2) -> S(T) measured 15% slower. Per CTA shared memory: Q (64 / 128 KB) and a ring of 32 KB units (4 / 3), consumed
+// in order K(j + 1), V(j); a K unit is 64 keys x 256 channels (head 512: two per tile), a V unit 128
+// keys x 128 channels. The even CTA's barriers collect both CTAs' TMA bytes (q_full, r_full) and both
+// CTAs' softmax arrivals (p_full, o_empty: 256); MMA completion is committed to the barriers of both
+// CTAs (r_empty, s_full, pv_done, q_empty).
 //
 //   warp 0      TMA producer (this CTA's Q and its half of every unit)
 //   warp 1      TMEM allocation (both CTAs); in the even CTA lane 0 issues the S = Q K^T MMAs
@@ -71,9 +76,9 @@ struct ApCfg {
     static constexpr int UNITS = DQK == 256 ? 4 : 3;
     static constexpr int OFF_R = Q_BYTES;
     static constexpr int OFF_BAR = OFF_R + UNITS * AP_UNIT;
-    // q, ring full/empty, s full/empty, p[2], pv[2], drain[2], q_empty, o_empty; split softmax: pair
-    // handshakes [4 quadrants][2]
-    static constexpr int N_BARS = 1 + 2 * UNITS + 2 + 4 + 2 + 2 + (SPLIT ? 8 : 0);
+    // q, ring full/empty, s_full[2], s_empty, p[2], pv[2], drain[2], q_empty, o_empty; split softmax:
+    // pair handshakes [4 quadrants][2]
+    static constexpr int N_BARS = 1 + 2 * UNITS + 3 + 4 + 2 + 2 + (SPLIT ? 8 : 0);
     static constexpr int OFF_X = OFF_BAR + N_BARS * 8 + 16;  // split softmax: maxima [2 slots][2 halves][128], sums [2][128]
     static constexpr int SMEM = 1024 + OFF_X + (SPLIT ? 3 * 1024 : 0);
 };
@@ -84,7 +89,7 @@ static_assert(ApCfg<256>::SMEM <= 227 * 1024 && ApCfg<512>::SMEM <= 227 * 1024, 
 // unit boundary the next unit's Q load (once every S MMA of the previous unit has completed:
 // q_empty) and its first S = Q K^T run under the previous unit's last P V and O epilogue; its first
 // P V waits until the softmax threads have read O out (o_empty). Barrier phases follow running
-// counts: T = key tiles so far (s_full / s_empty, p_full / pv_done), X = split-softmax handshakes,
+// counts: T = key tiles so far (s_full, p_full, pv_done), X = split-softmax handshakes,
 // U = units with keys so far (q_full, q_empty, o_empty); units without keys are skipped by every role.
 template <int DQK>
 __global__ void __launch_bounds__(ApCfg<DQK>::THREADS, 1)
@@ -92,6 +97,7 @@ __global__ void __launch_bounds__(ApCfg<DQK>::THREADS, 1)
                           const __grid_constant__ CUtensorMap tmV, AttParams prm) {
     using Cfg = ApCfg<DQK>;
     constexpr bool SPLIT = Cfg::SPLIT;
+    constexpr bool SDB = DQK == 512;  // double-buffered S, P over S
     constexpr int SM_ARRIVALS = 2 * 32 * Cfg::NSW;  // softmax threads of both CTAs
     constexpr int AP_UNITS = Cfg::UNITS;
     constexpr int KU = Cfg::KU;
@@ -101,8 +107,8 @@ __global__ void __launch_bounds__(ApCfg<DQK>::THREADS, 1)
     uint64_t* q_full = bars;
     uint64_t* r_full = bars + 1;
     uint64_t* r_empty = r_full + AP_UNITS;
-    uint64_t* s_full = r_empty + AP_UNITS;
-    uint64_t* s_empty = s_full + 1;
+    uint64_t* s_full = r_empty + AP_UNITS;  // [2]: S buffer (head 256: [0] only)
+    uint64_t* s_empty = s_full + 2;         // head 256: S read by both CTAs' softmax threads
     uint64_t* p_full = s_empty + 1;
     uint64_t* pv_done = p_full + 2;
     uint64_t* drain = pv_done + 2;
@@ -144,7 +150,8 @@ __global__ void __launch_bounds__(ApCfg<DQK>::THREADS, 1)
             mbar_init(&r_full[u], 1);
             mbar_init(&r_empty[u], 1);
         }
-        mbar_init(s_full, 1);
+        mbar_init(&s_full[0], 1);
+        mbar_init(&s_full[1], 1);
         mbar_init(s_empty, SM_ARRIVALS);
         for (int b = 0; b < 2; b++) {
             mbar_init(&p_full[b], SM_ARRIVALS);
@@ -166,7 +173,7 @@ __global__ void __launch_bounds__(ApCfg<DQK>::THREADS, 1)
     // Both CTAs' barriers are initialised (and TMEM allocated) before either CTA touches the other's.
     cluster_sync();
     const uint32_t tmem = *tmem_slot;
-    const uint32_t t_s = tmem;
+    const uint32_t t_s = tmem;  // SDB: S / P buffer b at t_s + 128 b; else S at t_s, P[b] at t_p + 64 b
     const uint32_t t_p = tmem + 128;
     const uint32_t t_o = tmem + 256;
     auto on_even = [&](uint64_t* b) { return mapa_shared(smem_u32(b), 0); };
@@ -235,9 +242,17 @@ __global__ void __launch_bounds__(ApCfg<DQK>::THREADS, 1)
                     auto unit_k = [&](int j, int ku) { return base + (j == 0 ? ku : KU + (j - 1) * (KU + 1) + ku); };
                     if (!mbar_wait(q_full, U & 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) goto done;
                     for (int j = 0; j < n_kt; j++, T++) {
-                        // S is free once both CTAs' softmax(T - 1) have copied it into registers.
-                        if (!mbar_wait(s_empty, (T & 1) ^ 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) goto done;
+                        if constexpr (SDB) {
+                            // S buffer T % 2 was last read by P V(T - 2) (its P; its S before that).
+                            if (T >= 2 &&
+                                !mbar_wait(&pv_done[T & 1], ((T - 2) >> 1) & 1, EG2_DEV_TIMEOUT_ATTN, abort_flag))
+                                goto done;
+                        } else {
+                            // S is free once both CTAs' softmax(T - 1) have copied it into registers.
+                            if (!mbar_wait(s_empty, (T & 1) ^ 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) goto done;
+                        }
                         tc_fence_after();
+                        const uint32_t t_sb = SDB ? t_s + (uint32_t)(T & 1) * 128 : t_s;
                         for (int ku = 0; ku < KU; ku++) {
                             const int iu = unit_k(j, ku), u = iu % AP_UNITS;
                             if (!mbar_wait(&r_full[u], (iu / AP_UNITS) & 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) goto done;
@@ -246,12 +261,12 @@ __global__ void __launch_bounds__(ApCfg<DQK>::THREADS, 1)
                             for (int c = 0; c < 4; c++) {
 #pragma unroll
                                 for (int kk = 0; kk < 4; kk++)
-                                    mma_bf16_pair(t_s, dq0 + (uint64_t)((4 * ku + c) * (16384 >> 4) + 2 * kk),
+                                    mma_bf16_pair(t_sb, dq0 + (uint64_t)((4 * ku + c) * (16384 >> 4) + 2 * kk),
                                                   db + (uint64_t)(c * (8192 >> 4) + 2 * kk), idesc_s, (ku | c | kk) != 0);
                             }
                             mma_commit_pair_both(&r_empty[u]);
                         }
-                        mma_commit_pair_both(s_full);
+                        mma_commit_pair_both(&s_full[SDB ? (T & 1) : 0]);
                     }
                     mma_commit_pair_both(q_empty);  // Q may be replaced once these MMAs are done
                     base += n_kt * (KU + 1);
@@ -278,7 +293,8 @@ __global__ void __launch_bounds__(ApCfg<DQK>::THREADS, 1)
                         // 16 keys per MMA: 8 packed P columns, 16 V rows (2048 bytes per 64-channel chunk).
 #pragma unroll
                         for (int kk = 0; kk < AP_BN / 16; kk++)
-                            mma_bf16_pair_ts(t_o, t_p + b * (AP_BN / 2) + kk * 8, dv + (uint64_t)(kk * (2048 >> 4)),
+                            mma_bf16_pair_ts(t_o, (SDB ? t_s + b * 128 : t_p + b * (AP_BN / 2)) + kk * 8,
+                                             dv + (uint64_t)(kk * (2048 >> 4)),
                                              idesc_o, (j | kk) != 0);
                         mma_commit_pair_both(&r_empty[u]);
                         mma_commit_pair_both(&pv_done[b]);
@@ -330,21 +346,19 @@ __global__ void __launch_bounds__(ApCfg<DQK>::THREADS, 1)
             const int ptok = pu.q0r + r / G;
             const int head = pu.g * G + r % G;
             bf16_t* orow = prm.out + ((long)(pu.tile.row0 + ptok) * prm.nh + head) * prm.hd + pu.dsplit * ATT_DV + ch * 128;
-#pragma unroll 1
-            for (int c = 0; c < OC / 32; c++) {
-                uint32_t o[32];
-                tmem_ld32(t_o + ch * 128 + c * 32 + lane_off, o);
-                tmem_ld_wait();
-                if (ptok < pu.tile.len) {
+            const bool live = ptok < pu.tile.len;
+            tmem_pipelined<32>(t_o + ch * 128 + lane_off, OC / 32, [&](int c, uint32_t(&o)[32]) -> bool {
+                if (live) {
                     uint4* d = reinterpret_cast<uint4*>(orow + c * 32);
 #pragma unroll
                     for (int q = 0; q < 4; q++)
-                        d[q] = make_uint4(pack_bf16x2(__uint_as_float(o[8 * q + 0]) * inv, __uint_as_float(o[8 * q + 1]) * inv),
-                                          pack_bf16x2(__uint_as_float(o[8 * q + 2]) * inv, __uint_as_float(o[8 * q + 3]) * inv),
-                                          pack_bf16x2(__uint_as_float(o[8 * q + 4]) * inv, __uint_as_float(o[8 * q + 5]) * inv),
-                                          pack_bf16x2(__uint_as_float(o[8 * q + 6]) * inv, __uint_as_float(o[8 * q + 7]) * inv));
+                        d[q] = make_uint4(bf16x2_bits(__uint_as_float(o[8 * q + 0]) * inv, __uint_as_float(o[8 * q + 1]) * inv),
+                                          bf16x2_bits(__uint_as_float(o[8 * q + 2]) * inv, __uint_as_float(o[8 * q + 3]) * inv),
+                                          bf16x2_bits(__uint_as_float(o[8 * q + 4]) * inv, __uint_as_float(o[8 * q + 5]) * inv),
+                                          bf16x2_bits(__uint_as_float(o[8 * q + 6]) * inv, __uint_as_float(o[8 * q + 7]) * inv));
                 }
-            }
+                return true;
+            });
             // O has been read: the next unit's first P V may overwrite it.
             tc_fence_before();
             arrive_even(o_empty);
@@ -360,7 +374,8 @@ __global__ void __launch_bounds__(ApCfg<DQK>::THREADS, 1)
             float m_used = -INFINITY, l = 0.f;
             for (int j = 0; j < n_kt; j++, T++) {
                 const int b = T & 1;
-                if (!mbar_wait(s_full, T & 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) {
+                const uint32_t t_sb = SDB ? t_s + (uint32_t)b * 128 : t_s;
+                if (!mbar_wait(&s_full[SDB ? b : 0], SDB ? (T >> 1) & 1 : T & 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) {
                     ok = false;
                     break;
                 }
@@ -370,13 +385,15 @@ __global__ void __launch_bounds__(ApCfg<DQK>::THREADS, 1)
 #pragma unroll
                     for (int c = 0; c < NC / 32; c++) {
                         uint32_t s0[32];
-                        tmem_ld32(t_s + ch * 64 + 32 * c + lane_off, s0);
+                        tmem_ld32(t_sb + ch * 64 + 32 * c + lane_off, s0);
                         tmem_ld_wait();
 #pragma unroll
                         for (int q = 0; q < 32; q++) sv[32 * c + q] = __uint_as_float(s0[q]);
                     }
-                    tc_fence_before();
-                    arrive_even(s_empty);
+                    if constexpr (!SDB) {
+                        tc_fence_before();
+                        arrive_even(s_empty);
+                    }
                 }
                 // Valid key columns of this row in this tile, relative to this thread's first column.
                 const int kbase = x.k_lo + j * AP_BN + ch * 64;
@@ -438,8 +455,10 @@ __global__ void __launch_bounds__(ApCfg<DQK>::THREADS, 1)
                     tmem_st_wait();
                 }
                 l *= factor;
-                // P buffer b was last read by P V(T - 2) (possibly of the previous unit).
-                if (T >= 2) {
+                if constexpr (SDB) {
+                    // P goes over S in buffer b: this thread has read its S.
+                } else if (T >= 2) {
+                    // P buffer b was last read by P V(T - 2) (possibly of the previous unit).
                     if (!mbar_wait(&pv_done[b], ((T - 2) >> 1) & 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) {
                         ok = false;
                         break;
@@ -459,7 +478,7 @@ __global__ void __launch_bounds__(ApCfg<DQK>::THREADS, 1)
                         pk[q] = bf16x2_bits(p0, p1);
                         lsum[q & 3] += __uint_as_float(pk[q] << 16) + __uint_as_float(pk[q] & 0xffff0000u);
                     }
-                    tmem_st32(t_p + b * (AP_BN / 2) + 32 * (ch + half) + lane_off, pk);
+                    tmem_st32((SDB ? t_sb : t_p + b * (AP_BN / 2)) + 32 * (ch + half) + lane_off, pk);
                 }
                 l += (lsum[0] + lsum[1]) + (lsum[2] + lsum[3]);
                 tmem_st_wait();

@@ -387,6 +387,48 @@ EG2_DEV void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
 EG2_DEV void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 EG2_DEV void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
+template <int W>
+EG2_DEV void tmem_ldw(uint32_t taddr, uint32_t (&r)[W]) {
+    if constexpr (W == 16)
+        tmem_ld16(taddr, r);
+    else
+        tmem_ld32(taddr, r);
+}
+// After tcgen05.wait::ld: the registers of the waited-for loads count as written here, so no use of
+// them is scheduled before the wait.
+template <int W>
+EG2_DEV void reg_fence(uint32_t (&r)[W]) {
+#pragma unroll
+    for (int j = 0; j < W; j++) asm volatile("" : "+r"(r[j]));
+}
+// Walks n chunks of W TMEM columns (chunk c at taddr + c * W) with the load of chunk c + 1 in flight
+// while body(c, regs) processes chunk c (for loops with nothing else to hide the TMEM latency
+// behind). body returns false to stop (its loads are waited for first).
+template <int W, typename F>
+EG2_DEV bool tmem_pipelined(uint32_t taddr, int n, F&& body) {
+    uint32_t ra[W], rb[W];
+    tmem_ldw<W>(taddr, ra);
+#pragma unroll 1
+    for (int c = 0; c < n; c += 2) {
+        tmem_ld_wait();
+        reg_fence<W>(ra);
+        if (c + 1 < n) tmem_ldw<W>(taddr + (c + 1) * W, rb);
+        if (!body(c, ra)) {
+            tmem_ld_wait();
+            return false;
+        }
+        if (c + 1 >= n) break;
+        tmem_ld_wait();
+        reg_fence<W>(rb);
+        if (c + 2 < n) tmem_ldw<W>(taddr + (c + 2) * W, ra);
+        if (!body(c + 1, rb)) {
+            tmem_ld_wait();
+            return false;
+        }
+    }
+    return true;
+}
+
 // ---------------------------------------------------------------------------------------------
 // UMMA descriptors
 // ---------------------------------------------------------------------------------------------
