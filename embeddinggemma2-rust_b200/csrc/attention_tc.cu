@@ -80,7 +80,9 @@ struct ApCfg {
     // pair handshakes [4 quadrants][2]
     static constexpr int N_BARS = 1 + 2 * UNITS + 3 + 4 + 2 + 2 + (SPLIT ? 8 : 0);
     static constexpr int OFF_X = OFF_BAR + N_BARS * 8 + 16;  // split softmax: maxima [2 slots][2 halves][128], sums [2][128]
-    static constexpr int SMEM = 1024 + OFF_X + (SPLIT ? 3 * 1024 : 0);
+    // Head 256: per softmax warp a 2 KB staging tile for the O epilogue's TMA stores (1 KB aligned).
+    static constexpr int OFF_STG = SPLIT ? ((OFF_X + 3 * 1024 + 1023) / 1024) * 1024 : OFF_X;
+    static constexpr int SMEM = 1024 + OFF_STG + (SPLIT ? NSW * 2048 : 0);
 };
 static_assert(ApCfg<256>::SMEM <= 227 * 1024 && ApCfg<512>::SMEM <= 227 * 1024, "attention pair: shared memory");
 
@@ -94,7 +96,7 @@ static_assert(ApCfg<256>::SMEM <= 227 * 1024 && ApCfg<512>::SMEM <= 227 * 1024, 
 template <int DQK>
 __global__ void __launch_bounds__(ApCfg<DQK>::THREADS, 1)
     attention_pair_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                          const __grid_constant__ CUtensorMap tmV, AttParams prm) {
+                          const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO, AttParams prm) {
     using Cfg = ApCfg<DQK>;
     constexpr bool SPLIT = Cfg::SPLIT;
     constexpr bool SDB = DQK == 512;  // double-buffered S, P over S
@@ -347,6 +349,39 @@ __global__ void __launch_bounds__(ApCfg<DQK>::THREADS, 1)
             const int head = pu.g * G + r % G;
             bf16_t* orow = prm.out + ((long)(pu.tile.row0 + ptok) * prm.nh + head) * prm.hd + pu.dsplit * ATT_DV + ch * 128;
             const bool live = ptok < pu.tile.len;
+            if constexpr (SPLIT) {
+                // Every row of the warp in the sequence: 32 x 32 chunks through the warp's staging tile
+                // (64-byte swizzle) by TMA store -- one 3-D box [32 channels][G heads][32 / G tokens]
+                // is exactly the warp's 32 rows. (Direct per-row stores touched 32 rows per store
+                // instruction and held the unit boundary up for ~6k cycles.)
+                if (__all_sync(0xffffffffu, live)) {
+                    uint8_t* stg = smem + Cfg::OFF_STG + sw * 2048;
+                    const uint32_t swz = (uint32_t)((lane >> 1) & 3);
+                    const int tok0 = pu.tile.row0 + pu.q0r + (32 * e) / G;
+                    tmem_pipelined<32>(t_o + ch * 128 + lane_off, OC / 32, [&](int c, uint32_t(&o)[32]) -> bool {
+                        uint32_t pk[16];
+#pragma unroll
+                        for (int q = 0; q < 16; q++)
+                            pk[q] = bf16x2_bits(__uint_as_float(o[2 * q]) * inv, __uint_as_float(o[2 * q + 1]) * inv);
+                        if (lane == 0) bulk_wait_read<0>();  // the tile's previous store is read out
+                        __syncwarp();
+#pragma unroll
+                        for (int j = 0; j < 4; j++)
+                            *reinterpret_cast<uint4*>(stg + lane * 64 + ((j ^ swz) << 4)) =
+                                make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
+                        fence_proxy_async();
+                        __syncwarp();
+                        if (lane == 0) {
+                            tma_store_3d(&tmO, stg, pu.dsplit * ATT_DV + ch * 128 + c * 32, pu.g * G, tok0);
+                            bulk_commit();
+                        }
+                        return true;
+                    });
+                    tc_fence_before();
+                    arrive_even(o_empty);
+                    return true;
+                }
+            }
             tmem_pipelined<32>(t_o + ch * 128 + lane_off, OC / 32, [&](int c, uint32_t(&o)[32]) -> bool {
                 if (live) {
                     uint4* d = reinterpret_cast<uint4*>(orow + c * 32);
@@ -499,6 +534,10 @@ __global__ void __launch_bounds__(ApCfg<DQK>::THREADS, 1)
             pT = T - 1;
         }
         if (pend && ok && !*abort_flag) finish();
+        if constexpr (SPLIT) {
+            if (lane == 0) bulk_wait_all();  // the O stores are complete before the CTA ends
+            __syncwarp();
+        }
     }
 done:
     // Every MMA the even CTA issued (into both CTAs' TMEM) has completed before either CTA frees it:
@@ -528,8 +567,8 @@ int attention_tc_tile_tokens(int nh, int nkv, int hd) {
 
 // As many clusters as can be resident at once (at most one per work unit); each walks its units.
 template <int DQK>
-static int launch_pair(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const AttParams& prm,
-                       cudaStream_t s) {
+static int launch_pair(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& mo,
+                       const AttParams& prm, cudaStream_t s) {
     using Cfg = ApCfg<DQK>;
     auto kern = attention_pair_kernel<DQK>;
     static int max_clusters[64] = {0};
@@ -556,7 +595,7 @@ static int launch_pair(const CUtensorMap& mq, const CUtensorMap& mk, const CUten
     const long units = (long)prm.n_tiles * prm.nkv * prm.nsplit;
     const int clusters = units < max_clusters[dev] ? (int)units : max_clusters[dev];
     cfg.gridDim = dim3((unsigned)(2 * clusters), 1, 1);
-    return cudaLaunchKernelEx(&cfg, kern, mq, mk, mv, prm) == cudaSuccess ? 0 : -3;
+    return cudaLaunchKernelEx(&cfg, kern, mq, mk, mv, mo, prm) == cudaSuccess ? 0 : -3;
 }
 
 int attention_tc(const bf16_t* q, const bf16_t* k, const bf16_t* v, bf16_t* out, long rows, const AttnTile* tiles,
@@ -565,13 +604,19 @@ int attention_tc(const bf16_t* q, const bf16_t* k, const bf16_t* v, bf16_t* out,
     if ((hd != 256 && hd != 512) || !attention_tc_tile_tokens(nh, nkv, hd)) return -1;
     const int G = nh / nkv;
     const int tq = 128 / G;  // query tokens per CTA (128 MMA rows)
-    CUtensorMap mq, mk, mv;
+    CUtensorMap mq, mk, mv, mo;
     const CUtensorMapDataType dt = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
     // q [rows, nh, hd]: box (64 ch, G heads, tq tokens) -> 128 rows of 128 B.
     if (make_tmap_3d(&mq, dt, q, hd, nh, rows, (uint64_t)hd * 2, (uint64_t)nh * hd * 2, 64, G, tq) ||
         make_tmap_3d(&mk, dt, k, hd, nkv, rows, (uint64_t)hd * 2, (uint64_t)nkv * hd * 2, 64, 1, ATT_KBOX) ||
         make_tmap_3d(&mv, dt, v, hd, nkv, rows, (uint64_t)hd * 2, (uint64_t)nkv * hd * 2, 64, 1, AP_BN))
         return -1;
+    // out [rows, nh, hd] for the O epilogue's TMA stores (head 256): box (32 ch, G heads, 32 / G tokens)
+    // = one warp's 32 rows, 64-byte swizzle.
+    if (hd == 256 && make_tmap_3d(&mo, dt, out, hd, nh, rows, (uint64_t)hd * 2, (uint64_t)nh * hd * 2, 32, G, 32 / G,
+                                  CU_TENSOR_MAP_SWIZZLE_64B))
+        return -1;
+    if (hd != 256) mo = mq;  // unused
     AttParams prm;
     prm.tiles = tiles;
     prm.out = out;
@@ -584,7 +629,7 @@ int attention_tc(const bf16_t* q, const bf16_t* k, const bf16_t* v, bf16_t* out,
     prm.nsplit = hd / ATT_DV;
     prm.n_tiles = n_tiles;
     // CTA pairs: clusters of 2 walking the (pair tile, K/V head, 256-channel half of O) units.
-    return hd == 256 ? launch_pair<256>(mq, mk, mv, prm, s) : launch_pair<512>(mq, mk, mv, prm, s);
+    return hd == 256 ? launch_pair<256>(mq, mk, mv, mo, prm, s) : launch_pair<512>(mq, mk, mv, mo, prm, s);
 }
 
 

@@ -217,6 +217,12 @@ EG2_DEV void tma_store_2d(const CUtensorMap* m, const void* src, int x, int y) {
                  "r"(smem_u32(src)), "r"(x), "r"(y)
                  : "memory");
 }
+EG2_DEV void tma_store_3d(const CUtensorMap* m, const void* src, int x, int y, int z) {
+    asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+                     reinterpret_cast<uint64_t>(m)),
+                 "r"(smem_u32(src)), "r"(x), "r"(y), "r"(z)
+                 : "memory");
+}
 EG2_DEV void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 // All but the newest N groups have finished reading their shared-memory sources.
 template <int N>

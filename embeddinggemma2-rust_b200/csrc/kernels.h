@@ -79,7 +79,8 @@ int make_tmap_2d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint6
                  CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B);
 // 3-D variant: dims (d0, d1, d2) with byte strides s1 (dim 1) and s2 (dim 2); box (b0, b1, b2).
 int make_tmap_3d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t d0, uint64_t d1, uint64_t d2,
-                 uint64_t s1, uint64_t s2, uint32_t b0, uint32_t b1, uint32_t b2);
+                 uint64_t s1, uint64_t s2, uint32_t b0, uint32_t b1, uint32_t b2,
+                 CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B);
 
 // Whether EPI_QKV applies to a head configuration (whole heads per 256-column tile).
 bool qkv_fusable(const QkvEpilogue& q);

@@ -64,7 +64,7 @@ int make_tmap_2d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint6
 }
 
 int make_tmap_3d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t d0, uint64_t d1, uint64_t d2,
-                 uint64_t s1, uint64_t s2, uint32_t b0, uint32_t b1, uint32_t b2) {
+                 uint64_t s1, uint64_t s2, uint32_t b0, uint32_t b1, uint32_t b2, CUtensorMapSwizzle swizzle) {
     EncodeTiledFn fn = encode_tiled();
     if (!fn) return -3;
     cuuint64_t dims[3] = {d0, d1, d2};
@@ -72,7 +72,7 @@ int make_tmap_3d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint6
     cuuint32_t box[3] = {b0, b1, b2};
     cuuint32_t es[3] = {1, 1, 1};
     CUresult r = fn(m, dt, 3, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                    swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS ? 0 : -1;
 }
 
