@@ -53,9 +53,11 @@ EG2_DEV uint32_t bf16x2_bits(float lo, float hi) {
 
 // sin and cos of an angle of moderate size (|a| < 2^12 * 2 pi): Cody-Waite reduction by 2 pi
 // (6.28125 has 8 significant bits, so k * 6.28125 is exact for |k| < 2^15), then the MUFU
-// approximations, which are accurate to ~4e-7 absolute on [-pi, pi].
+// approximations, which are accurate to ~4e-7 absolute on [-pi, pi]. k = the nearest integer to
+// a / (2 pi), ties to even, by adding and subtracting 1.5 * 2^23 (exact for |a / (2 pi)| < 2^22; the
+// same value as rintf, on the FMA pipe instead of a rounding instruction).
 EG2_DEV void sincos_reduced(float a, float& s, float& c) {
-    const float k = rintf(a * 0.15915494309189535f);
+    const float k = __fsub_rn(__fadd_rn(a * 0.15915494309189535f, 12582912.f), 12582912.f);
     float r = fmaf(-k, 6.28125f, a);
     r = fmaf(-k, 1.9353071795864769e-3f, r);
     s = __sinf(r);

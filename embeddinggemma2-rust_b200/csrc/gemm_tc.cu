@@ -39,6 +39,10 @@ struct InTraits<float> {
 
 constexpr int GEMM_BM = 128;
 constexpr int GEMM_THREADS = 320;
+// WIDE (the sliding-layer QKV epilogue): 16 epilogue warps, two per TMEM lane quadrant and set, each
+// taking half of the tile's columns. That epilogue is latency-bound (~0.3 IPC per warp) and longer than
+// the main loop, so with two accumulators the tile period is (epilogue + main loop) / 2.
+constexpr int gemm_threads(bool wide) { return wide ? 576 : GEMM_THREADS; }
 
 // PAIR: 2-CTA clusters computing 256 x BN tiles with tcgen05.mma.cta_group::2 (M = 256): each CTA
 // loads its own 128 rows of A and half (BN / 2 rows) of B, so per SM a K block moves 32 KB into and
@@ -48,22 +52,26 @@ constexpr int GEMM_THREADS = 320;
 // shared-memory slots (instead of the 2.5 KB staging tile of the register path) -- EPI_ADD_NORM
 // for its residual reads and h / t writes, EPI_PLE_GATE for its PLE inputs and outputs, EPI_QKV
 // and EPI_GELU_GU for their outputs. The main loop gives up stages for them.
-template <int BN, bool PAIR = false, bool TIO = false>
+template <int BN, bool PAIR = false, bool TIO = false, bool WIDE = false>
 struct GemmCfg {
+    static constexpr int NEPI = WIDE ? 16 : 8;  // epilogue warps
     static constexpr int A_BYTES = GEMM_BM * 128;
     static constexpr int B_BYTES = (PAIR ? BN / 2 : BN) * 128;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
     static constexpr int STAGES = TIO ? (PAIR ? 4 : 3) : PAIR ? 6 : (BN == 256) ? 4 : 6;
     // Barriers follow the stages; TIO slots must start on a 1 KB boundary.
     static constexpr int OFF_STAGE = STAGES * STAGE_BYTES + (TIO ? 1024 : 256);
-    static constexpr int STAGE_WARP = TIO ? 8192 : 32 * (64 + 16);  // 32 rows x 64 B + 16 B pad
-    static constexpr int OFF_W = OFF_STAGE + 8 * STAGE_WARP;        // EPI_QKV: norm weights, inv freqs
+    // 32 rows x 64 B + 16 B pad; TIO: four 2 KB slots (WIDE: two)
+    static constexpr int STAGE_WARP = TIO ? (WIDE ? 4096 : 8192) : 32 * (64 + 16);
+    static constexpr int OFF_W = OFF_STAGE + NEPI * STAGE_WARP;  // EPI_QKV: norm weights, inv freqs
     // EPI_QKV: norm weights + inverse frequencies (<= 3 KB). Cluster modes: this CTA's halves of the
     // norm weights (EPI_QKV_PAIR: wq, wk and 128 inverse frequencies, 2.5 KB), exchange slots
     // [set][slot][128 rows] at +X_OFF (2 KB), exchange barriers [set][slot] at +XB_OFF.
+    // WIDE: the halves' partial sums of squares [set][quadrant][slot][half][32] (4 KB) at +X_OFF,
+    // their barriers [set][quadrant][slot] at +XB_OFF.
     static constexpr int X_OFF = 2560;
-    static constexpr int XB_OFF = X_OFF + 2048;
-    static constexpr int W_BYTES = XB_OFF + 64;
+    static constexpr int XB_OFF = X_OFF + (WIDE ? 4096 : 2048);
+    static constexpr int W_BYTES = XB_OFF + (WIDE ? 128 : 64);
     static constexpr int SMEM_BYTES = 1024 + OFF_W + W_BYTES;
     static constexpr uint32_t TMEM_COLS = 2 * BN;
 };
@@ -127,14 +135,15 @@ struct alignas(64) EpiMaps {
 };
 
 // TIO store of a 32-row x 32-column bf16 chunk (lane i holds row i) at (x, y) of map m, through
-// slot n % 4 of the warp's four 2 KB slots (64-byte swizzle: row r's 16-byte unit j at
+// slot n % NSLOT of the warp's 2 KB slots (64-byte swizzle: row r's 16-byte unit j at
 // r * 64 + 16 * (j ^ ((r >> 1) & 3)), conflict-free for lane = row). The slot's previous store (the
-// 4th newest bulk group of lane 0) must have been read out first. Rows past the tensor are not
+// NSLOT-th newest bulk group of lane 0) must have been read out first. Rows past the tensor are not
 // written. All 32 lanes call it with the same n.
+template <int NSLOT = 4>
 EG2_DEV void tio_store32(const CUtensorMap* m, uint8_t* slots, int n, const float (&v)[32], int x, int y) {
     const int lane = threadIdx.x & 31;
-    uint8_t* buf = slots + (n & 3) * 2048;
-    if (lane == 0) bulk_wait_read<3>();
+    uint8_t* buf = slots + (n % NSLOT) * 2048;
+    if (lane == 0) bulk_wait_read<NSLOT - 1>();
     __syncwarp();
     const uint32_t sw = (uint32_t)((lane >> 1) & 3);
     uint8_t* row = buf + lane * 64;
@@ -149,6 +158,118 @@ EG2_DEV void tio_store32(const CUtensorMap* m, uint8_t* slots, int n, const floa
         tma_store_2d(m, buf, x, y);
         bulk_commit();
     }
+}
+
+// EPI_QKV, 256-wide heads, WIDE: this warp takes half hw of the tile's 128 rotation pairs (pairs
+// 64 hw .. 64 hw + 63: columns 64 hw.. and 128 + 64 hw..), in sub-chunks of 16 pairs. The head's sum of
+// squares is completed with the other half's partial (the other warp of this TMEM lane quadrant and
+// set): both write their partial to slot X % 2 and meet on that slot's mbarrier (64 arrivals, bounded
+// wait); a slot is rewritten only after the partner has passed the next meeting, i.e. has read it.
+// Outputs (16 columns of bf16 per store, 32-byte swizzle: row r's 16-byte unit j at
+// r * 32 + 16 * (j ^ ((r >> 2) & 1))) leave by TMA store through the warp's two 2 KB slots, a
+// sub-chunk's x1 and x2 pieces sharing a slot, a proxy fence and a bulk group. Same arithmetic as
+// epilogue_qkv256 except the order in which the sum of squares is added up. Returns false when a wait
+// ran out.
+EG2_DEV bool epilogue_qkv256_wide(const QkvEpilogue& Q, uint32_t tbase, int row0, int M, int n0, uint8_t* slots,
+                                  const float* wsm, const EpiMaps& em, int& nst, int hw, float* xv, uint64_t* xb,
+                                  int& X, volatile int* abort_flag) {
+    const int lane = threadIdx.x & 31;
+    const int row = row0 + lane;
+    const int qw = Q.nh * 256, kw = Q.nkv * 256;
+    int head, which;
+    const float* w;
+    bool rot;
+    if (n0 < qw) {
+        head = n0 >> 8, w = wsm, rot = true, which = 0;
+    } else if (n0 < qw + kw) {
+        head = (n0 - qw) >> 8, w = wsm + 256, rot = true, which = 1;
+    } else {
+        head = (n0 - qw - kw) >> 8, w = nullptr, rot = false, which = 2;
+    }
+    const bool live = row < M;
+    const float pf = (rot && live) ? (float)(Q.pos ? Q.pos[(long)row * Q.pos_stride] : row) : 0.f;
+    const int c0 = 64 * hw;  // this half's first pair
+    float ss = 0.f;
+#pragma unroll 1
+    for (int c = 0; c < 64; c += 32) {
+        uint32_t r0[32], r1[32];
+        tmem_ld32(tbase + c0 + c, r0);
+        tmem_ld32(tbase + 128 + c0 + c, r1);
+        tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 32; j++) {
+            ss = fmaf(__uint_as_float(r0[j]), __uint_as_float(r0[j]), ss);
+            ss = fmaf(__uint_as_float(r1[j]), __uint_as_float(r1[j]), ss);
+        }
+    }
+    {
+        float* slot = xv + (X & 1) * 64;
+        slot[hw * 32 + lane] = ss;
+        mbar_arrive(&xb[X & 1]);
+        if (!mbar_wait(&xb[X & 1], (X >> 1) & 1, EG2_DEV_TIMEOUT_GEMM, abort_flag)) return false;
+        ss += *reinterpret_cast<volatile float*>(slot + (hw ^ 1) * 32 + lane);
+        X++;
+    }
+    const float inv = 1.0f / sqrtf(ss / 256.f + Q.eps);
+    const float* invs = wsm + 512;
+    const int col1 = head * 256;
+    const uint32_t sw32 = (uint32_t)((lane >> 2) & 1);
+    // A sub-chunk's two 16-column pieces (x1 at col, x2 at col + 128) go into the two 1 KB halves of
+    // slot nst % 2 behind one proxy fence, then lane 0 issues both TMA stores as one bulk group.
+    auto store_pair = [&](const float (&v1)[16], const float (&v2)[16], int col) {
+        uint32_t p1[8], p2[8];
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            p1[j] = bf16x2_bits(v1[2 * j], v1[2 * j + 1]);
+            p2[j] = bf16x2_bits(v2[2 * j], v2[2 * j + 1]);
+        }
+        uint8_t* buf = slots + (nst & 1) * 2048;
+        if (lane == 0) bulk_wait_read<1>();  // the slot's previous stores are read out
+        __syncwarp();
+#pragma unroll
+        for (int j = 0; j < 2; j++) {
+            *reinterpret_cast<uint4*>(buf + lane * 32 + ((j ^ sw32) << 4)) =
+                make_uint4(p1[4 * j], p1[4 * j + 1], p1[4 * j + 2], p1[4 * j + 3]);
+            *reinterpret_cast<uint4*>(buf + 1024 + lane * 32 + ((j ^ sw32) << 4)) =
+                make_uint4(p2[4 * j], p2[4 * j + 1], p2[4 * j + 2], p2[4 * j + 3]);
+        }
+        fence_proxy_async();
+        __syncwarp();
+        if (lane == 0) {
+            tma_store_2d(&em.m[which], buf, col, row0);
+            tma_store_2d(&em.m[which], buf + 1024, col + 128, row0);
+            bulk_commit();
+        }
+        nst++;
+    };
+#pragma unroll 1
+    for (int sc = 0; sc < 4; sc++) {
+        const int p = c0 + 16 * sc;  // first pair of the sub-chunk
+        float x1[16], x2[16];
+        {
+            uint32_t a[16], b[16];
+            tmem_ld16(tbase + p, a);
+            tmem_ld16(tbase + 128 + p, b);
+            tmem_ld_wait();
+#pragma unroll
+            for (int t = 0; t < 16; t++) {
+                x1[t] = __uint_as_float(a[t]) * inv;
+                x2[t] = __uint_as_float(b[t]) * inv;
+            }
+        }
+        if (rot) {
+#pragma unroll
+            for (int t = 0; t < 16; t++) {
+                const float a1 = x1[t] * w[p + t], a2 = x2[t] * w[128 + p + t];
+                float sj, cj;
+                sincos_reduced(pf * invs[p + t], sj, cj);
+                x1[t] = a1 * cj - a2 * sj;
+                x2[t] = a2 * cj + a1 * sj;
+            }
+        }
+        store_pair(x1, x2, col1 + p);
+    }
+    return true;
 }
 
 // EPI_QKV with one 256-wide head per tile and RoPE over the whole head (pairs i, i + 128): the same
@@ -374,14 +495,16 @@ EG2_DEV void warp_load32_finish(const uint4 (&b)[8], float (&v)[32], uint8_t* st
 }
 
 // em: the tensor maps of the epilogue's TMA I/O (TIO only).
-template <typename TIn, int BN, int EPI, typename TOut, bool PAIR = false, bool TIO = false>
-__global__ void __launch_bounds__(GEMM_THREADS, 1)
+template <typename TIn, int BN, int EPI, typename TOut, bool PAIR = false, bool TIO = false, bool WIDE = false>
+__global__ void __launch_bounds__(gemm_threads(WIDE), 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ EpiMaps em, int M, int N, int K, GemmEpilogue epi) {
+    static_assert(!WIDE || (EPI == EPI_QKV && PAIR && TIO), "WIDE: the pair QKV epilogue with TMA stores");
+    constexpr int NTHREADS = gemm_threads(WIDE);
     static_assert(!TIO || (BN == 256 && (EPI == EPI_ADD_NORM || EPI == EPI_GROUP_NORM || EPI == EPI_QKV_PAIR ||
                                          (PAIR && (EPI == EPI_QKV || EPI == EPI_PLE_GATE || EPI == EPI_GELU_GU)))),
                   "TMA epilogue I/O: the cluster epilogues, and the pair QKV / PLE-gate / GELU epilogues");
-    using Cfg = GemmCfg<BN, PAIR, TIO>;
+    using Cfg = GemmCfg<BN, PAIR, TIO, WIDE>;
     constexpr int BK = InTraits<TIn>::BK;
     constexpr int STAGES = Cfg::STAGES;
     extern __shared__ uint8_t smem_raw[];
@@ -424,11 +547,16 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         }
         for (int a = 0; a < 2; a++) {
             mbar_init(&tfull[a], 1);
-            mbar_init(&tempty[a], PAIR ? 256 : 128);  // PAIR: both CTAs' epilogue sets free the accumulator
+            // Every epilogue thread of the set (PAIR: of both CTAs) frees the accumulator.
+            mbar_init(&tempty[a], (WIDE ? 256 : 128) * (PAIR ? 2 : 1));
         }
         mbar_init(drain, 1);
-        if constexpr (TIO) {
+        if constexpr (TIO && !WIDE) {
             for (int x = 0; x < 32; x++) mbar_init(&hbar[x], 1);
+        }
+        if constexpr (WIDE) {
+            uint64_t* xb = reinterpret_cast<uint64_t*>(smem + Cfg::OFF_W + Cfg::XB_OFF);
+            for (int x = 0; x < 16; x++) mbar_init(&xb[x], 64);  // both half-warps of a quadrant
         }
         if constexpr (CL) {
             uint64_t* xb = reinterpret_cast<uint64_t*>(smem + Cfg::OFF_W + Cfg::XB_OFF);
@@ -448,7 +576,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         // q_norm / k_norm weights and the inverse frequencies, once per CTA.
         float* wsm = reinterpret_cast<float*>(smem + Cfg::OFF_W);
         const int hd = epi.qkv.hd, nf = epi.qkv.part / 2;
-        for (int i = threadIdx.x; i < 2 * hd + nf; i += GEMM_THREADS)
+        for (int i = threadIdx.x; i < 2 * hd + nf; i += NTHREADS)
             wsm[i] = i < hd ? epi.qkv.wq[i] : i < 2 * hd ? epi.qkv.wk[i - hd] : epi.qkv.inv_freq[i - 2 * hd];
     }
     if constexpr (EPI == EPI_QKV_PAIR) {
@@ -456,7 +584,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         // 128 r + t, or 256 + 128 r + t - 128), then the inverse frequencies of its 128 rotated pairs.
         float* wsm = reinterpret_cast<float*>(smem + Cfg::OFF_W);
         const int r = (int)crank;
-        for (int i = threadIdx.x; i < 2 * BN + 128; i += GEMM_THREADS) {
+        for (int i = threadIdx.x; i < 2 * BN + 128; i += NTHREADS) {
             const int t = i & (BN - 1);
             const int ch = t < 128 ? 128 * r + t : 256 + 128 * r + (t - 128);
             wsm[i] = i < BN ? epi.qkv.wq[ch] : i < 2 * BN ? epi.qkv.wk[ch] : epi.qkv.inv_freq[128 * r + (i - 2 * BN)];
@@ -465,7 +593,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         // This CTA's halves of the norm weights (the same for every 512-column group).
         float* wsm = reinterpret_cast<float*>(smem + Cfg::OFF_W);
         const int n0 = (int)crank * BN;
-        for (int i = threadIdx.x; i < 2 * BN; i += GEMM_THREADS)
+        for (int i = threadIdx.x; i < 2 * BN; i += NTHREADS)
             wsm[i] = i < BN ? epi.an.w1[n0 + i] : (epi.an.w2 ? epi.an.w2[n0 + i - BN] : 0.f);
     }
     if (warp == 1) {
@@ -572,13 +700,15 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         }
     } else {
         const int e = warp & 3;           // TMEM lane quadrant this warp may access
-        const int set = (warp - 2) >> 2;  // epilogue set = accumulator it owns
+        const int set = WIDE ? (warp - 2) >> 3 : (warp - 2) >> 2;  // epilogue set = accumulator it owns
+        const int hw = WIDE ? ((warp - 2) >> 2) & 1 : 0;              // WIDE: half of the tile's columns
         const float* wsm = reinterpret_cast<const float*>(smem + Cfg::OFF_W);
         uint8_t* stage = smem + Cfg::OFF_STAGE + (warp - 2) * Cfg::STAGE_WARP;
         TOut* out = reinterpret_cast<TOut*>(epi.out);
         // TIO: residual chunk g (16 columns; 16 per tile) goes to slot g % 4 of this warp, its load
         // completing phase (g / 4) % 2 of hb[g % 4]. Loads issued / chunks consumed so far:
-        uint64_t* hb = hbar + (warp - 2) * 4;
+        uint64_t* hb = hbar + (WIDE ? 0 : (warp - 2) * 4);
+        int xq = 0;  // WIDE: sum-of-squares meetings so far
         int ld_issued = 0, ld_used = 0;
         int nst = 0;  // TIO output stores issued by this warp (slot nst % 4)
         int k = 0;    // tiles this set has taken: its k-th completion of tfull[set]
@@ -858,7 +988,15 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
                     }
                 }
             } else if constexpr (EPI == EPI_QKV) {
-                epilogue_qkv<TOut, BN, TIO>(epi, tbase, row0, M, n0, stage, wsm, em, nst);
+                if constexpr (WIDE) {
+                    float* xv = reinterpret_cast<float*>(smem + Cfg::OFF_W + Cfg::X_OFF) + (set * 4 + e) * 128;
+                    uint64_t* xbq = reinterpret_cast<uint64_t*>(smem + Cfg::OFF_W + Cfg::XB_OFF) + (set * 4 + e) * 2;
+                    if (!epilogue_qkv256_wide(epi.qkv, tbase, row0, M, n0, stage, wsm, em, nst, hw, xv, xbq, xq,
+                                              abort_flag))
+                        break;
+                } else {
+                    epilogue_qkv<TOut, BN, TIO>(epi, tbase, row0, M, n0, stage, wsm, em, nst);
+                }
             } else if constexpr (EPI == EPI_PLE_GATE && TIO) {
                 // GELU(gate) x ple[:, layer] in 16-column chunks: the inputs arrive by TMA in slot
                 // c % 4 (f32, 64-byte swizzle), the bf16 result replaces them there (32-byte swizzle:
@@ -1033,11 +1171,11 @@ static int launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N,
 // Clusters of two CTAs (the cluster epilogues, and CTA-pair MMAs), as many as can be resident at
 // once (the loop over tiles is persistent, so every launched cluster must run concurrently with
 // the others).
-template <int EPI, typename TOut, bool PAIR = false, bool TIO = false>
+template <int EPI, typename TOut, bool PAIR = false, bool TIO = false, bool WIDE = false>
 static int launch_cluster(const CUtensorMap& ta, const CUtensorMap& tb, const EpiMaps& em, int M, int N, int K,
                           const GemmEpilogue& epi, cudaStream_t s) {
-    using Cfg = GemmCfg<256, PAIR, TIO>;
-    auto kern = gemm_tc_kernel<bf16_t, 256, EPI, TOut, PAIR, TIO>;
+    using Cfg = GemmCfg<256, PAIR, TIO, WIDE>;
+    auto kern = gemm_tc_kernel<bf16_t, 256, EPI, TOut, PAIR, TIO, WIDE>;
     static int max_clusters[64] = {0};
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -3;
@@ -1047,7 +1185,7 @@ static int launch_cluster(const CUtensorMap& ta, const CUtensorMap& tb, const Ep
     attr[0].val.clusterDim.x = 2;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
-    cfg.blockDim = dim3(GEMM_THREADS, 1, 1);
+    cfg.blockDim = dim3(gemm_threads(WIDE), 1, 1);
     cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
     cfg.stream = s;
     cfg.attrs = attr;
@@ -1137,12 +1275,16 @@ int gemm_tc(GemmKind kind, const void* A, long lda, const void* W, long ldw, int
             case EPI_QKV: {
                 const QkvEpilogue& q = epi.qkv;
                 if (q.hd == 256 && q.part == 256) {
+                    // q / k / v in 16 x 32 boxes (32-byte swizzle) for the WIDE epilogue's stores.
                     EpiMaps em = {};
-                    if (out_map(&em.m[0], q.q, (long)q.nh * 256, (long)q.nh * 256) ||
-                        out_map(&em.m[1], q.k, (long)q.nkv * 256, (long)q.nkv * 256) ||
-                        out_map(&em.m[2], q.v, (long)q.nkv * 256, (long)q.nkv * 256))
+                    auto qkv_map = [&](CUtensorMap* m, const void* base, long cols) {
+                        return make_tmap_2d(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, base, cols, M, cols * 2, 16, 32,
+                                            CU_TENSOR_MAP_SWIZZLE_32B);
+                    };
+                    if (qkv_map(&em.m[0], q.q, (long)q.nh * 256) || qkv_map(&em.m[1], q.k, (long)q.nkv * 256) ||
+                        qkv_map(&em.m[2], q.v, (long)q.nkv * 256))
                         return -1;
-                    return launch_cluster<EPI_QKV, bf16_t, true, true>(ta, tb, em, M, N, K, epi, s);
+                    return launch_cluster<EPI_QKV, bf16_t, true, true, true>(ta, tb, em, M, N, K, epi, s);
                 }
                 return launch_cluster<EPI_QKV, bf16_t, true>(ta, tb, none, M, N, K, epi, s);
             }
