@@ -382,15 +382,17 @@ __global__ void __launch_bounds__(ApCfg<DQK>::THREADS, 1)
                     return true;
                 }
             }
+            // 32-byte stores: each instruction writes whole sectors of 32 rows.
             tmem_pipelined<32>(t_o + ch * 128 + lane_off, OC / 32, [&](int c, uint32_t(&o)[32]) -> bool {
                 if (live) {
-                    uint4* d = reinterpret_cast<uint4*>(orow + c * 32);
 #pragma unroll
-                    for (int q = 0; q < 4; q++)
-                        d[q] = make_uint4(bf16x2_bits(__uint_as_float(o[8 * q + 0]) * inv, __uint_as_float(o[8 * q + 1]) * inv),
-                                          bf16x2_bits(__uint_as_float(o[8 * q + 2]) * inv, __uint_as_float(o[8 * q + 3]) * inv),
-                                          bf16x2_bits(__uint_as_float(o[8 * q + 4]) * inv, __uint_as_float(o[8 * q + 5]) * inv),
-                                          bf16x2_bits(__uint_as_float(o[8 * q + 6]) * inv, __uint_as_float(o[8 * q + 7]) * inv));
+                    for (int q = 0; q < 2; q++) {
+                        uint32_t pk[8];
+#pragma unroll
+                        for (int j = 0; j < 8; j++)
+                            pk[j] = bf16x2_bits(__uint_as_float(o[16 * q + 2 * j]) * inv, __uint_as_float(o[16 * q + 2 * j + 1]) * inv);
+                        st_global_v8(orow + c * 32 + 16 * q, pk);
+                    }
                 }
                 return true;
             });

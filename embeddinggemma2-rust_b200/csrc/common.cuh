@@ -226,6 +226,12 @@ EG2_DEV void tma_store_3d(const CUtensorMap* m, const void* src, int x, int y, i
                  : "memory");
 }
 EG2_DEV void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// 32-byte store (p 32-byte aligned): a warp of these writes whole 32-byte sectors.
+EG2_DEV void st_global_v8(void* p, const uint32_t (&v)[8]) {
+    asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(p), "r"(v[0]), "r"(v[1]), "r"(v[2]),
+                 "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+                 : "memory");
+}
 // All but the newest N groups have finished reading their shared-memory sources.
 template <int N>
 EG2_DEV void bulk_wait_read() {
