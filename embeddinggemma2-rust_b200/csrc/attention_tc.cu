@@ -328,7 +328,7 @@ __global__ void __launch_bounds__(ApCfg<DQK>::THREADS, 1)
         // The O epilogue of a unit runs after the next unit's first P has been written (so that P does
         // not wait behind it); pend / pu / pl / pT: the unit waiting for it, its row sum, its last tile.
         bool pend = false;
-        Unit pu;
+        Unit pu{};
         float pl = 0.f;
         int pT = 0;
         auto finish = [&]() -> bool {

@@ -534,11 +534,19 @@ __global__ void __launch_bounds__(gemm_threads(WIDE), 1)
     const int tiles_mp = (tiles_m + 1) / 2;
     const int t_first = (CL || PAIR) ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
     const int t_step = (CL || PAIR) ? (int)(gridDim.x >> 1) : (int)gridDim.x;
-    const int t_count = CL ? tiles_m * groups : PAIR ? tiles_mp * tiles_n : tiles_m * tiles_n;
+    // K split (EPI_STORE on CTA pairs): linear id t = base tile * S + slice; slice s covers K blocks
+    // [s * kbs, s * kbs + kbs).
+    const int S = (EPI == EPI_STORE && PAIR && epi.ksplit > 1) ? epi.ksplit : 1;
+    const int kbs = kblocks / S;
+    const int t_count = (CL ? tiles_m * groups : PAIR ? tiles_mp * tiles_n : tiles_m * tiles_n) * S;
     auto tile_m0 = [&](int t) {
+        t /= S;
         return PAIR ? (t / tiles_n) * 2 * GEMM_BM + (int)crank * GEMM_BM : (CL ? t / groups : t / tiles_n) * GEMM_BM;
     };
-    auto tile_n0 = [&](int t) { return CL ? (t % groups) * 512 + (int)crank * BN : (t % tiles_n) * BN; };
+    auto tile_n0 = [&](int t) {
+        t /= S;
+        return CL ? (t % groups) * 512 + (int)crank * BN : (t % tiles_n) * BN;
+    };
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; s++) {
@@ -617,7 +625,8 @@ __global__ void __launch_bounds__(gemm_threads(WIDE), 1)
                 // (No L2 prefetch of the epilogue's inputs here: 128 bulk prefetches per tile from this
                 // thread delayed the main loop's loads more than they saved -- measured on B200.)
                 const int m0 = tile_m0(tile), n0 = tile_n0(tile);
-                for (int kb = 0; kb < kblocks; kb++) {
+                const int kb0 = (tile % S) * kbs;
+                for (int kb = kb0; kb < kb0 + kbs; kb++) {
                     if (!mbar_wait(&empty[stage], phase ^ 1, EG2_DEV_TIMEOUT_GEMM, abort_flag)) goto done;
                     uint8_t* sa = smem + stage * Cfg::STAGE_BYTES;
                     if constexpr (PAIR) {
@@ -652,7 +661,7 @@ __global__ void __launch_bounds__(gemm_threads(WIDE), 1)
                 if (!mbar_wait(&tempty[acc], acc_phase ^ 1, EG2_DEV_TIMEOUT_GEMM, abort_flag)) goto done;
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + acc * BN;
-                for (int kb = 0; kb < kblocks; kb++) {
+                for (int kb = 0; kb < kbs; kb++) {
                     if (!mbar_wait(&full[stage], phase, EG2_DEV_TIMEOUT_GEMM, abort_flag)) goto done;
                     tc_fence_after();
                     const uint64_t ad = da0 + (uint64_t)(stage * (Cfg::STAGE_BYTES >> 4));
@@ -681,7 +690,7 @@ __global__ void __launch_bounds__(gemm_threads(WIDE), 1)
                 if (!mbar_wait(&tempty[acc], acc_phase ^ 1, EG2_DEV_TIMEOUT_GEMM, abort_flag)) goto done;
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + acc * BN;
-                for (int kb = 0; kb < kblocks; kb++) {
+                for (int kb = 0; kb < kbs; kb++) {
                     if (!mbar_wait(&full[stage], phase, EG2_DEV_TIMEOUT_GEMM, abort_flag)) goto done;
                     tc_fence_after();
                     const uint64_t ad = da0 + (uint64_t)(stage * (Cfg::STAGE_BYTES >> 4));
@@ -1089,6 +1098,7 @@ __global__ void __launch_bounds__(gemm_threads(WIDE), 1)
                         warp_store32<TOut>(out, epi.ldo, row0, M, n0 / 2 + c * 32, v, stage);
                 }
             } else {
+                TOut* dst = out + (S > 1 ? (long)(tile % S) * epi.split_stride : 0L);  // K split: slice's partial
 #pragma unroll 1
                 for (int c = 0; c < BN / 32; c++) {
                     float v[32];
@@ -1101,7 +1111,7 @@ __global__ void __launch_bounds__(gemm_threads(WIDE), 1)
                     }
 #pragma unroll
                     for (int j = 0; j < 32; j++) v[j] *= epi.scale;
-                    warp_store32<TOut>(out, epi.ldo, row0, M, n0 + c * 32, v, stage);
+                    warp_store32<TOut>(dst, epi.ldo, row0, M, n0 + c * 32, v, stage);
                 }
             }
             tc_fence_before();
@@ -1200,7 +1210,8 @@ static int launch_cluster(const CUtensorMap& ta, const CUtensorMap& tb, const Ep
     }
     const int tiles_m = (M + GEMM_BM - 1) / GEMM_BM;
     if (N % (PAIR ? 256 : 512)) return -1;
-    const long tiles = PAIR ? (long)((tiles_m + 1) / 2) * (N / 256) : (long)tiles_m * (N / 512);
+    const long tiles = PAIR ? (long)((tiles_m + 1) / 2) * (N / 256) * (epi.ksplit > 1 ? epi.ksplit : 1)
+                            : (long)tiles_m * (N / 512);
     const int clusters = tiles < max_clusters[dev] ? (int)tiles : max_clusters[dev];
     cfg.gridDim = dim3(2 * clusters, 1, 1);
     return cudaLaunchKernelEx(&cfg, kern, ta, tb, em, M, N, K, epi) == cudaSuccess ? 0 : -3;
@@ -1250,6 +1261,7 @@ int gemm_tc(GemmKind kind, const void* A, long lda, const void* W, long ldw, int
         return make_tmap_2d(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, base, cols, M, ld * 2, 32, 32,
                             CU_TENSOR_MAP_SWIZZLE_64B);
     };
+    if (epi.ksplit > 1 && (!pair || epi.mode != EPI_STORE || !epi.out_f32 || (K / BK) % epi.ksplit)) return -1;
     if (pair) {
         switch (epi.mode) {
             case EPI_STORE:

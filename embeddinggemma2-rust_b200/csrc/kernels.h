@@ -65,6 +65,10 @@ struct GemmEpilogue {
     long aux_ld = 0;
     int aux_off = 0;
     float scale = 1.f;
+    // EPI_STORE, CTA pairs: split the K range into ksplit equal slices, slice s of every tile written
+    // (f32) at out + s * split_stride -- for passes too short to spread the weights over the SMs.
+    int ksplit = 1;
+    long split_stride = 0;
     QkvEpilogue qkv;
     AddNormEpilogue an;
 };
@@ -100,6 +104,12 @@ int rms_norm_inplace(float* x, const float* w, long rows, int dim, float eps, fl
 template <typename TI, typename TT>
 int add_norm(float* h, const TI* o, const float* w1, TT* t, const float* w2, long rows, int dim, float eps,
              float scalar, cudaStream_t s);
+// GELU(g) x ple[:, layer] (bf16 out [rows, p]) for g given as nsplit f32 partial sums stride apart.
+int ple_gate_split(const float* part, int nsplit, long stride, const float* ple, long ple_ld, int ple_off, bf16_t* out,
+                   long rows, int p, cudaStream_t s);
+// add_norm over o given as nsplit f32 partial sums o_stride elements apart (dim 512, bf16 t).
+int add_norm_split(float* h, const float* o, int nsplit, long o_stride, const float* w1, bf16_t* t, const float* w2,
+                   long rows, int dim, float eps, float scalar, cudaStream_t s);
 // Per-head RMSNorm (q, k weighted; v not) and RoPE on q and k, from the fused projection output
 // qkv[row, (nh + 2 nkv) * hd]. cs/sn: [positions, rope_w] tables; part = rotation width (hd or hd / 2).
 template <typename TI, typename TO>

@@ -108,9 +108,12 @@ int rms_norm_inplace(float* x, const float* w, long rows, int dim, float eps, fl
 }
 
 // ---------------------------------------------------------------------------------------------
+// o may be split into nsplit partial sums (K slices of the producing GEMM), o_stride elements apart,
+// added in slice order.
 template <typename TI, typename TT, int VPL>
 __global__ void add_norm_kernel(float* __restrict__ h, const TI* __restrict__ o, const float* __restrict__ w1,
-                                TT* __restrict__ t, const float* __restrict__ w2, long rows, float eps, float scalar) {
+                                TT* __restrict__ t, const float* __restrict__ w2, long rows, float eps, float scalar,
+                                int nsplit = 1, long o_stride = 0) {
     const long row = (long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (row >= rows) return;
     constexpr int dim = 32 * VPL;
@@ -118,6 +121,11 @@ __global__ void add_norm_kernel(float* __restrict__ h, const TI* __restrict__ o,
     const long base = row * dim + c0;
     float v[VPL], hv[VPL], wv[VPL];
     ld_row<VPL>(o + base, v);
+    for (int sp = 1; sp < nsplit; sp++) {
+        ld_row<VPL>(o + sp * o_stride + base, hv);
+#pragma unroll
+        for (int i = 0; i < VPL; i++) v[i] += hv[i];
+    }
     ld_row<VPL>(h + base, hv);
     ld_row<VPL>(w1 + c0, wv);
     float ss = 0.f;
@@ -155,6 +163,46 @@ int add_norm(float* h, const TI* o, const float* w1, TT* t, const float* w2, lon
         add_norm_kernel<TI, TT, 24><<<grid, 32 * wpb, 0, s>>>(h, o, w1, t, w2, rows, eps, scalar);
     else
         return -1;
+    return cudaGetLastError() == cudaSuccess ? 0 : -3;
+}
+int add_norm_split(float* h, const float* o, int nsplit, long o_stride, const float* w1, bf16_t* t, const float* w2,
+                   long rows, int dim, float eps, float scalar, cudaStream_t s) {
+    if (rows <= 0) return 0;
+    if (dim != 512 || nsplit < 1) return -1;
+    const int wpb = 8;
+    const unsigned grid = (unsigned)((rows + wpb - 1) / wpb);
+    add_norm_kernel<float, bf16_t, 16><<<grid, 32 * wpb, 0, s>>>(h, o, w1, t, w2, rows, eps, scalar, nsplit, o_stride);
+    return cudaGetLastError() == cudaSuccess ? 0 : -3;
+}
+// GELU(g) x ple[:, layer] for g given as nsplit f32 partial sums (K slices), summed in slice order;
+// the same arithmetic as the PLE-gate GEMM epilogue (gelu_fast). Four columns per thread.
+__global__ void ple_gate_split_kernel(const float* __restrict__ part, int nsplit, long stride,
+                                      const float* __restrict__ ple, long ple_ld, int ple_off, bf16_t* __restrict__ out,
+                                      long rows, int p) {
+    const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;  // 4-column group
+    const int gpr = p / 4;
+    if (i >= rows * gpr) return;
+    const long r = i / gpr;
+    const int c = (int)(i % gpr) * 4;
+    float4 g = *reinterpret_cast<const float4*>(part + r * p + c);
+    for (int sp = 1; sp < nsplit; sp++) {
+        const float4 x = *reinterpret_cast<const float4*>(part + sp * stride + r * p + c);
+        g.x += x.x, g.y += x.y, g.z += x.z, g.w += x.w;
+    }
+    const float4 e = *reinterpret_cast<const float4*>(ple + r * ple_ld + ple_off + c);
+    uint2 o;
+    o.x = bf16x2_bits(gelu_fast(g.x) * e.x, gelu_fast(g.y) * e.y);
+    o.y = bf16x2_bits(gelu_fast(g.z) * e.z, gelu_fast(g.w) * e.w);
+    *reinterpret_cast<uint2*>(out + r * p + c) = o;
+}
+
+int ple_gate_split(const float* part, int nsplit, long stride, const float* ple, long ple_ld, int ple_off, bf16_t* out,
+                   long rows, int p, cudaStream_t s) {
+    if (rows <= 0) return 0;
+    if (p % 4 || ple_ld % 4 || ple_off % 4 || nsplit < 1) return -1;
+    const long n = rows * (p / 4);
+    ple_gate_split_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(part, nsplit, stride, ple, ple_ld, ple_off, out,
+                                                                      rows, p);
     return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
 template int add_norm<float, float>(float*, const float*, const float*, float*, const float*, long, int, float, float, cudaStream_t);

@@ -344,6 +344,11 @@ struct VLayerW {
     float *input_ln, *post_attn_ln, *pre_ff_ln, *post_ff_ln, *q_norm, *k_norm;
 };
 
+// Short passes (<= kSplitRows rows) split the K range of the N = 512 projections (up to kSplitMax
+// slices) so the weights are streamed by many SMs.
+constexpr int kSplitMax = 8;
+constexpr long kSplitRows = 256;
+
 struct Work {
     long cap = 0;
     float *hidden = nullptr, *ple = nullptr, *out = nullptr, *x_in = nullptr;
@@ -360,6 +365,7 @@ struct Work {
     int* seq_meta = nullptr;
     long pool_scratch_cap = 0;
     double* pool_scratch = nullptr;
+    float* osplit = nullptr;  // K-split partial sums of short passes' N = 512 projections [8][256][512]
 };
 
 }  // namespace eg2
@@ -691,6 +697,7 @@ static void ensure_work(eg2_ctx* c, long rows, long n_tiles) {
         w.ids = (uint32_t*)dalloc(c, cap * 4);
         w.cap = cap;
     }
+    if (!w.osplit && bf16_mode(c)) w.osplit = (float*)dalloc(c, (size_t)kSplitMax * kSplitRows * 512 * 4);
     if (n_tiles > w.tiles_cap) {
         CK(cudaStreamSynchronize(c->stream));
         dfree(c, w.tiles);
@@ -799,6 +806,26 @@ static void gemm_add_norm(eg2_ctx* c, const void* x, long ldx, const void* W, lo
     Work& w = c->w;
     const int h = c->tc.hidden;
     if (bf16_mode(c) && h == 512 && !getenv("EG2_NO_ADD_NORM_FUSION")) {
+        const int kb = K / 64, S = kb >= 16 ? kSplitMax : kb / 2;
+        if (rows <= kSplitRows && w.osplit && S >= 2 && kb % S == 0) {
+            // A short pass: one cluster per 512-column row block would stream the whole weight
+            // matrix through two SMs. Split K over S slices instead (S x 2 clusters, f32 partials),
+            // then sum the partials and update the residual in a row kernel (same arithmetic as the
+            // fused epilogue, the sum taken in slice order).
+            GemmEpilogue e;
+            e.mode = EPI_STORE;
+            e.out_f32 = 1;
+            e.out = w.osplit;
+            e.ldo = h;
+            e.ksplit = S;
+            e.split_stride = rows * h;
+            KL(gemm_tc(GEMM_BF16, x, ldx, W, K, (int)rows, h, K, e, c->stream), label);
+            KL(add_norm_split(w.hidden, w.osplit, S, rows * h, w1, (bf16_t*)w.t, w2, rows, h, c->tc.eps, scalar,
+                              c->stream),
+               "add_norm_split");
+            mark(c, label);
+            return;
+        }
         GemmEpilogue e;
         e.mode = EPI_ADD_NORM;
         e.out = w.t;
@@ -908,7 +935,21 @@ static void enqueue_text(eg2_ctx* c, long rows, const std::vector<TileSet>& tset
         mark(c, "gemm gate|up + gelu");
         // t = hidden (as the per-layer-input gate's input, bf16 in bf16 mode).
         gemm_add_norm<T>(c, w.gate, ff, L.down, rows, ff, L.post_ff_ln, nullptr, 1.f, "gemm down (+ add_norm)");
-        gemm(c, t, h, L.pg, (int)rows, p, h, w.pg, p, EPI_PLE_GATE, f32, 1.f, w.ple, (long)nl * p, i * p);
+        if (bf16_mode(c) && rows <= kSplitRows && w.osplit && p == 512 && h % 128 == 0) {
+            // Short pass: the K range split over 4 slices (f32 partials), then GELU x ple in a row kernel.
+            GemmEpilogue e;
+            e.mode = EPI_STORE;
+            e.out_f32 = 1;
+            e.out = w.osplit;
+            e.ldo = p;
+            e.ksplit = 4;
+            e.split_stride = rows * p;
+            KL(gemm_tc(GEMM_BF16, t, h, L.pg, h, (int)rows, p, h, e, c->stream), "gemm ple_gate");
+            KL(ple_gate_split(w.osplit, 4, rows * p, w.ple, (long)nl * p, i * p, (bf16_t*)w.pg, rows, p, c->stream),
+               "ple_gate_split");
+        } else {
+            gemm(c, t, h, L.pg, (int)rows, p, h, w.pg, p, EPI_PLE_GATE, f32, 1.f, w.ple, (long)nl * p, i * p);
+        }
         mark(c, "gemm ple_gate");
         const float* next_w = (i + 1 < nl) ? c->layers[i + 1].input_ln : c->final_norm;
         gemm_add_norm<T>(c, w.pg, p, L.pp, rows, p, L.ple_post_norm, next_w, L.layer_scalar, "gemm ple_proj (+ add_norm)");
