@@ -174,6 +174,10 @@ __global__ void __launch_bounds__(ApCfg<DQK>::THREADS, 1)
     tc_fence_after();
     // Both CTAs' barriers are initialised (and TMEM allocated) before either CTA touches the other's.
     cluster_sync();
+    // Programmatic dependent launch: q / k / v and the tile list are read only after the previous
+    // kernel has completed.
+    grid_dep_launch();
+    grid_dep_wait();
     const uint32_t tmem = *tmem_slot;
     const uint32_t t_s = tmem;  // SDB: S / P buffer b at t_s + 128 b; else S at t_s, P[b] at t_p + 64 b
     const uint32_t t_p = tmem + 128;
@@ -577,11 +581,13 @@ static int launch_pair(const CUtensorMap& mq, const CUtensorMap& mk, const CUten
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -3;
     cudaLaunchConfig_t cfg = {};
-    cudaLaunchAttribute la[1];
+    cudaLaunchAttribute la[2];
     la[0].id = cudaLaunchAttributeClusterDimension;
     la[0].val.clusterDim.x = 2;
     la[0].val.clusterDim.y = 1;
     la[0].val.clusterDim.z = 1;
+    la[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    la[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.blockDim = dim3(Cfg::THREADS, 1, 1);
     cfg.dynamicSmemBytes = Cfg::SMEM;
     cfg.stream = s;
@@ -597,6 +603,7 @@ static int launch_pair(const CUtensorMap& mq, const CUtensorMap& mk, const CUten
     const long units = (long)prm.n_tiles * prm.nkv * prm.nsplit;
     const int clusters = units < max_clusters[dev] ? (int)units : max_clusters[dev];
     cfg.gridDim = dim3((unsigned)(2 * clusters), 1, 1);
+    cfg.numAttrs = pdl_enabled() ? 2 : 1;
     return cudaLaunchKernelEx(&cfg, kern, mq, mk, mv, mo, prm) == cudaSuccess ? 0 : -3;
 }
 

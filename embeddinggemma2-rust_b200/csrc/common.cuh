@@ -226,6 +226,12 @@ EG2_DEV void tma_store_3d(const CUtensorMap* m, const void* src, int x, int y, i
                  : "memory");
 }
 EG2_DEV void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Programmatic dependent launch: let the next kernel on the stream start launching (its CTAs run
+// their prologue up to grid_dep_wait), and wait until the previous kernel has completed and its
+// writes are visible (returns at once when this kernel was not launched as a dependent).
+EG2_DEV void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+EG2_DEV void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // 32-byte store (p 32-byte aligned): a warp of these writes whole 32-byte sectors.
 EG2_DEV void st_global_v8(void* p, const uint32_t (&v)[8]) {
     asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(p), "r"(v[0]), "r"(v[1]), "r"(v[2]),

@@ -616,6 +616,11 @@ __global__ void __launch_bounds__(gemm_threads(WIDE), 1)
     const uint32_t tmem_base = *tmem_slot;
     // The peer CTA's barriers must be initialised before anyone arrives on them.
     if constexpr (CL || PAIR) cluster_sync();
+    // Launched as a programmatic dependent: the prologue above ran while the previous kernel was
+    // finishing; the next kernel may start its own now, and this one reads its inputs only once the
+    // previous kernel has completed.
+    grid_dep_launch();
+    grid_dep_wait();
 
     if (warp == 0) {
         if (lane == 0) {
@@ -1174,8 +1179,17 @@ static int launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N,
     const int tiles = ((M + GEMM_BM - 1) / GEMM_BM) * (N / BN);
     const int grid = tiles < num_sms() ? tiles : num_sms();
     const EpiMaps none = {};  // no TMA epilogue I/O here
-    kern<<<grid, GEMM_THREADS, Cfg::SMEM_BYTES, s>>>(ta, tb, none, M, N, K, epi);
-    return cudaGetLastError() == cudaSuccess ? 0 : -3;
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.gridDim = dim3(grid, 1, 1);
+    cfg.blockDim = dim3(GEMM_THREADS, 1, 1);
+    cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
+    cfg.stream = s;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kern, ta, tb, none, M, N, K, epi) == cudaSuccess ? 0 : -3;
 }
 
 // Clusters of two CTAs (the cluster epilogues, and CTA-pair MMAs), as many as can be resident at
@@ -1190,16 +1204,18 @@ static int launch_cluster(const CUtensorMap& ta, const CUtensorMap& tb, const Ep
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -3;
     cudaLaunchConfig_t cfg = {};
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 2;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.blockDim = dim3(gemm_threads(WIDE), 1, 1);
     cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
     cfg.stream = s;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = 1;  // the occupancy query takes the cluster shape only
     if (!max_clusters[dev]) {
         if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES) != cudaSuccess)
             return -3;
@@ -1214,6 +1230,7 @@ static int launch_cluster(const CUtensorMap& ta, const CUtensorMap& tb, const Ep
                             : (long)tiles_m * (N / 512);
     const int clusters = tiles < max_clusters[dev] ? (int)tiles : max_clusters[dev];
     cfg.gridDim = dim3(2 * clusters, 1, 1);
+    cfg.numAttrs = pdl_enabled() ? 2 : 1;
     return cudaLaunchKernelEx(&cfg, kern, ta, tb, em, M, N, K, epi) == cudaSuccess ? 0 : -3;
 }
 

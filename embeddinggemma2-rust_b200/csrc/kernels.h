@@ -75,6 +75,9 @@ struct GemmEpilogue {
 
 // Number of SMs of the current device (cached per device).
 int num_sms();
+// Launch the tensor-core kernels as programmatic dependents of the previous kernel on the stream
+// (their prologue overlaps its tail); EG2_NO_PDL=1 turns it off.
+bool pdl_enabled();
 
 // 2-D K-major tensor map with 128-byte swizzle: `inner` elements per row (the K extent),
 // `outer` rows, `row_bytes` between rows; box = box_inner x box_outer.

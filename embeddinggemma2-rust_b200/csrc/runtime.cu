@@ -76,6 +76,14 @@ int make_tmap_3d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint6
     return r == CUDA_SUCCESS ? 0 : -1;
 }
 
+bool pdl_enabled() {
+    static const bool on = [] {
+        const char* e = getenv("EG2_NO_PDL");
+        return !(e && e[0] == '1');
+    }();
+    return on;
+}
+
 int num_sms() {
     static int cache[64] = {0};
     int dev = 0;
