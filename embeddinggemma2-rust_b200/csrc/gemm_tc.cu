@@ -276,9 +276,9 @@ EG2_DEV bool epilogue_qkv256_wide(const QkvEpilogue& Q, uint32_t tbase, int row0
 // arithmetic as the general form below with the head geometry known at compile time, the position
 // read once per tile (before pass 1, so its latency hides behind the TMEM reads) and two TMEM loads
 // in flight per wait.
-template <typename TOut, bool TIO>
+template <typename TOut>
 EG2_DEV void epilogue_qkv256(const QkvEpilogue& Q, uint32_t tbase, int row0, int M, int n0, uint8_t* stage,
-                             const float* wsm, const EpiMaps& em, int& nst) {
+                             const float* wsm) {
     const int row = row0 + (int)(threadIdx.x & 31);
     const int qw = Q.nh * 256, kw = Q.nkv * 256;
     TOut* base;
@@ -335,28 +335,22 @@ EG2_DEV void epilogue_qkv256(const QkvEpilogue& Q, uint32_t tbase, int row0, int
                 x2[t] = a2 * cj + a1 * sj;
             }
         }
-        if constexpr (TIO) {
-            tio_store32(&em.m[which], stage, nst++, x1, (int)col1 + c * 32, row0);
-            tio_store32(&em.m[which], stage, nst++, x2, (int)col1 + 128 + c * 32, row0);
-        } else {
-            warp_store32<TOut>(base, ldo, row0, M, col1 + c * 32, x1, stage);
-            warp_store32<TOut>(base, ldo, row0, M, col1 + 128 + c * 32, x2, stage);
-        }
+        warp_store32<TOut>(base, ldo, row0, M, col1 + c * 32, x1, stage);
+        warp_store32<TOut>(base, ldo, row0, M, col1 + 128 + c * 32, x2, stage);
     }
 }
 
-template <typename TOut, int BN, bool TIO>
+template <typename TOut, int BN>
 EG2_DEV void epilogue_qkv(const GemmEpilogue& epi, uint32_t tbase, int row0, int M, int n0, uint8_t* stage,
-                          const float* wsm, const EpiMaps& em, int& nst) {
+                          const float* wsm) {
     const int row = row0 + (int)(threadIdx.x & 31);
     const QkvEpilogue& Q = epi.qkv;
     if constexpr (BN == 256) {
         if (Q.hd == 256 && Q.part == 256) {
-            epilogue_qkv256<TOut, TIO>(Q, tbase, row0, M, n0, stage, wsm, em, nst);
+            epilogue_qkv256<TOut>(Q, tbase, row0, M, n0, stage, wsm);
             return;
         }
     }
-    if constexpr (TIO) return;  // TIO is only launched for the 256-wide form (checked on the host)
     const int hd = Q.hd, qw = Q.nh * hd, kw = Q.nkv * hd;
     TOut* base;
     int nheads, head0;
@@ -1009,7 +1003,7 @@ __global__ void __launch_bounds__(gemm_threads(WIDE), 1)
                                               abort_flag))
                         break;
                 } else {
-                    epilogue_qkv<TOut, BN, TIO>(epi, tbase, row0, M, n0, stage, wsm, em, nst);
+                    epilogue_qkv<TOut, BN>(epi, tbase, row0, M, n0, stage, wsm);
                 }
             } else if constexpr (EPI == EPI_PLE_GATE && TIO) {
                 // GELU(gate) x ple[:, layer] in 16-column chunks: the inputs arrive by TMA in slot
