@@ -67,11 +67,13 @@ struct GemmCfg {
     // EPI_QKV: norm weights + inverse frequencies (<= 3 KB). Cluster modes: this CTA's halves of the
     // norm weights (EPI_QKV_PAIR: wq, wk and 128 inverse frequencies, 2.5 KB), exchange slots
     // [set][slot][128 rows] at +X_OFF (2 KB), exchange barriers [set][slot] at +XB_OFF.
-    // WIDE: the halves' partial sums of squares [set][quadrant][slot][half][32] (4 KB) at +X_OFF,
-    // their barriers [set][quadrant][slot] at +XB_OFF.
+    // WIDE: the two half-warps' partial sums of squares [set][quadrant][slot][half][32] (4 KB) at
+    // +XW_OFF, their barriers [set][quadrant][slot] at +XWB_OFF.
     static constexpr int X_OFF = 2560;
-    static constexpr int XB_OFF = X_OFF + (WIDE ? 4096 : 2048);
-    static constexpr int W_BYTES = XB_OFF + (WIDE ? 128 : 64);
+    static constexpr int XB_OFF = X_OFF + 2048;
+    static constexpr int XW_OFF = XB_OFF + 64;
+    static constexpr int XWB_OFF = XW_OFF + 4096;
+    static constexpr int W_BYTES = WIDE ? XWB_OFF + 128 : XB_OFF + 64;
     static constexpr int SMEM_BYTES = 1024 + OFF_W + W_BYTES;
     static constexpr uint32_t TMEM_COLS = 2 * BN;
 };
@@ -493,7 +495,8 @@ template <typename TIn, int BN, int EPI, typename TOut, bool PAIR = false, bool 
 __global__ void __launch_bounds__(gemm_threads(WIDE), 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ EpiMaps em, int M, int N, int K, GemmEpilogue epi) {
-    static_assert(!WIDE || (EPI == EPI_QKV && PAIR && TIO), "WIDE: the pair QKV epilogue with TMA stores");
+    static_assert(!WIDE || (EPI == EPI_QKV && PAIR && TIO) || (EPI == EPI_QKV_PAIR && TIO),
+                  "WIDE: the QKV epilogues with TMA stores");
     constexpr int NTHREADS = gemm_threads(WIDE);
     static_assert(!TIO || (BN == 256 && (EPI == EPI_ADD_NORM || EPI == EPI_GROUP_NORM || EPI == EPI_QKV_PAIR ||
                                          (PAIR && (EPI == EPI_QKV || EPI == EPI_PLE_GATE || EPI == EPI_GELU_GU)))),
@@ -557,7 +560,7 @@ __global__ void __launch_bounds__(gemm_threads(WIDE), 1)
             for (int x = 0; x < 32; x++) mbar_init(&hbar[x], 1);
         }
         if constexpr (WIDE) {
-            uint64_t* xb = reinterpret_cast<uint64_t*>(smem + Cfg::OFF_W + Cfg::XB_OFF);
+            uint64_t* xb = reinterpret_cast<uint64_t*>(smem + Cfg::OFF_W + Cfg::XWB_OFF);
             for (int x = 0; x < 16; x++) mbar_init(&xb[x], 64);  // both half-warps of a quadrant
         }
         if constexpr (CL) {
@@ -759,7 +762,119 @@ __global__ void __launch_bounds__(gemm_threads(WIDE), 1)
                 }
                 return part + *reinterpret_cast<volatile float*>(mine);
             };
-            if constexpr (EPI == EPI_QKV_PAIR) {
+            if constexpr (EPI == EPI_QKV_PAIR && WIDE) {
+                // 16 warps: this warp takes chunk pairs c = 2 hw, 2 hw + 1 (columns 32 c.. and
+                // 128 + 32 c.. of the CTA's half-head tile, in 16-pair sub-chunks). The head's sum of
+                // squares: the quadrant's two half-warps meet first (as the sliding-layer WIDE form),
+                // then the 8-warp form's exchange with the peer CTA (half 0 sends; both halves wait and
+                // read; a slot is rewritten only after the peer has this CTA's next value, which half 0
+                // sends after the next local meeting, i.e. after half 1 has read the slot).
+                const QkvEpilogue& Q = epi.qkv;
+                const int hidx = n0 / 512;
+                int head, which;
+                const float* w;
+                bool rot;
+                if (hidx < Q.nh) {
+                    head = hidx, w = wsm, rot = true, which = 0;
+                } else if (hidx < Q.nh + Q.nkv) {
+                    head = hidx - Q.nh, w = wsm + BN, rot = true, which = 1;
+                } else {
+                    head = hidx - Q.nh - Q.nkv, w = nullptr, rot = false, which = 2;
+                }
+                float ss = 0.f;
+#pragma unroll 1
+                for (int cc = 0; cc < 2; cc++) {
+                    const int c = 2 * hw + cc;
+                    uint32_t r0[32], r1[32];
+                    tmem_ld32(tbase + c * 32, r0);
+                    tmem_ld32(tbase + 128 + c * 32, r1);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int j = 0; j < 32; j++) {
+                        ss = fmaf(__uint_as_float(r0[j]), __uint_as_float(r0[j]), ss);
+                        ss = fmaf(__uint_as_float(r1[j]), __uint_as_float(r1[j]), ss);
+                    }
+                }
+                {
+                    float* xvl = reinterpret_cast<float*>(smem + Cfg::OFF_W + Cfg::XW_OFF) + (set * 4 + e) * 128 + (xq & 1) * 64;
+                    uint64_t* xbl = reinterpret_cast<uint64_t*>(smem + Cfg::OFF_W + Cfg::XWB_OFF) + (set * 4 + e) * 2 + (xq & 1);
+                    xvl[hw * 32 + lane] = ss;
+                    mbar_arrive(xbl);
+                    if (!mbar_wait(xbl, (xq >> 1) & 1, EG2_DEV_TIMEOUT_GEMM, abort_flag)) break;
+                    ss += *reinterpret_cast<volatile float*>(xvl + (hw ^ 1) * 32 + lane);
+                    xq++;
+                }
+                float tot;
+                {
+                    float* xv = reinterpret_cast<float*>(smem + Cfg::OFF_W + Cfg::X_OFF);  // [set][slot][128]
+                    uint64_t* xb = reinterpret_cast<uint64_t*>(smem + Cfg::OFF_W + Cfg::XB_OFF);
+                    const int rl = 32 * e + lane, x = set * 2 + (k & 1);
+                    float* mine = xv + x * 128 + rl;
+                    if (hw == 0) {
+                        if (rl == 0) mbar_arrive_expect_tx(&xb[x], 128 * 4);
+                        st_async_f32(mapa_shared(smem_u32(mine), crank ^ 1u), ss, mapa_shared(smem_u32(&xb[x]), crank ^ 1u));
+                    }
+                    if (!mbar_wait(&xb[x], (k >> 1) & 1, EG2_DEV_TIMEOUT_GEMM, abort_flag)) break;
+                    tot = ss + *reinterpret_cast<volatile float*>(mine);
+                }
+                const float inv = 1.0f / sqrtf(tot / 512.f + Q.eps);
+                const float* invs = wsm + 2 * BN;
+                const int col1 = head * 512 + 128 * (int)crank, col2 = col1 + 256;
+                const bool live = row < M;
+                const float pf = (rot && live) ? (float)(Q.pos ? Q.pos[(long)row * Q.pos_stride] : row) : 0.f;
+                const uint32_t sw32 = (uint32_t)((lane >> 2) & 1);
+#pragma unroll 1
+                for (int sc = 0; sc < 4; sc++) {
+                    const int p = 64 * hw + 16 * sc;  // first pair (tile column) of the sub-chunk
+                    float x1[16], x2[16];
+                    {
+                        uint32_t a[16], b[16];
+                        tmem_ld16(tbase + p, a);
+                        tmem_ld16(tbase + 128 + p, b);
+                        tmem_ld_wait();
+#pragma unroll
+                        for (int t = 0; t < 16; t++) {
+                            x1[t] = __uint_as_float(a[t]) * inv;
+                            x2[t] = __uint_as_float(b[t]) * inv;
+                        }
+                    }
+                    if (rot) {
+#pragma unroll
+                        for (int t = 0; t < 16; t++) {
+                            const float a1 = x1[t] * w[p + t], a2 = x2[t] * w[128 + p + t];
+                            float sj, cj;
+                            sincos_reduced(pf * invs[p + t], sj, cj);
+                            x1[t] = a1 * cj - a2 * sj;
+                            x2[t] = a2 * cj + a1 * sj;
+                        }
+                    }
+                    // Both 16-column pieces into the two 1 KB halves of slot nst % 2, one fence and group.
+                    uint32_t p1[8], p2[8];
+#pragma unroll
+                    for (int j = 0; j < 8; j++) {
+                        p1[j] = bf16x2_bits(x1[2 * j], x1[2 * j + 1]);
+                        p2[j] = bf16x2_bits(x2[2 * j], x2[2 * j + 1]);
+                    }
+                    uint8_t* buf = stage + (nst & 1) * 2048;
+                    if (lane == 0) bulk_wait_read<1>();
+                    __syncwarp();
+#pragma unroll
+                    for (int j = 0; j < 2; j++) {
+                        *reinterpret_cast<uint4*>(buf + lane * 32 + ((j ^ sw32) << 4)) =
+                            make_uint4(p1[4 * j], p1[4 * j + 1], p1[4 * j + 2], p1[4 * j + 3]);
+                        *reinterpret_cast<uint4*>(buf + 1024 + lane * 32 + ((j ^ sw32) << 4)) =
+                            make_uint4(p2[4 * j], p2[4 * j + 1], p2[4 * j + 2], p2[4 * j + 3]);
+                    }
+                    fence_proxy_async();
+                    __syncwarp();
+                    if (lane == 0) {
+                        tma_store_2d(&em.m[which], buf, col1 + p, row0);
+                        tma_store_2d(&em.m[which], buf + 1024, col2 + p, row0);
+                        bulk_commit();
+                    }
+                    nst++;
+                }
+            } else if constexpr (EPI == EPI_QKV_PAIR) {
                 // One head per 512-column group; as EPI_QKV (rowops.cu qkv_post_kernel arithmetic) with
                 // the head's sum of squares completed by the exchange (slots alternate by tile parity).
                 const QkvEpilogue& Q = epi.qkv;
@@ -997,8 +1112,8 @@ __global__ void __launch_bounds__(gemm_threads(WIDE), 1)
                 }
             } else if constexpr (EPI == EPI_QKV) {
                 if constexpr (WIDE) {
-                    float* xv = reinterpret_cast<float*>(smem + Cfg::OFF_W + Cfg::X_OFF) + (set * 4 + e) * 128;
-                    uint64_t* xbq = reinterpret_cast<uint64_t*>(smem + Cfg::OFF_W + Cfg::XB_OFF) + (set * 4 + e) * 2;
+                    float* xv = reinterpret_cast<float*>(smem + Cfg::OFF_W + Cfg::XW_OFF) + (set * 4 + e) * 128;
+                    uint64_t* xbq = reinterpret_cast<uint64_t*>(smem + Cfg::OFF_W + Cfg::XWB_OFF) + (set * 4 + e) * 2;
                     if (!epilogue_qkv256_wide(epi.qkv, tbase, row0, M, n0, stage, wsm, em, nst, hw, xv, xbq, xq,
                                               abort_flag))
                         break;
@@ -1350,13 +1465,16 @@ int gemm_tc(GemmKind kind, const void* A, long lda, const void* W, long ldw, int
             case EPI_QKV_PAIR: {
                 const QkvEpilogue& q = epi.qkv;
                 if (!qkv_pair_fusable(q) || N != (q.nh + 2 * q.nkv) * 512) return -1;
-                // q / k / v by TMA store, 32 x 32 boxes.
+                // q / k / v by TMA store, 16 x 32 boxes (32-byte swizzle) for the 16-warp epilogue.
                 EpiMaps em = {};
-                if (out_map(&em.m[0], q.q, (long)q.nh * 512, (long)q.nh * 512) ||
-                    out_map(&em.m[1], q.k, (long)q.nkv * 512, (long)q.nkv * 512) ||
-                    out_map(&em.m[2], q.v, (long)q.nkv * 512, (long)q.nkv * 512))
+                auto qkv_map = [&](CUtensorMap* m, const void* base, long cols) {
+                    return make_tmap_2d(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, base, cols, M, cols * 2, 16, 32,
+                                        CU_TENSOR_MAP_SWIZZLE_32B);
+                };
+                if (qkv_map(&em.m[0], q.q, (long)q.nh * 512) || qkv_map(&em.m[1], q.k, (long)q.nkv * 512) ||
+                    qkv_map(&em.m[2], q.v, (long)q.nkv * 512))
                     return -1;
-                return launch_cluster<EPI_QKV_PAIR, bf16_t, false, true>(ta, tb, em, M, N, K, epi, s);
+                return launch_cluster<EPI_QKV_PAIR, bf16_t, false, true, true>(ta, tb, em, M, N, K, epi, s);
             }
         }
     } else {
