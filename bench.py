@@ -137,8 +137,8 @@ def ncu_traffic(kernel_label: str):
     return None
 
 
-def make_checkpoint(dirpath: Path):
-    pkg("weights").make_random_checkpoint(dirpath, seed=0, vision=False)
+def make_checkpoint(dirpath: Path, vision: bool = False):
+    pkg("weights").make_random_checkpoint(dirpath, seed=0, vision=vision)
 
 
 MIXED_DOCS, MIXED_LO, MIXED_HI, MIXED_SEED = 64, 128, 2208, 7
@@ -203,6 +203,56 @@ def run_long(tb, cfg, stream):
             "gpus": 1}
 
 
+VISION_IMAGES, VISION_GRID, VISION_SEED = 32, 48, 5
+QUERIES, QUERY_LEN, QUERY_SEED = 4096, 17, 17
+
+
+def run_c5(dev, tb, cfg, stream):
+    """C5 on one GPU: (1) the vision tower over 32 seeded uniform-noise images of 48 x 48 = 2,304
+    patches (a 768 x 768 image after the reference's resize rule), one eg2_vision_encode call per image
+    with host patches in and host soft tokens out, wall-clock time per call (the call returns after
+    its work completes); (2) 4,096 queries of 17 seeded ids as one packed pass on device buffers."""
+    import torch
+
+    B = pkg("backend")
+    vt = B.VisionBackend(dev)
+    rng = np.random.default_rng(VISION_SEED)
+    g = VISION_GRID
+    pos = np.array([[x, y] for y in range(g) for x in range(g)], dtype=np.int32)
+    images = [rng.random((g * g, 3 * cfg.vision.patch_size ** 2), dtype=np.float32) for _ in range(VISION_IMAGES)]
+    for img in images[:3]:
+        vt.encode(img, pos, g, g)
+    t0 = time.perf_counter()
+    for img in images:
+        soft = vt.encode(img, pos, g, g)
+    vis_s = time.perf_counter() - t0
+    assert np.isfinite(soft).all()
+
+    ids = np.random.default_rng(QUERY_SEED).integers(0, cfg.text.vocab_size, size=QUERIES * QUERY_LEN).astype(np.uint32)
+    ids_dev = torch.from_numpy(ids.view(np.int32)).cuda()
+    out_dev = torch.empty((QUERIES, sum(DIMS)), dtype=torch.float32, device="cuda")
+    lens = [QUERY_LEN] * QUERIES
+    for _ in range(3):
+        tb.embed_ids_device(ids_dev.data_ptr(), lens, DIMS, out_dev.data_ptr(), stream.cuda_stream)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 5
+    e0.record(stream)
+    for _ in range(reps):
+        tb.embed_ids_device(ids_dev.data_ptr(), lens, DIMS, out_dev.data_ptr(), stream.cuda_stream)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    q_ms = e0.elapsed_time(e1) / reps
+    return {"vision": {"images": VISION_IMAGES, "patches_per_image": g * g, "soft_tokens_per_image": int(soft.shape[0]),
+                       "ms_per_image": round(vis_s * 1000.0 / VISION_IMAGES, 3),
+                       "images_per_s": round(VISION_IMAGES / vis_s, 2),
+                       "call": "eg2_vision_encode (host patches -> host soft tokens), one image per call",
+                       "data": f"uniform noise patches in [0, 1), seed {VISION_SEED}"},
+            "queries": {"queries": QUERIES, "tokens": QUERY_LEN, "ms_per_batch": round(q_ms, 3),
+                        "queries_per_s": round(QUERIES / (q_ms / 1000.0), 1), "gpus": 1,
+                        "call": "eg2_embed_packed_device, one packed pass"}}
+
+
 # ---------------------------------------------------------------------------------------------
 def cpu_baseline_run(model_dir: Path, docs: int, seed: int):
     """The oracle (C restatement of the reference CPU f32 path) on `docs` documents of SEQ_LEN."""
@@ -253,6 +303,7 @@ def main():
     ap.add_argument("--docs-per-gpu", type=int, default=64)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-c5", action="store_true", help="skip the vision / 4,096-query leg")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -287,7 +338,7 @@ def main():
     tmp = Path(tempfile.gettempdir()) / f"eg2_bench_ckpt_{os.environ.get('MASTER_PORT', 'solo')}"
     if rank == 0:
         tmp.mkdir(parents=True, exist_ok=True)
-        make_checkpoint(tmp)
+        make_checkpoint(tmp, vision=True)
     barrier()
     dev = B.Device(tmp, local, "bf16")
     tb = B.TextBackend(dev)
@@ -353,6 +404,8 @@ def main():
     mixed = run_mixed(tb, cfg, stream, rank, world, args, barrier, max_over_ranks)
     # ---- C4: one 11,774-token document (rank 0 only; the other ranks wait at the next barrier) ----
     long_case = run_long(tb, cfg, stream) if rank == 0 else None
+    # ---- C5 on one GPU: vision tower per image, and a batch of 4,096 short queries (rank 0 only) ----
+    c5 = run_c5(dev, tb, cfg, stream) if rank == 0 and not args.no_c5 else None
     barrier()
 
     # ---- per-op device time shares (CUDA events around each op, one profiled step) ----
@@ -425,6 +478,7 @@ def main():
             "cpu_baseline": cpu,
             "mixed_c3": mixed,
             "long_c4": long_case,
+            "c5": c5,
         }
         print(json.dumps(line))
     dev.close()

@@ -562,9 +562,306 @@ done:
     }
 }
 
+// ---------------------------------------------------------------------------------------------
+// Head 64 (the vision tower: 12 query heads, each with its own K/V head), one CTA per (256 query
+// tokens, head): two 128-row query tiles share every K / V tile.
+//
+// Per 128-key tile and query tile the tensor work is 2 x 256 cycles (S = Q K^T at N = 128, K = 64;
+// O += P V at N = 64, K = 128) while the softmax needs ~1,000 cycles of exp2 on the SM's MUFU units,
+// so the kernel is softmax-bound: the two query tiles' softmax warp groups run concurrently and the
+// MMAs of one run under the other's softmax. TMEM (512 columns): S_h at [128 h, 128 h + 128), P_h
+// (packed bf16 pairs) at [256 + 64 h, +64), O_h at [384 + 64 h, +64). S_h(j + 1) is computed as soon
+// as softmax_h(j) has copied S_h(j) into registers; P_h(j + 1) is written once P V_h(j) has completed.
+// K / V ring of 16 KB units ([128 keys x 64 channels], 128-byte swizzle) in the order K(0), then per
+// key tile j K(j + 1) (if any) and V(j).
+//
+//   warp 0       TMA producer
+//   warp 1       TMEM allocation; lane 0 issues S = Q K^T
+//   warps 2..5   softmax and O epilogue of query tile 0 (one thread per row); warps 6..9 of tile 1
+//   warp 10      lane 0 issues O += P V
+// ---------------------------------------------------------------------------------------------
+constexpr int A64_UNIT = 16384;
+constexpr int A64_RING = 6;
+constexpr int A64_PV_WARP = 10;
+constexpr int A64_THREADS = 32 * (A64_PV_WARP + 1);
+constexpr int A64_OFF_R = 2 * A64_UNIT;
+constexpr int A64_OFF_BAR = A64_OFF_R + A64_RING * A64_UNIT;
+// q, ring full / empty, s_full[2], s_empty[2], p_full[2], pv_done[2], drain[2]
+constexpr int A64_N_BARS = 1 + 2 * A64_RING + 10;
+constexpr int A64_SMEM = 1024 + A64_OFF_BAR + A64_N_BARS * 8 + 16;
+
+__global__ void __launch_bounds__(A64_THREADS, 1)
+    attention_d64_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                         const __grid_constant__ CUtensorMap tmV, AttParams prm) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + A64_OFF_BAR);
+    uint64_t* q_full = bars;
+    uint64_t* r_full = bars + 1;
+    uint64_t* r_empty = r_full + A64_RING;
+    uint64_t* s_full = r_empty + A64_RING;
+    uint64_t* s_empty = s_full + 2;
+    uint64_t* p_full = s_empty + 2;
+    uint64_t* pv_done = p_full + 2;
+    uint64_t* drain = pv_done + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + A64_N_BARS);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int head = (int)blockIdx.y;
+    const AttnTile tile = prm.tiles[blockIdx.x];
+    const int W = prm.window;
+    const int q_last = min(tile.q0 + 256, tile.len) - 1;
+    const int k_lo = (W >= 0) ? max(0, tile.q0 - W) : 0;
+    const int k_hi = (W >= 0) ? min(tile.len, q_last + W + 1) : tile.len;
+    const int n_kt = tile.len > 0 ? (k_hi - k_lo + 127) / 128 : 0;
+
+    if (threadIdx.x == 0) {
+        mbar_init(q_full, 1);
+        for (int u = 0; u < A64_RING; u++) {
+            mbar_init(&r_full[u], 1);
+            mbar_init(&r_empty[u], 1);
+        }
+        for (int h = 0; h < 2; h++) {
+            mbar_init(&s_full[h], 1);
+            mbar_init(&s_empty[h], 128);
+            mbar_init(&p_full[h], 128);
+            mbar_init(&pv_done[h], 1);
+            mbar_init(&drain[h], 1);
+        }
+        *abort_flag = 0;
+        fence_mbarrier_init();
+    }
+    if (warp == 1) tmem_alloc(tmem_slot, 512);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const uint32_t t_s = tmem, t_p = tmem + 256, t_o = tmem + 384;
+    // Ring positions of K(j) and V(j).
+    auto ring_k = [&](int j) { return j == 0 ? 0 : 2 * j - 1; };
+    auto ring_v = [&](int j) { return j + 1 < n_kt ? 2 * j + 2 : 2 * j + 1; };
+
+    if (n_kt == 0) {
+        // Padding tile: nothing to do.
+    } else if (warp == 0) {
+        if (lane == 0) {
+            int issued = 0;  // ring loads issued so far (load i: slot i % A64_RING, phase (i / A64_RING) & 1)
+            mbar_arrive_expect_tx(q_full, 2 * A64_UNIT);
+            for (int h = 0; h < 2; h++)
+                tma_load_3d(smem + h * A64_UNIT, &tmQ, q_full, 0, head, tile.row0 + tile.q0 + 128 * h);
+            int u = 0;
+            uint32_t uph = 0;
+            auto load = [&](const CUtensorMap* m, int j) -> bool {
+                if (!mbar_wait(&r_empty[u], uph ^ 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) return false;
+                mbar_arrive_expect_tx(&r_full[u], A64_UNIT);
+                tma_load_3d(smem + A64_OFF_R + u * A64_UNIT, m, &r_full[u], 0, head, tile.row0 + k_lo + 128 * j);
+                issued++;
+                if (++u == A64_RING) {
+                    u = 0;
+                    uph ^= 1;
+                }
+                return true;
+            };
+            bool ok = load(&tmK, 0);
+            for (int j = 0; ok && j < n_kt; j++) {
+                if (j + 1 < n_kt) ok = load(&tmK, j + 1);
+                if (ok) ok = load(&tmV, j);
+            }
+            // Every load has landed before the CTA may end (on the error path too).
+            mbar_drain(q_full, 0, 200000000ull);
+            for (int i = max(0, issued - A64_RING); i < issued; i++)
+                mbar_drain(&r_full[i % A64_RING], (uint32_t)((i / A64_RING) & 1), 200000000ull);
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            constexpr uint32_t idesc_s = umma_idesc(128, 128, 1);
+            const uint64_t dk0 = umma_desc_sw128(smem_u32(smem + A64_OFF_R), 16, 1024);
+            if (!mbar_wait(q_full, 0, EG2_DEV_TIMEOUT_ATTN, abort_flag)) goto done;
+            for (int j = 0; j < n_kt; j++) {
+                const int iu = ring_k(j), u = iu % A64_RING;
+                if (!mbar_wait(&r_full[u], (iu / A64_RING) & 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) goto done;
+                for (int h = 0; h < 2; h++) {
+                    // S_h is free once softmax_h(j - 1) has copied it into registers.
+                    if (j >= 1 && !mbar_wait(&s_empty[h], (j - 1) & 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) goto done;
+                    tc_fence_after();
+                    const uint64_t dq = umma_desc_sw128(smem_u32(smem + h * A64_UNIT), 16, 1024);
+#pragma unroll
+                    for (int kk = 0; kk < 4; kk++)
+                        mma_bf16(t_s + 128 * h, dq + (uint64_t)(2 * kk), dk0 + (uint64_t)(u * (A64_UNIT >> 4) + 2 * kk),
+                                 idesc_s, kk != 0);
+                    mma_commit(&s_full[h]);
+                }
+                mma_commit(&r_empty[u]);
+            }
+        }
+    } else if (warp == A64_PV_WARP) {
+        if (lane == 0) {
+            constexpr uint32_t idesc_o = umma_idesc(128, 64, 1, /*b_mn_major=*/true);
+            const uint64_t dv0 = umma_desc_sw128(smem_u32(smem + A64_OFF_R), 16384, 1024);
+            for (int j = 0; j < n_kt; j++) {
+                const int iu = ring_v(j), u = iu % A64_RING;
+                if (!mbar_wait(&r_full[u], (iu / A64_RING) & 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) goto done;
+                for (int h = 0; h < 2; h++) {
+                    if (!mbar_wait(&p_full[h], j & 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) goto done;
+                    tc_fence_after();
+                    // 16 keys per MMA: 8 packed P columns, 16 V rows (2,048 bytes).
+#pragma unroll
+                    for (int kk = 0; kk < 8; kk++)
+                        mma_bf16_ts(t_o + 64 * h, t_p + 64 * h + 8 * kk, dv0 + (uint64_t)(u * (A64_UNIT >> 4) + kk * (2048 >> 4)),
+                                    idesc_o, (j | kk) != 0);
+                    mma_commit(&pv_done[h]);
+                }
+                mma_commit(&r_empty[u]);
+            }
+        }
+    } else {
+        const int h = (warp - 2) >> 2;
+        const int e = warp & 3;
+        const int r = 32 * e + lane;
+        const uint32_t lane_off = (uint32_t)(32 * e) << 16;
+        const int tok = tile.q0 + 128 * h + r;
+        const bool row_valid = tok < tile.len;
+        const float LOG2E = 1.4426950408889634f;
+        float m_used = -INFINITY, l = 0.f;
+        bool ok = true;
+        for (int j = 0; j < n_kt; j++) {
+            if (!mbar_wait(&s_full[h], j & 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            uint32_t su[128];
+#pragma unroll
+            for (int c = 0; c < 4; c++) tmem_ld32(t_s + 128 * h + 32 * c + lane_off, *reinterpret_cast<uint32_t(*)[32]>(su + 32 * c));
+            tmem_ld_wait();
+            tc_fence_before();
+            mbar_arrive(&s_empty[h]);
+            float* sv = reinterpret_cast<float*>(su);
+            const int kbase = k_lo + 128 * j;
+            int lo_c = 0, hi_c = min(128, tile.len - kbase);
+            if (W >= 0 && row_valid) {
+                lo_c = max(lo_c, tok - W - kbase);
+                hi_c = min(hi_c, tok + W + 1 - kbase);
+            }
+            if (!__all_sync(0xffffffffu, lo_c <= 0 && hi_c >= 128)) {
+#pragma unroll
+                for (int c = 0; c < 128; c++) sv[c] = (c >= lo_c && c < hi_c) ? sv[c] : -INFINITY;
+            }
+            float mx[8];
+#pragma unroll
+            for (int c = 0; c < 8; c++) mx[c] = sv[c];
+#pragma unroll
+            for (int c = 8; c < 128; c++) mx[c & 7] = fmaxf(mx[c & 7], sv[c]);
+            const float mt =
+                fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+            float factor = 1.f;
+            bool need = false;
+            if (mt > m_used) {
+                if (m_used == -INFINITY) {
+                    m_used = mt;
+                } else if ((mt - m_used) * LOG2E > ATT_RESCALE_LOG2) {
+                    factor = ex2_approx((m_used - mt) * LOG2E);
+                    m_used = mt;
+                    need = true;
+                }
+            }
+            if (j >= 1) {
+                // P V_h(j - 1) has read P_h and added into O_h: both may be rewritten.
+                if (!mbar_wait(&pv_done[h], (j - 1) & 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                if (__any_sync(0xffffffffu, need)) {
+#pragma unroll 1
+                    for (int c = 0; c < 2; c++) {
+                        uint32_t o[32];
+                        tmem_ld32(t_o + 64 * h + 32 * c + lane_off, o);
+                        tmem_ld_wait();
+#pragma unroll
+                        for (int q = 0; q < 32; q++) o[q] = __float_as_uint(__uint_as_float(o[q]) * factor);
+                        tmem_st32(t_o + 64 * h + 32 * c + lane_off, o);
+                    }
+                }
+            }
+            l *= factor;
+            // Row sum over the bf16-ROUNDED probabilities that multiply V (weights sum to exactly l).
+            const float bias = (m_used == -INFINITY) ? 0.f : -m_used * LOG2E;
+            float lsum[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int qtr = 0; qtr < 4; qtr++) {
+                uint32_t pk[16];
+#pragma unroll
+                for (int q = 0; q < 16; q++) {
+                    const float p0 = ex2_approx(fmaf(sv[32 * qtr + 2 * q], LOG2E, bias));
+                    const float p1 = ex2_approx(fmaf(sv[32 * qtr + 2 * q + 1], LOG2E, bias));
+                    pk[q] = bf16x2_bits(p0, p1);
+                    lsum[q & 3] += __uint_as_float(pk[q] << 16) + __uint_as_float(pk[q] & 0xffff0000u);
+                }
+                tmem_st16(t_p + 64 * h + 16 * qtr + lane_off, pk);
+            }
+            l += (lsum[0] + lsum[1]) + (lsum[2] + lsum[3]);
+            tmem_st_wait();
+            tc_fence_before();
+            mbar_arrive(&p_full[h]);
+        }
+        if (ok && mbar_wait(&pv_done[h], (n_kt - 1) & 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) {
+            tc_fence_after();
+            const float inv = (l > 0.f) ? 1.f / l : 0.f;
+            bf16_t* orow = prm.out + ((long)(tile.row0 + tok) * prm.nh + head) * 64;
+#pragma unroll 1
+            for (int c = 0; c < 2; c++) {
+                uint32_t o[32];
+                tmem_ld32(t_o + 64 * h + 32 * c + lane_off, o);
+                tmem_ld_wait();
+                if (row_valid) {
+#pragma unroll
+                    for (int q = 0; q < 2; q++) {
+                        uint32_t pk[8];
+#pragma unroll
+                        for (int i = 0; i < 8; i++)
+                            pk[i] = bf16x2_bits(__uint_as_float(o[16 * q + 2 * i]) * inv,
+                                                __uint_as_float(o[16 * q + 2 * i + 1]) * inv);
+                        st_global_v8(orow + 32 * c + 16 * q, pk);
+                    }
+                }
+            }
+        }
+    }
+done:
+    // Every MMA has completed before TMEM is freed: each issuing thread waits for its own.
+    if (n_kt > 0 && (warp == 1 || warp == A64_PV_WARP) && lane == 0) {
+        uint64_t* d = &drain[warp == 1 ? 0 : 1];
+        mma_commit(d);
+        mbar_wait(d, 0, EG2_DEV_TIMEOUT_ATTN, nullptr);
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 512);
+    }
+}
+
+static int launch_d64(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const AttParams& prm,
+                      cudaStream_t s) {
+    static bool attr_set[64] = {false};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -3;
+    if (!attr_set[dev]) {
+        if (cudaFuncSetAttribute(attention_d64_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, A64_SMEM) != cudaSuccess)
+            return -3;
+        attr_set[dev] = true;
+    }
+    attention_d64_kernel<<<dim3((unsigned)prm.n_tiles, (unsigned)prm.nh, 1), A64_THREADS, A64_SMEM, s>>>(mq, mk, mv, prm);
+    return cudaGetLastError() == cudaSuccess ? 0 : -3;
+}
+
 int attention_tc_tile_tokens(int nh, int nkv, int hd) {
     if (nkv <= 0 || nh % nkv) return 0;
     const int G = nh / nkv;
+    if (hd == 64) return G == 1 ? 256 : 0;  // two 128-row query tiles of one head
     if (128 % G) return 0;
     // CTA pairs: one tile covers both CTAs' 128 rows.
     (void)hd;
@@ -610,8 +907,29 @@ static int launch_pair(const CUtensorMap& mq, const CUtensorMap& mk, const CUten
 int attention_tc(const bf16_t* q, const bf16_t* k, const bf16_t* v, bf16_t* out, long rows, const AttnTile* tiles,
                  int n_tiles, int nh, int nkv, int hd, int window, cudaStream_t s) {
     if (rows <= 0 || n_tiles <= 0) return 0;
-    if ((hd != 256 && hd != 512) || !attention_tc_tile_tokens(nh, nkv, hd)) return -1;
+    if ((hd != 64 && hd != 256 && hd != 512) || !attention_tc_tile_tokens(nh, nkv, hd)) return -1;
     const int G = nh / nkv;
+    if (hd == 64) {
+        // q / k / v [rows, heads, 64]: box (64 ch, 1 head, 128 tokens) = 128 rows of 128 B.
+        CUtensorMap mq, mk, mv;
+        const CUtensorMapDataType dt = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+        if (make_tmap_3d(&mq, dt, q, 64, nh, rows, 128, (uint64_t)nh * 128, 64, 1, 128) ||
+            make_tmap_3d(&mk, dt, k, 64, nkv, rows, 128, (uint64_t)nkv * 128, 64, 1, 128) ||
+            make_tmap_3d(&mv, dt, v, 64, nkv, rows, 128, (uint64_t)nkv * 128, 64, 1, 128))
+            return -1;
+        AttParams prm{};
+        prm.tiles = tiles;
+        prm.out = out;
+        prm.nh = nh;
+        prm.nkv = nkv;
+        prm.hd = 64;
+        prm.window = window;
+        prm.G = 1;
+        prm.tq = 256;
+        prm.nsplit = 1;
+        prm.n_tiles = n_tiles;
+        return launch_d64(mq, mk, mv, prm, s);
+    }
     const int tq = 128 / G;  // query tokens per CTA (128 MMA rows)
     CUtensorMap mq, mk, mv, mo;
     const CUtensorMapDataType dt = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;

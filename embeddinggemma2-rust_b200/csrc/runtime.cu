@@ -406,8 +406,8 @@ struct eg2_ctx {
     void *v_x = nullptr, *v_t = nullptr, *v_qkv = nullptr, *v_q = nullptr, *v_k = nullptr, *v_v = nullptr, *v_a = nullptr,
          *v_o = nullptr, *v_gate = nullptr, *v_gu = nullptr;
     int *v_pos = nullptr, *v_seq_start = nullptr, *v_seq_len = nullptr;
-    eg2::AttnTile* v_tiles = nullptr;
-    long v_tiles_cap = 0;
+    eg2::AttnTile* v_tiles = nullptr;            // head-64 attention tiles of the current image
+    std::vector<int32_t> v_pos_host;              // positions the RoPE tables in v_cs / v_sn were built for
     int* bad_flag = nullptr;
     // CUDA graphs of short embedding passes (<= 128 rows), one per (row bucket, pooled dims); a graph
     // holds device addresses, so any device (re)allocation (buf_gen) invalidates it.
@@ -1082,6 +1082,10 @@ static void enqueue_vision(eg2_ctx* c, long n, int gh, int gw) {
             KL(attention_simt<float>((const float*)c->v_q, (const float*)c->v_k, (const float*)c->v_v, (float*)c->v_a,
                                      c->v_seq_start, c->v_seq_len, n, nh, nkv, hd, -1, c->stream),
                "attention");
+        else if (attention_tc_tile_tokens(nh, nkv, hd) == 256 && hd == 64)
+            KL(attention_tc((const bf16_t*)c->v_q, (const bf16_t*)c->v_k, (const bf16_t*)c->v_v, (bf16_t*)c->v_a, n,
+                            c->v_tiles, (int)((n + 255) / 256), nh, nkv, hd, -1, c->stream),
+               "attention_tc");
         else
             KL(attention_simt<bf16_t>((const bf16_t*)c->v_q, (const bf16_t*)c->v_k, (const bf16_t*)c->v_v, (bf16_t*)c->v_a,
                                       c->v_seq_start, c->v_seq_len, n, nh, nkv, hd, -1, c->stream),
@@ -1487,7 +1491,7 @@ int eg2_vision_encode(eg2_ctx* c, const float* patches, const int32_t* pos_xy, i
             void** bufs[] = {(void**)&c->v_hidden, (void**)&c->v_pooled, (void**)&c->v_cs, (void**)&c->v_sn, (void**)&c->v_soft,
                              (void**)&c->v_inv,
                              &c->v_x, &c->v_t, &c->v_qkv, &c->v_q, &c->v_k, &c->v_v, &c->v_a, &c->v_o, &c->v_gate, &c->v_gu,
-                             (void**)&c->v_pos, (void**)&c->v_seq_start, (void**)&c->v_seq_len};
+                             (void**)&c->v_pos, (void**)&c->v_seq_start, (void**)&c->v_seq_len, (void**)&c->v_tiles};
             for (void** b : bufs) {
                 dfree(c, *b);
                 *b = nullptr;
@@ -1512,27 +1516,42 @@ int eg2_vision_encode(eg2_ctx* c, const float* patches, const int32_t* pos_xy, i
             c->v_pos = (int*)dalloc(c, cap * 2 * 4);
             c->v_seq_start = (int*)dalloc(c, cap * 4);
             c->v_seq_len = (int*)dalloc(c, cap * 4);
+            c->v_tiles = (AttnTile*)dalloc(c, (cap / 256 + 1) * sizeof(AttnTile));
+            c->v_pos_host.clear();
             c->vcap = cap;
         }
-        // Axial RoPE tables [n, hd / 2]: x angles in the first hd / 4 entries, y in the next (src/vision.rs:114-136).
-        std::vector<float> inv = rope_inv_freq(vc.theta, hd / 2);
-        const int q4 = hd / 4;
-        std::vector<float> cs((size_t)n * (hd / 2)), sn((size_t)n * (hd / 2));
-        for (long t = 0; t < n; t++)
-            for (int axis = 0; axis < 2; axis++)
-                for (int i = 0; i < q4; i++) {
-                    const float f = (float)pos_xy[2 * t + axis] * inv[i];
-                    const int col = axis * q4 + i;
-                    cs[(size_t)t * (hd / 2) + col] = cosf(f);
-                    sn[(size_t)t * (hd / 2) + col] = sinf(f);
-                }
-        CK(cudaMemcpyAsync(c->v_inv, inv.data(), inv.size() * 4, cudaMemcpyHostToDevice, c->stream));
-        std::vector<int> zeros(n, 0), lens_v(n, (int)n);
-        CK(cudaMemcpyAsync(c->v_cs, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice, c->stream));
-        CK(cudaMemcpyAsync(c->v_sn, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice, c->stream));
-        CK(cudaMemcpyAsync(c->v_pos, pos_xy, n * 2 * 4, cudaMemcpyHostToDevice, c->stream));
-        CK(cudaMemcpyAsync(c->v_seq_start, zeros.data(), n * 4, cudaMemcpyHostToDevice, c->stream));
-        CK(cudaMemcpyAsync(c->v_seq_len, lens_v.data(), n * 4, cudaMemcpyHostToDevice, c->stream));
+        // Position-dependent tables, rebuilt only when the positions differ from the previous image's
+        // (images of one size share them).
+        if (c->v_pos_host.size() != (size_t)(2 * n) ||
+            std::memcmp(c->v_pos_host.data(), pos_xy, (size_t)n * 2 * sizeof(int32_t)) != 0) {
+            // Axial RoPE tables [n, hd / 2]: x angles in the first hd / 4 entries, y in the next (src/vision.rs:114-136).
+            std::vector<float> inv = rope_inv_freq(vc.theta, hd / 2);
+            const int q4 = hd / 4;
+            std::vector<float> cs((size_t)n * (hd / 2)), sn((size_t)n * (hd / 2));
+            for (long t = 0; t < n; t++)
+                for (int axis = 0; axis < 2; axis++)
+                    for (int i = 0; i < q4; i++) {
+                        const float f = (float)pos_xy[2 * t + axis] * inv[i];
+                        const int col = axis * q4 + i;
+                        cs[(size_t)t * (hd / 2) + col] = cosf(f);
+                        sn[(size_t)t * (hd / 2) + col] = sinf(f);
+                    }
+            // One sequence of n patches: row metadata for the CUDA-core attention, 256-token tiles for
+            // the tensor-core one.
+            std::vector<int> zeros(n, 0), lens_v(n, (int)n);
+            std::vector<AttnTile> tiles;
+            for (int q0 = 0; q0 < n; q0 += 256) tiles.push_back(AttnTile{0, (int)n, q0});
+            CK(cudaMemcpyAsync(c->v_inv, inv.data(), inv.size() * 4, cudaMemcpyHostToDevice, c->stream));
+            CK(cudaMemcpyAsync(c->v_cs, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice, c->stream));
+            CK(cudaMemcpyAsync(c->v_sn, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice, c->stream));
+            CK(cudaMemcpyAsync(c->v_pos, pos_xy, n * 2 * 4, cudaMemcpyHostToDevice, c->stream));
+            CK(cudaMemcpyAsync(c->v_seq_start, zeros.data(), n * 4, cudaMemcpyHostToDevice, c->stream));
+            CK(cudaMemcpyAsync(c->v_seq_len, lens_v.data(), n * 4, cudaMemcpyHostToDevice, c->stream));
+            CK(cudaMemcpyAsync(c->v_tiles, tiles.data(), tiles.size() * sizeof(AttnTile), cudaMemcpyHostToDevice, c->stream));
+            // The host vectors die at the end of this block.
+            CK(cudaStreamSynchronize(c->stream));
+            c->v_pos_host.assign(pos_xy, pos_xy + 2 * n);
+        }
         CK(cudaMemcpyAsync(c->v_x, patches, n * pd * 4, cudaMemcpyHostToDevice, c->stream));
         // 2 (x - 0.5) into the GEMM input buffer in the storage type.
         if (bf16_mode(c))

@@ -49,7 +49,8 @@ def sample(rng, rows, width, sigma, bf16):
     return W.bf16_round(a) if bf16 else a
 
 
-CONFIGS = [(4, 2, 256, [None, 512, 7]), (4, 1, 512, [None, 7])]
+# Text sliding (head 256) and global (head 512) layers; the vision tower (12 heads of 64, one K/V head each).
+CONFIGS = [(4, 2, 256, [None, 512, 7]), (4, 1, 512, [None, 7]), (12, 12, 64, [None, 7])]
 
 
 @pytest.mark.parametrize("nh,nkv,hd,windows", CONFIGS)

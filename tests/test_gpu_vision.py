@@ -22,7 +22,10 @@ def test_vision_soft_tokens(prec, oracle_vision, request):
     dev = request.getfixturevalue(f"dev_{prec}")
     vb = B.VisionBackend(dev)
     prof = V.for_precision(prec)
-    for gh, gw in ((12, 12), (6, 21)):
+    # 576 patches: three 256-token attention tiles, the last with 64 live rows. 12 x 12 and 6 x 24
+    # have the same patch count with different positions (the position tables are rebuilt), and the
+    # second 24 x 24 image reuses the tables of the first.
+    for gh, gw in ((12, 12), (6, 24), (6, 21), (24, 24), (24, 24)):
         patches, pos = image(gh, gw, gh * 100 + gw)
         pooled_want, soft_want = oracle_vision.encode(patches, pos, gh, gw)
         soft, pooled = vb.encode(patches, pos, gh, gw, pooled=True)
