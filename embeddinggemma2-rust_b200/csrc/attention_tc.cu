@@ -24,6 +24,8 @@ constexpr float ATT_RESCALE_LOG2 = 8.f;
 struct AttParams {
     const AttnTile* tiles;
     bf16_t* out;
+    const int* seq_start;  // per row: first row of its sequence (null: a tile's rows are one sequence)
+    const int* seq_len;
     int nh, nkv, hd, window, G, tq, nsplit, n_tiles;
 };
 
@@ -412,6 +414,12 @@ __global__ void __launch_bounds__(ApCfg<DQK>::THREADS, 1)
             const AttnTile& tile = x.tile;
             const int tok = x.q0r + r / G;
             const bool row_valid = tok < tile.len;
+            // Keys of this row's sequence, relative to the tile's first row.
+            int rs = 0, re = tile.len;
+            if (prm.seq_start && row_valid) {
+                rs = prm.seq_start[tile.row0 + tok] - tile.row0;
+                re = rs + prm.seq_len[tile.row0 + tok];
+            }
             float m_used = -INFINITY, l = 0.f;
             for (int j = 0; j < n_kt; j++, T++) {
                 const int b = T & 1;
@@ -438,7 +446,7 @@ __global__ void __launch_bounds__(ApCfg<DQK>::THREADS, 1)
                 }
                 // Valid key columns of this row in this tile, relative to this thread's first column.
                 const int kbase = x.k_lo + j * AP_BN + ch * 64;
-                int lo_c = 0, hi_c = min(NC, tile.len - kbase);
+                int lo_c = max(0, rs - kbase), hi_c = min(NC, re - kbase);
                 if (W >= 0 && row_valid) {
                     lo_c = max(lo_c, tok - W - kbase);
                     hi_c = min(hi_c, tok + W + 1 - kbase);
@@ -722,6 +730,11 @@ __global__ void __launch_bounds__(A64_THREADS, 1)
         const uint32_t lane_off = (uint32_t)(32 * e) << 16;
         const int tok = tile.q0 + 128 * h + r;
         const bool row_valid = tok < tile.len;
+        int rs = 0, re = tile.len;  // keys of this row's sequence, relative to the tile's first row
+        if (prm.seq_start && row_valid) {
+            rs = prm.seq_start[tile.row0 + tok] - tile.row0;
+            re = rs + prm.seq_len[tile.row0 + tok];
+        }
         const float LOG2E = 1.4426950408889634f;
         float m_used = -INFINITY, l = 0.f;
         bool ok = true;
@@ -739,7 +752,7 @@ __global__ void __launch_bounds__(A64_THREADS, 1)
             mbar_arrive(&s_empty[h]);
             float* sv = reinterpret_cast<float*>(su);
             const int kbase = k_lo + 128 * j;
-            int lo_c = 0, hi_c = min(128, tile.len - kbase);
+            int lo_c = max(0, rs - kbase), hi_c = min(128, re - kbase);
             if (W >= 0 && row_valid) {
                 lo_c = max(lo_c, tok - W - kbase);
                 hi_c = min(hi_c, tok + W + 1 - kbase);
@@ -905,7 +918,8 @@ static int launch_pair(const CUtensorMap& mq, const CUtensorMap& mk, const CUten
 }
 
 int attention_tc(const bf16_t* q, const bf16_t* k, const bf16_t* v, bf16_t* out, long rows, const AttnTile* tiles,
-                 int n_tiles, int nh, int nkv, int hd, int window, cudaStream_t s) {
+                 int n_tiles, int nh, int nkv, int hd, int window, cudaStream_t s, const int* seq_start,
+                 const int* seq_len) {
     if (rows <= 0 || n_tiles <= 0) return 0;
     if ((hd != 64 && hd != 256 && hd != 512) || !attention_tc_tile_tokens(nh, nkv, hd)) return -1;
     const int G = nh / nkv;
@@ -920,6 +934,8 @@ int attention_tc(const bf16_t* q, const bf16_t* k, const bf16_t* v, bf16_t* out,
         AttParams prm{};
         prm.tiles = tiles;
         prm.out = out;
+        prm.seq_start = seq_start;
+        prm.seq_len = seq_len;
         prm.nh = nh;
         prm.nkv = nkv;
         prm.hd = 64;
@@ -947,6 +963,8 @@ int attention_tc(const bf16_t* q, const bf16_t* k, const bf16_t* v, bf16_t* out,
     AttParams prm;
     prm.tiles = tiles;
     prm.out = out;
+    prm.seq_start = seq_start;
+    prm.seq_len = seq_len;
     prm.nh = nh;
     prm.nkv = nkv;
     prm.hd = hd;

@@ -140,9 +140,14 @@ int vision_pool(const float* x, float* out, int gh, int gw, int hdim, int k, flo
 struct AttnTile {
     int row0, len, q0;
 };
-// Tensor-core flash attention, bf16 q/k/v/out, GQA-packed query tiles (attention_tc.cu).
+// Tensor-core flash attention, bf16 q/k/v/out, GQA-packed query tiles (attention_tc.cu). A tile is
+// (row0, len, q0): query tokens q0.. of the len rows from row0, keys among those rows. With
+// seq_start / seq_len (per row: first row and length of its sequence) each row also masks the keys
+// outside its own sequence, so one tile may hold several whole short sequences (q0 = 0); without them
+// a tile's rows are one sequence.
 int attention_tc(const bf16_t* q, const bf16_t* k, const bf16_t* v, bf16_t* out, long rows, const AttnTile* tiles,
-                 int n_tiles, int nh, int nkv, int hd, int window, cudaStream_t s);
+                 int n_tiles, int nh, int nkv, int hd, int window, cudaStream_t s, const int* seq_start = nullptr,
+                 const int* seq_len = nullptr);
 // attention_tc with its tile list built in a fixed device array instead of allocated memory (noalloc.cu).
 int attention_noalloc(const bf16_t* q, const bf16_t* k, const bf16_t* v, bf16_t* out, const int32_t* lens, int n_seq,
                       int nh, int nkv, int hd, int window, cudaStream_t s);

@@ -866,7 +866,8 @@ void attention<bf16_t>(eg2_ctx* c, const bf16_t* q, const bf16_t* k, const bf16_
                        int nkv, int hd, int window, const int* seq_start, const int* seq_len, const AttnTile* tiles,
                        int n_tiles) {
     if (c->use_tc_attention && tiles)
-        KL(attention_tc(q, k, v, out, rows, tiles, n_tiles, nh, nkv, hd, window, c->stream), "attention_tc");
+        KL(attention_tc(q, k, v, out, rows, tiles, n_tiles, nh, nkv, hd, window, c->stream, seq_start, seq_len),
+           "attention_tc");
     else
         KL(attention_simt<bf16_t>(q, k, v, out, seq_start, seq_len, rows, nh, nkv, hd, window, c->stream), "attention_simt");
 }
@@ -996,11 +997,28 @@ static std::vector<TileSet> prepare_pass(eg2_ctx* c, const int32_t* lens, int n_
             ts.hd = kd.second;
             ts.offset = (long)tiles.size();
             const int tq = attention_tc_tile_tokens(tc.nh, kd.first, kd.second);
+            // A sequence of tq tokens or more gets its own tiles. Shorter ones share a tile with their
+            // short neighbours while the group fits in tq rows: the tile spans the group's rows and each
+            // row masks the keys outside its own sequence (the kernel reads the per-row sequence
+            // bounds), so a batch of short queries takes few tiles instead of one per query.
             long row0 = 0;
+            int g_row0 = 0, g_rows = 0;  // open group of short sequences
+            auto close_group = [&]() {
+                if (g_rows > 0) tiles.push_back(AttnTile{g_row0, g_rows, 0});
+                g_rows = 0;
+            };
             for (int s = 0; s < n_seq; s++) {
-                for (int q0 = 0; q0 < lens[s]; q0 += tq) tiles.push_back(AttnTile{(int)row0, lens[s], q0});
+                if (lens[s] < tq) {
+                    if (g_rows + lens[s] > tq) close_group();
+                    if (g_rows == 0) g_row0 = (int)row0;
+                    g_rows += lens[s];
+                } else {
+                    close_group();
+                    for (int q0 = 0; q0 < lens[s]; q0 += tq) tiles.push_back(AttnTile{(int)row0, lens[s], q0});
+                }
                 row0 += lens[s];
             }
+            close_group();
             if (tile_slots > 0) {
                 if ((long)tiles.size() - ts.offset > tile_slots) fail(EG2_ERR_INVALID, "tile list exceeds its slots");
                 while ((long)tiles.size() - ts.offset < tile_slots) tiles.push_back(AttnTile{0, 0, 0});

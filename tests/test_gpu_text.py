@@ -42,7 +42,10 @@ def check_embeddings(got: dict, want: np.ndarray, profile, label):
 @pytest.fixture(scope="module")
 def cases(oracle_text):
     out = {}
-    for name, lens in {"short": [17, 3, 27, 1], "doc": [700], "mixed": [130, 600, 64, 65, 1100]}.items():
+    # "short" and "queries": short sequences share attention tiles (several groups, closed by a long
+    # sequence or by the tile size).
+    for name, lens in {"short": [17, 3, 27, 1], "doc": [700], "mixed": [130, 600, 64, 65, 1100],
+                       "queries": [5, 64, 9, 33, 120, 1, 61, 300, 17, 17, 17, 40, 2, 90, 127, 128, 31, 33]}.items():
         seqs = ids_for(lens, zlib.crc32(name.encode()) % 1000)
         out[name] = (seqs, oracle_text.embed_ids(seqs))
     return out
