@@ -228,8 +228,32 @@ def run_c5(dev, tb, cfg, stream):
     vis_s = time.perf_counter() - t0
     assert np.isfinite(soft).all()
 
-    ids = np.random.default_rng(QUERY_SEED).integers(0, cfg.text.vocab_size, size=QUERIES * QUERY_LEN).astype(np.uint32)
-    ids_dev = torch.from_numpy(ids.view(np.int32)).cuda()
+    # Whole image embedding the way the reference's embed path does it (src/model.rs:448-480): the
+    # prompt <bos> <boi> 256 x <image> <eoi> <eos> is embedded, the soft tokens replace the
+    # placeholder rows, the 260-row sequence runs through the text backbone (host buffers,
+    # eg2_forward_packed) and the per-token states are mean-pooled and L2-normalised on the host.
+    n_soft = soft.shape[0]
+    raw = cfg.raw
+    ids = np.array([2, raw["boi_token_id"]] + [raw["image_token_id"]] * n_soft + [raw["eoi_token_id"], 1], dtype=np.uint32)
+
+    def embed_image(img):
+        sv = vt.encode(img, pos, g, g)
+        e = tb.embed_tokens(ids)
+        e[2:2 + n_soft] = sv
+        states = tb.forward_packed(e, [len(ids)])
+        v = states.astype(np.float64).mean(0)
+        return v / max(np.linalg.norm(v), 1e-12)
+
+    for img in images[:3]:
+        embed_image(img)
+    t0 = time.perf_counter()
+    for img in images:
+        emb = embed_image(img)
+    img_s = time.perf_counter() - t0
+    assert np.isfinite(emb).all()
+
+    q_ids = np.random.default_rng(QUERY_SEED).integers(0, cfg.text.vocab_size, size=QUERIES * QUERY_LEN).astype(np.uint32)
+    ids_dev = torch.from_numpy(q_ids.view(np.int32)).cuda()
     out_dev = torch.empty((QUERIES, sum(DIMS)), dtype=torch.float32, device="cuda")
     lens = [QUERY_LEN] * QUERIES
     for _ in range(3):
@@ -248,6 +272,10 @@ def run_c5(dev, tb, cfg, stream):
                        "images_per_s": round(VISION_IMAGES / vis_s, 2),
                        "call": "eg2_vision_encode (host patches -> host soft tokens), one image per call",
                        "data": f"uniform noise patches in [0, 1), seed {VISION_SEED}"},
+            "image_embed": {"images": VISION_IMAGES, "tokens": int(len(ids)),
+                            "ms_per_image": round(img_s * 1000.0 / VISION_IMAGES, 3),
+                            "images_per_s": round(VISION_IMAGES / img_s, 2),
+                            "call": "eg2_vision_encode + eg2_embed_tokens + eg2_forward_packed (host buffers) + host mean/L2"},
             "queries": {"queries": QUERIES, "tokens": QUERY_LEN, "ms_per_batch": round(q_ms, 3),
                         "queries_per_s": round(QUERIES / (q_ms / 1000.0), 1), "gpus": 1,
                         "call": "eg2_embed_packed_device, one packed pass"}}

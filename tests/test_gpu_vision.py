@@ -32,3 +32,16 @@ def test_vision_soft_tokens(prec, oracle_vision, request):
         c = V.vec_check(f"{prec} soft {gh}x{gw}", soft, soft_want, prof.soft_tokens)
         assert c.passed(), str(c)
         print(c)
+
+
+def test_vision_full_size_image(dev_bf16, oracle_vision):
+    """The benchmarked image size: 48 x 48 = 2,304 patches (a 768 x 768 image after the reference's
+    resize), nine full 256-token attention tiles per head, 256 soft tokens."""
+    vb = B.VisionBackend(dev_bf16)
+    patches, pos = image(48, 48, 4848)
+    _, soft_want = oracle_vision.encode(patches, pos, 48, 48)
+    soft = vb.encode(patches, pos, 48, 48)
+    assert soft.shape == (256, 512)
+    c = V.vec_check("bf16 soft 48x48", soft, soft_want, V.for_precision("bf16").soft_tokens)
+    assert c.passed(), str(c)
+    print(c)
