@@ -203,6 +203,27 @@ def run_long(tb, cfg, stream):
             "gpus": 1}
 
 
+def run_latency(tb, cfg):
+    """Per-call latency of the reference's own single-request cases, on one GPU through the host-buffer
+    API (eg2_embed_packed via TextBackend.embed_ids): one 2,208-token document per call (the reference
+    quotes 47.6 ms per document in bf16 on an RTX A3000, README.md:78) and one 17-token query per call
+    (2.5 ms there, CUDA-graph replay, README.md:77). Wall clock per call, median of 20 after warm-up."""
+    out = {}
+    rng = np.random.default_rng(2208)
+    for name, n in (("doc_2208", SEQ_LEN), ("query_17", 17)):
+        ids = rng.integers(0, cfg.text.vocab_size, size=n).astype(np.uint32)
+        for _ in range(3):
+            tb.embed_ids([ids])
+        ts = []
+        for _ in range(20):
+            t0 = time.perf_counter()
+            tb.embed_ids([ids])
+            ts.append(time.perf_counter() - t0)
+        out[name] = {"tokens": n, "ms_per_call": round(statistics.median(ts) * 1000.0, 3),
+                     "call": "eg2_embed_packed (host ids -> host embeddings), one sequence per call"}
+    return out
+
+
 VISION_IMAGES, VISION_GRID, VISION_SEED = 32, 48, 5
 QUERIES, QUERY_LEN, QUERY_SEED = 4096, 17, 17
 
@@ -434,6 +455,8 @@ def main():
     long_case = run_long(tb, cfg, stream) if rank == 0 else None
     # ---- C5 on one GPU: vision tower per image, and a batch of 4,096 short queries (rank 0 only) ----
     c5 = run_c5(dev, tb, cfg, stream) if rank == 0 and not args.no_c5 else None
+    # ---- single-request latency (rank 0 only) ----
+    latency = run_latency(tb, cfg) if rank == 0 and not args.no_c5 else None
     barrier()
 
     # ---- per-op device time shares (CUDA events around each op, one profiled step) ----
@@ -507,6 +530,7 @@ def main():
             "mixed_c3": mixed,
             "long_c4": long_case,
             "c5": c5,
+            "latency": latency,
         }
         print(json.dumps(line))
     dev.close()
