@@ -352,10 +352,21 @@ struct VLayerW {
     float *input_ln, *post_attn_ln, *pre_ff_ln, *post_ff_ln, *q_norm, *k_norm;
 };
 
-// Short passes (<= kSplitRows rows) split the K range of the N = 512 projections (up to kSplitMax
-// slices) so the weights are streamed by many SMs.
-constexpr int kSplitMax = 8;
-constexpr long kSplitRows = 256;
+// Passes of up to kSplitRowsMax rows split the K range of the N = 512 projections into slices (f32
+// partial sums, added in slice order by a row kernel), so that the weights are streamed by many SMs:
+// unsplit, such a pass has only ceil(rows / 128) two-CTA clusters per projection, each streaming half
+// the weight matrix. Up to 8 slices for passes of at most kSplitRowsSmall rows, 4 above (the partial
+// sums' traffic grows with rows x slices), never fewer than 2 K blocks per slice. The slice count
+// depends only on the row regime and K, so a sequence's bits are the same in any pass of its regime.
+constexpr long kSplitRowsSmall = 1024;
+constexpr long kSplitRowsMax = 4096;
+constexpr long kSplitElems = 16384L * 512;  // partial-sum buffer: slices x rows x 512 (f32)
+static int split_slices(long rows, int kb) {
+    if (rows > kSplitRowsMax) return 1;
+    int S = std::min(rows <= kSplitRowsSmall ? 8 : 4, kb / 2);
+    while (S > 1 && kb % S) S--;
+    return S >= 2 ? S : 1;
+}
 
 struct Work {
     long cap = 0;
@@ -705,7 +716,7 @@ static void ensure_work(eg2_ctx* c, long rows, long n_tiles) {
         w.ids = (uint32_t*)dalloc(c, cap * 4);
         w.cap = cap;
     }
-    if (!w.osplit && bf16_mode(c)) w.osplit = (float*)dalloc(c, (size_t)kSplitMax * kSplitRows * 512 * 4);
+    if (!w.osplit && bf16_mode(c)) w.osplit = (float*)dalloc(c, (size_t)kSplitElems * 4);
     if (n_tiles > w.tiles_cap) {
         CK(cudaStreamSynchronize(c->stream));
         dfree(c, w.tiles);
@@ -814,12 +825,12 @@ static void gemm_add_norm(eg2_ctx* c, const void* x, long ldx, const void* W, lo
     Work& w = c->w;
     const int h = c->tc.hidden;
     if (bf16_mode(c) && h == 512 && !getenv("EG2_NO_ADD_NORM_FUSION")) {
-        const int kb = K / 64, S = kb >= 16 ? kSplitMax : kb / 2;
-        if (rows <= kSplitRows && w.osplit && S >= 2 && kb % S == 0) {
-            // A short pass: one cluster per 512-column row block would stream the whole weight
-            // matrix through two SMs. Split K over S slices instead (S x 2 clusters, f32 partials),
-            // then sum the partials and update the residual in a row kernel (same arithmetic as the
-            // fused epilogue, the sum taken in slice order).
+        const int S = split_slices(rows, K / 64);
+        if (w.osplit && S >= 2 && S * rows <= kSplitElems / h) {
+            // A pass of few rows: one cluster per 128-row block would stream the whole weight matrix
+            // through few SMs. Split K over S slices instead (S x 2 clusters per 256 rows, f32
+            // partials), then sum the partials and update the residual in a row kernel (same
+            // arithmetic as the fused epilogue, the sum taken in slice order).
             GemmEpilogue e;
             e.mode = EPI_STORE;
             e.out_f32 = 1;
@@ -944,17 +955,19 @@ static void enqueue_text(eg2_ctx* c, long rows, const std::vector<TileSet>& tset
         mark(c, "gemm gate|up + gelu");
         // t = hidden (as the per-layer-input gate's input, bf16 in bf16 mode).
         gemm_add_norm<T>(c, w.gate, ff, L.down, rows, ff, L.post_ff_ln, nullptr, 1.f, "gemm down (+ add_norm)");
-        if (bf16_mode(c) && rows <= kSplitRows && w.osplit && p == 512 && h % 128 == 0) {
-            // Short pass: the K range split over 4 slices (f32 partials), then GELU x ple in a row kernel.
+        const int Sg = split_slices(rows, h / 64);
+        if (bf16_mode(c) && Sg >= 2 && w.osplit && p == 512 && h % 128 == 0 && Sg * rows <= kSplitElems / p) {
+            // A pass of few rows: the K range split into slices (f32 partials), then GELU x ple in a
+            // row kernel.
             GemmEpilogue e;
             e.mode = EPI_STORE;
             e.out_f32 = 1;
             e.out = w.osplit;
             e.ldo = p;
-            e.ksplit = 4;
+            e.ksplit = Sg;
             e.split_stride = rows * p;
             KL(gemm_tc(GEMM_BF16, t, h, L.pg, h, (int)rows, p, h, e, c->stream), "gemm ple_gate");
-            KL(ple_gate_split(w.osplit, 4, rows * p, w.ple, (long)nl * p, i * p, (bf16_t*)w.pg, rows, p, c->stream),
+            KL(ple_gate_split(w.osplit, Sg, rows * p, w.ple, (long)nl * p, i * p, (bf16_t*)w.pg, rows, p, c->stream),
                "ple_gate_split");
         } else {
             gemm(c, t, h, L.pg, (int)rows, p, h, w.pg, p, EPI_PLE_GATE, f32, 1.f, w.ple, (long)nl * p, i * p);

@@ -127,10 +127,12 @@ def test_repeated_calls_are_deterministic(dev_bf16):
 
 def test_add_norm_fusion_matches_kernel_path(cases, request, monkeypatch):
     """The o / down / ple_proj GEMMs with the residual update and norms in their epilogue (2-CTA
-    clusters exchanging row sums of squares) against the GEMM + add_norm kernel path."""
+    clusters exchanging row sums of squares) against the GEMM + add_norm kernel path. The fused
+    epilogue runs on passes above 4,096 rows (smaller ones split K), hence the extra 2,200 tokens."""
     dev = request.getfixturevalue("dev_bf16")
     tb = B.TextBackend(dev)
-    seqs = cases["mixed"][0] + cases["short"][0]
+    seqs = cases["mixed"][0] + cases["short"][0] + ids_for([2200], 77)
+    assert sum(len(x) for x in seqs) > 4096
     fused = tb.embed_ids(seqs)
     monkeypatch.setenv("EG2_NO_ADD_NORM_FUSION", "1")
     plain = tb.embed_ids(seqs)
