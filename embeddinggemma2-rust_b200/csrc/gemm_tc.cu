@@ -615,32 +615,68 @@ __global__ void __launch_bounds__(gemm_threads(WIDE), 1)
     if constexpr (CL || PAIR) cluster_sync();
     // Launched as a programmatic dependent: the prologue above ran while the previous kernel was
     // finishing; the next kernel may start its own now, and this one reads its inputs only once the
-    // previous kernel has completed.
+    // previous kernel has completed. With at most two tiles per CTA (passes of few rows, where the
+    // kernel's start-up latency is a large part of its time) the producer waits later, after
+    // requesting its first weight tiles (the weights do not depend on the previous kernel); warp 0's
+    // other lanes touch no memory. Long passes keep the plain order: there a CTA's start-up is a small
+    // part of its time.
+    const bool early_w = t_count <= 2 * t_step;
     grid_dep_launch();
-    grid_dep_wait();
+    if (warp != 0 || !early_w) grid_dep_wait();
 
     if (warp == 0) {
         if (lane == 0) {
-            int stage = 0;
+            // Stage st's byte count, and its activation (A) and weight (B) tiles. A is requested first:
+            // it comes from HBM, the weights mostly from L2.
+            auto expect = [&](int st) {
+                if constexpr (PAIR) {
+                    // Both CTAs' bytes complete on the even CTA's barrier.
+                    if (lead) mbar_arrive_expect_tx(&full[st], 2 * Cfg::STAGE_BYTES);
+                } else {
+                    mbar_arrive_expect_tx(&full[st], Cfg::STAGE_BYTES);
+                }
+            };
+            auto load_a = [&](int st, int tile, int kb) {
+                uint8_t* sa = smem + st * Cfg::STAGE_BYTES;
+                if constexpr (PAIR)
+                    tma_load_2d_pair(sa, &tmA, mapa_shared(smem_u32(&full[st]), 0), kb * BK, tile_m0(tile));
+                else
+                    tma_load_2d(sa, &tmA, &full[st], kb * BK, tile_m0(tile));
+            };
+            auto load_b = [&](int st, int tile, int kb) {
+                uint8_t* sa = smem + st * Cfg::STAGE_BYTES;
+                if constexpr (PAIR)
+                    tma_load_2d_pair(sa + Cfg::A_BYTES, &tmB, mapa_shared(smem_u32(&full[st]), 0), kb * BK,
+                                     tile_n0(tile) + (int)crank * (BN / 2));
+                else
+                    tma_load_2d(sa + Cfg::A_BYTES, &tmB, &full[st], kb * BK, tile_n0(tile));
+            };
+            // early_w: the first STAGES weight tiles go out before the wait for the previous kernel.
+            int n_pre = 0;
+            if (early_w) {
+                for (int tile = t_first; tile < t_count && n_pre < STAGES; tile += t_step) {
+                    const int kb0 = (tile % S) * kbs;
+                    for (int kb = kb0; kb < kb0 + kbs && n_pre < STAGES; kb++, n_pre++) {
+                        expect(n_pre);
+                        load_b(n_pre, tile, kb);
+                    }
+                }
+                grid_dep_wait();
+            }
+            int stage = 0, e = 0;
             uint32_t phase = 0;
             for (int tile = t_first; tile < t_count; tile += t_step) {
                 // (No L2 prefetch of the epilogue's inputs here: 128 bulk prefetches per tile from this
                 // thread delayed the main loop's loads more than they saved -- measured on B200.)
-                const int m0 = tile_m0(tile), n0 = tile_n0(tile);
                 const int kb0 = (tile % S) * kbs;
-                for (int kb = kb0; kb < kb0 + kbs; kb++) {
-                    if (!mbar_wait(&empty[stage], phase ^ 1, EG2_DEV_TIMEOUT_GEMM, abort_flag)) goto done;
-                    uint8_t* sa = smem + stage * Cfg::STAGE_BYTES;
-                    if constexpr (PAIR) {
-                        // Both CTAs' bytes complete on the even CTA's barrier.
-                        if (lead) mbar_arrive_expect_tx(&full[stage], 2 * Cfg::STAGE_BYTES);
-                        const uint32_t bar = mapa_shared(smem_u32(&full[stage]), 0);
-                        tma_load_2d_pair(sa, &tmA, bar, kb * BK, m0);
-                        tma_load_2d_pair(sa + Cfg::A_BYTES, &tmB, bar, kb * BK, n0 + (int)crank * (BN / 2));
+                for (int kb = kb0; kb < kb0 + kbs; kb++, e++) {
+                    if (e >= n_pre) {
+                        if (!mbar_wait(&empty[stage], phase ^ 1, EG2_DEV_TIMEOUT_GEMM, abort_flag)) goto done;
+                        expect(stage);
+                        load_a(stage, tile, kb);
+                        load_b(stage, tile, kb);
                     } else {
-                        mbar_arrive_expect_tx(&full[stage], Cfg::STAGE_BYTES);
-                        tma_load_2d(sa, &tmA, &full[stage], kb * BK, m0);
-                        tma_load_2d(sa + Cfg::A_BYTES, &tmB, &full[stage], kb * BK, n0);
+                        load_a(stage, tile, kb);
                     }
                     if (++stage == STAGES) {
                         stage = 0;

@@ -61,6 +61,9 @@ EG2_DEV void st_row(bf16_t* p, const float (&v)[VPL]) {
 template <typename TO, int VPL>
 __global__ void rms_norm_kernel(const float* __restrict__ x, TO* __restrict__ out, const float* __restrict__ w, long rows,
                                 float eps, float pre) {
+    // The next kernel (a GEMM launched as a programmatic dependent) may start its prologue and weight
+    // loads now; it reads this kernel's output only after this kernel has completed.
+    grid_dep_launch();
     const long row = (long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (row >= rows) return;
     constexpr int dim = 32 * VPL;
@@ -114,6 +117,7 @@ template <typename TI, typename TT, int VPL>
 __global__ void add_norm_kernel(float* __restrict__ h, const TI* __restrict__ o, const float* __restrict__ w1,
                                 TT* __restrict__ t, const float* __restrict__ w2, long rows, float eps, float scalar,
                                 int nsplit = 1, long o_stride = 0) {
+    grid_dep_launch();  // as in rms_norm_kernel
     const long row = (long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (row >= rows) return;
     constexpr int dim = 32 * VPL;
@@ -179,6 +183,7 @@ int add_norm_split(float* h, const float* o, int nsplit, long o_stride, const fl
 __global__ void ple_gate_split_kernel(const float* __restrict__ part, int nsplit, long stride,
                                       const float* __restrict__ ple, long ple_ld, int ple_off, bf16_t* __restrict__ out,
                                       long rows, int p) {
+    grid_dep_launch();  // as in rms_norm_kernel
     const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;  // 4-column group
     const int gpr = p / 4;
     if (i >= rows * gpr) return;
