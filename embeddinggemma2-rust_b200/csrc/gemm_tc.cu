@@ -636,29 +636,29 @@ __global__ void __launch_bounds__(gemm_threads(WIDE), 1)
                     mbar_arrive_expect_tx(&full[st], Cfg::STAGE_BYTES);
                 }
             };
-            auto load_a = [&](int st, int tile, int kb) {
+            auto load_a = [&](int st, int m0, int kb) {
                 uint8_t* sa = smem + st * Cfg::STAGE_BYTES;
                 if constexpr (PAIR)
-                    tma_load_2d_pair(sa, &tmA, mapa_shared(smem_u32(&full[st]), 0), kb * BK, tile_m0(tile));
+                    tma_load_2d_pair(sa, &tmA, mapa_shared(smem_u32(&full[st]), 0), kb * BK, m0);
                 else
-                    tma_load_2d(sa, &tmA, &full[st], kb * BK, tile_m0(tile));
+                    tma_load_2d(sa, &tmA, &full[st], kb * BK, m0);
             };
-            auto load_b = [&](int st, int tile, int kb) {
+            auto load_b = [&](int st, int n0, int kb) {
                 uint8_t* sa = smem + st * Cfg::STAGE_BYTES;
                 if constexpr (PAIR)
                     tma_load_2d_pair(sa + Cfg::A_BYTES, &tmB, mapa_shared(smem_u32(&full[st]), 0), kb * BK,
-                                     tile_n0(tile) + (int)crank * (BN / 2));
+                                     n0 + (int)crank * (BN / 2));
                 else
-                    tma_load_2d(sa + Cfg::A_BYTES, &tmB, &full[st], kb * BK, tile_n0(tile));
+                    tma_load_2d(sa + Cfg::A_BYTES, &tmB, &full[st], kb * BK, n0);
             };
             // early_w: the first STAGES weight tiles go out before the wait for the previous kernel.
             int n_pre = 0;
             if (early_w) {
                 for (int tile = t_first; tile < t_count && n_pre < STAGES; tile += t_step) {
-                    const int kb0 = (tile % S) * kbs;
+                    const int kb0 = (tile % S) * kbs, n0 = tile_n0(tile);
                     for (int kb = kb0; kb < kb0 + kbs && n_pre < STAGES; kb++, n_pre++) {
                         expect(n_pre);
-                        load_b(n_pre, tile, kb);
+                        load_b(n_pre, n0, kb);
                     }
                 }
                 grid_dep_wait();
@@ -668,15 +668,16 @@ __global__ void __launch_bounds__(gemm_threads(WIDE), 1)
             for (int tile = t_first; tile < t_count; tile += t_step) {
                 // (No L2 prefetch of the epilogue's inputs here: 128 bulk prefetches per tile from this
                 // thread delayed the main loop's loads more than they saved -- measured on B200.)
+                const int m0 = tile_m0(tile), n0 = tile_n0(tile);
                 const int kb0 = (tile % S) * kbs;
                 for (int kb = kb0; kb < kb0 + kbs; kb++, e++) {
                     if (e >= n_pre) {
                         if (!mbar_wait(&empty[stage], phase ^ 1, EG2_DEV_TIMEOUT_GEMM, abort_flag)) goto done;
                         expect(stage);
-                        load_a(stage, tile, kb);
-                        load_b(stage, tile, kb);
+                        load_a(stage, m0, kb);
+                        load_b(stage, n0, kb);
                     } else {
-                        load_a(stage, tile, kb);
+                        load_a(stage, m0, kb);
                     }
                     if (++stage == STAGES) {
                         stage = 0;
