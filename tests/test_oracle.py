@@ -1,10 +1,12 @@
 """The CPU oracle, pinned before it is trusted.
 
 * against golden vectors made from transformers' Gemma4 modules on the same seeded checkpoint
-  (tests/golden/make_golden.py) -- the upstream implementation the reference's own dumps come from;
+  (tests/golden/make_golden.py for the text backbone, make_golden_vision.py for the vision tower) -- the
+  upstream implementation the reference's own dumps come from;
 * op by op against exact float64 restatements (the method of examples/check_attention.rs:31-52);
 * packing: a packed pass equals its sequences run one by one (src/text.rs:131-135).
 """
+import base64
 import json
 from pathlib import Path
 
@@ -16,6 +18,7 @@ from conftest import pkg
 
 V = pkg("verify")
 GOLDEN = Path(__file__).parent / "golden" / "golden_text.json"
+GOLDEN_VISION = Path(__file__).parent / "golden" / "golden_vision.json"
 
 
 def exact_attention(q, k, v, lens, nh, nkv, hd, window):
@@ -143,3 +146,20 @@ def test_vision_oracle_shapes(oracle_vision):
     assert np.isfinite(soft).all()
     with pytest.raises(ValueError):
         oracle_vision.encode(patches[:50], pos[:50], 5, 10)
+
+
+def test_vision_oracle_matches_golden(oracle_vision):
+    """The vision tower (src/vision.rs:223-273) and the multimodal embedder against transformers'
+    Gemma4VisionModel + Gemma4MultimodalEmbedder on the same checkpoint and patches: 6 x 6, 3 x 9 and
+    3 x 3 grids (4, 3 and 1 soft tokens). The pooled states carry the sqrt(768) scale (hundreds), so
+    they are compared relative to their largest magnitude; the soft tokens are O(1)."""
+    g = json.loads(GOLDEN_VISION.read_text())
+    for case in g["cases"]:
+        gh, gw = case["grid"]
+        patches = np.frombuffer(base64.b64decode(case["patches_f32_b64"]), dtype="<f4").reshape(gh * gw, -1)
+        pos = np.array(case["positions"], dtype=np.int32)
+        pooled, soft = oracle_vision.encode(patches, pos, gh, gw)
+        pw, sw = np.array(case["pooled"], np.float32), np.array(case["soft"], np.float32)
+        assert pooled.shape == pw.shape and soft.shape == sw.shape
+        assert np.abs(pooled - pw).max() <= 1e-5 * np.abs(pw).max(), (gh, gw)
+        assert np.abs(soft - sw).max() <= 1e-5, (gh, gw)
