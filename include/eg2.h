@@ -107,7 +107,9 @@ int eg2_gemm(int kind, const void* A, int64_t lda, const void* W, int64_t ldw, v
 
 /* Block-diagonal bidirectional attention, scale 1, window radius `window` (< 0: global).
  * q [rows, nh, hd], k / v [rows, nkv, hd], out [rows, nh, hd]; lens host array.
- * kind: EG2_BF16 (bf16 storage, tcgen05 flash kernel), EG2_F32 (f32 CUDA cores). */
+ * kind: EG2_BF16 (bf16 storage, tcgen05 flash kernels: hd 256 or 512 with nh / nkv dividing 128,
+ * as in the text layers, or hd 64 with nh == nkv, as in the vision tower; one sequence per query
+ * tile), EG2_F32 (f32 CUDA cores, any hd up to 512). */
 int eg2_attention(int kind, const void* q, const void* k, const void* v, void* out, const int32_t* lens, int n_seq,
                   int nh, int nkv, int hd, int window, void* stream);
 
