@@ -125,16 +125,14 @@ def measured_peaks():
 
 
 def ncu_traffic(kernel_label: str):
-    """DRAM bytes per launch of a kernel, from the committed ncu summary (profiles/*.md lines
-    `traffic <label>: <bytes> bytes/launch`), else None."""
-    for f in sorted((ROOT / "profiles").glob("*.md")):
-        for ln in f.read_text().splitlines():
-            if ln.startswith(f"traffic {kernel_label}:"):
-                try:
-                    return float(ln.split(":")[1].split()[0])
-                except (IndexError, ValueError):
-                    pass
-    return None
+    """DRAM bytes per launch of a kernel at this bench's size, from profiles/traffic.json (one ncu
+    capture per kernel, scaled by the rows processed), else None."""
+    f = ROOT / "profiles" / "traffic.json"
+    try:
+        entry = json.loads(f.read_text())["kernels"].get(kernel_label)
+    except (OSError, ValueError, KeyError):
+        return None
+    return float(entry["bytes_per_launch"]) if entry else None
 
 
 def make_checkpoint(dirpath: Path, vision: bool = False):

@@ -872,12 +872,11 @@ static int launch_d64(const CUtensorMap& mq, const CUtensorMap& mk, const CUtens
 }
 
 int attention_tc_tile_tokens(int nh, int nkv, int hd) {
-    if (nkv <= 0 || nh % nkv) return 0;
+    if (nh <= 0 || nkv <= 0 || nh % nkv) return 0;
     const int G = nh / nkv;
     if (hd == 64) return G == 1 ? 256 : 0;  // two 128-row query tiles of one head
-    if (128 % G) return 0;
+    if ((hd != 256 && hd != 512) || 128 % G) return 0;
     // CTA pairs: one tile covers both CTAs' 128 rows.
-    (void)hd;
     return 256 / G;
 }
 

@@ -2,18 +2,20 @@
 //
 // eg2_attention keeps its per-call scratch -- the sequence lengths and the list of query tiles the
 // tensor-core kernel walks -- in device buffers it allocates and frees on every call. Some callers
-// cannot allow that: a serving engine that reserves all device memory for its own pool up front, a
-// caller recording CUDA work into a graph (where allocation calls are not permitted while the
-// stream is being captured), or a latency-critical path where the implicit device synchronisation of
-// cudaMalloc / cudaFree would stall other streams. For them this variant keeps the scratch in a
-// file-scope device array of fixed size that every GPU loading the library holds until the process
-// exits, builds the tile list there with a small kernel, and calls no allocating routine.
+// cannot allow that: a serving engine that reserves all device memory for its own pool up front (a
+// cudaMalloc behind its back can fail or fragment that pool), or a latency-critical path where the
+// implicit device synchronisation of cudaMalloc / cudaFree would stall work on other streams. For
+// them this variant keeps the scratch in a file-scope device array of fixed size that every GPU
+// loading the library holds until the process exits, builds the tile list there with a small
+// kernel, and calls no allocating routine.
 //
 // Limits: at most EG2_NOALLOC_MAX_SEQ sequences and EG2_NOALLOC_MAX_TILES query tiles per call
 // (a tile is tokens-per-tile query rows of one sequence: 64 for 4 query heads over 2 K/V heads,
 // 32 for 4 over 1), i.e. about 4 M rows for sliding-window layers; larger calls are rejected.
 // All calls share the one array and leave their contents in it: two calls that overlap on the GPU
 // (different streams, or different host threads, with no ordering between them) race on it.
+// The call is asynchronous: a bounded device wait that ran out is reported through the device
+// status word (eg2_device_status), which the caller reads after synchronising the stream.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -93,9 +95,11 @@ static NoAllocScratch* scratch_address() {
 
 int attention_noalloc(const bf16_t* q, const bf16_t* k, const bf16_t* v, bf16_t* out, const int32_t* lens, int n_seq,
                       int nh, int nkv, int hd, int window, cudaStream_t s) {
+    // Every argument is checked on the host before anything is copied or launched.
+    if (!q || !k || !v || !out || !lens || n_seq <= 0 || n_seq > EG2_NOALLOC_MAX_SEQ) return -1;
+    if (nh <= 0 || nkv <= 0 || nh % nkv) return -1;
     const int tq = attention_tc_tile_tokens(nh, nkv, hd);
-    if (!q || !k || !v || !out || !lens || n_seq <= 0 || tq <= 0) return -1;
-    if (n_seq > EG2_NOALLOC_MAX_SEQ) return -1;
+    if (tq <= 0) return -1;
     long rows = 0, n_tiles = 0;
     for (int i = 0; i < n_seq; i++) {
         if (lens[i] <= 0) return -1;
@@ -106,6 +110,8 @@ int attention_noalloc(const bf16_t* q, const bf16_t* k, const bf16_t* v, bf16_t*
     NoAllocScratch* sc = scratch_address();
     if (!sc) return -3;
     // The lengths go into the array (from the caller's host memory), then the tile list is built there.
+    // From pageable host memory the copy reads `lens` before cudaMemcpyAsync returns; from page-locked
+    // memory it is asynchronous and reads `lens` when the stream reaches it.
     // (Addresses inside the device array are formed by offset arithmetic; nothing is dereferenced here.)
     int* d_lens = reinterpret_cast<int*>(reinterpret_cast<char*>(sc) + offsetof(NoAllocScratch, lens));
     AttnTile* d_tiles = reinterpret_cast<AttnTile*>(reinterpret_cast<char*>(sc) + offsetof(NoAllocScratch, tiles));

@@ -115,14 +115,18 @@ int eg2_attention(int kind, const void* q, const void* k, const void* v, void* o
 
 /* No counterpart in the reference. The tensor-core attention of eg2_attention (kind EG2_BF16,
  * same arguments and results) without any device allocation, for callers that cannot call
- * cudaMalloc: engines that hand all device memory to their own pool up front, code recording into
- * a CUDA graph, latency-critical paths that cannot take cudaMalloc's implicit synchronisation.
- * Its scratch (sequence lengths and the query-tile list) lives in one fixed 1 MiB device array per
- * GPU, held until the process exits; calls with more than 65536 sequences or 65536 query tiles
- * (~4 M rows at 64 tokens per tile) return EG2_ERR_INVALID. The first call on a device looks the
- * array up (make that first call before any stream capture). All calls share the array: calls
- * that overlap on the GPU (unordered streams or threads) race. The call is asynchronous on
- * `stream` and reads `lens` from host memory before it returns. */
+ * cudaMalloc: engines that hand all device memory to their own pool up front (an allocation behind
+ * the pool's back can fail or fragment it), and latency-critical paths that cannot take
+ * cudaMalloc's implicit device synchronisation. Its scratch (sequence lengths and the query-tile
+ * list) lives in one fixed 1 MiB device array per GPU, held until the process exits; calls with
+ * more than 65536 sequences or 65536 query tiles (~4 M rows at 64 tokens per tile) return
+ * EG2_ERR_INVALID before anything is copied or launched. The first call on a device looks the
+ * array's device address up (make that first call before any stream capture). All calls share the
+ * array and it keeps the last call's contents: calls that overlap on the GPU (unordered streams or
+ * threads) race. The call is asynchronous on `stream`: `lens` in pageable host memory is read before
+ * the call returns; in page-locked memory it is read when the stream reaches the copy and must stay
+ * unchanged until then. A bounded device wait that ran out is not returned as EG2_ERR_TIMEOUT here:
+ * synchronise the stream, then read eg2_device_status() (non-zero: the result is not valid). */
 int eg2_attention_noalloc(const void* q, const void* k, const void* v, void* out, const int32_t* lens, int n_seq,
                           int nh, int nkv, int hd, int window, void* stream);
 

@@ -1,12 +1,13 @@
 """eg2_attention_noalloc through the C ABI, against eg2_attention (kind EG2_BF16) on the same inputs.
 
-The allocation-free entry point is for callers that cannot call cudaMalloc -- engines that hand
-all device memory to their own pool, code recording into a CUDA graph, latency-critical paths
-that cannot take cudaMalloc's implicit synchronisation. Its scratch (sequence lengths and the
-query-tile list) sits in one fixed device array that every call shares and that keeps the last
-call's contents, so the test makes calls in a row with different shapes: each must match the
-allocating entry point exactly (both run the same tensor-core kernel over the same tile list),
-and a later call must not pick up anything a previous one left behind.
+The allocation-free entry point is for callers that cannot call cudaMalloc: engines that hand all
+device memory to their own pool up front, and latency-critical paths that cannot take cudaMalloc's
+implicit device synchronisation. Its scratch (sequence lengths and the query-tile list) sits in one
+fixed device array that every call shares and that keeps the last call's contents, so the test makes
+calls in a row with different shapes: each must match the allocating entry point exactly (both run
+the same tensor-core kernel over the same tile list), and a later call must not pick up anything a
+previous one left behind. The call reports a bounded device wait that ran out only through the
+device status word, which the test reads after synchronising.
 
 This file is named to be collected last.
 """
@@ -60,15 +61,32 @@ def test_noalloc_matches_allocating_entry_point_on_consecutive_calls():
         q, k, v = _inputs(sum(lens), nh, nkv, hd, seed=100 + i)
         got = _run(lib.eg2_attention_noalloc, q, k, v, lens, nh, nkv, hd, window)
         want = _run(_allocating, q, k, v, lens, nh, nkv, hd, window)
+        assert lib.eg2_device_status() == 0
         assert np.isfinite(W.bf16_bits_to_f32(got.view(np.uint16))).all()
         np.testing.assert_array_equal(got, want)
 
 
 def test_noalloc_rejects_calls_beyond_its_fixed_scratch():
+    """Every rejection happens on the host before anything is copied or launched, so the small q / k /
+    v buffers are never read even where the lengths describe millions of rows."""
     lib = L.load()
     q, k, v = _inputs(8, 4, 2, 256, seed=7)
     out = torch.zeros((8, 1024), dtype=torch.int16, device="cuda")
-    too_many = [1] * 65537
-    rc = lib.eg2_attention_noalloc(C.c_void_p(q.data_ptr()), C.c_void_p(k.data_ptr()), C.c_void_p(v.data_ptr()),
-                                   C.c_void_p(out.data_ptr()), L.i32_array(too_many), len(too_many), 4, 2, 256, 512, None)
-    assert rc == -1
+    before = out.clone()
+
+    def call(lens, nh=4, nkv=2, hd=256, window=512):
+        return lib.eg2_attention_noalloc(C.c_void_p(q.data_ptr()), C.c_void_p(k.data_ptr()), C.c_void_p(v.data_ptr()),
+                                         C.c_void_p(out.data_ptr()), L.i32_array(lens), len(lens), nh, nkv, hd, window,
+                                         None)
+
+    assert call([1] * 65537) == -1            # more sequences than the array holds
+    assert call([65] * 40000) == -1           # fewer sequences, but 80,000 query tiles of 64 rows
+    assert call([5, 0, 3]) == -1              # an empty sequence
+    assert call([5, -2]) == -1                # a negative length
+    assert call([8], nh=0) == -1              # no query heads
+    assert call([8], nkv=0) == -1             # no K/V heads
+    assert call([8], nh=4, nkv=3) == -1       # query heads not a multiple of K/V heads
+    assert call([8], hd=128) == -1            # a head size the kernels do not take
+    torch.cuda.synchronize()
+    assert torch.equal(out, before)
+    assert lib.eg2_device_status() == 0
