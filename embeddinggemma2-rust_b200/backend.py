@@ -17,6 +17,7 @@ from pathlib import Path
 import numpy as np
 
 from . import lib as L
+from . import shard
 from .config import ModelConfig
 
 MATRYOSHKA_DIMS = (512, 256, 128)
@@ -59,6 +60,12 @@ class Device:
     def set_stream(self, stream_ptr: int | None) -> None:
         self.check(self._lib.eg2_set_stream(self.handle, C.c_void_p(stream_ptr or 0)))
 
+    def pass_policy(self) -> tuple[int, int]:
+        """``(max_rows, precise_max)`` of this context's pass policy (:func:`plan_passes`)."""
+        rows, pmax = C.c_int64(), C.c_int()
+        self.check(self._lib.eg2_pass_policy(self.handle, C.byref(rows), C.byref(pmax)))
+        return rows.value, pmax.value
+
     def profile(self, enable: bool) -> None:
         self.check(self._lib.eg2_profile(self.handle, 1 if enable else 0))
 
@@ -66,6 +73,25 @@ class Device:
         buf = C.create_string_buffer(1 << 16)
         self.check(self._lib.eg2_profile_read(self.handle, buf, len(buf)))
         return json.loads(buf.value.decode())
+
+
+def plan_passes(lens, max_rows: int, precise_max: int = 0) -> list[tuple[list[int], bool]]:
+    """The library's pass policy (``eg2_plan_passes``): ``[(sequence indices, runs_in_tf32), ...]``.
+
+    Consecutive sequences in call order share a pass of at most ``max_rows`` rows, as the reference's
+    ``embed_prepared`` packs inputs into passes of at most ``PACK_TOKENS`` rows (src/model.rs:508-521);
+    sequences of at most ``precise_max`` tokens form their own (TF32) passes."""
+    lens_l = [int(x) for x in lens]
+    n = len(lens_l)
+    pass_of = (C.c_int32 * max(1, n))()
+    precise = (C.c_int32 * max(1, n))()
+    rc = L.load().eg2_plan_passes(L.i32_array(lens_l), n, int(max_rows), int(precise_max), pass_of, precise)
+    if rc < 0:
+        raise L.Eg2Error(rc, "invalid pass-policy arguments")
+    out = [([], bool(precise[p])) for p in range(rc)]
+    for s in range(n):
+        out[pass_of[s]][0].append(s)
+    return out
 
 
 class TextBackend:
@@ -164,3 +190,31 @@ class VisionBackend:
             self.dev.handle, patches.ctypes.data, pos.ctypes.data_as(C.POINTER(C.c_int32)), grid_h, grid_w,
             pooled_a.ctypes.data if pooled else None, soft.ctypes.data))
         return (soft, pooled_a) if pooled else soft
+
+
+def embed_on_gpus(backends: list[TextBackend], ids_list, dims=MATRYOSHKA_DIMS):
+    """Embed token-id sequences over several GPUs from one process: one :class:`TextBackend` (one
+    device context) per GPU, each driven by its own host thread on its longest-first share of the
+    documents (``shard.dispatch``). A GPU whose call fails with anything but an input error is dropped
+    and its documents are re-queued on the others; a document with invalid input gets a
+    ``shard.DocumentError`` in its slot. Returns ({dim: [n, dim] array}, report); rows of failed
+    documents are NaN."""
+    all_dims = [backends[0].dev.embedding_dim] + [int(d) for d in dims]
+    total = sum(all_dims)
+
+    def worker(tb):
+        def embed(seqs):
+            r = tb.embed_ids(seqs, dims)
+            return np.concatenate([r[d] for d in all_dims], axis=1)
+        return embed
+
+    rows, report = shard.dispatch([worker(tb) for tb in backends], list(ids_list))
+    flat = np.full((len(rows), total), np.nan, np.float32)
+    for i, r in enumerate(rows):
+        if not isinstance(r, shard.DocumentError):
+            flat[i] = r
+    out, off = {}, 0
+    for d in all_dims:
+        out[d] = flat[:, off:off + d]
+        off += d
+    return out, report

@@ -437,13 +437,28 @@ struct eg2_ctx {
     std::vector<cudaEvent_t> event_pool;
     std::map<std::string, std::pair<double, long>> prof;
     bool use_tc_attention = true;
+    // Pass policy. A call is split into passes of at most pass_rows packed rows (a longer sequence
+    // gets a pass of its own), consecutive sequences in call order; in bf16 contexts, sequences of at
+    // most precise_max tokens run on `precise`, a TF32 context (f32 activations, TF32 GEMMs, f32
+    // attention) over the same checkpoint, sharing this context's embedding table and stream.
+    long pass_rows = 0;
+    int precise_max = 0;
+    eg2_ctx* precise = nullptr;
+    bool embed_table_shared = false;
+    // Multi-pass staging (device): the call's token ids of one pass, and the pooled results of the
+    // whole call until every pass has succeeded.
+    long stage_ids_cap = 0, stage_out_cap = 0;
+    uint32_t* stage_ids = nullptr;
+    float* stage_out = nullptr;
 
     ~eg2_ctx();
 };
 
 namespace eg2 {
 
-static void* dalloc(eg2_ctx* c, size_t bytes) {
+// Device allocation owned by the context. Buffers a captured graph reads bump buf_gen (the graph holds
+// their addresses); staging buffers no graph reads pass graph_visible = false.
+static void* dalloc(eg2_ctx* c, size_t bytes, bool graph_visible = true) {
     void* p = nullptr;
     if (bytes == 0) bytes = 16;
     cudaError_t e = cudaMalloc(&p, bytes);
@@ -452,15 +467,29 @@ static void* dalloc(eg2_ctx* c, size_t bytes) {
         fail(e == cudaErrorMemoryAllocation ? EG2_ERR_OOM : EG2_ERR_CUDA, "cudaMalloc(%zu): %s", bytes, cudaGetErrorString(e));
     }
     c->allocs.push_back(p);
-    c->buf_gen++;
+    if (graph_visible) c->buf_gen++;
     return p;
 }
-static void dfree(eg2_ctx* c, void* p) {
+static void dfree(eg2_ctx* c, void* p, bool graph_visible = true) {
     if (!p) return;
     auto it = std::find(c->allocs.begin(), c->allocs.end(), p);
     if (it != c->allocs.end()) c->allocs.erase(it);
     cudaFree(p);
-    c->buf_gen++;
+    if (graph_visible) c->buf_gen++;
+}
+
+// Fail before allocating when `need` bytes of device memory are not free, with a message that says what
+// to change (the reference's Gpu::ensure_fits, src/gpu/mod.rs:480-505).
+static void ensure_fits(size_t need, const char* what, long rows) {
+    size_t free_b = 0, total_b = 0;
+    CK(cudaMemGetInfo(&free_b, &total_b));
+    if (need > free_b) {
+        const double gb = 1024.0 * 1024.0 * 1024.0;
+        fail(EG2_ERR_OOM,
+             "%s for a pass of %ld rows needs about %.1f GB of GPU memory, but %.1f GB of the %.1f GB is free; "
+             "lower the pass size (EG2_PASS_ROWS) or the longest sequence",
+             what, rows, need / gb, free_b / gb, total_b / gb);
+    }
 }
 
 static bool bf16_mode(const eg2_ctx* c) { return c->precision == EG2_BF16; }
@@ -596,6 +625,7 @@ static void load_text(eg2_ctx* c, const SafeTensors& st) {
     // Token-embedding table stays bf16 on the device (the device-side gather of eg2_embed_packed).
     const TensorInfo& et = st.info("language_model.embed_tokens.weight", {tc.vocab, h});
     if (et.dtype != "BF16") fail(EG2_ERR_IO, "embed_tokens must be BF16");
+    if (c->embed_table) return;  // shared with the context this one serves (see eg2_ctx::precise)
     c->embed_table = (uint16_t*)dalloc(c, (size_t)tc.vocab * h * 2);
     CK(cudaMemcpy(c->embed_table, st.bytes(et), (size_t)tc.vocab * h * 2, cudaMemcpyHostToDevice));
 }
@@ -697,6 +727,11 @@ static void ensure_work(eg2_ctx* c, long rows, long n_tiles) {
             max_qkv = std::max(max_qkv, (tc.nh + 2 * L.nkv) * L.hd);
         }
         const size_t as = act_size(c);
+        const size_t per_row = (size_t)tc.hidden * 4 + (size_t)tc.layers * tc.ple * 4 + (size_t)tc.emb * 4 +
+                               (size_t)tc.hidden * as + (size_t)max_qkv * 4 + (size_t)(2 * max_q + 2 * max_kv) * as +
+                               (size_t)tc.hidden * 4 + (size_t)tc.inter * as + (size_t)tc.ple * as +
+                               (c->precision == EG2_F32 ? 2 * (size_t)tc.inter * 4 : 0) + 16;
+        ensure_fits(per_row * cap, "the text workspace", rows);
         w.hidden = (float*)dalloc(c, cap * tc.hidden * 4);
         w.ple = (float*)dalloc(c, cap * (long)tc.layers * tc.ple * 4);
         w.out = (float*)dalloc(c, cap * tc.emb * 4);
@@ -1149,6 +1184,7 @@ using namespace eg2;
 
 eg2_ctx::~eg2_ctx() {
     if (stream) cudaStreamSynchronize(stream);
+    delete precise;
     for (auto& g : graphs)
         if (g.exec) cudaGraphExecDestroy(g.exec);
     if (capture_stream) cudaStreamDestroy(capture_stream);
@@ -1184,17 +1220,34 @@ static int guarded(eg2_ctx* c, F&& f) {
 
 extern "C" {
 
-int eg2_open(int device, int precision, const char* model_dir, eg2_ctx** out) {
-    if (!out || !model_dir || precision < EG2_F32 || precision > EG2_BF16) {
-        g_open_error = "invalid argument";
-        return EG2_ERR_INVALID;
-    }
-    *out = nullptr;
+}  // extern "C"
+
+// Rows of one device pass: 64 documents of 2,208 tokens (141,312 rows, the throughput plateau on a
+// B200 at ~11 GB of bf16 workspace) plus room for a slightly larger pack. EG2_PASS_ROWS overrides.
+constexpr long kPassRowsDefault = 147456;
+// Sequences of at most this many tokens run in TF32 inside bf16 contexts. Their bf16 rounding errors
+// are not averaged over many tokens by the mean pool: measured on the random-init checkpoint, 1-5-token
+// documents reach 3.4e-3 to 4.3e-3 max-abs against the f32 oracle in bf16 (the bf16 profile allows
+// 4e-3), 17-token ones 2.8e-3, and TF32 stays near 5e-4. EG2_PRECISE_MAX_TOKENS overrides (0: off).
+constexpr int kPreciseMaxDefault = 16;
+
+static long env_long(const char* name, long dflt, long lo, long hi) {
+    const char* e = getenv(name);
+    if (!e || !*e) return dflt;
+    char* end = nullptr;
+    const long v = strtol(e, &end, 10);
+    if (end == e || v < lo || v > hi) return dflt;
+    return v;
+}
+
+// Open one context. text_only skips the vision tower; shared_table (device, bf16) is used as the
+// token-embedding table instead of uploading a copy.
+static int open_ctx(int device, int precision, const std::string& dir, bool text_only, uint16_t* shared_table,
+                    eg2_ctx** out) {
     eg2_ctx* c = new eg2_ctx();
     c->device = device;
     c->precision = precision;
-    int prev = 0;
-    cudaGetDevice(&prev);
+    c->pass_rows = env_long("EG2_PASS_ROWS", kPassRowsDefault, 1024, 1L << 30);
     try {
         CK(cudaSetDevice(device));
         int major = 0, minor = 0;
@@ -1203,30 +1256,55 @@ int eg2_open(int device, int precision, const char* model_dir, eg2_ctx** out) {
         if (major != 10 || minor != 0) fail(EG2_ERR_CUDA, "device %d is sm_%d%d; this library is built for sm_100a", device, major, minor);
         CK(cudaStreamCreateWithFlags(&c->own_stream, cudaStreamNonBlocking));
         c->stream = c->own_stream;
-        std::string dir(model_dir);
         parse_config(dir, c->tc, c->vc);
+        if (text_only) c->vc.present = false;
         SafeTensors st(dir + "/model.safetensors");
+        if (shared_table) {
+            c->embed_table = shared_table;
+            c->embed_table_shared = true;
+        }
         load_text(c, st);
         load_vision(c, st);
         c->bad_flag = (int*)dalloc(c, 4);
         CK(cudaMemset(c->bad_flag, 0, 4));
         const char* env = getenv("EG2_SIMT_ATTENTION");
         if (env && env[0] == '1') c->use_tc_attention = false;
+        if (precision == EG2_BF16 && !text_only) {
+            c->precise_max = (int)env_long("EG2_PRECISE_MAX_TOKENS", kPreciseMaxDefault, 0, 4096);
+            if (c->precise_max > 0) {
+                const int rc = open_ctx(device, EG2_TF32, dir, true, c->embed_table, &c->precise);
+                if (rc != EG2_OK) fail(rc, "opening the TF32 context for short sequences: %s", g_open_error.c_str());
+            }
+        }
         CK(cudaDeviceSynchronize());
     } catch (Fail& e) {
         g_open_error = e.msg;
         delete c;
-        cudaSetDevice(prev);
         return e.code;
     } catch (std::exception& e) {
         g_open_error = e.what();
         delete c;
-        cudaSetDevice(prev);
         return EG2_ERR_IO;
     }
-    cudaSetDevice(prev);
     *out = c;
     return EG2_OK;
+}
+
+extern "C" {
+
+int eg2_open(int device, int precision, const char* model_dir, eg2_ctx** out) {
+    if (!out || !model_dir || precision < EG2_F32 || precision > EG2_BF16) {
+        g_open_error = "invalid argument";
+        return EG2_ERR_INVALID;
+    }
+    *out = nullptr;
+    int prev = 0;
+    cudaGetDevice(&prev);
+    eg2_ctx* c = nullptr;
+    const int rc = open_ctx(device, precision, std::string(model_dir), false, nullptr, &c);
+    cudaSetDevice(prev);
+    if (rc == EG2_OK) *out = c;
+    return rc;
 }
 
 void eg2_close(eg2_ctx* c) {
@@ -1262,15 +1340,112 @@ int eg2_embed_tokens(eg2_ctx* c, const uint32_t* ids, int64_t n, float* out) {
         if (n == 0) return;
         for (int64_t i = 0; i < n; i++)
             if ((int64_t)ids[i] >= c->tc.vocab) fail(EG2_ERR_INVALID, "token id %u out of range", ids[i]);
-        ensure_work(c, n, 0);
+        // In chunks of at most one pass's rows, so the workspace stays bounded for any n.
+        const long chunk = std::min<long>(n, c->pass_rows);
+        ensure_work(c, chunk, 0);
         Work& w = c->w;
-        CK(cudaMemcpyAsync(w.ids, ids, n * 4, cudaMemcpyHostToDevice, c->stream));
-        KL(embed_gather(c->embed_table, c->tc.vocab, c->tc.hidden, w.ids, n, sqrtf((float)c->tc.hidden), w.hidden,
-                        c->bad_flag, c->stream),
-           "embed_gather");
-        CK(cudaMemcpyAsync(out, w.hidden, n * c->tc.hidden * 4, cudaMemcpyDeviceToHost, c->stream));
+        const int h = c->tc.hidden;
+        for (int64_t i0 = 0; i0 < n; i0 += chunk) {
+            const long m = std::min<long>(chunk, n - i0);
+            CK(cudaMemcpyAsync(w.ids, ids + i0, m * 4, cudaMemcpyHostToDevice, c->stream));
+            KL(embed_gather(c->embed_table, c->tc.vocab, h, w.ids, m, sqrtf((float)h), w.hidden, c->bad_flag, c->stream),
+               "embed_gather");
+            CK(cudaMemcpyAsync(out + i0 * h, w.hidden, m * h * 4, cudaMemcpyDeviceToHost, c->stream));
+        }
         CK(cudaStreamSynchronize(c->stream));
     });
+}
+
+// ---------------------------------------------------------------------------------------------
+// Pass policy (the reference's embed_prepared packs consecutive inputs greedily into passes of at
+// most PACK_TOKENS = 2,048 rows, a longer sequence forming a pass of its own, src/model.rs:157-158,
+// :508-521). Here the cap is sized for a B200 (one 64 x 2,208-token pass, the throughput plateau,
+// with ~11 GB of workspace), so one call of any size runs in a bounded workspace; and in bf16
+// contexts the sequences of at most `precise_max` tokens form their own passes on the TF32 context.
+// A pass is a set of consecutive sequences of one class in call order, so its results are the same
+// bits as a call holding only those sequences.
+// ---------------------------------------------------------------------------------------------
+struct Pass {
+    std::vector<int> seqs;  // the call's sequence indices, ascending
+    long rows = 0;
+    bool precise = false;
+};
+
+static std::vector<Pass> plan_passes(const int32_t* lens, int n_seq, long max_rows, int precise_max) {
+    std::vector<Pass> done;
+    Pass open[2];
+    open[1].precise = true;
+    for (int s = 0; s < n_seq; s++) {
+        const int k = (precise_max > 0 && lens[s] <= precise_max) ? 1 : 0;
+        if (!open[k].seqs.empty() && open[k].rows + lens[s] > max_rows) {
+            done.push_back(std::move(open[k]));
+            open[k] = Pass();
+            open[k].precise = k == 1;
+        }
+        open[k].seqs.push_back(s);
+        open[k].rows += lens[s];
+    }
+    for (int k = 0; k < 2; k++)
+        if (!open[k].seqs.empty()) done.push_back(std::move(open[k]));
+    return done;
+}
+
+// Sequences of a pass that are consecutive in the call: call sequences [seq0, seq0 + nseq), the
+// pass's sequences [pseq0, ...), call rows [row0, row0 + rows) at pass row prow0.
+struct Run {
+    int seq0, nseq, pseq0;
+    long row0, prow0, rows;
+};
+
+static std::vector<Run> pass_runs(const Pass& p, const std::vector<long>& seq_row0, const int32_t* lens) {
+    std::vector<Run> runs;
+    long prow = 0;
+    for (size_t i = 0; i < p.seqs.size(); i++) {
+        const int s = p.seqs[i];
+        if (!runs.empty() && runs.back().seq0 + runs.back().nseq == s) {
+            runs.back().nseq++;
+            runs.back().rows += lens[s];
+        } else {
+            runs.push_back(Run{s, 1, (int)i, seq_row0[s], prow, (long)lens[s]});
+        }
+        prow += lens[s];
+    }
+    return runs;
+}
+
+static std::vector<long> row_offsets(const int32_t* lens, int n_seq) {
+    std::vector<long> r0(n_seq);
+    long r = 0;
+    for (int s = 0; s < n_seq; s++) {
+        r0[s] = r;
+        r += lens[s];
+    }
+    return r0;
+}
+
+// The passes of a call on context c (the TF32 context takes the short sequences of bf16 contexts).
+static std::vector<Pass> call_plan(eg2_ctx* c, const int32_t* lens, int n_seq) {
+    const int pmax = (c->precise && bf16_mode(c)) ? c->precise_max : 0;
+    if (c->precise) c->precise->stream = c->stream;
+    return plan_passes(lens, n_seq, c->pass_rows, pmax);
+}
+
+// Grow-only staging buffers of the parent context (no captured graph reads them).
+static void ensure_stage(eg2_ctx* c, long ids_rows, long out_floats) {
+    if (ids_rows > c->stage_ids_cap) {
+        CK(cudaStreamSynchronize(c->stream));
+        dfree(c, c->stage_ids, false);
+        c->stage_ids = nullptr;
+        c->stage_ids_cap = std::max(ids_rows, 4096L);
+        c->stage_ids = (uint32_t*)dalloc(c, c->stage_ids_cap * 4, false);
+    }
+    if (out_floats > c->stage_out_cap) {
+        CK(cudaStreamSynchronize(c->stream));
+        dfree(c, c->stage_out, false);
+        c->stage_out = nullptr;
+        c->stage_out_cap = std::max(out_floats, 4096L);
+        c->stage_out = (float*)dalloc(c, c->stage_out_cap * 4, false);
+    }
 }
 
 static int forward_impl(eg2_ctx* c, const float* embeds, const int32_t* lens, int n_seq, float* out, void* stream,
@@ -1286,15 +1461,30 @@ static int forward_impl(eg2_ctx* c, const float* embeds, const int32_t* lens, in
         const long rows = check_lens(lens, n_seq);
         if (rows == 0) return;
         if (!embeds || !out) fail(EG2_ERR_INVALID, "null buffer");
-        auto sets = prepare_pass(c, lens, n_seq, rows);
-        Work& w = c->w;
-        CK(cudaMemcpyAsync(w.hidden, embeds, rows * c->tc.hidden * 4,
-                           device_ptrs ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, c->stream));
-        run_text(c, rows, sets);
-        CK(cudaMemcpyAsync(out, w.out, rows * c->tc.emb * 4, device_ptrs ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost,
-                           c->stream));
-        check_device_status(c);
-        collect_marks(c);
+        const int h = c->tc.hidden, emb = c->tc.emb;
+        const cudaMemcpyKind in_kind = device_ptrs ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
+        const cudaMemcpyKind out_kind = device_ptrs ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost;
+        const auto plan = call_plan(c, lens, n_seq);
+        const auto seq_row0 = row_offsets(lens, n_seq);
+        // Each pass runs, is checked, then writes its rows of `out`: an argument error leaves `out`
+        // untouched; a device failure in a later pass of a multi-pass call leaves the rows of the passes
+        // before it written.
+        for (const Pass& p : plan) {
+            eg2_ctx* x = p.precise ? c->precise : c;
+            const auto runs = pass_runs(p, seq_row0, lens);
+            std::vector<int32_t> plens;
+            for (int s : p.seqs) plens.push_back(lens[s]);
+            // The pass's embeddings into x's workspace, then its 24 layers; the per-token states land in x->w.out.
+            const auto sets = prepare_pass(x, plens.data(), (int)plens.size(), p.rows);
+            for (const Run& r : runs)
+                CK(cudaMemcpyAsync(x->w.hidden + r.prow0 * h, embeds + r.row0 * h, r.rows * h * 4, in_kind, c->stream));
+            run_text(x, p.rows, sets);
+            check_device_status(c);
+            collect_marks(c);
+            for (const Run& r : runs)
+                CK(cudaMemcpyAsync(out + r.row0 * emb, x->w.out + r.prow0 * emb, r.rows * emb * 4, out_kind, c->stream));
+        }
+        CK(cudaStreamSynchronize(c->stream));
     });
 }
 
@@ -1305,14 +1495,15 @@ int eg2_forward_packed_device(eg2_ctx* c, const float* embeds, const int32_t* le
     return forward_impl(c, embeds, lens, n_seq, out, stream, true);
 }
 
-// Short passes (<= 128 rows, bf16): rows are padded to a bucket of 16 / 32 / 64 / 128 with one extra
-// sequence of token 0, the attention tile lists and the pooled-sequence list to bucket + 1 entries
-// (empty ones have length 0), so every launch of the pass has the same parameters for any split of
-// the bucket into sequences. The pass (gather, 24 layers, pool) is captured once per (bucket, dims)
-// into a CUDA graph and replayed with new metadata: ~175 launches become one (the reference captures
-// graphs per row bucket for the same reason, src/gpu/text.rs:475-516).
+// Short passes (<= 128 rows, bf16 or TF32): rows are padded to a bucket of 16 / 32 / 64 / 128 with one
+// extra sequence of token 0, the attention tile lists and the pooled-sequence list to bucket + 1
+// entries (empty ones have length 0), so every launch of the pass has the same parameters for any
+// split of the bucket into sequences. The pass (gather, 24 layers, pool) is captured once per
+// (bucket, dims) into a CUDA graph and replayed with new metadata: ~175 launches become one (the
+// reference captures graphs per row bucket for the same reason, src/gpu/text.rs:475-516). The pooled
+// results are left in c->w.pooled.
 static void embed_graph(eg2_ctx* c, const uint32_t* ids, const int32_t* lens, int n_seq, long rows, const int32_t* dims,
-                        int n_dims, int total, float* out, bool device_ptrs) {
+                        int n_dims, int total, bool ids_on_device) {
     const int B = rows <= 16 ? 16 : rows <= 32 ? 32 : rows <= 64 ? 64 : 128;
     const int S = B + 1;  // pooled-sequence slots
     std::vector<int32_t> lp(lens, lens + n_seq);
@@ -1350,9 +1541,8 @@ static void embed_graph(eg2_ctx* c, const uint32_t* ids, const int32_t* lens, in
     int* seq_meta = w.seq_meta;
     CK(cudaMemcpyAsync(seq_meta, meta.data(), meta.size() * 4, cudaMemcpyHostToDevice, c->stream));
     CK(cudaMemcpyAsync(w.dims, dims, n_dims * 4, cudaMemcpyHostToDevice, c->stream));
-    CK(cudaMemsetAsync(c->bad_flag, 0, 4, c->stream));
     CK(cudaMemsetAsync(w.ids, 0, (size_t)B * 4, c->stream));
-    CK(cudaMemcpyAsync(w.ids, ids, rows * 4, device_ptrs ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, c->stream));
+    CK(cudaMemcpyAsync(w.ids, ids, rows * 4, ids_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, c->stream));
     auto body = [&]() {
         KL(embed_gather(c->embed_table, c->tc.vocab, c->tc.hidden, w.ids, B, sqrtf((float)c->tc.hidden), w.hidden,
                         c->bad_flag, c->stream),
@@ -1403,12 +1593,64 @@ static void embed_graph(eg2_ctx* c, const uint32_t* ids, const int32_t* lens, in
         }
         g->bucket = B, g->n_dims = n_dims, g->total = total, g->gen = c->buf_gen, g->launches = n_launch, g->exec = exec;
     }
-    CK(cudaMemcpyAsync(out, w.pooled, (size_t)n_seq * total * 4, device_ptrs ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost,
-                       c->stream));
-    int bad = 0;
-    CK(cudaMemcpyAsync(&bad, c->bad_flag, 4, cudaMemcpyDeviceToHost, c->stream));
-    check_device_status(c);
-    if (bad) fail(EG2_ERR_INVALID, "token id out of range");
+}
+
+// One embedding pass of context c over `n_seq` sequences packed back to back (rows = sum(lens)), token
+// ids at `ids` (host or device memory): pooled embeddings and their cuts in c->w.pooled [n_seq, total].
+// Enqueued on c->stream; the caller reads c->bad_flag and the device status.
+static void embed_pass(eg2_ctx* c, const uint32_t* ids, bool ids_on_device, const int32_t* lens, int n_seq, long rows,
+                       const int32_t* dims, int n_dims, int total) {
+    const bool graph_kind = (bf16_mode(c) && c->use_tc_attention) || c->precision == EG2_TF32;
+    if (graph_kind && !c->profiling && rows <= 128 && !getenv("EG2_NO_GRAPHS")) {
+        embed_graph(c, ids, lens, n_seq, rows, dims, n_dims, total, ids_on_device);
+        return;
+    }
+    auto sets = prepare_pass(c, lens, n_seq, rows);
+    Work& w = c->w;
+    if ((long)n_seq * total > w.pooled_cap || !w.dims) {
+        CK(cudaStreamSynchronize(c->stream));
+        dfree(c, w.pooled);
+        w.pooled_cap = std::max((long)n_seq * total, 4096L);
+        w.pooled = (float*)dalloc(c, w.pooled_cap * 4);
+        if (!w.dims) w.dims = (int*)dalloc(c, 64);
+    }
+    std::vector<int> st(n_seq), ln(n_seq);
+    long r = 0;
+    for (int s = 0; s < n_seq; s++) {
+        st[s] = (int)r;
+        ln[s] = lens[s];
+        r += lens[s];
+    }
+    // Per-sequence start / length for the pool kernel.
+    if (n_seq > w.seq_meta_cap) {
+        CK(cudaStreamSynchronize(c->stream));
+        dfree(c, w.seq_meta);
+        w.seq_meta_cap = std::max(n_seq, 1024);
+        w.seq_meta = (int*)dalloc(c, 2L * w.seq_meta_cap * 4);
+    }
+    int* seq_meta = w.seq_meta;
+    CK(cudaMemcpyAsync(seq_meta, st.data(), n_seq * 4, cudaMemcpyHostToDevice, c->stream));
+    CK(cudaMemcpyAsync(seq_meta + n_seq, ln.data(), n_seq * 4, cudaMemcpyHostToDevice, c->stream));
+    CK(cudaMemcpyAsync(w.dims, dims, n_dims * 4, cudaMemcpyHostToDevice, c->stream));
+    CK(cudaMemcpyAsync(w.ids, ids, rows * 4, ids_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, c->stream));
+    KL(embed_gather(c->embed_table, c->tc.vocab, c->tc.hidden, w.ids, rows, sqrtf((float)c->tc.hidden), w.hidden,
+                    c->bad_flag, c->stream),
+       "embed_gather");
+    run_text(c, rows, sets);
+    int max_len = 0;
+    for (int s2 = 0; s2 < n_seq; s2++) max_len = std::max(max_len, (int)lens[s2]);
+    const long need = pool_scratch_doubles(n_seq, max_len, c->tc.emb);
+    if (need > w.pool_scratch_cap) {
+        CK(cudaStreamSynchronize(c->stream));
+        dfree(c, w.pool_scratch);
+        w.pool_scratch_cap = std::max(need, 1L << 20);
+        w.pool_scratch = (double*)dalloc(c, w.pool_scratch_cap * 8);
+    }
+    KL(pool_rows(w.out, seq_meta, seq_meta + n_seq, n_seq, max_len, c->tc.emb, w.dims, n_dims, total, w.pooled,
+                 w.pool_scratch, c->stream),
+       "pool");
+    g_launches.fetch_add(1, std::memory_order_relaxed);  // pool_rows is two launches
+    mark(c, "pool");
 }
 
 static int embed_impl(eg2_ctx* c, const uint32_t* ids, const int32_t* lens, int n_seq, const int32_t* dims, int n_dims,
@@ -1432,64 +1674,55 @@ static int embed_impl(eg2_ctx* c, const uint32_t* ids, const int32_t* lens, int 
         if (!device_ptrs)
             for (long i = 0; i < rows; i++)
                 if ((int64_t)ids[i] >= c->tc.vocab) fail(EG2_ERR_INVALID, "token id %u out of range", ids[i]);
-        if (bf16_mode(c) && c->use_tc_attention && !c->profiling && rows <= 128 && !getenv("EG2_NO_GRAPHS")) {
-            embed_graph(c, ids, lens, n_seq, rows, dims, n_dims, total, out, device_ptrs);
-            return;
-        }
-        auto sets = prepare_pass(c, lens, n_seq, rows);
-        Work& w = c->w;
-        if ((long)n_seq * total > w.pooled_cap || !w.dims) {
-            CK(cudaStreamSynchronize(c->stream));
-            dfree(c, w.pooled);
-            w.pooled_cap = std::max((long)n_seq * total, 4096L);
-            w.pooled = (float*)dalloc(c, w.pooled_cap * 4);
-            if (!w.dims) w.dims = (int*)dalloc(c, 64);
-        }
-        std::vector<int> st(n_seq), ln(n_seq);
-        long r = 0;
-        for (int s = 0; s < n_seq; s++) {
-            st[s] = (int)r;
-            ln[s] = lens[s];
-            r += lens[s];
-        }
-        // Per-sequence start / length for the pool kernel.
-        if (n_seq > w.seq_meta_cap) {
-            CK(cudaStreamSynchronize(c->stream));
-            dfree(c, w.seq_meta);
-            w.seq_meta_cap = std::max(n_seq, 1024);
-            w.seq_meta = (int*)dalloc(c, 2L * w.seq_meta_cap * 4);
-        }
-        int* seq_meta = w.seq_meta;
-        CK(cudaMemcpyAsync(seq_meta, st.data(), n_seq * 4, cudaMemcpyHostToDevice, c->stream));
-        CK(cudaMemcpyAsync(seq_meta + n_seq, ln.data(), n_seq * 4, cudaMemcpyHostToDevice, c->stream));
-        CK(cudaMemcpyAsync(w.dims, dims, n_dims * 4, cudaMemcpyHostToDevice, c->stream));
+        const auto plan = call_plan(c, lens, n_seq);
         CK(cudaMemsetAsync(c->bad_flag, 0, 4, c->stream));
-        CK(cudaMemcpyAsync(w.ids, ids, rows * 4, device_ptrs ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, c->stream));
-        KL(embed_gather(c->embed_table, c->tc.vocab, c->tc.hidden, w.ids, rows, sqrtf((float)c->tc.hidden), w.hidden,
-                        c->bad_flag, c->stream),
-           "embed_gather");
-        run_text(c, rows, sets);
-        int max_len = 0;
-        for (int s2 = 0; s2 < n_seq; s2++) max_len = std::max(max_len, (int)lens[s2]);
-        const long need = pool_scratch_doubles(n_seq, max_len, c->tc.emb);
-        if (need > w.pool_scratch_cap) {
-            CK(cudaStreamSynchronize(c->stream));
-            dfree(c, w.pool_scratch);
-            w.pool_scratch_cap = std::max(need, 1L << 20);
-            w.pool_scratch = (double*)dalloc(c, w.pool_scratch_cap * 8);
+        if (c->precise) CK(cudaMemsetAsync(c->precise->bad_flag, 0, 4, c->stream));
+        const float* result = nullptr;
+        if (plan.size() == 1) {
+            eg2_ctx* x = plan[0].precise ? c->precise : c;
+            embed_pass(x, ids, device_ptrs, lens, n_seq, rows, dims, n_dims, total);
+            result = x->w.pooled;
+        } else {
+            // Several passes: each pass's ids are gathered into one contiguous buffer, its pooled rows
+            // scattered into the call's result buffer, which reaches `out` once every pass succeeded.
+            long max_pass = 0;
+            for (const Pass& p : plan) max_pass = std::max(max_pass, p.rows);
+            ensure_stage(c, device_ptrs ? max_pass : 0, (long)n_seq * total);
+            const auto seq_row0 = row_offsets(lens, n_seq);
+            for (const Pass& p : plan) {
+                eg2_ctx* x = p.precise ? c->precise : c;
+                const auto runs = pass_runs(p, seq_row0, lens);
+                std::vector<int32_t> plens;
+                for (int s : p.seqs) plens.push_back(lens[s]);
+                std::vector<uint32_t> hids;
+                const uint32_t* pids;
+                if (device_ptrs) {
+                    for (const Run& r : runs)
+                        CK(cudaMemcpyAsync(c->stage_ids + r.prow0, ids + r.row0, r.rows * 4, cudaMemcpyDeviceToDevice,
+                                           c->stream));
+                    pids = c->stage_ids;
+                } else {
+                    hids.resize(p.rows);
+                    for (const Run& r : runs) memcpy(hids.data() + r.prow0, ids + r.row0, r.rows * 4);
+                    pids = hids.data();
+                }
+                // (A host `pids` is pageable: its copy completes before embed_pass returns.)
+                embed_pass(x, pids, device_ptrs, plens.data(), (int)plens.size(), p.rows, dims, n_dims, total);
+                for (const Run& r : runs)
+                    CK(cudaMemcpyAsync(c->stage_out + (long)r.seq0 * total, x->w.pooled + (long)r.pseq0 * total,
+                                       (long)r.nseq * total * 4, cudaMemcpyDeviceToDevice, c->stream));
+            }
+            result = c->stage_out;
         }
-        KL(pool_rows(w.out, seq_meta, seq_meta + n_seq, n_seq, max_len, c->tc.emb, w.dims, n_dims, total, w.pooled,
-                     w.pool_scratch, c->stream),
-           "pool");
-        g_launches.fetch_add(1, std::memory_order_relaxed);  // pool_rows is two launches
-        mark(c, "pool");
-        CK(cudaMemcpyAsync(out, w.pooled, (size_t)n_seq * total * 4,
-                           device_ptrs ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost, c->stream));
-        int bad = 0;
+        int bad = 0, bad_precise = 0;
         CK(cudaMemcpyAsync(&bad, c->bad_flag, 4, cudaMemcpyDeviceToHost, c->stream));
+        if (c->precise) CK(cudaMemcpyAsync(&bad_precise, c->precise->bad_flag, 4, cudaMemcpyDeviceToHost, c->stream));
         check_device_status(c);
         collect_marks(c);
-        if (bad) fail(EG2_ERR_INVALID, "token id out of range");
+        if (bad || bad_precise) fail(EG2_ERR_INVALID, "token id out of range");
+        CK(cudaMemcpyAsync(out, result, (size_t)n_seq * total * 4, device_ptrs ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost,
+                           c->stream));
+        CK(cudaStreamSynchronize(c->stream));
     });
 }
 
@@ -1500,6 +1733,26 @@ int eg2_embed_packed(eg2_ctx* c, const uint32_t* ids, const int32_t* lens, int n
 int eg2_embed_packed_device(eg2_ctx* c, const uint32_t* ids, const int32_t* lens, int n_seq, const int32_t* dims,
                             int n_dims, float* out, void* stream) {
     return embed_impl(c, ids, lens, n_seq, dims, n_dims, out, stream, true);
+}
+
+int eg2_plan_passes(const int32_t* lens, int n_seq, int64_t max_rows, int precise_max, int32_t* pass_of_seq,
+                    int32_t* pass_precise) {
+    if (n_seq < 0 || (n_seq > 0 && (!lens || !pass_of_seq)) || max_rows <= 0 || precise_max < 0) return EG2_ERR_INVALID;
+    for (int s = 0; s < n_seq; s++)
+        if (lens[s] <= 0) return EG2_ERR_INVALID;
+    const auto plan = plan_passes(lens, n_seq, (long)max_rows, precise_max);
+    for (size_t p = 0; p < plan.size(); p++) {
+        for (int s : plan[p].seqs) pass_of_seq[s] = (int32_t)p;
+        if (pass_precise) pass_precise[p] = plan[p].precise ? 1 : 0;
+    }
+    return (int)plan.size();
+}
+
+int eg2_pass_policy(const eg2_ctx* c, int64_t* max_rows, int* precise_max) {
+    if (!c) return EG2_ERR_INVALID;
+    if (max_rows) *max_rows = c->pass_rows;
+    if (precise_max) *precise_max = (c->precise && c->precision == EG2_BF16) ? c->precise_max : 0;
+    return EG2_OK;
 }
 
 int eg2_vision_encode(eg2_ctx* c, const float* patches, const int32_t* pos_xy, int gh, int gw, float* out_pooled,

@@ -67,6 +67,8 @@ def load(build_if_missing: bool = True) -> C.CDLL:
         "eg2_gemm": (C.c_int, [C.c_int, _P, C.c_int64, _P, C.c_int64, _P, C.c_int64, C.c_int, C.c_int, C.c_int, C.c_int, _P]),
         "eg2_attention": (C.c_int, [C.c_int, _P, _P, _P, _P, _I32P, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, _P]),
         "eg2_attention_noalloc": (C.c_int, [_P, _P, _P, _P, _I32P, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, _P]),
+        "eg2_plan_passes": (C.c_int, [_I32P, C.c_int, C.c_int64, C.c_int, _I32P, _I32P]),
+        "eg2_pass_policy": (C.c_int, [_P, C.POINTER(C.c_int64), C.POINTER(C.c_int)]),
         "eg2_launch_count": (C.c_longlong, []),
         "eg2_device_status": (C.c_int, []),
         "eg2_device_status_reset": (None, []),

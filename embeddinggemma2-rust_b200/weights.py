@@ -194,9 +194,13 @@ def vision_tensor_specs(cfg: dict) -> list[tuple[str, tuple[int, ...], str]]:
 
 
 def make_random_checkpoint(
-    dirpath: str | Path, seed: int = 0, cfg: dict | None = None, vision: bool = True
+    dirpath: str | Path, seed: int = 0, cfg: dict | None = None, vision: bool = True, unit_qk_norms: bool = False
 ) -> Path:
-    """Write ``config.json`` + ``model.safetensors`` (BF16) with seeded random-init weights."""
+    """Write ``config.json`` + ``model.safetensors`` (BF16) with seeded random-init weights.
+
+    ``unit_qk_norms=True`` writes the workload's literal init (every norm weight 1, q/k norms included):
+    the chaotic checkpoint described in the module docstring, kept for the test that shows why the
+    default scales the q/k norms."""
     cfg = cfg or synthetic_config()
     d = Path(dirpath)
     write_config(d, cfg)
@@ -204,6 +208,8 @@ def make_random_checkpoint(
     tensors: dict[str, np.ndarray] = {}
     for name, shape, init in specs:
         if init == "ones":
+            tensors[name] = np.full(shape, _ONE_BF16, dtype=np.uint16)
+        elif init == "qk" and unit_qk_norms:
             tensors[name] = np.full(shape, _ONE_BF16, dtype=np.uint16)
         elif init == "qk":
             tensors[name] = np.full(shape, f32_to_bf16_bits(np.float32(shape[0] ** -0.25))[()], dtype=np.uint16)

@@ -69,7 +69,9 @@ int eg2_embed_tokens(eg2_ctx* ctx, const uint32_t* ids, int64_t n, float* out);
  * (rows = sum(lens)); embeds [rows, hidden]. Host buffers. */
 int eg2_forward_packed(eg2_ctx* ctx, const float* embeds, const int32_t* lens, int n_seq, float* out);
 /* Same with device buffers; `lens` stays a host array. Work is enqueued on `stream` (or the
- * context's stream) and the call returns after it completes. */
+ * context's stream) and the call returns after it completes. A call of several passes (see
+ * eg2_plan_passes) writes each pass's rows once that pass has completed: an argument error leaves
+ * `out` untouched, a device failure in a later pass leaves the earlier passes' rows written. */
 int eg2_forward_packed_device(eg2_ctx* ctx, const float* embeds, const int32_t* lens, int n_seq, float* out,
                               void* stream);
 
@@ -80,6 +82,20 @@ int eg2_embed_packed(eg2_ctx* ctx, const uint32_t* ids, const int32_t* lens, int
                      int n_dims, float* out);
 int eg2_embed_packed_device(eg2_ctx* ctx, const uint32_t* ids, const int32_t* lens, int n_seq, const int32_t* dims,
                             int n_dims, float* out, void* stream);
+
+/* Pass policy of eg2_forward_packed / eg2_embed_packed (both variants). A call is split into device
+ * passes of consecutive sequences in call order, each of at most max_rows packed rows (a longer
+ * sequence gets a pass of its own), as the reference's embed_prepared packs inputs into passes of at
+ * most PACK_TOKENS rows (src/model.rs:157-158, :508-521), so any call runs in a bounded workspace;
+ * in bf16 contexts the sequences of at most precise_max tokens form their own passes, computed in
+ * TF32 (their bf16 rounding errors are not averaged out by the mean pool). Each pass gives the same
+ * bits as a call holding only its sequences. eg2_plan_passes computes the plan without a device:
+ * pass_of_seq[n_seq] receives each sequence's pass, pass_precise (room for n_seq entries, may be NULL)
+ * 1 for the TF32 passes; it returns the number of passes or a negative EG2_ERR_* code.
+ * eg2_pass_policy reports a context's max_rows and precise_max (0 when no pass runs in TF32). */
+int eg2_plan_passes(const int32_t* lens, int n_seq, int64_t max_rows, int precise_max, int32_t* pass_of_seq,
+                    int32_t* pass_precise);
+int eg2_pass_policy(const eg2_ctx* ctx, int64_t* max_rows, int* precise_max);
 
 /* Vision tower over one patched image: patches [n, 3*p*p] in [0, 1], pos_xy [n, 2] (x, y),
  * n = grid_h * grid_w. out_pooled [n/k^2, vision_hidden] (3x3-pooled states * sqrt(hidden), the

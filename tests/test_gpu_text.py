@@ -1,6 +1,7 @@
 """Text backbone parity through the C ABI against the CPU oracle, per precision profile
 (src/verify.rs:66-110): embeddings and their 512/256/128 Matryoshka cuts."""
 import json
+import sys
 import zlib
 from pathlib import Path
 
@@ -9,6 +10,8 @@ import pytest
 
 import oracle as O
 from conftest import pkg
+
+sys.path.insert(0, str(Path(__file__).parent / "golden"))
 
 B = pkg("backend")
 V = pkg("verify")
@@ -64,7 +67,13 @@ def test_embed_ids_parity(prec, cases, request):
 
 @pytest.mark.parametrize("prec", ["bf16", "f32"])
 def test_forward_packed_rows(prec, oracle_text, request):
-    """The drop-in call itself: per-token states [rows, 768] for host embeddings."""
+    """The drop-in call itself: per-token states [rows, 768] for host embeddings, row by row.
+
+    f32: every element within 2e-5 of the oracle (relative to the row's largest). bf16 and TF32 are
+    specified on pooled embeddings (src/verify.rs:85-110); a single token's state gets no averaging
+    over the sequence, so each unit-normalised row is held to twice the embedding profile's error
+    (max-abs 2 x 4e-3, 1 - cos at most 2 x 9e-5), and the rows pooled on the host, as the
+    reference's embed_prepared does (src/model.rs:530-535), must meet the profile itself."""
     dev = request.getfixturevalue(f"dev_{prec}")
     tb = B.TextBackend(dev)
     lens = [5, 64, 200]
@@ -74,10 +83,20 @@ def test_forward_packed_rows(prec, oracle_text, request):
     np.testing.assert_array_equal(tb.embed_tokens(ids), e)
     got = tb.forward_packed(e, lens)
     want = oracle_text.forward_packed(e, lens)
-    tol = 2e-5 if prec == "f32" else 0.08
-    assert np.abs(got - want).max() < tol * max(1.0, float(np.abs(want).max()))
-    if prec != "f32":
-        assert V.cosine(got, want) > 0.9999
+    if prec == "f32":
+        scale = np.maximum(1.0, np.abs(want).max(axis=1, keepdims=True))
+        assert (np.abs(got - want) / scale).max() < 2e-5
+    else:
+        gn = got / np.linalg.norm(got, axis=1, keepdims=True)
+        wn = want / np.linalg.norm(want, axis=1, keepdims=True)
+        max_abs = np.abs(gn - wn).max(axis=1)
+        cos = (gn * wn).sum(axis=1)
+        print(f"per-token rows: worst max|d| {max_abs.max():.2e}, min cos {cos.min():.8f}")
+        assert max_abs.max() <= 2 * V.BF16.embedding.max_abs
+        assert cos.min() >= 1 - 2 * (1 - V.BF16.embedding.min_cos)
+        pooled = O.pool(got, lens)
+        cuts = {768: pooled, **{d: O.truncate_and_normalize(pooled, d) for d in (512, 256, 128)}}
+        check_embeddings(cuts, O.pool(want, lens), V.BF16, "bf16/pooled rows")
 
 
 def test_golden_through_gpu(dev_bf16):
@@ -141,3 +160,34 @@ def test_add_norm_fusion_matches_kernel_path(cases, request, monkeypatch):
         cos = (fused[d] * plain[d]).sum(1) / (np.linalg.norm(fused[d], axis=1) * np.linalg.norm(plain[d], axis=1))
         print(f"fused vs kernel path @{d}: max|d| {diff:.2e} min cos {cos.min():.8f}")
         assert diff <= 2e-3 and cos.min() >= 0.99995
+
+
+FIXTURES = Path(__file__).parent / "golden" / "oracle_fixtures.npz"
+
+
+@pytest.fixture(scope="module")
+def oracle_fixtures():
+    import make_oracle_fixtures as M
+
+    f = np.load(FIXTURES)
+    return M, f
+
+
+@pytest.mark.parametrize("prec", ["f32", "tf32", "bf16"])
+def test_c1_against_oracle_fixture(prec, oracle_fixtures, request):
+    """BASELINE configs[0] (C1): one 512-token sequence of seed-0 uniform ids, all three precisions
+    against the oracle's result committed in tests/golden/oracle_fixtures.npz."""
+    M, f = oracle_fixtures
+    seqs = M.case_ids("c1")
+    got = B.TextBackend(request.getfixturevalue(f"dev_{prec}")).embed_ids(seqs)
+    check_embeddings(got, f["c1_emb"], V.for_precision(prec), f"{prec}/c1")
+
+
+def test_c3_against_oracle_fixture(dev_bf16, oracle_fixtures):
+    """C3: the 64 mixed-length documents of the bench's mixed leg (lengths uniform in [128, 2,208],
+    seed 7) in one bf16 call, each against the oracle."""
+    M, f = oracle_fixtures
+    seqs = M.case_ids("c3")
+    assert [len(x) for x in seqs] == list(f["c3_lens"])
+    got = B.TextBackend(dev_bf16).embed_ids(seqs)
+    check_embeddings(got, f["c3_emb"], V.BF16, "bf16/c3")

@@ -163,3 +163,27 @@ def test_vision_oracle_matches_golden(oracle_vision):
         assert pooled.shape == pw.shape and soft.shape == sw.shape
         assert np.abs(pooled - pw).max() <= 1e-5 * np.abs(pw).max(), (gh, gw)
         assert np.abs(soft - sw).max() <= 1e-5, (gh, gw)
+
+
+def test_oracle_fixtures_match_this_checkpoint_and_c1(oracle_text, tmp_path):
+    """The committed oracle fixtures (tests/golden/oracle_fixtures.npz, written by
+    make_oracle_fixtures.py) belong to this checkpoint, and the oracle reproduces their C1 case --
+    BASELINE configs[0] as stated: one 512-token sequence of seed-0 uniform ids through the CPU f32
+    path, pooled, L2-normalised, with its 512/256/128 cuts."""
+    import sys
+
+    golden = Path(__file__).parent / "golden"
+    sys.path.insert(0, str(golden))
+    import make_oracle_fixtures as M
+
+    f = np.load(golden / "oracle_fixtures.npz")
+    pkg("weights").make_random_checkpoint(tmp_path, seed=0, vision=False)
+    assert str(f["checkpoint_sha256"]) == M.checkpoint_sha256(tmp_path)
+    seqs = M.case_ids("c1")
+    got = oracle_text.embed_ids(seqs)
+    np.testing.assert_allclose(got, f["c1_emb"], rtol=0, atol=1e-6)
+    for d in (512, 256, 128):
+        cut = O.truncate_and_normalize(got, d)
+        assert cut.shape == (1, d) and abs(np.linalg.norm(cut) - 1) < 1e-6
+    assert [len(x) for x in M.case_ids("c3")] == list(f["c3_lens"])
+    assert [len(x) for x in M.case_ids("c4")] == list(f["c4_lens"])
