@@ -10,8 +10,8 @@
 // kernel, and calls no allocating routine.
 //
 // Limits: at most EG2_NOALLOC_MAX_SEQ sequences and EG2_NOALLOC_MAX_TILES query tiles per call
-// (a tile is tokens-per-tile query rows of one sequence: 64 for 4 query heads over 2 K/V heads,
-// 32 for 4 over 1), i.e. about 4 M rows for sliding-window layers; larger calls are rejected.
+// (a tile is up to 128 query tokens of one sequence for 4 query heads over 2 K/V heads of 256, 64 for
+// 4 over 1 of 512, 256 for head 64), i.e. 4 M to 16 M rows; larger calls are rejected.
 // All calls share the one array and leave their contents in it: two calls that overlap on the GPU
 // (different streams, or different host threads, with no ordering between them) race on it.
 // The call is asynchronous: a bounded device wait that ran out is reported through the device

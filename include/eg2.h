@@ -135,9 +135,10 @@ int eg2_attention(int kind, const void* q, const void* k, const void* v, void* o
  * the pool's back can fail or fragment it), and latency-critical paths that cannot take
  * cudaMalloc's implicit device synchronisation. Its scratch (sequence lengths and the query-tile
  * list) lives in one fixed 1 MiB device array per GPU, held until the process exits; calls with
- * more than 65536 sequences or 65536 query tiles (~4 M rows at 64 tokens per tile) return
- * EG2_ERR_INVALID before anything is copied or launched. The first call on a device looks the
- * array's device address up (make that first call before any stream capture). All calls share the
+ * more than 65536 sequences or 65536 query tiles (4 M to 16 M rows: a tile holds 64, 128 or 256
+ * query tokens by head layout) return EG2_ERR_INVALID before anything is copied or launched. The
+ * first call on a device looks the array's device address up (make that first call before any
+ * stream capture). All calls share the
  * array and it keeps the last call's contents: calls that overlap on the GPU (unordered streams or
  * threads) race. The call is asynchronous on `stream`: `lens` in pageable host memory is read before
  * the call returns; in page-locked memory it is read when the stream reaches the copy and must stay

@@ -67,26 +67,31 @@ def test_noalloc_matches_allocating_entry_point_on_consecutive_calls():
 
 
 def test_noalloc_rejects_calls_beyond_its_fixed_scratch():
-    """Every rejection happens on the host before anything is copied or launched, so the small q / k /
-    v buffers are never read even where the lengths describe millions of rows."""
+    """Every rejection happens on the host before anything is copied or launched. The q / k / v / out
+    buffers are nonetheless sized for the rows each call describes, so that a call the limits failed to
+    catch would still stay inside its buffers."""
     lib = L.load()
-    q, k, v = _inputs(8, 4, 2, 256, seed=7)
-    out = torch.zeros((8, 1024), dtype=torch.int16, device="cuda")
-    before = out.clone()
 
     def call(lens, nh=4, nkv=2, hd=256, window=512):
-        return lib.eg2_attention_noalloc(C.c_void_p(q.data_ptr()), C.c_void_p(k.data_ptr()), C.c_void_p(v.data_ptr()),
-                                         C.c_void_p(out.data_ptr()), L.i32_array(lens), len(lens), nh, nkv, hd, window,
-                                         None)
+        rows = max(1, sum(max(0, x) for x in lens))
+        q = torch.zeros((rows, max(1, nh) * hd), dtype=torch.int16, device="cuda")
+        kv = torch.zeros((rows, max(1, nkv) * hd), dtype=torch.int16, device="cuda")
+        out = torch.full((rows, max(1, nh) * hd), 7, dtype=torch.int16, device="cuda")
+        rc = lib.eg2_attention_noalloc(C.c_void_p(q.data_ptr()), C.c_void_p(kv.data_ptr()), C.c_void_p(kv.data_ptr()),
+                                       C.c_void_p(out.data_ptr()), L.i32_array(lens), len(lens), nh, nkv, hd, window,
+                                       None)
+        torch.cuda.synchronize()
+        assert bool((out == 7).all()), "a rejected call wrote its output"
+        return rc
 
-    assert call([1] * 65537) == -1            # more sequences than the array holds
-    assert call([65] * 40000) == -1           # fewer sequences, but 80,000 query tiles of 64 rows
-    assert call([5, 0, 3]) == -1              # an empty sequence
-    assert call([5, -2]) == -1                # a negative length
-    assert call([8], nh=0) == -1              # no query heads
-    assert call([8], nkv=0) == -1             # no K/V heads
-    assert call([8], nh=4, nkv=3) == -1       # query heads not a multiple of K/V heads
-    assert call([8], hd=128) == -1            # a head size the kernels do not take
-    torch.cuda.synchronize()
-    assert torch.equal(out, before)
+    # Query tokens per tile: 128 for 4 query heads over 2 K/V heads of 256, 64 for 4 over 1 of 512.
+    assert call([1] * 65537) == -1                      # more sequences than the array holds
+    assert call([129] + [1] * 65535) == -1              # 65,536 sequences, but 65,537 query tiles
+    assert call([65] + [1] * 65535, nkv=1, hd=512, window=-1) == -1  # the same with 64-token tiles
+    assert call([5, 0, 3]) == -1                        # an empty sequence
+    assert call([5, -2]) == -1                          # a negative length
+    assert call([8], nh=0) == -1                        # no query heads
+    assert call([8], nkv=0) == -1                       # no K/V heads
+    assert call([8], nh=4, nkv=3) == -1                 # query heads not a multiple of K/V heads
+    assert call([8], hd=128) == -1                      # a head size the kernels do not take
     assert lib.eg2_device_status() == 0
