@@ -172,11 +172,13 @@ def run_mixed(tb, cfg, stream, rank, world, args, barrier, max_over_ranks):
         step()
     e1.record(stream)
     torch.cuda.synchronize()
-    ms = max_over_ranks(e0.elapsed_time(e1))
+    local_ms = e0.elapsed_time(e1)
+    ms = max_over_ranks(local_ms)
     return {"value": round(MIXED_DOCS * args.steps / (ms / 1000.0), 2), "unit": "docs/s", "docs": MIXED_DOCS,
             "tokens": int(all_lens.sum()), "lengths": f"uniform integers in [{MIXED_LO}, {MIXED_HI}], seed {MIXED_SEED}",
             "scaling": "strong (64 documents split over the GPUs longest-first by estimated cost)",
-            "ms_per_step": round(ms / args.steps, 3)}
+            "ms_per_step": round(ms / args.steps, 3)}, {"docs": len(lens), "tokens": int(sum(lens)),
+                                                        "ms_per_step": round(local_ms / args.steps, 3)}
 
 
 def run_long(tb, cfg, stream):
@@ -351,6 +353,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-c5", action="store_true", help="skip the vision / 4,096-query leg")
+    ap.add_argument("--only-step", action="store_true",
+                    help="time the device step alone and exit (the form used for ncu captures of its kernels)")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -424,6 +428,14 @@ def main():
     launches = (L.load().eg2_launch_count() - launches0) // max(1, args.steps)
     ms = max_over_ranks(ms_local)
     value = world * n_docs * args.steps / (ms / 1000.0)
+    if args.only_step:
+        if rank == 0:
+            print(json.dumps({"metric": METRIC, "value": round(value, 2), "unit": "docs/s", "n_gpus": world,
+                              "steps": args.steps, "ms_per_step": round(ms / args.steps, 3), "only_step": True}))
+        dev.close()
+        if world > 1:
+            dist.destroy_process_group()
+        return
 
     # ---- end to end through the host-buffer C ABI (ids in, pooled embeddings out) ----
     dev.set_stream(None)
@@ -448,7 +460,7 @@ def main():
 
     # ---- C3: 64 documents of mixed length, sharded over the ranks (strong scaling) ----
     dev.set_stream(stream.cuda_stream)
-    mixed = run_mixed(tb, cfg, stream, rank, world, args, barrier, max_over_ranks)
+    mixed, mixed_local = run_mixed(tb, cfg, stream, rank, world, args, barrier, max_over_ranks)
     # ---- C4: one 11,774-token document (rank 0 only; the other ranks wait at the next barrier) ----
     long_case = run_long(tb, cfg, stream) if rank == 0 else None
     # ---- C5 on one GPU: vision tower per image, and a batch of 4,096 short queries (rank 0 only) ----
@@ -456,6 +468,16 @@ def main():
     # ---- single-request latency (rank 0 only) ----
     latency = run_latency(tb, cfg) if rank == 0 and not args.no_c5 else None
     barrier()
+
+    # ---- per-rank attribution: each rank's own device time, clocks and throttle reasons, C3 share ----
+    mine = {"rank": rank, "device": torch.cuda.get_device_name(local), "ms_per_step": round(ms_local / args.steps, 3),
+            "clocks": clocks,
+            "per_rank": per_rank, "mixed_c3": mixed_local}
+    if world > 1:
+        per_rank = [None] * world
+        dist.all_gather_object(per_rank, mine)
+    else:
+        per_rank = [mine]
 
     # ---- per-op device time shares (CUDA events around each op, one profiled step) ----
     dev.set_stream(stream.cuda_stream)
@@ -524,6 +546,7 @@ def main():
                     "d2h_bytes_per_step": int(n_docs * total_dims * 4), "call": "eg2_embed_packed (host ids -> host embeddings)"},
             "gpu_launches": int(launches),
             "clocks": clocks,
+            "per_rank": per_rank,
             "cpu_baseline": cpu,
             "mixed_c3": mixed,
             "long_c4": long_case,
