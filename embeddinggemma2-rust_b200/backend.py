@@ -191,6 +191,28 @@ class VisionBackend:
             pooled_a.ctypes.data if pooled else None, soft.ctypes.data))
         return (soft, pooled_a) if pooled else soft
 
+    def encode_batch(self, patches: np.ndarray, positions: np.ndarray, grid_h: int, grid_w: int, pooled: bool = False):
+        """Soft tokens ``[n_images, n / k^2, text_hidden]`` of several images of one patch grid in one
+        device pass (``eg2_vision_encode_batch``); ``patches`` is ``[n_images, n, 3 p^2]``, the positions
+        ``[n, 2]`` are shared."""
+        patches = np.ascontiguousarray(patches, dtype=np.float32)
+        pos = np.ascontiguousarray(positions, dtype=np.int32)
+        n = grid_h * grid_w
+        if patches.ndim != 3 or patches.shape[1] != n or pos.shape != (n, 2):
+            raise L.Eg2Error(-1, "malformed patches")
+        vc = self.dev.cfg.vision
+        if vc is None:
+            raise L.Eg2Error(-1, "the checkpoint has no vision tower")
+        n_img = patches.shape[0]
+        k = vc.pooling_kernel_size
+        n_out = (grid_h // k) * (grid_w // k)
+        soft = np.empty((n_img, n_out, self.dev.hidden), dtype=np.float32)
+        pooled_a = np.empty((n_img, n_out, vc.hidden_size), dtype=np.float32) if pooled else None
+        self.dev.check(self.dev._lib.eg2_vision_encode_batch(
+            self.dev.handle, patches.ctypes.data, pos.ctypes.data_as(C.POINTER(C.c_int32)), n_img, grid_h, grid_w,
+            pooled_a.ctypes.data if pooled else None, soft.ctypes.data))
+        return (soft, pooled_a) if pooled else soft
+
 
 def embed_on_gpus(backends: list[TextBackend], ids_list, dims=MATRYOSHKA_DIMS):
     """Embed token-id sequences over several GPUs from one process: one :class:`TextBackend` (one

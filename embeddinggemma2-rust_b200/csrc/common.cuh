@@ -343,11 +343,12 @@ EG2_DEV void tma_load_2d_pair(void* dst, const CUtensorMap* m, uint32_t bar, int
         "l"(reinterpret_cast<uint64_t>(m)), "r"(bar), "r"(x), "r"(y)
         : "memory");
 }
-// Same, arriving on the mbarrier at this shared-memory offset in both CTAs of the pair.
-EG2_DEV void mma_commit_pair_both(uint64_t* bar) {
+// Same, arriving on the mbarrier at this shared-memory offset in both CTAs of the pair: cluster ranks
+// pair_base and pair_base + 1 (pair_base = 0 in 2-CTA clusters; 0 or 2 in clusters of two pairs).
+EG2_DEV void mma_commit_pair_both(uint64_t* bar, uint32_t pair_base = 0) {
     asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
                      smem_u32(bar)),
-                 "h"((uint16_t)3)
+                 "h"((uint16_t)(3u << pair_base))
                  : "memory");
 }
 // TMA tile load into this CTA's shared memory whose completion (bytes) is signalled on the mbarrier

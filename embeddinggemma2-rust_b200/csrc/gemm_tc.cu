@@ -523,26 +523,37 @@ __global__ void __launch_bounds__(gemm_threads(WIDE), 1)
     // PAIR: the cluster's 256-row x BN tiles, this CTA's 128 rows fixed by its rank.
     constexpr bool AN = EPI == EPI_ADD_NORM;
     constexpr bool CL = AN || EPI == EPI_GROUP_NORM || EPI == EPI_QKV_PAIR;
-    static_assert(!(CL && PAIR), "cluster epilogues and CTA-pair MMAs are separate kernels");
+    // QUAD: a cluster epilogue on CTA-pair MMAs -- clusters of four CTAs, two MMA pairs. Cluster rank
+    // r: MMA pair r >> 1 computes columns [256 (r >> 1), +256) of each 512-column group, its CTA r & 1
+    // rows [128 (r & 1), +128) of the cluster's 256-row block; the row sums of squares are exchanged
+    // with rank r ^ 2, which holds the same rows' other column half.
+    constexpr bool QUAD = CL && PAIR;
+    static_assert(!QUAD || EPI == EPI_ADD_NORM || EPI == EPI_GROUP_NORM, "QUAD: the add-norm and group-norm epilogues");
     static_assert(!PAIR || sizeof(TIn) == 2, "CTA-pair MMAs are bf16 only");
     const int groups = N / 512;
     const uint32_t crank = (CL || PAIR) ? cluster_ctarank() : 0u;
-    const bool lead = crank == 0;
+    const uint32_t prow = PAIR ? (crank & 1u) : crank;       // PAIR: this CTA's row half of the pair tile
+    const uint32_t pcol = QUAD ? (crank >> 1) : crank;       // cluster epilogues: column half of the group
+    const uint32_t pair_base = crank & ~1u;                  // PAIR: the even CTA of this CTA's MMA pair
+    const uint32_t xpeer = QUAD ? (crank ^ 2u) : (crank ^ 1u);  // CL: the CTA with the other column half
+    const bool lead = PAIR ? prow == 0 : crank == 0;
     const int tiles_mp = (tiles_m + 1) / 2;
-    const int t_first = (CL || PAIR) ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
-    const int t_step = (CL || PAIR) ? (int)(gridDim.x >> 1) : (int)gridDim.x;
+    constexpr int CSHIFT = QUAD ? 2 : 1;  // log2 of the cluster size
+    const int t_first = (CL || PAIR) ? (int)(blockIdx.x >> CSHIFT) : (int)blockIdx.x;
+    const int t_step = (CL || PAIR) ? (int)(gridDim.x >> CSHIFT) : (int)gridDim.x;
     // K split (EPI_STORE on CTA pairs): linear id t = base tile * S + slice; slice s covers K blocks
     // [s * kbs, s * kbs + kbs).
     const int S = (EPI == EPI_STORE && PAIR && epi.ksplit > 1) ? epi.ksplit : 1;
     const int kbs = kblocks / S;
-    const int t_count = (CL ? tiles_m * groups : PAIR ? tiles_mp * tiles_n : tiles_m * tiles_n) * S;
+    const int t_count = (QUAD ? tiles_mp * groups : CL ? tiles_m * groups : PAIR ? tiles_mp * tiles_n : tiles_m * tiles_n) * S;
     auto tile_m0 = [&](int t) {
         t /= S;
-        return PAIR ? (t / tiles_n) * 2 * GEMM_BM + (int)crank * GEMM_BM : (CL ? t / groups : t / tiles_n) * GEMM_BM;
+        if (QUAD) return (t / groups) * 2 * GEMM_BM + (int)prow * GEMM_BM;
+        return PAIR ? (t / tiles_n) * 2 * GEMM_BM + (int)prow * GEMM_BM : (CL ? t / groups : t / tiles_n) * GEMM_BM;
     };
     auto tile_n0 = [&](int t) {
         t /= S;
-        return CL ? (t % groups) * 512 + (int)crank * BN : (t % tiles_n) * BN;
+        return CL ? (t % groups) * 512 + (int)pcol * BN : (t % tiles_n) * BN;
     };
 
     if (threadIdx.x == 0) {
@@ -597,7 +608,7 @@ __global__ void __launch_bounds__(gemm_threads(WIDE), 1)
     } else if constexpr (CL) {
         // This CTA's halves of the norm weights (the same for every 512-column group).
         float* wsm = reinterpret_cast<float*>(smem + Cfg::OFF_W);
-        const int n0 = (int)crank * BN;
+        const int n0 = (int)pcol * BN;
         for (int i = threadIdx.x; i < 2 * BN; i += NTHREADS)
             wsm[i] = i < BN ? epi.an.w1[n0 + i] : (epi.an.w2 ? epi.an.w2[n0 + i - BN] : 0.f);
     }
@@ -639,15 +650,15 @@ __global__ void __launch_bounds__(gemm_threads(WIDE), 1)
             auto load_a = [&](int st, int m0, int kb) {
                 uint8_t* sa = smem + st * Cfg::STAGE_BYTES;
                 if constexpr (PAIR)
-                    tma_load_2d_pair(sa, &tmA, mapa_shared(smem_u32(&full[st]), 0), kb * BK, m0);
+                    tma_load_2d_pair(sa, &tmA, mapa_shared(smem_u32(&full[st]), pair_base), kb * BK, m0);
                 else
                     tma_load_2d(sa, &tmA, &full[st], kb * BK, m0);
             };
             auto load_b = [&](int st, int n0, int kb) {
                 uint8_t* sa = smem + st * Cfg::STAGE_BYTES;
                 if constexpr (PAIR)
-                    tma_load_2d_pair(sa + Cfg::A_BYTES, &tmB, mapa_shared(smem_u32(&full[st]), 0), kb * BK,
-                                     n0 + (int)crank * (BN / 2));
+                    tma_load_2d_pair(sa + Cfg::A_BYTES, &tmB, mapa_shared(smem_u32(&full[st]), pair_base), kb * BK,
+                                     n0 + (int)prow * (BN / 2));
                 else
                     tma_load_2d(sa + Cfg::A_BYTES, &tmB, &full[st], kb * BK, n0);
             };
@@ -708,13 +719,13 @@ __global__ void __launch_bounds__(gemm_threads(WIDE), 1)
                     mma_bf16_pair(d_tmem, ad, bd, idesc, kb != 0);
 #pragma unroll
                     for (int kk = 1; kk < 4; kk++) mma_bf16_pair(d_tmem, ad + 2 * kk, bd + 2 * kk, idesc, 1);
-                    mma_commit_pair_both(&empty[stage]);
+                    mma_commit_pair_both(&empty[stage], pair_base);
                     if (++stage == STAGES) {
                         stage = 0;
                         phase ^= 1;
                     }
                 }
-                mma_commit_pair_both(&tfull[acc]);
+                mma_commit_pair_both(&tfull[acc], pair_base);
             }
         } else if (lane == 0 && !PAIR) {
             constexpr uint32_t idesc = umma_idesc(GEMM_BM, BN, InTraits<TIn>::FMT);
@@ -788,7 +799,7 @@ __global__ void __launch_bounds__(gemm_threads(WIDE), 1)
                 float* xv = reinterpret_cast<float*>(smem + Cfg::OFF_W + Cfg::X_OFF);  // [set][slot][128]
                 uint64_t* xb = reinterpret_cast<uint64_t*>(smem + Cfg::OFF_W + Cfg::XB_OFF);
                 const int rl = 32 * e + lane;
-                const uint32_t peer = crank ^ 1u;
+                const uint32_t peer = xpeer;
                 const int x = set * 2 + slot;
                 float* mine = xv + x * 128 + rl;
                 if (rl == 0) mbar_arrive_expect_tx(&xb[x], 128 * 4);
@@ -1269,7 +1280,7 @@ __global__ void __launch_bounds__(gemm_threads(WIDE), 1)
             if (!PAIR || lead)
                 mbar_arrive(&tempty[set]);
             else
-                mbar_arrive_remote(mapa_shared(smem_u32(&tempty[set]), 0));
+                mbar_arrive_remote(mapa_shared(smem_u32(&tempty[set]), pair_base));
         }
         if constexpr (TIO) {
             // Every TMA store has completed and every residual load issued has landed (bounded, for
@@ -1338,21 +1349,23 @@ static int launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N,
     return cudaLaunchKernelEx(&cfg, kern, ta, tb, none, M, N, K, epi) == cudaSuccess ? 0 : -3;
 }
 
-// Clusters of two CTAs (the cluster epilogues, and CTA-pair MMAs), as many as can be resident at
-// once (the loop over tiles is persistent, so every launched cluster must run concurrently with
-// the others).
+// Clusters of two CTAs (the cluster epilogues, and CTA-pair MMAs), or of four (a cluster epilogue on
+// CTA-pair MMAs), as many as can be resident at once (the loop over tiles is persistent, so every
+// launched cluster must run concurrently with the others).
 template <int EPI, typename TOut, bool PAIR = false, bool TIO = false, bool WIDE = false>
 static int launch_cluster(const CUtensorMap& ta, const CUtensorMap& tb, const EpiMaps& em, int M, int N, int K,
                           const GemmEpilogue& epi, cudaStream_t s) {
     using Cfg = GemmCfg<256, PAIR, TIO, WIDE>;
     auto kern = gemm_tc_kernel<bf16_t, 256, EPI, TOut, PAIR, TIO, WIDE>;
+    constexpr bool QUAD = PAIR && (EPI == EPI_ADD_NORM || EPI == EPI_GROUP_NORM);
+    constexpr int CSIZE = QUAD ? 4 : 2;
     static int max_clusters[64] = {0};
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -3;
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.x = CSIZE;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
     attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -1365,17 +1378,18 @@ static int launch_cluster(const CUtensorMap& ta, const CUtensorMap& tb, const Ep
     if (!max_clusters[dev]) {
         if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES) != cudaSuccess)
             return -3;
-        cfg.gridDim = dim3(2 * num_sms(), 1, 1);
+        cfg.gridDim = dim3(CSIZE * num_sms(), 1, 1);
         int n = 0;
         if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) return -3;
         max_clusters[dev] = n;
     }
     const int tiles_m = (M + GEMM_BM - 1) / GEMM_BM;
-    if (N % (PAIR ? 256 : 512)) return -1;
-    const long tiles = PAIR ? (long)((tiles_m + 1) / 2) * (N / 256) * (epi.ksplit > 1 ? epi.ksplit : 1)
-                            : (long)tiles_m * (N / 512);
+    if (N % ((PAIR && !QUAD) ? 256 : 512)) return -1;
+    const long tiles = QUAD ? (long)((tiles_m + 1) / 2) * (N / 512)
+                       : PAIR ? (long)((tiles_m + 1) / 2) * (N / 256) * (epi.ksplit > 1 ? epi.ksplit : 1)
+                              : (long)tiles_m * (N / 512);
     const int clusters = tiles < max_clusters[dev] ? (int)tiles : max_clusters[dev];
-    cfg.gridDim = dim3(2 * clusters, 1, 1);
+    cfg.gridDim = dim3(CSIZE * clusters, 1, 1);
     cfg.numAttrs = pdl_enabled() ? 2 : 1;
     return cudaLaunchKernelEx(&cfg, kern, ta, tb, em, M, N, K, epi) == cudaSuccess ? 0 : -3;
 }
@@ -1388,6 +1402,11 @@ static bool gemm_pair_enabled() {
         return !(e && e[0] == '1');
     }();
     return on;
+}
+
+static bool quad_enabled() {
+    const char* e = getenv("EG2_ADD_NORM_NO_QUAD");  // read per call: the A/B test switches it in-process
+    return !(e && e[0] == '1');
 }
 
 bool qkv_pair_fusable(const QkvEpilogue& q) {
@@ -1417,7 +1436,11 @@ int gemm_tc(GemmKind kind, const void* A, long lda, const void* W, long ldw, int
     // weight tile, BN / 2 rows); the cluster epilogues and TF32 on single-CTA MMAs.
     const bool pair = !tf32 && (epi.mode == EPI_STORE || epi.mode == EPI_GELU_GU || epi.mode == EPI_PLE_GATE ||
                                 epi.mode == EPI_QKV) && gemm_pair_enabled();
-    if (make_tmap_2d(&tb, dt, W, K, N, ldw * esize, BK, pair ? BN / 2 : BN)) return -1;
+    // The add-norm epilogue on CTA-pair MMAs (clusters of four): each CTA streams half of the weight
+    // tile. EG2_ADD_NORM_NO_QUAD=1 keeps the single-CTA main loop (same results: both accumulate K in
+    // the same 64-element blocks).
+    const bool quad = !tf32 && epi.mode == EPI_ADD_NORM && quad_enabled();
+    if (make_tmap_2d(&tb, dt, W, K, N, ldw * esize, BK, (pair || quad) ? BN / 2 : BN)) return -1;
     const EpiMaps none = {};
     // bf16 output tensor [M, cols] (row stride ld elements) as 32 x 32 TMA store boxes.
     auto out_map = [&](CUtensorMap* m, const void* base, long cols, long ld) {
@@ -1488,7 +1511,8 @@ int gemm_tc(GemmKind kind, const void* A, long lda, const void* W, long ldw, int
                                  CU_TENSOR_MAP_SWIZZLE_64B) ||
                     out_map(&em.m[1], epi.out, 512, epi.ldo))
                     return -1;
-                return launch_cluster<EPI_ADD_NORM, bf16_t, false, true>(ta, tb, em, M, N, K, epi, s);
+                return quad ? launch_cluster<EPI_ADD_NORM, bf16_t, true, true>(ta, tb, em, M, N, K, epi, s)
+                            : launch_cluster<EPI_ADD_NORM, bf16_t, false, true>(ta, tb, em, M, N, K, epi, s);
             }
             case EPI_GROUP_NORM: {
                 if (N % 512 || !epi.an.w1 || !epi.out || epi.ldo % 4) return -1;

@@ -112,12 +112,16 @@ struct Fail {
     va_end(ap);
     throw Fail{code, buf};
 }
+// On failure the runtime's last-error slot is cleared too, so a later launch check on this thread does
+// not report this call's (non-sticky) error as its own.
 #define CK(call)                                                                                      \
     do {                                                                                              \
         cudaError_t e_ = (call);                                                                      \
-        if (e_ != cudaSuccess)                                                                        \
+        if (e_ != cudaSuccess) {                                                                      \
+            cudaGetLastError();                                                                       \
             fail(e_ == cudaErrorMemoryAllocation ? EG2_ERR_OOM : EG2_ERR_CUDA, "%s: %s (%s:%d)", #call, \
                  cudaGetErrorString(e_), __FILE__, __LINE__);                                         \
+        }                                                                                             \
     } while (0)
 // Kernel launches issued by this library (all contexts), for the benchmark's launch count.
 static std::atomic<long long> g_launches{0};
@@ -417,7 +421,8 @@ struct eg2_ctx {
     void *v_x = nullptr, *v_t = nullptr, *v_qkv = nullptr, *v_q = nullptr, *v_k = nullptr, *v_v = nullptr, *v_a = nullptr,
          *v_o = nullptr, *v_gate = nullptr, *v_gu = nullptr;
     int *v_pos = nullptr, *v_seq_start = nullptr, *v_seq_len = nullptr;
-    eg2::AttnTile* v_tiles = nullptr;            // head-64 attention tiles of the current image
+    eg2::AttnTile* v_tiles = nullptr;            // head-64 attention tiles of the current images
+    long v_tiles_cap = 0;
     std::vector<int32_t> v_pos_host;              // positions the RoPE tables in v_cs / v_sn were built for
     int* bad_flag = nullptr;
     // CUDA graphs of short embedding passes (<= 128 rows), one per (row bucket, pooled dims); a graph
@@ -936,7 +941,7 @@ static void enqueue_text(eg2_ctx* c, long rows, const std::vector<TileSet>& tset
     const float eps = tc.eps;
     const bool f32 = std::is_same<T, float>::value;
     T* t = (T*)w.t;
-    mark(c, "start");
+    mark(c, "set-up + gather");
     // PLE prologue: ple = rmsnorm(embeds . W_ple^T * h^-0.5) * ple_norm per (token, layer) row.
     const void* x_in = w.hidden;
     if (!f32) {
@@ -1121,7 +1126,9 @@ static void run_text(eg2_ctx* c, long rows, const std::vector<TileSet>& sets) {
 // Vision tower (src/vision.rs:223-273)
 // ---------------------------------------------------------------------------------------------
 template <typename T>
-static void enqueue_vision(eg2_ctx* c, long n, int gh, int gw) {
+// n rows: the patches of n_img images of gh x gw patches each, image after image (so the images stack
+// along the patch rows: a gh-row band per image, and pooling windows never cross two images).
+static void enqueue_vision(eg2_ctx* c, long n, int gh, int gw, int n_img, int n_tiles) {
     const VisionCfg& vc = c->vc;
     const int h = vc.hidden, ff = vc.inter, nh = vc.nh, nkv = vc.nkv, hd = vc.hd, pd = 3 * vc.patch * vc.patch;
     const bool f32 = std::is_same<T, float>::value;
@@ -1150,7 +1157,7 @@ static void enqueue_vision(eg2_ctx* c, long n, int gh, int gw) {
                "attention");
         else if (attention_tc_tile_tokens(nh, nkv, hd) == 256 && hd == 64)
             KL(attention_tc((const bf16_t*)c->v_q, (const bf16_t*)c->v_k, (const bf16_t*)c->v_v, (bf16_t*)c->v_a, n,
-                            c->v_tiles, (int)((n + 255) / 256), nh, nkv, hd, -1, c->stream),
+                            c->v_tiles, n_tiles, nh, nkv, hd, -1, c->stream),
                "attention_tc");
         else
             KL(attention_simt<bf16_t>((const bf16_t*)c->v_q, (const bf16_t*)c->v_k, (const bf16_t*)c->v_v, (bf16_t*)c->v_a,
@@ -1167,14 +1174,25 @@ static void enqueue_vision(eg2_ctx* c, long n, int gh, int gw) {
            "add_norm");
         mark(c, "vision mlp");
     }
-    const int oh = gh / vc.pool, ow = gw / vc.pool;
-    KL(vision_pool(c->v_hidden, c->v_pooled, gh, gw, h, vc.pool, sqrtf((float)h), c->stream), "vision_pool");
-    // Multimodal embedder: scale-free RMSNorm, then 768 -> text hidden in f32 (src/vision.rs:167-170).
+    const long oh = (long)n_img * (gh / vc.pool), ow = gw / vc.pool;
+    KL(vision_pool(c->v_hidden, c->v_pooled, (int)(n_img * gh), gw, h, vc.pool, sqrtf((float)h), c->stream), "vision_pool");
+    // Multimodal embedder: scale-free RMSNorm, then 768 -> text hidden (src/vision.rs:167-170; f32 on the
+    // reference's host). f32 mode keeps the f32 CUDA-core GEMM; the tensor-core modes run it as a TF32
+    // tcgen05 GEMM on the f32 weights (10-bit mantissa inputs, f32 accumulation).
     float* normed = (float*)c->v_o;  // reuse: oh*ow*h f32 fits (act buffer sized n*h*4)
-    KL(rms_norm_rows<float>(c->v_pooled, normed, nullptr, (long)oh * ow, h, eps, 1.f, c->stream), "rms_norm");
-    KL(gemm_f32(normed, h, (const float*)c->v_embed_proj, h, c->v_soft, c->tc.hidden, oh * ow, c->tc.hidden, h, 1.f,
-                c->stream),
-       "gemm_f32");
+    KL(rms_norm_rows<float>(c->v_pooled, normed, nullptr, oh * ow, h, eps, 1.f, c->stream), "rms_norm");
+    if (f32 && c->precision == EG2_F32) {
+        KL(gemm_f32(normed, h, (const float*)c->v_embed_proj, h, c->v_soft, c->tc.hidden, (int)(oh * ow), c->tc.hidden, h,
+                    1.f, c->stream),
+           "gemm_f32");
+    } else {
+        GemmEpilogue e;
+        e.mode = EPI_STORE;
+        e.out_f32 = 1;
+        e.out = c->v_soft;
+        e.ldo = c->tc.hidden;
+        KL(gemm_tc(GEMM_TF32, normed, h, c->v_embed_proj, h, (int)(oh * ow), c->tc.hidden, h, e, c->stream), "gemm_tc tf32");
+    }
     mark(c, "vision pool + embed");
 }
 
@@ -1674,6 +1692,7 @@ static int embed_impl(eg2_ctx* c, const uint32_t* ids, const int32_t* lens, int 
         if (!device_ptrs)
             for (long i = 0; i < rows; i++)
                 if ((int64_t)ids[i] >= c->tc.vocab) fail(EG2_ERR_INVALID, "token id %u out of range", ids[i]);
+        mark(c, "call");  // profiling: the interval up to the first kernel is the host's set-up of the pass
         const auto plan = call_plan(c, lens, n_seq);
         CK(cudaMemsetAsync(c->bad_flag, 0, 4, c->stream));
         if (c->precise) CK(cudaMemsetAsync(c->precise->bad_flag, 0, 4, c->stream));
@@ -1718,11 +1737,12 @@ static int embed_impl(eg2_ctx* c, const uint32_t* ids, const int32_t* lens, int 
         CK(cudaMemcpyAsync(&bad, c->bad_flag, 4, cudaMemcpyDeviceToHost, c->stream));
         if (c->precise) CK(cudaMemcpyAsync(&bad_precise, c->precise->bad_flag, 4, cudaMemcpyDeviceToHost, c->stream));
         check_device_status(c);
-        collect_marks(c);
         if (bad || bad_precise) fail(EG2_ERR_INVALID, "token id out of range");
         CK(cudaMemcpyAsync(out, result, (size_t)n_seq * total * 4, device_ptrs ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost,
                            c->stream));
+        mark(c, "checks + output");
         CK(cudaStreamSynchronize(c->stream));
+        collect_marks(c);
     });
 }
 
@@ -1755,19 +1775,23 @@ int eg2_pass_policy(const eg2_ctx* c, int64_t* max_rows, int* precise_max) {
     return EG2_OK;
 }
 
-int eg2_vision_encode(eg2_ctx* c, const float* patches, const int32_t* pos_xy, int gh, int gw, float* out_pooled,
-                      float* out_soft) {
+// The vision tower over n_img images of one patch grid (gh x gw, positions pos_xy shared), stacked
+// image after image into one device pass.
+static int vision_impl(eg2_ctx* c, const float* patches, const int32_t* pos_xy, int n_img, int gh, int gw,
+                       float* out_pooled, float* out_soft) {
     return guarded(c, [&] {
         VisionCfg& vc = c->vc;
         if (!vc.present) fail(EG2_ERR_INVALID, "the checkpoint has no vision tower");
         const int k = vc.pool;
-        const long n = (long)gh * gw;
+        const long per = (long)gh * gw;
         if (gh <= 0 || gw <= 0 || gh % k || gw % k)
             fail(EG2_ERR_INVALID, "patch grid %dx%d is empty or not divisible by the pooling kernel %d", gh, gw, k);
+        if (n_img <= 0 || per * n_img > (1L << 26)) fail(EG2_ERR_INVALID, "bad image count %d", n_img);
         if (!patches || !pos_xy) fail(EG2_ERR_INVALID, "null buffer");
-        for (long t = 0; t < n; t++)
+        for (long t = 0; t < per; t++)
             if (pos_xy[2 * t] < 0 || pos_xy[2 * t] >= vc.pos_size || pos_xy[2 * t + 1] < 0 || pos_xy[2 * t + 1] >= vc.pos_size)
                 fail(EG2_ERR_INVALID, "patch position outside the %d-entry position table", vc.pos_size);
+        const long n = per * n_img;
         const int h = vc.hidden, ff = vc.inter, nh = vc.nh, nkv = vc.nkv, hd = vc.hd, pd = 3 * vc.patch * vc.patch;
         const size_t as = act_size(c);
         if (n > c->vcap) {
@@ -1780,7 +1804,12 @@ int eg2_vision_encode(eg2_ctx* c, const float* patches, const int32_t* pos_xy, i
                 dfree(c, *b);
                 *b = nullptr;
             }
+            c->v_tiles_cap = 0;
             const long cap = ((n + 1023) / 1024) * 1024;
+            const size_t per_row = (size_t)h * 4 * 3 + (size_t)c->tc.hidden * 4 + (size_t)hd * 4 + (size_t)pd * 4 +
+                                   (size_t)std::max(h, pd) * as + (size_t)(nh + 2 * nkv) * hd * (4 + as) +
+                                   (size_t)nh * hd * as + (size_t)ff * as + (c->precision == EG2_F32 ? 2 * (size_t)ff * 4 : 0) + 16;
+            ensure_fits(per_row * cap, "the vision workspace", n);
             c->v_hidden = (float*)dalloc(c, cap * h * 4);
             c->v_pooled = (float*)dalloc(c, cap * h * 4);
             c->v_soft = (float*)dalloc(c, cap * c->tc.hidden * 4);
@@ -1800,41 +1829,60 @@ int eg2_vision_encode(eg2_ctx* c, const float* patches, const int32_t* pos_xy, i
             c->v_pos = (int*)dalloc(c, cap * 2 * 4);
             c->v_seq_start = (int*)dalloc(c, cap * 4);
             c->v_seq_len = (int*)dalloc(c, cap * 4);
-            c->v_tiles = (AttnTile*)dalloc(c, (cap / 256 + 1) * sizeof(AttnTile));
+            c->v_tiles_cap = 0;
             c->v_pos_host.clear();
             c->vcap = cap;
         }
-        // Position-dependent tables, rebuilt only when the positions differ from the previous image's
-        // (images of one size share them).
-        if (c->v_pos_host.size() != (size_t)(2 * n) ||
-            std::memcmp(c->v_pos_host.data(), pos_xy, (size_t)n * 2 * sizeof(int32_t)) != 0) {
+        // Query tiles: 256 patches of one image each, so their count depends on the image count as well
+        // as on the rows.
+        const int n_tiles = (int)(n_img * ((per + 255) / 256));
+        if (n_tiles > c->v_tiles_cap) {
+            CK(cudaStreamSynchronize(c->stream));
+            dfree(c, c->v_tiles);
+            c->v_tiles_cap = std::max<long>(n_tiles, c->vcap / 256 + 1);
+            c->v_tiles = (AttnTile*)dalloc(c, c->v_tiles_cap * sizeof(AttnTile));
+            c->v_pos_host.clear();  // the tile list is rebuilt with the tables below
+        }
+        // Position-dependent tables, rebuilt only when the positions (or the image count) differ from the
+        // previous call's (images of one size share them).
+        if (c->v_pos_host.size() != (size_t)(2 * per + 1) || c->v_pos_host[2 * per] != n_img ||
+            std::memcmp(c->v_pos_host.data(), pos_xy, (size_t)per * 2 * sizeof(int32_t)) != 0) {
             // Axial RoPE tables [n, hd / 2]: x angles in the first hd / 4 entries, y in the next (src/vision.rs:114-136).
             std::vector<float> inv = rope_inv_freq(vc.theta, hd / 2);
             const int q4 = hd / 4;
             std::vector<float> cs((size_t)n * (hd / 2)), sn((size_t)n * (hd / 2));
-            for (long t = 0; t < n; t++)
+            std::vector<int32_t> pos((size_t)n * 2);
+            for (long t = 0; t < n; t++) {
+                const long tp = t % per;
+                pos[2 * t] = pos_xy[2 * tp];
+                pos[2 * t + 1] = pos_xy[2 * tp + 1];
                 for (int axis = 0; axis < 2; axis++)
                     for (int i = 0; i < q4; i++) {
-                        const float f = (float)pos_xy[2 * t + axis] * inv[i];
+                        const float f = (float)pos_xy[2 * tp + axis] * inv[i];
                         const int col = axis * q4 + i;
                         cs[(size_t)t * (hd / 2) + col] = cosf(f);
                         sn[(size_t)t * (hd / 2) + col] = sinf(f);
                     }
-            // One sequence of n patches: row metadata for the CUDA-core attention, 256-token tiles for
+            }
+            // Each image is one sequence: row metadata for the CUDA-core attention, 256-token tiles for
             // the tensor-core one.
-            std::vector<int> zeros(n, 0), lens_v(n, (int)n);
+            std::vector<int> starts(n), lens_v(n, (int)per);
             std::vector<AttnTile> tiles;
-            for (int q0 = 0; q0 < n; q0 += 256) tiles.push_back(AttnTile{0, (int)n, q0});
+            for (int im = 0; im < n_img; im++) {
+                for (long t = 0; t < per; t++) starts[im * per + t] = (int)(im * per);
+                for (int q0 = 0; q0 < per; q0 += 256) tiles.push_back(AttnTile{(int)(im * per), (int)per, q0});
+            }
             CK(cudaMemcpyAsync(c->v_inv, inv.data(), inv.size() * 4, cudaMemcpyHostToDevice, c->stream));
             CK(cudaMemcpyAsync(c->v_cs, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice, c->stream));
             CK(cudaMemcpyAsync(c->v_sn, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice, c->stream));
-            CK(cudaMemcpyAsync(c->v_pos, pos_xy, n * 2 * 4, cudaMemcpyHostToDevice, c->stream));
-            CK(cudaMemcpyAsync(c->v_seq_start, zeros.data(), n * 4, cudaMemcpyHostToDevice, c->stream));
+            CK(cudaMemcpyAsync(c->v_pos, pos.data(), pos.size() * 4, cudaMemcpyHostToDevice, c->stream));
+            CK(cudaMemcpyAsync(c->v_seq_start, starts.data(), n * 4, cudaMemcpyHostToDevice, c->stream));
             CK(cudaMemcpyAsync(c->v_seq_len, lens_v.data(), n * 4, cudaMemcpyHostToDevice, c->stream));
             CK(cudaMemcpyAsync(c->v_tiles, tiles.data(), tiles.size() * sizeof(AttnTile), cudaMemcpyHostToDevice, c->stream));
             // The host vectors die at the end of this block.
             CK(cudaStreamSynchronize(c->stream));
-            c->v_pos_host.assign(pos_xy, pos_xy + 2 * n);
+            c->v_pos_host.assign(pos_xy, pos_xy + 2 * per);
+            c->v_pos_host.push_back(n_img);
         }
         CK(cudaMemcpyAsync(c->v_x, patches, n * pd * 4, cudaMemcpyHostToDevice, c->stream));
         // 2 (x - 0.5) into the GEMM input buffer in the storage type.
@@ -1843,15 +1891,26 @@ int eg2_vision_encode(eg2_ctx* c, const float* patches, const int32_t* pos_xy, i
         else
             KL(cast_rows<float>((const float*)c->v_x, (float*)c->v_t, n * pd, 2.f, -0.5f, c->stream), "cast");
         if (bf16_mode(c))
-            enqueue_vision<bf16_t>(c, n, gh, gw);
+            enqueue_vision<bf16_t>(c, n, gh, gw, n_img, n_tiles);
         else
-            enqueue_vision<float>(c, n, gh, gw);
-        const long no = (long)(gh / k) * (gw / k);
+            enqueue_vision<float>(c, n, gh, gw, n_img, n_tiles);
+        const long no = (long)n_img * (gh / k) * (gw / k);
+        check_device_status(c);
         if (out_pooled) CK(cudaMemcpyAsync(out_pooled, c->v_pooled, no * h * 4, cudaMemcpyDeviceToHost, c->stream));
         if (out_soft) CK(cudaMemcpyAsync(out_soft, c->v_soft, no * c->tc.hidden * 4, cudaMemcpyDeviceToHost, c->stream));
-        check_device_status(c);
+        CK(cudaStreamSynchronize(c->stream));
         collect_marks(c);
     });
+}
+
+int eg2_vision_encode(eg2_ctx* c, const float* patches, const int32_t* pos_xy, int gh, int gw, float* out_pooled,
+                      float* out_soft) {
+    return vision_impl(c, patches, pos_xy, 1, gh, gw, out_pooled, out_soft);
+}
+
+int eg2_vision_encode_batch(eg2_ctx* c, const float* patches, const int32_t* pos_xy, int n_images, int gh, int gw,
+                            float* out_pooled, float* out_soft) {
+    return vision_impl(c, patches, pos_xy, n_images, gh, gw, out_pooled, out_soft);
 }
 
 int eg2_profile(eg2_ctx* c, int enable) {

@@ -61,6 +61,7 @@ def load(build_if_missing: bool = True) -> C.CDLL:
         "eg2_embed_packed": (C.c_int, [_P, _P, _I32P, C.c_int, _I32P, C.c_int, _P]),
         "eg2_embed_packed_device": (C.c_int, [_P, _P, _I32P, C.c_int, _I32P, C.c_int, _P, _P]),
         "eg2_vision_encode": (C.c_int, [_P, _P, _I32P, C.c_int, C.c_int, _P, _P]),
+        "eg2_vision_encode_batch": (C.c_int, [_P, _P, _I32P, C.c_int, C.c_int, C.c_int, _P, _P]),
         "eg2_set_stream": (C.c_int, [_P, _P]),
         "eg2_profile": (C.c_int, [_P, C.c_int]),
         "eg2_profile_read": (C.c_int, [_P, C.c_char_p, C.c_int]),

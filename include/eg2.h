@@ -104,6 +104,15 @@ int eg2_pass_policy(const eg2_ctx* ctx, int64_t* max_rows, int* precise_max);
 int eg2_vision_encode(eg2_ctx* ctx, const float* patches, const int32_t* pos_xy, int grid_h, int grid_w,
                       float* out_pooled, float* out_soft);
 
+/* The vision tower over n_images images of one patch grid, in one device pass (the reference encodes
+ * image by image, VisionBackend::encode, src/gpu/vision.rs:97-219; here the images are stacked so
+ * the GEMMs and the attention grid cover all of them). patches [n_images, n, 3*p*p]; pos_xy [n, 2],
+ * shared by every image; out_pooled [n_images * n/k^2, vision_hidden], out_soft
+ * [n_images * n/k^2, text_hidden], image after image; either may be NULL. Each image's results equal
+ * an eg2_vision_encode call on it alone, up to the summation order of the row blocks. */
+int eg2_vision_encode_batch(eg2_ctx* ctx, const float* patches, const int32_t* pos_xy, int n_images, int grid_h,
+                            int grid_w, float* out_pooled, float* out_soft);
+
 /* Run on a caller-owned CUDA stream (cudaStream_t); NULL restores the context's own stream. */
 int eg2_set_stream(eg2_ctx* ctx, void* stream);
 

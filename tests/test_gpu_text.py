@@ -191,3 +191,20 @@ def test_c3_against_oracle_fixture(dev_bf16, oracle_fixtures):
     assert [len(x) for x in seqs] == list(f["c3_lens"])
     got = B.TextBackend(dev_bf16).embed_ids(seqs)
     check_embeddings(got, f["c3_emb"], V.BF16, "bf16/c3")
+
+
+def test_add_norm_quad_clusters_match_single_cta_main_loop(request, monkeypatch):
+    """The add-norm GEMMs on CTA-pair MMAs (clusters of four CTAs: two MMA pairs, one per 256-column half,
+    exchanging row sums across the pairs) against the single-CTA main loop (clusters of two), on a pass
+    above the 4,096-row split-K regime with a partial last 256-row block. Both accumulate K in the same
+    64-element blocks, so the embeddings agree to the last bits or very nearly."""
+    dev = request.getfixturevalue("dev_bf16")
+    tb = B.TextBackend(dev)
+    seqs = ids_for([2208, 1500, 700, 33, 90], 31)  # 4,531 rows: 17 full 256-row blocks + 179 rows
+    quad = tb.embed_ids(seqs)
+    monkeypatch.setenv("EG2_ADD_NORM_NO_QUAD", "1")
+    single = tb.embed_ids(seqs)
+    for d in (768, 128):
+        diff = np.abs(quad[d] - single[d]).max()
+        print(f"quad vs single-CTA add-norm @{d}: max|d| {diff:.2e} (bit-equal: {bool(diff == 0)})")
+        assert diff <= 1e-5

@@ -17,7 +17,7 @@ def image(gh, gw, seed):
     return patches, pos
 
 
-@pytest.mark.parametrize("prec", ["bf16", "f32"])
+@pytest.mark.parametrize("prec", ["bf16", "tf32", "f32"])
 def test_vision_soft_tokens(prec, oracle_vision, request):
     dev = request.getfixturevalue(f"dev_{prec}")
     vb = B.VisionBackend(dev)
@@ -45,3 +45,32 @@ def test_vision_full_size_image(dev_bf16, oracle_vision):
     c = V.vec_check("bf16 soft 48x48", soft, soft_want, V.for_precision("bf16").soft_tokens)
     assert c.passed(), str(c)
     print(c)
+
+
+@pytest.mark.parametrize("prec", ["bf16", "f32"])
+def test_vision_batch_equals_single_images(prec, request):
+    """eg2_vision_encode_batch stacks the images into one pass: each image's soft tokens and pooled states
+    are the bits of that image encoded alone (every kernel's result for a row depends only on that row,
+    its own image's keys and its own pooling window)."""
+    vb = B.VisionBackend(request.getfixturevalue(f"dev_{prec}"))
+    for gh, gw, n in ((12, 12, 3), (24, 24, 5), (6, 21, 2)):
+        imgs = [image(gh, gw, 7000 + 31 * i + gh)[0] for i in range(n)]
+        pos = image(gh, gw, 0)[1]
+        soft_b, pooled_b = vb.encode_batch(np.stack(imgs), pos, gh, gw, pooled=True)
+        for i, img in enumerate(imgs):
+            soft, pooled = vb.encode(img, pos, gh, gw, pooled=True)
+            np.testing.assert_array_equal(soft_b[i], soft)
+            np.testing.assert_array_equal(pooled_b[i], pooled)
+
+
+def test_vision_batch_parity(dev_bf16, oracle_vision):
+    """Eight full-size images (48 x 48 patches) in one call, each against the oracle."""
+    vb = B.VisionBackend(dev_bf16)
+    imgs = [image(48, 48, 900 + i)[0] for i in range(8)]
+    pos = image(48, 48, 0)[1]
+    soft = vb.encode_batch(np.stack(imgs), pos, 48, 48)
+    for i in (0, 7):
+        _, want = oracle_vision.encode(imgs[i], pos, 48, 48)
+        c = V.vec_check(f"bf16 batch soft [{i}]", soft[i], want, V.for_precision("bf16").soft_tokens)
+        assert c.passed(), str(c)
+        print(c)
