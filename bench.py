@@ -248,6 +248,13 @@ def run_c5(dev, tb, cfg, stream):
         soft = vt.encode(img, pos, g, g)
     vis_s = time.perf_counter() - t0
     assert np.isfinite(soft).all()
+    # The same 32 images as one batched call (eg2_vision_encode_batch: one device pass over all of them).
+    batch = np.stack(images)
+    vt.encode_batch(batch[:4], pos, g, g)
+    t0 = time.perf_counter()
+    soft_b = vt.encode_batch(batch, pos, g, g)
+    vis_batch_s = time.perf_counter() - t0
+    assert np.isfinite(soft_b).all()
 
     # Whole image embedding the way the reference's embed path does it (src/model.rs:448-480): the
     # prompt <bos> <boi> 256 x <image> <eoi> <eos> is embedded, the soft tokens replace the
@@ -292,6 +299,9 @@ def run_c5(dev, tb, cfg, stream):
                        "ms_per_image": round(vis_s * 1000.0 / VISION_IMAGES, 3),
                        "images_per_s": round(VISION_IMAGES / vis_s, 2),
                        "call": "eg2_vision_encode (host patches -> host soft tokens), one image per call",
+                       "batched_ms_per_image": round(vis_batch_s * 1000.0 / VISION_IMAGES, 3),
+                       "batched_images_per_s": round(VISION_IMAGES / vis_batch_s, 2),
+                       "batched_call": f"eg2_vision_encode_batch, all {VISION_IMAGES} images in one call",
                        "data": f"uniform noise patches in [0, 1), seed {VISION_SEED}"},
             "image_embed": {"images": VISION_IMAGES, "tokens": int(len(ids)),
                             "ms_per_image": round(img_s * 1000.0 / VISION_IMAGES, 3),

@@ -1404,9 +1404,13 @@ static bool gemm_pair_enabled() {
     return on;
 }
 
+// Measured neutral on B200 (64 x 2,208-token step, same box: down 7.54 vs 7.76 ms, o 5.72 vs 5.52, ple_proj
+// 4.59 vs 4.31, at 1,511 vs 1,477 MHz): the add-norm epilogue, not the main loop's shared-memory
+// traffic, sets these GEMMs' pace, and clusters of four leave some SMs without a cluster. Off by default;
+// EG2_ADD_NORM_QUAD=1 selects it (read per call: the A/B test switches it in-process).
 static bool quad_enabled() {
-    const char* e = getenv("EG2_ADD_NORM_NO_QUAD");  // read per call: the A/B test switches it in-process
-    return !(e && e[0] == '1');
+    const char* e = getenv("EG2_ADD_NORM_QUAD");
+    return e && e[0] == '1';
 }
 
 bool qkv_pair_fusable(const QkvEpilogue& q) {
@@ -1436,9 +1440,9 @@ int gemm_tc(GemmKind kind, const void* A, long lda, const void* W, long ldw, int
     // weight tile, BN / 2 rows); the cluster epilogues and TF32 on single-CTA MMAs.
     const bool pair = !tf32 && (epi.mode == EPI_STORE || epi.mode == EPI_GELU_GU || epi.mode == EPI_PLE_GATE ||
                                 epi.mode == EPI_QKV) && gemm_pair_enabled();
-    // The add-norm epilogue on CTA-pair MMAs (clusters of four): each CTA streams half of the weight
-    // tile. EG2_ADD_NORM_NO_QUAD=1 keeps the single-CTA main loop (same results: both accumulate K in
-    // the same 64-element blocks).
+    // The add-norm epilogue on CTA-pair MMAs (clusters of four, opt-in): each CTA streams half of the
+    // weight tile (same results as the single-CTA main loop: both accumulate K in the same 64-element
+    // blocks).
     const bool quad = !tf32 && epi.mode == EPI_ADD_NORM && quad_enabled();
     if (make_tmap_2d(&tb, dt, W, K, N, ldw * esize, BK, (pair || quad) ? BN / 2 : BN)) return -1;
     const EpiMaps none = {};

@@ -201,9 +201,9 @@ def test_add_norm_quad_clusters_match_single_cta_main_loop(request, monkeypatch)
     dev = request.getfixturevalue("dev_bf16")
     tb = B.TextBackend(dev)
     seqs = ids_for([2208, 1500, 700, 33, 90], 31)  # 4,531 rows: 17 full 256-row blocks + 179 rows
-    quad = tb.embed_ids(seqs)
-    monkeypatch.setenv("EG2_ADD_NORM_NO_QUAD", "1")
     single = tb.embed_ids(seqs)
+    monkeypatch.setenv("EG2_ADD_NORM_QUAD", "1")
+    quad = tb.embed_ids(seqs)
     for d in (768, 128):
         diff = np.abs(quad[d] - single[d]).max()
         print(f"quad vs single-CTA add-norm @{d}: max|d| {diff:.2e} (bit-equal: {bool(diff == 0)})")
