@@ -255,6 +255,11 @@ def run_c5(dev, tb, cfg, stream):
     soft_b = vt.encode_batch(batch, pos, g, g)
     vis_batch_s = time.perf_counter() - t0
     assert np.isfinite(soft_b).all()
+    # Device time per op group of the batched call (CUDA events around each group, one profiled call).
+    dev.profile(True)
+    vt.encode_batch(batch, pos, g, g)
+    vis_prof = dev.profile_read()
+    dev.profile(False)
 
     # Whole image embedding the way the reference's embed path does it (src/model.rs:448-480): the
     # prompt <bos> <boi> 256 x <image> <eoi> <eos> is embedded, the soft tokens replace the
@@ -302,6 +307,7 @@ def run_c5(dev, tb, cfg, stream):
                        "batched_ms_per_image": round(vis_batch_s * 1000.0 / VISION_IMAGES, 3),
                        "batched_images_per_s": round(VISION_IMAGES / vis_batch_s, 2),
                        "batched_call": f"eg2_vision_encode_batch, all {VISION_IMAGES} images in one call",
+                       "batched_op_ms": {k: round(v[0], 3) for k, v in sorted(vis_prof.items(), key=lambda kv: -kv[1][0])},
                        "data": f"uniform noise patches in [0, 1), seed {VISION_SEED}"},
             "image_embed": {"images": VISION_IMAGES, "tokens": int(len(ids)),
                             "ms_per_image": round(img_s * 1000.0 / VISION_IMAGES, 3),

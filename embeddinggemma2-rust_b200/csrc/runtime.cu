@@ -1165,14 +1165,18 @@ static void enqueue_vision(eg2_ctx* c, long n, int gh, int gw, int n_img, int n_
                "attention");
         mark(c, "vision attention");
         gemm(c, c->v_a, nh * hd, L.o, (int)n, h, nh * hd, c->v_o, h, EPI_STORE, true);
+        mark(c, "vision gemm o");
         KL((add_norm<float, T>(c->v_hidden, (const float*)c->v_o, L.post_attn_ln, t, L.pre_ff_ln, n, h, eps, 1.f, c->stream)), "add_norm");
+        mark(c, "vision add_norm");
         gemm(c, t, h, L.gu, (int)n, 2 * ff, h, c->v_gate, ff, EPI_GELU_GU, f32, 1.f, nullptr, 0, 0, c->v_gu);
+        mark(c, "vision gemm gate|up + gelu");
         gemm(c, c->v_gate, ff, L.down, (int)n, h, ff, c->v_o, h, EPI_STORE, true);
+        mark(c, "vision gemm down");
         const float* next_w = (l + 1 < vc.layers) ? c->vlayers[l + 1].input_ln : nullptr;
         KL((add_norm<float, T>(c->v_hidden, (const float*)c->v_o, L.post_ff_ln, next_w ? t : (T*)nullptr, next_w, n, h, eps, 1.f,
                            c->stream)),
            "add_norm");
-        mark(c, "vision mlp");
+        mark(c, "vision add_norm");
     }
     const long oh = (long)n_img * (gh / vc.pool), ow = gw / vc.pool;
     KL(vision_pool(c->v_hidden, c->v_pooled, (int)(n_img * gh), gw, h, vc.pool, sqrtf((float)h), c->stream), "vision_pool");
