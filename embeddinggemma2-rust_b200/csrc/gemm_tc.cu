@@ -52,13 +52,15 @@ constexpr int gemm_threads(bool wide) { return wide ? 576 : GEMM_THREADS; }
 // shared-memory slots (instead of the 2.5 KB staging tile of the register path) -- EPI_ADD_NORM
 // for its residual reads and h / t writes, EPI_PLE_GATE for its PLE inputs and outputs, EPI_QKV
 // and EPI_GELU_GU for their outputs. The main loop gives up stages for them.
-template <int BN, bool PAIR = false, bool TIO = false, bool WIDE = false>
+// DUAL (EPI_PLE_FUSED): two products per tile, each BN = 128 wide, in four TMEM accumulators (two per
+// epilogue set); 32 KB stages, four of them.
+template <int BN, bool PAIR = false, bool TIO = false, bool WIDE = false, bool DUAL = false>
 struct GemmCfg {
     static constexpr int NEPI = WIDE ? 16 : 8;  // epilogue warps
     static constexpr int A_BYTES = GEMM_BM * 128;
     static constexpr int B_BYTES = (PAIR ? BN / 2 : BN) * 128;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-    static constexpr int STAGES = TIO ? (PAIR ? 4 : 3) : PAIR ? 6 : (BN == 256) ? 4 : 6;
+    static constexpr int STAGES = DUAL ? 4 : TIO ? (PAIR ? 4 : 3) : PAIR ? 6 : (BN == 256) ? 4 : 6;
     // Barriers follow the stages; TIO slots must start on a 1 KB boundary.
     static constexpr int OFF_STAGE = STAGES * STAGE_BYTES + (TIO ? 1024 : 256);
     // 32 rows x 64 B + 16 B pad; TIO: four 2 KB slots (WIDE: two)
@@ -69,13 +71,14 @@ struct GemmCfg {
     // [set][slot][128 rows] at +X_OFF (2 KB), exchange barriers [set][slot] at +XB_OFF.
     // WIDE: the two half-warps' partial sums of squares [set][quadrant][slot][half][32] (4 KB) at
     // +XW_OFF, their barriers [set][quadrant][slot] at +XWB_OFF.
+    // DUAL: exchange slots [set][slot][source rank 0..3][128 rows] (8 KB).
     static constexpr int X_OFF = 2560;
-    static constexpr int XB_OFF = X_OFF + 2048;
+    static constexpr int XB_OFF = X_OFF + (DUAL ? 8192 : 2048);
     static constexpr int XW_OFF = XB_OFF + 64;
     static constexpr int XWB_OFF = XW_OFF + 4096;
     static constexpr int W_BYTES = WIDE ? XWB_OFF + 128 : XB_OFF + 64;
     static constexpr int SMEM_BYTES = 1024 + OFF_W + W_BYTES;
-    static constexpr uint32_t TMEM_COLS = 2 * BN;
+    static constexpr uint32_t TMEM_COLS = DUAL ? 4 * BN : 2 * BN;
 };
 
 // GELU (tanh form) for the tensor-core epilogues: 0.5 x (1 + tanh(u)) = x * sigmoid(2 u), with
@@ -499,9 +502,11 @@ __global__ void __launch_bounds__(gemm_threads(WIDE), 1)
                   "WIDE: the QKV epilogues with TMA stores");
     constexpr int NTHREADS = gemm_threads(WIDE);
     static_assert(!TIO || (BN == 256 && (EPI == EPI_ADD_NORM || EPI == EPI_GROUP_NORM || EPI == EPI_QKV_PAIR ||
-                                         (PAIR && (EPI == EPI_QKV || EPI == EPI_PLE_GATE || EPI == EPI_GELU_GU)))),
+                                         (PAIR && (EPI == EPI_QKV || EPI == EPI_PLE_GATE || EPI == EPI_GELU_GU)))) ||
+                      (BN == 128 && EPI == EPI_PLE_FUSED && !PAIR),
                   "TMA epilogue I/O: the cluster epilogues, and the pair QKV / PLE-gate / GELU epilogues");
-    using Cfg = GemmCfg<BN, PAIR, TIO, WIDE>;
+    constexpr bool DUAL = EPI == EPI_PLE_FUSED;
+    using Cfg = GemmCfg<BN, PAIR, TIO, WIDE, DUAL>;
     constexpr int BK = InTraits<TIn>::BK;
     constexpr int STAGES = Cfg::STAGES;
     extern __shared__ uint8_t smem_raw[];
@@ -522,7 +527,7 @@ __global__ void __launch_bounds__(gemm_threads(WIDE), 1)
     // (row block, 512-column group) pairs, the 256-column half fixed by the CTA's rank.
     // PAIR: the cluster's 256-row x BN tiles, this CTA's 128 rows fixed by its rank.
     constexpr bool AN = EPI == EPI_ADD_NORM;
-    constexpr bool CL = AN || EPI == EPI_GROUP_NORM || EPI == EPI_QKV_PAIR;
+    constexpr bool CL = AN || EPI == EPI_GROUP_NORM || EPI == EPI_QKV_PAIR || DUAL;
     // QUAD: a cluster epilogue on CTA-pair MMAs -- clusters of four CTAs, two MMA pairs. Cluster rank
     // r: MMA pair r >> 1 computes columns [256 (r >> 1), +256) of each 512-column group, its CTA r & 1
     // rows [128 (r & 1), +128) of the cluster's 256-row block; the row sums of squares are exchanged
@@ -538,13 +543,14 @@ __global__ void __launch_bounds__(gemm_threads(WIDE), 1)
     const uint32_t xpeer = QUAD ? (crank ^ 2u) : (crank ^ 1u);  // CL: the CTA with the other column half
     const bool lead = PAIR ? prow == 0 : crank == 0;
     const int tiles_mp = (tiles_m + 1) / 2;
-    constexpr int CSHIFT = QUAD ? 2 : 1;  // log2 of the cluster size
+    constexpr int CSHIFT = (QUAD || DUAL) ? 2 : 1;  // log2 of the cluster size
     const int t_first = (CL || PAIR) ? (int)(blockIdx.x >> CSHIFT) : (int)blockIdx.x;
     const int t_step = (CL || PAIR) ? (int)(gridDim.x >> CSHIFT) : (int)gridDim.x;
     // K split (EPI_STORE on CTA pairs): linear id t = base tile * S + slice; slice s covers K blocks
     // [s * kbs, s * kbs + kbs).
     const int S = (EPI == EPI_STORE && PAIR && epi.ksplit > 1) ? epi.ksplit : 1;
-    const int kbs = kblocks / S;
+    // DUAL: K blocks [0, kblocks) feed the first product, [kblocks, 2 kblocks) the second.
+    const int kbs = DUAL ? 2 * kblocks : kblocks / S;
     const int t_count = (QUAD ? tiles_mp * groups : CL ? tiles_m * groups : PAIR ? tiles_mp * tiles_n : tiles_m * tiles_n) * S;
     auto tile_m0 = [&](int t) {
         t /= S;
@@ -585,7 +591,7 @@ __global__ void __launch_bounds__(gemm_threads(WIDE), 1)
         if constexpr (TIO) {  // the maps this epilogue uses
             tma_prefetch_desc(&em.m[0]);
             if constexpr (EPI != EPI_GELU_GU && EPI != EPI_GROUP_NORM) tma_prefetch_desc(&em.m[1]);
-            if constexpr (EPI == EPI_QKV || EPI == EPI_QKV_PAIR) tma_prefetch_desc(&em.m[2]);
+            if constexpr (EPI == EPI_QKV || EPI == EPI_QKV_PAIR || DUAL) tma_prefetch_desc(&em.m[2]);
         }
     }
     if constexpr (EPI == EPI_QKV) {
@@ -651,6 +657,8 @@ __global__ void __launch_bounds__(gemm_threads(WIDE), 1)
                 uint8_t* sa = smem + st * Cfg::STAGE_BYTES;
                 if constexpr (PAIR)
                     tma_load_2d_pair(sa, &tmA, mapa_shared(smem_u32(&full[st]), pair_base), kb * BK, m0);
+                else if (DUAL && kb >= kblocks)
+                    tma_load_2d(sa, &em.m[1], &full[st], (kb - kblocks) * BK, m0);
                 else
                     tma_load_2d(sa, &tmA, &full[st], kb * BK, m0);
             };
@@ -659,6 +667,8 @@ __global__ void __launch_bounds__(gemm_threads(WIDE), 1)
                 if constexpr (PAIR)
                     tma_load_2d_pair(sa + Cfg::A_BYTES, &tmB, mapa_shared(smem_u32(&full[st]), pair_base), kb * BK,
                                      n0 + (int)prow * (BN / 2));
+                else if (DUAL && kb >= kblocks)
+                    tma_load_2d(sa + Cfg::A_BYTES, &em.m[2], &full[st], (kb - kblocks) * BK, epi.aux_off + n0);
                 else
                     tma_load_2d(sa + Cfg::A_BYTES, &tmB, &full[st], kb * BK, n0);
             };
@@ -739,15 +749,19 @@ __global__ void __launch_bounds__(gemm_threads(WIDE), 1)
                 const uint32_t acc_phase = (local >> 1) & 1;
                 if (!mbar_wait(&tempty[acc], acc_phase ^ 1, EG2_DEV_TIMEOUT_GEMM, abort_flag)) goto done;
                 tc_fence_after();
-                const uint32_t d_tmem = tmem_base + acc * BN;
+                const uint32_t d_tmem = tmem_base + acc * (DUAL ? 2 * BN : BN);
                 for (int kb = 0; kb < kbs; kb++) {
                     if (!mbar_wait(&full[stage], phase, EG2_DEV_TIMEOUT_GEMM, abort_flag)) goto done;
                     tc_fence_after();
                     const uint64_t ad = da0 + (uint64_t)(stage * (Cfg::STAGE_BYTES >> 4));
                     const uint64_t bd = ad + (uint64_t)(Cfg::A_BYTES >> 4);
-                    mma_bf16_or_tf32<TIn>(d_tmem, ad, bd, idesc, kb != 0);
+                    // DUAL: the second product accumulates into the next BN columns.
+                    const bool second = DUAL && kb >= kblocks;
+                    const uint32_t d_acc = d_tmem + (second ? BN : 0);
+                    const uint32_t first_k = (kb != 0 && kb != (DUAL ? kblocks : -1)) ? 1u : 0u;
+                    mma_bf16_or_tf32<TIn>(d_acc, ad, bd, idesc, first_k);
 #pragma unroll
-                    for (int kk = 1; kk < 4; kk++) mma_bf16_or_tf32<TIn>(d_tmem, ad + 2 * kk, bd + 2 * kk, idesc, 1);
+                    for (int kk = 1; kk < 4; kk++) mma_bf16_or_tf32<TIn>(d_acc, ad + 2 * kk, bd + 2 * kk, idesc, 1);
                     mma_commit(&empty[stage]);
                     if (++stage == STAGES) {
                         stage = 0;
@@ -789,7 +803,7 @@ __global__ void __launch_bounds__(gemm_threads(WIDE), 1)
             tc_fence_after();
             const int m0 = tile_m0(tile), n0 = tile_n0(tile);
             const int row0 = m0 + 32 * e, row = row0 + lane;
-            const uint32_t tbase = tmem_base + ((uint32_t)(32 * e) << 16) + set * BN;
+            const uint32_t tbase = tmem_base + ((uint32_t)(32 * e) << 16) + set * (DUAL ? 2 * BN : BN);
             // Cluster modes: sends this row's partial sum to the peer CTA (same slot there, st.async
             // counting 4 bytes on the peer's barrier) and returns the total once the peer's 128 values
             // (512 bytes, expected by this set's first thread) have landed here. Both CTAs add the same
@@ -990,6 +1004,84 @@ __global__ void __launch_bounds__(gemm_threads(WIDE), 1)
                         warp_store32<TOut>(base, ldo, row0, M, col1 + c * 32, x1, stage);
                         warp_store32<TOut>(base, ldo, row0, M, col2 + c * 32, x2, stage);
                     }
+                }
+            } else if constexpr (DUAL) {
+                // This layer's PLE slice p (second accumulator, BN columns after the gate g): the row
+                // sums of squares of this CTA's 128 columns of p * scale go to the three other CTAs of
+                // the cluster (st.async into each peer's slot [set][parity][this rank]); every CTA adds
+                // the four partials in rank order, so all quarters of a row use the same norm. The slot
+                // alternates with the set's tile parity, which is also the handshake (a peer writes this
+                // set's slot for tile k + 2 only after it has this CTA's value for tile k + 1, sent after
+                // this tile's slot was read here). Then out = bf16(gelu(g) * (p * scale * inv * w)): the
+                // arithmetic of EPI_GROUP_NORM's stored value times the PLE-gate epilogue's GELU.
+                const float* w1s = wsm;
+                float ss = 0.f;
+#pragma unroll 1
+                for (int c = 0; c < BN / 32; c += 2) {
+                    uint32_t r0[32], r1[32];
+                    tmem_ld32(tbase + BN + c * 32, r0);
+                    tmem_ld32(tbase + BN + c * 32 + 32, r1);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int j = 0; j < 32; j++) {
+                        const float a = __uint_as_float(r0[j]) * epi.scale, b = __uint_as_float(r1[j]) * epi.scale;
+                        ss = fmaf(a, a, ss);
+                        ss = fmaf(b, b, ss);
+                    }
+                }
+                float inv;
+                {
+                    float* xv = reinterpret_cast<float*>(smem + Cfg::OFF_W + Cfg::X_OFF);     // [set][slot][src][128]
+                    uint64_t* xb = reinterpret_cast<uint64_t*>(smem + Cfg::OFF_W + Cfg::XB_OFF);  // [set][slot]
+                    const int rl = 32 * e + lane;
+                    const int x = set * 2 + (k & 1);
+                    float* slots = xv + x * 4 * 128;
+                    if (rl == 0) mbar_arrive_expect_tx(&xb[x], 3 * 128 * 4);
+#pragma unroll
+                    for (uint32_t pr = 0; pr < 4; pr++)
+                        if (pr != crank)
+                            st_async_f32(mapa_shared(smem_u32(slots + crank * 128 + rl), pr), ss,
+                                         mapa_shared(smem_u32(&xb[x]), pr));
+                    if (!mbar_wait(&xb[x], (k >> 1) & 1, EG2_DEV_TIMEOUT_GEMM, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    float tot = 0.f;
+#pragma unroll
+                    for (int src = 0; src < 4; src++)
+                        tot += (src == (int)crank) ? ss : *reinterpret_cast<volatile float*>(slots + src * 128 + rl);
+                    inv = 1.0f / sqrtf(tot / 512.f + epi.an.eps);
+                }
+                // 16-column chunks, bf16 through the slots (32-byte swizzle: row r's 16-byte unit j at
+                // r * 32 + 16 * (j ^ ((r >> 2) & 1))) and out by TMA store.
+                const uint32_t sw32 = (uint32_t)((lane >> 2) & 1);
+#pragma unroll 1
+                for (int c = 0; c < BN / 16; c++) {
+                    uint32_t g[16], pv[16];
+                    tmem_ld16(tbase + c * 16, g);
+                    tmem_ld16(tbase + BN + c * 16, pv);
+                    tmem_ld_wait();
+                    uint32_t pk[8];
+#pragma unroll
+                    for (int j = 0; j < 8; j++) {
+                        const float e0 = __uint_as_float(pv[2 * j]) * epi.scale * inv * w1s[c * 16 + 2 * j];
+                        const float e1 = __uint_as_float(pv[2 * j + 1]) * epi.scale * inv * w1s[c * 16 + 2 * j + 1];
+                        pk[j] = bf16x2_bits(gelu_fast(__uint_as_float(g[2 * j])) * e0, gelu_fast(__uint_as_float(g[2 * j + 1])) * e1);
+                    }
+                    uint8_t* slotp = stage + (nst & 3) * 2048;
+                    if (lane == 0) bulk_wait_read<3>();  // the slot's previous store is read out
+                    __syncwarp();
+#pragma unroll
+                    for (int j = 0; j < 2; j++)
+                        *reinterpret_cast<uint4*>(slotp + lane * 32 + ((j ^ sw32) << 4)) =
+                            make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
+                    fence_proxy_async();
+                    __syncwarp();
+                    if (lane == 0) {
+                        tma_store_2d(&em.m[0], slotp, n0 + 16 * c, row0);
+                        bulk_commit();
+                    }
+                    nst++;
                 }
             } else if constexpr (EPI == EPI_GROUP_NORM) {
                 // One exchange per tile; the slot alternates with the tile's parity, which is also the
@@ -1352,13 +1444,14 @@ static int launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N,
 // Clusters of two CTAs (the cluster epilogues, and CTA-pair MMAs), or of four (a cluster epilogue on
 // CTA-pair MMAs), as many as can be resident at once (the loop over tiles is persistent, so every
 // launched cluster must run concurrently with the others).
-template <int EPI, typename TOut, bool PAIR = false, bool TIO = false, bool WIDE = false>
+template <int EPI, typename TOut, bool PAIR = false, bool TIO = false, bool WIDE = false, int BNT = 256>
 static int launch_cluster(const CUtensorMap& ta, const CUtensorMap& tb, const EpiMaps& em, int M, int N, int K,
                           const GemmEpilogue& epi, cudaStream_t s) {
-    using Cfg = GemmCfg<256, PAIR, TIO, WIDE>;
-    auto kern = gemm_tc_kernel<bf16_t, 256, EPI, TOut, PAIR, TIO, WIDE>;
+    constexpr bool DUAL = EPI == EPI_PLE_FUSED;
+    using Cfg = GemmCfg<BNT, PAIR, TIO, WIDE, DUAL>;
+    auto kern = gemm_tc_kernel<bf16_t, BNT, EPI, TOut, PAIR, TIO, WIDE>;
     constexpr bool QUAD = PAIR && (EPI == EPI_ADD_NORM || EPI == EPI_GROUP_NORM);
-    constexpr int CSIZE = QUAD ? 4 : 2;
+    constexpr int CSIZE = (QUAD || DUAL) ? 4 : 2;
     static int max_clusters[64] = {0};
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -3;
@@ -1555,6 +1648,32 @@ int gemm_tc(GemmKind kind, const void* A, long lda, const void* W, long ldw, int
         }
     }
     return -1;
+}
+
+int gemm_ple_fused(const bf16_t* t, const bf16_t* x, const bf16_t* w_gate, const bf16_t* w_ple_all, int layer,
+                   const float* norm_w, float scale, float eps, bf16_t* out, int M, cudaStream_t s) {
+    if (M <= 0) return 0;
+    if (!t || !x || !w_gate || !w_ple_all || !norm_w || !out || layer < 0) return -1;
+    constexpr int P = 512, BNT = 128;
+    const CUtensorMapDataType dt = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+    CUtensorMap ta, tb;
+    EpiMaps em = {};
+    // A operands [M, 512] in 64 x 128 boxes; weight rows in 64 x 128 boxes (one 128-column quarter);
+    // the output in 16 x 32 boxes with the 32-byte swizzle of the epilogue's slots.
+    if (make_tmap_2d(&ta, dt, t, P, M, P * 2, 64, GEMM_BM) || make_tmap_2d(&tb, dt, w_gate, P, P, P * 2, 64, BNT) ||
+        make_tmap_2d(&em.m[0], dt, out, P, M, P * 2, 16, 32, CU_TENSOR_MAP_SWIZZLE_32B) ||
+        make_tmap_2d(&em.m[1], dt, x, P, M, P * 2, 64, GEMM_BM) ||
+        make_tmap_2d(&em.m[2], dt, w_ple_all, P, (uint64_t)(layer + 1) * P, P * 2, 64, BNT))
+        return -1;
+    GemmEpilogue e;
+    e.mode = EPI_PLE_FUSED;
+    e.out = out;
+    e.ldo = P;
+    e.aux_off = layer * P;
+    e.scale = scale;
+    e.an.w1 = norm_w;
+    e.an.eps = eps;
+    return launch_cluster<EPI_PLE_FUSED, bf16_t, false, true, false, BNT>(ta, tb, em, M, P, P, e, s);
 }
 
 }  // namespace eg2

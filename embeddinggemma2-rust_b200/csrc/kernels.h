@@ -25,6 +25,10 @@ enum EpiMode : int {
                          // must be in the pair layout (qkv_pair_row): half r holds head channels
                          // [128 r, 128 r + 128) and [256 + 128 r, 256 + 128 r + 128), so every rotated pair
                          // (i, i + 256) is inside one half
+    EPI_PLE_FUSED = 7,   // the PLE gate with this layer's PLE slice computed in the same kernel: two products per
+                         // tile, g = A . W^T and p = A2 . W2[aux_off .., :]^T (A2, W2: tensor maps of the
+                         // launch), out = bf16(gelu(g) * (p * scale / rms(p * scale) * an.w1[col])), the RMS over
+                         // each row's 512 columns; clusters of four CTAs, one per 128-column quarter
 };
 
 // Pair layout of a 512-channel head: weight row n' (0..511) of the permuted head holds original
@@ -95,6 +99,12 @@ bool qkv_pair_fusable(const QkvEpilogue& q);
 // C = A . W^T on tcgen05 (bf16 or tf32 inputs). N must be a multiple of 256, K of 64 (bf16) / 32 (tf32).
 int gemm_tc(GemmKind kind, const void* A, long lda, const void* W, long ldw, int M, int N, int K,
             const GemmEpilogue& epi, cudaStream_t s);
+// EPI_PLE_FUSED (bf16, N = K = 512): out[M, 512] = bf16(gelu(t . w_gate^T) * plenorm(x . w_ple[layer]^T)),
+// where plenorm(v) = rms_norm(v * scale) * norm_w over the row's 512 columns (the PLE prologue of
+// src/text.rs:145-149 for one layer, fused into that layer's gate, src/text.rs:218-224). w_ple_all is the
+// stacked [layers * 512, 512] PLE model projection.
+int gemm_ple_fused(const bf16_t* t, const bf16_t* x, const bf16_t* w_gate, const bf16_t* w_ple_all, int layer,
+                   const float* norm_w, float scale, float eps, bf16_t* out, int M, cudaStream_t s);
 // f32 CUDA-core GEMM (the float32 precision path): out f32 [M, ldo] = scale * A . W^T.
 int gemm_f32(const float* A, long lda, const float* W, long ldw, float* out, long ldo, int M, int N, int K, float scale,
              cudaStream_t s);

@@ -373,10 +373,11 @@ static int split_slices(long rows, int kb) {
 }
 
 struct Work {
-    long cap = 0;
+    long cap = 0, ple_cap = 0;
     float *hidden = nullptr, *ple = nullptr, *out = nullptr, *x_in = nullptr;
     void *t = nullptr, *qkv = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *a = nullptr, *o = nullptr,
          *gate = nullptr, *pg = nullptr, *gu = nullptr;
+    void* xb = nullptr;  // bf16 mode: the pass's input embeddings in bf16 (the PLE projection's input)
     int *pos = nullptr, *seq_start = nullptr, *seq_len = nullptr;
     uint32_t* ids = nullptr;
     long tiles_cap = 0;
@@ -712,15 +713,23 @@ static void ensure_rope(eg2_ctx* c, long max_len) {
     }
 }
 
+// Whether a pass of `rows` rows computes each layer's PLE slice inside the PLE-gate GEMM
+// (EPI_PLE_FUSED: bf16, above the split-K regime); such a pass needs no [rows, layers, 512] PLE tensor.
+static bool ple_fused_pass(const eg2_ctx* c, long rows) {
+    return bf16_mode(c) && c->tc.ple == 512 && c->tc.hidden == 512 && split_slices(rows, c->tc.hidden / 64) < 2 &&
+           !getenv("EG2_NO_PLE_FUSION");
+}
+
 static void ensure_work(eg2_ctx* c, long rows, long n_tiles) {
     Work& w = c->w;
     const TextCfg& tc = c->tc;
     if (rows > w.cap) {
         CK(cudaStreamSynchronize(c->stream));
         long cap = ((rows + 1023) / 1024) * 1024;
-        void** bufs[] = {(void**)&w.hidden, (void**)&w.ple, (void**)&w.out, (void**)&w.t, (void**)&w.qkv, (void**)&w.q,
+        void** bufs[] = {(void**)&w.hidden, (void**)&w.out, (void**)&w.t, (void**)&w.qkv, (void**)&w.q,
                          (void**)&w.k, (void**)&w.v, (void**)&w.a, (void**)&w.o, (void**)&w.gate, (void**)&w.pg,
-                         (void**)&w.gu, (void**)&w.pos, (void**)&w.seq_start, (void**)&w.seq_len, (void**)&w.ids};
+                         (void**)&w.gu, (void**)&w.pos, (void**)&w.seq_start, (void**)&w.seq_len, (void**)&w.ids,
+                         (void**)&w.xb};
         for (void** b : bufs) {
             dfree(c, *b);
             *b = nullptr;
@@ -732,13 +741,12 @@ static void ensure_work(eg2_ctx* c, long rows, long n_tiles) {
             max_qkv = std::max(max_qkv, (tc.nh + 2 * L.nkv) * L.hd);
         }
         const size_t as = act_size(c);
-        const size_t per_row = (size_t)tc.hidden * 4 + (size_t)tc.layers * tc.ple * 4 + (size_t)tc.emb * 4 +
+        const size_t per_row = (size_t)tc.hidden * 4 + (size_t)tc.emb * 4 + (size_t)tc.hidden * 2 +
                                (size_t)tc.hidden * as + (size_t)max_qkv * 4 + (size_t)(2 * max_q + 2 * max_kv) * as +
                                (size_t)tc.hidden * 4 + (size_t)tc.inter * as + (size_t)tc.ple * as +
                                (c->precision == EG2_F32 ? 2 * (size_t)tc.inter * 4 : 0) + 16;
         ensure_fits(per_row * cap, "the text workspace", rows);
         w.hidden = (float*)dalloc(c, cap * tc.hidden * 4);
-        w.ple = (float*)dalloc(c, cap * (long)tc.layers * tc.ple * 4);
         w.out = (float*)dalloc(c, cap * tc.emb * 4);
         w.t = dalloc(c, cap * tc.hidden * as);
         w.qkv = dalloc(c, cap * max_qkv * 4);
@@ -750,11 +758,24 @@ static void ensure_work(eg2_ctx* c, long rows, long n_tiles) {
         w.gate = dalloc(c, cap * tc.inter * as);
         w.pg = dalloc(c, cap * tc.ple * as);
         w.gu = c->precision == EG2_F32 ? dalloc(c, cap * 2L * tc.inter * 4) : nullptr;
+        w.xb = bf16_mode(c) ? dalloc(c, cap * tc.hidden * 2) : nullptr;
         w.pos = (int*)dalloc(c, cap * 4);
         w.seq_start = (int*)dalloc(c, cap * 4);
         w.seq_len = (int*)dalloc(c, cap * 4);
         w.ids = (uint32_t*)dalloc(c, cap * 4);
         w.cap = cap;
+    }
+    // The PLE tensor [rows, layers, 512] f32 (48 KB per row), only for passes that read it.
+    const long ple_rows = ple_fused_pass(c, rows) ? 0 : rows;
+    if (ple_rows > w.ple_cap) {
+        CK(cudaStreamSynchronize(c->stream));
+        dfree(c, w.ple);
+        w.ple = nullptr;
+        const long cap = ((ple_rows + 1023) / 1024) * 1024;
+        const size_t bytes = (size_t)cap * tc.layers * tc.ple * 4;
+        ensure_fits(bytes, "the PLE tensor", rows);
+        w.ple = (float*)dalloc(c, bytes);
+        w.ple_cap = cap;
     }
     if (!w.osplit && bf16_mode(c)) w.osplit = (float*)dalloc(c, (size_t)kSplitElems * 4);
     if (n_tiles > w.tiles_cap) {
@@ -942,13 +963,19 @@ static void enqueue_text(eg2_ctx* c, long rows, const std::vector<TileSet>& tset
     const bool f32 = std::is_same<T, float>::value;
     T* t = (T*)w.t;
     mark(c, "set-up + gather");
-    // PLE prologue: ple = rmsnorm(embeds . W_ple^T * h^-0.5) * ple_norm per (token, layer) row.
+    // PLE prologue: ple = rmsnorm(embeds . W_ple^T * h^-0.5) * ple_norm per (token, layer) row. Passes
+    // above the split-K regime compute each layer's slice inside that layer's PLE-gate GEMM instead
+    // (EPI_PLE_FUSED), so the [rows, layers, 512] f32 tensor is never written.
+    const bool ple_fused = !f32 && ple_fused_pass(c, rows);
+    if (!ple_fused && w.ple_cap < rows) fail(EG2_ERR_INVALID, "PLE tensor smaller than the pass (switch changed between set-up and launch)");
     const void* x_in = w.hidden;
     if (!f32) {
-        KL(cast_rows<bf16_t>(w.hidden, (bf16_t*)w.t, rows * h, 1.f, 0.f, c->stream), "cast");
-        x_in = w.t;
+        KL(cast_rows<bf16_t>(w.hidden, (bf16_t*)w.xb, rows * h, 1.f, 0.f, c->stream), "cast");
+        x_in = w.xb;
     }
-    if (!f32 && bf16_mode(c) && p == 512) {
+    if (ple_fused) {
+        // (nothing here: the slices are computed layer by layer)
+    } else if (!f32 && bf16_mode(c) && p == 512) {
         // One GEMM: the per-(token, layer) RMSNorm runs in its epilogue (EPI_GROUP_NORM).
         GemmEpilogue e;
         e.mode = EPI_GROUP_NORM;
@@ -996,7 +1023,11 @@ static void enqueue_text(eg2_ctx* c, long rows, const std::vector<TileSet>& tset
         // t = hidden (as the per-layer-input gate's input, bf16 in bf16 mode).
         gemm_add_norm<T>(c, w.gate, ff, L.down, rows, ff, L.post_ff_ln, nullptr, 1.f, "gemm down (+ add_norm)");
         const int Sg = split_slices(rows, h / 64);
-        if (bf16_mode(c) && Sg >= 2 && w.osplit && p == 512 && h % 128 == 0 && Sg * rows <= kSplitElems / p) {
+        if (ple_fused) {
+            KL(gemm_ple_fused((const bf16_t*)t, (const bf16_t*)w.xb, (const bf16_t*)L.pg, (const bf16_t*)c->ple_proj, i,
+                              c->ple_norm, powf((float)h, -0.5f), eps, (bf16_t*)w.pg, (int)rows, c->stream),
+               "gemm ple_gate + ple slice");
+        } else if (bf16_mode(c) && Sg >= 2 && w.osplit && p == 512 && h % 128 == 0 && Sg * rows <= kSplitElems / p) {
             // A pass of few rows: the K range split into slices (f32 partials), then GELU x ple in a
             // row kernel.
             GemmEpilogue e;

@@ -208,3 +208,24 @@ def test_add_norm_quad_clusters_match_single_cta_main_loop(request, monkeypatch)
         diff = np.abs(quad[d] - single[d]).max()
         print(f"quad vs single-CTA add-norm @{d}: max|d| {diff:.2e} (bit-equal: {bool(diff == 0)})")
         assert diff <= 1e-5
+
+
+def test_ple_slices_fused_into_the_gate_match_the_ple_tensor_path(request, monkeypatch):
+    """Passes above the split-K regime compute each layer's PLE slice inside the PLE-gate GEMM (two
+    products per tile, the per-(token, layer) RMSNorm across a cluster of four CTAs) instead of reading it
+    from the [rows, layers, 512] f32 PLE tensor. The arithmetic is the same up to summation order (the norm's
+    sum of squares, the gate product's MMA shape), which moves the bf16 roundings of the gated input and
+    everything after it: the two paths agree within a quarter of the bf16 profile's max-abs and a tenth of
+    its 1 - cos, and each meets the profile against the oracle (test_c3_against_oracle_fixture,
+    test_long_documents_bf16)."""
+    dev = request.getfixturevalue("dev_bf16")
+    tb = B.TextBackend(dev)
+    seqs = ids_for([2208, 1500, 700, 33, 90], 41)  # 4,531 rows
+    fused = tb.embed_ids(seqs)
+    monkeypatch.setenv("EG2_NO_PLE_FUSION", "1")
+    tensor = tb.embed_ids(seqs)
+    for d in (768, 128):
+        diff = np.abs(fused[d] - tensor[d]).max()
+        cos = (fused[d] * tensor[d]).sum(1) / (np.linalg.norm(fused[d], axis=1) * np.linalg.norm(tensor[d], axis=1))
+        print(f"fused PLE vs PLE tensor @{d}: max|d| {diff:.2e} min cos {cos.min():.9f}")
+        assert diff <= 1e-3 and cos.min() >= 0.99999
