@@ -252,9 +252,10 @@ def run_c5(dev, tb, cfg, stream):
     # the patches in page-locked host memory (a serving host's input buffers), so the 226 MB upload runs
     # at the PCIe rate instead of through pageable staging.
     batch = torch.from_numpy(np.stack(images)).pin_memory().numpy()
-    vt.encode_batch(batch[:4], pos, g, g)
+    soft_pinned = torch.empty((VISION_IMAGES, soft.shape[0], soft.shape[1]), dtype=torch.float32).pin_memory().numpy()
+    vt.encode_batch(batch, pos, g, g, out=soft_pinned)  # warm-up at the timed size (per-size tables and workspace)
     t0 = time.perf_counter()
-    soft_b = vt.encode_batch(batch, pos, g, g)
+    soft_b = vt.encode_batch(batch, pos, g, g, out=soft_pinned)
     vis_batch_s = time.perf_counter() - t0
     assert np.isfinite(soft_b).all()
     # Device time per op group of the batched call (CUDA events around each group, one profiled call).
@@ -308,7 +309,7 @@ def run_c5(dev, tb, cfg, stream):
                        "call": "eg2_vision_encode (host patches -> host soft tokens), one image per call",
                        "batched_ms_per_image": round(vis_batch_s * 1000.0 / VISION_IMAGES, 3),
                        "batched_images_per_s": round(VISION_IMAGES / vis_batch_s, 2),
-                       "batched_call": f"eg2_vision_encode_batch, all {VISION_IMAGES} images in one call (patches in page-locked host memory)",
+                       "batched_call": f"eg2_vision_encode_batch, all {VISION_IMAGES} images in one call (patches in and soft tokens out through page-locked host memory)",
                        "batched_op_ms": {k: round(v[0], 3) for k, v in sorted(vis_prof.items(), key=lambda kv: -kv[1][0])},
                        "data": f"uniform noise patches in [0, 1), seed {VISION_SEED}"},
             "image_embed": {"images": VISION_IMAGES, "tokens": int(len(ids)),

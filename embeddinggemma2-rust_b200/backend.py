@@ -191,10 +191,12 @@ class VisionBackend:
             pooled_a.ctypes.data if pooled else None, soft.ctypes.data))
         return (soft, pooled_a) if pooled else soft
 
-    def encode_batch(self, patches: np.ndarray, positions: np.ndarray, grid_h: int, grid_w: int, pooled: bool = False):
+    def encode_batch(self, patches: np.ndarray, positions: np.ndarray, grid_h: int, grid_w: int, pooled: bool = False,
+                     out: np.ndarray | None = None):
         """Soft tokens ``[n_images, n / k^2, text_hidden]`` of several images of one patch grid in one
         device pass (``eg2_vision_encode_batch``); ``patches`` is ``[n_images, n, 3 p^2]``, the positions
-        ``[n, 2]`` are shared."""
+        ``[n, 2]`` are shared. ``out`` (f32, C-contiguous, that shape) receives the soft tokens if given,
+        e.g. a page-locked buffer."""
         patches = np.ascontiguousarray(patches, dtype=np.float32)
         pos = np.ascontiguousarray(positions, dtype=np.int32)
         n = grid_h * grid_w
@@ -206,7 +208,9 @@ class VisionBackend:
         n_img = patches.shape[0]
         k = vc.pooling_kernel_size
         n_out = (grid_h // k) * (grid_w // k)
-        soft = np.empty((n_img, n_out, self.dev.hidden), dtype=np.float32)
+        soft = out if out is not None else np.empty((n_img, n_out, self.dev.hidden), dtype=np.float32)
+        if soft.shape != (n_img, n_out, self.dev.hidden) or soft.dtype != np.float32 or not soft.flags.c_contiguous:
+            raise L.Eg2Error(-1, "malformed output buffer")
         pooled_a = np.empty((n_img, n_out, vc.hidden_size), dtype=np.float32) if pooled else None
         self.dev.check(self.dev._lib.eg2_vision_encode_batch(
             self.dev.handle, patches.ctypes.data, pos.ctypes.data_as(C.POINTER(C.c_int32)), n_img, grid_h, grid_w,

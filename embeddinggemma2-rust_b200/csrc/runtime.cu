@@ -1885,19 +1885,24 @@ static int vision_impl(eg2_ctx* c, const float* patches, const int32_t* pos_xy, 
             // Axial RoPE tables [n, hd / 2]: x angles in the first hd / 4 entries, y in the next (src/vision.rs:114-136).
             std::vector<float> inv = rope_inv_freq(vc.theta, hd / 2);
             const int q4 = hd / 4;
-            std::vector<float> cs((size_t)n * (hd / 2)), sn((size_t)n * (hd / 2));
+            // One image's tables, then copies for the other images of the call.
+            const size_t rw = (size_t)(hd / 2);
+            std::vector<float> cs((size_t)n * rw), sn((size_t)n * rw);
             std::vector<int32_t> pos((size_t)n * 2);
-            for (long t = 0; t < n; t++) {
-                const long tp = t % per;
-                pos[2 * t] = pos_xy[2 * tp];
-                pos[2 * t + 1] = pos_xy[2 * tp + 1];
+            for (long t = 0; t < per; t++)
                 for (int axis = 0; axis < 2; axis++)
                     for (int i = 0; i < q4; i++) {
-                        const float f = (float)pos_xy[2 * tp + axis] * inv[i];
+                        const float f = (float)pos_xy[2 * t + axis] * inv[i];
                         const int col = axis * q4 + i;
-                        cs[(size_t)t * (hd / 2) + col] = cosf(f);
-                        sn[(size_t)t * (hd / 2) + col] = sinf(f);
+                        cs[(size_t)t * rw + col] = cosf(f);
+                        sn[(size_t)t * rw + col] = sinf(f);
                     }
+            for (int im = 0; im < n_img; im++) {
+                if (im > 0) {
+                    std::copy(cs.begin(), cs.begin() + per * rw, cs.begin() + im * per * rw);
+                    std::copy(sn.begin(), sn.begin() + per * rw, sn.begin() + im * per * rw);
+                }
+                std::copy(pos_xy, pos_xy + 2 * per, pos.begin() + (size_t)im * per * 2);
             }
             // Each image is one sequence: row metadata for the CUDA-core attention, 256-token tiles for
             // the tensor-core one.
