@@ -322,17 +322,20 @@ def run_c5(dev, tb, cfg, stream):
 
 
 # ---------------------------------------------------------------------------------------------
-def cpu_baseline_run(model_dir: Path, docs: int, seed: int):
-    """The oracle (C restatement of the reference CPU f32 path) on `docs` documents of SEQ_LEN."""
+def cpu_baseline_run(model_dir: Path, docs: int, seed: int, seqs=None, want_out: bool = False):
+    """The oracle (C restatement of the reference CPU f32 path) on `docs` documents of SEQ_LEN (or on
+    `seqs`); with want_out, also returns its embeddings."""
     sys.path.insert(0, str(ROOT / "oracle"))
     import oracle as O
 
     m = O.OracleText(model_dir)
-    rng = np.random.default_rng(seed)
-    seqs = [rng.integers(0, 262144, size=SEQ_LEN).astype(np.uint32) for _ in range(docs)]
+    if seqs is None:
+        rng = np.random.default_rng(seed)
+        seqs = [rng.integers(0, 262144, size=SEQ_LEN).astype(np.uint32) for _ in range(docs)]
     t0 = time.perf_counter()
-    m.embed_ids(seqs)
-    return time.perf_counter() - t0, O.num_threads()
+    out = m.embed_ids(seqs)
+    dt = time.perf_counter() - t0
+    return (dt, O.num_threads(), out) if want_out else (dt, O.num_threads())
 
 
 def run_reference(args, rank, world):
@@ -545,10 +548,20 @@ def main():
     total_flops_doc = per_tok * SEQ_LEN + attention_flops(cfg, SEQ_LEN)
 
     cpu = None
+    parity = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        dt, threads = cpu_baseline_run(tmp, 1, 7)
+        # The sample is document 0 of the timed batch, so the oracle's result also checks the timed step's
+        # own output for that document against the bf16 profile (src/verify.rs:104-110).
+        dt, threads, want = cpu_baseline_run(tmp, 1, 0, seqs=[ids_host[:SEQ_LEN]], want_out=True)
         cpu = {"value": 1.0 / dt, "unit": "docs/s", "cores": threads, "kind": "port",
-               "sample": f"1 document x {SEQ_LEN} tokens through the oracle (C restatement of the reference CPU f32 path), {threads} threads"}
+               "sample": f"document 0 of the timed batch ({SEQ_LEN} tokens) through the oracle (C restatement of the reference CPU f32 path), {threads} threads"}
+        got = out_dev[0, :cfg.text.embedding_dim].float().cpu().numpy()
+        w = np.asarray(want, dtype=np.float64).reshape(-1)[:cfg.text.embedding_dim]
+        max_abs = float(np.abs(got - w).max())
+        cos = float(np.dot(got, w) / (np.linalg.norm(got) * np.linalg.norm(w)))
+        parity = {"doc": 0, "max_abs": max_abs, "cos": cos, "profile": "bf16: max|d| <= 4e-3, cos >= 0.99991",
+                  "ok": bool(max_abs <= V.BF16.embedding.max_abs and cos >= V.BF16.embedding.min_cos),
+                  "what": "the timed step's pooled, L2-normalised 768-d embedding of document 0 against the oracle"}
 
     if rank == 0:
         line = {
@@ -567,6 +580,7 @@ def main():
             "clocks": clocks,
             "per_rank": per_rank,
             "cpu_baseline": cpu,
+            "parity": parity,
             "mixed_c3": mixed,
             "long_c4": long_case,
             "c5": c5,
