@@ -546,9 +546,9 @@ __global__ void __launch_bounds__(gemm_threads(WIDE), 1)
     constexpr int CSHIFT = (QUAD || DUAL) ? 2 : 1;  // log2 of the cluster size
     const int t_first = (CL || PAIR) ? (int)(blockIdx.x >> CSHIFT) : (int)blockIdx.x;
     const int t_step = (CL || PAIR) ? (int)(gridDim.x >> CSHIFT) : (int)gridDim.x;
-    // K split (EPI_STORE on CTA pairs): linear id t = base tile * S + slice; slice s covers K blocks
+    // K split (EPI_STORE): linear id t = base tile * S + slice; slice s covers K blocks
     // [s * kbs, s * kbs + kbs).
-    const int S = (EPI == EPI_STORE && PAIR && epi.ksplit > 1) ? epi.ksplit : 1;
+    const int S = (EPI == EPI_STORE && epi.ksplit > 1) ? epi.ksplit : 1;
     // DUAL: K blocks [0, kblocks) feed the first product, [kblocks, 2 kblocks) the second.
     const int kbs = DUAL ? 2 * kblocks : kblocks / S;
     const int t_count = (QUAD ? tiles_mp * groups : CL ? tiles_m * groups : PAIR ? tiles_mp * tiles_n : tiles_m * tiles_n) * S;
@@ -1425,7 +1425,7 @@ static int launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N,
             return -3;
         attr_set = true;
     }
-    const int tiles = ((M + GEMM_BM - 1) / GEMM_BM) * (N / BN);
+    const int tiles = ((M + GEMM_BM - 1) / GEMM_BM) * (N / BN) * (epi.ksplit > 1 ? epi.ksplit : 1);
     const int grid = tiles < num_sms() ? tiles : num_sms();
     const EpiMaps none = {};  // no TMA epilogue I/O here
     cudaLaunchConfig_t cfg = {};
@@ -1544,7 +1544,9 @@ int gemm_tc(GemmKind kind, const void* A, long lda, const void* W, long ldw, int
         return make_tmap_2d(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, base, cols, M, ld * 2, 32, 32,
                             CU_TENSOR_MAP_SWIZZLE_64B);
     };
-    if (epi.ksplit > 1 && (!pair || epi.mode != EPI_STORE || !epi.out_f32 || (K / BK) % epi.ksplit)) return -1;
+    // K split: EPI_STORE with f32 partials (bf16 on CTA pairs, TF32 on single CTAs).
+    if (epi.ksplit > 1 && ((!pair && !tf32) || epi.mode != EPI_STORE || (!epi.out_f32 && !tf32) || (K / BK) % epi.ksplit))
+        return -1;
     if (pair) {
         switch (epi.mode) {
             case EPI_STORE:

@@ -117,11 +117,13 @@ int rms_norm_inplace(float* x, const float* w, long rows, int dim, float eps, fl
 template <typename TI, typename TT>
 int add_norm(float* h, const TI* o, const float* w1, TT* t, const float* w2, long rows, int dim, float eps,
              float scalar, cudaStream_t s);
-// GELU(g) x ple[:, layer] (bf16 out [rows, p]) for g given as nsplit f32 partial sums stride apart.
-int ple_gate_split(const float* part, int nsplit, long stride, const float* ple, long ple_ld, int ple_off, bf16_t* out,
+// GELU(g) x ple[:, layer] (out [rows, p]) for g given as nsplit f32 partial sums stride apart.
+template <typename TO>  // bf16_t (bf16 contexts) or float (TF32)
+int ple_gate_split(const float* part, int nsplit, long stride, const float* ple, long ple_ld, int ple_off, TO* out,
                    long rows, int p, cudaStream_t s);
-// add_norm over o given as nsplit f32 partial sums o_stride elements apart (dim 512, bf16 t).
-int add_norm_split(float* h, const float* o, int nsplit, long o_stride, const float* w1, bf16_t* t, const float* w2,
+// add_norm over o given as nsplit f32 partial sums o_stride elements apart (dim 512; t bf16 or f32).
+template <typename TT>
+int add_norm_split(float* h, const float* o, int nsplit, long o_stride, const float* w1, TT* t, const float* w2,
                    long rows, int dim, float eps, float scalar, cudaStream_t s);
 // Per-head RMSNorm (q, k weighted; v not) and RoPE on q and k, from the fused projection output
 // qkv[row, (nh + 2 nkv) * hd]. cs/sn: [positions, rope_w] tables; part = rotation width (hd or hd / 2).

@@ -169,19 +169,25 @@ int add_norm(float* h, const TI* o, const float* w1, TT* t, const float* w2, lon
         return -1;
     return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
-int add_norm_split(float* h, const float* o, int nsplit, long o_stride, const float* w1, bf16_t* t, const float* w2,
+template <typename TT>
+int add_norm_split(float* h, const float* o, int nsplit, long o_stride, const float* w1, TT* t, const float* w2,
                    long rows, int dim, float eps, float scalar, cudaStream_t s) {
     if (rows <= 0) return 0;
     if (dim != 512 || nsplit < 1) return -1;
     const int wpb = 8;
     const unsigned grid = (unsigned)((rows + wpb - 1) / wpb);
-    add_norm_kernel<float, bf16_t, 16><<<grid, 32 * wpb, 0, s>>>(h, o, w1, t, w2, rows, eps, scalar, nsplit, o_stride);
+    add_norm_kernel<float, TT, 16><<<grid, 32 * wpb, 0, s>>>(h, o, w1, t, w2, rows, eps, scalar, nsplit, o_stride);
     return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
+template int add_norm_split<bf16_t>(float*, const float*, int, long, const float*, bf16_t*, const float*, long, int, float,
+                                    float, cudaStream_t);
+template int add_norm_split<float>(float*, const float*, int, long, const float*, float*, const float*, long, int, float,
+                                   float, cudaStream_t);
 // GELU(g) x ple[:, layer] for g given as nsplit f32 partial sums (K slices), summed in slice order;
 // the same arithmetic as the PLE-gate GEMM epilogue (gelu_fast). Four columns per thread.
+template <typename TO>
 __global__ void ple_gate_split_kernel(const float* __restrict__ part, int nsplit, long stride,
-                                      const float* __restrict__ ple, long ple_ld, int ple_off, bf16_t* __restrict__ out,
+                                      const float* __restrict__ ple, long ple_ld, int ple_off, TO* __restrict__ out,
                                       long rows, int p) {
     grid_dep_launch();  // as in rms_norm_kernel
     const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;  // 4-column group
@@ -195,21 +201,29 @@ __global__ void ple_gate_split_kernel(const float* __restrict__ part, int nsplit
         g.x += x.x, g.y += x.y, g.z += x.z, g.w += x.w;
     }
     const float4 e = *reinterpret_cast<const float4*>(ple + r * ple_ld + ple_off + c);
-    uint2 o;
-    o.x = bf16x2_bits(gelu_fast(g.x) * e.x, gelu_fast(g.y) * e.y);
-    o.y = bf16x2_bits(gelu_fast(g.z) * e.z, gelu_fast(g.w) * e.w);
-    *reinterpret_cast<uint2*>(out + r * p + c) = o;
+    if constexpr (sizeof(TO) == 2) {
+        uint2 o;
+        o.x = bf16x2_bits(gelu_fast(g.x) * e.x, gelu_fast(g.y) * e.y);
+        o.y = bf16x2_bits(gelu_fast(g.z) * e.z, gelu_fast(g.w) * e.w);
+        *reinterpret_cast<uint2*>(out + r * p + c) = o;
+    } else {
+        *reinterpret_cast<float4*>(out + r * p + c) =
+            make_float4(gelu_fast(g.x) * e.x, gelu_fast(g.y) * e.y, gelu_fast(g.z) * e.z, gelu_fast(g.w) * e.w);
+    }
 }
 
-int ple_gate_split(const float* part, int nsplit, long stride, const float* ple, long ple_ld, int ple_off, bf16_t* out,
+template <typename TO>
+int ple_gate_split(const float* part, int nsplit, long stride, const float* ple, long ple_ld, int ple_off, TO* out,
                    long rows, int p, cudaStream_t s) {
     if (rows <= 0) return 0;
     if (p % 4 || ple_ld % 4 || ple_off % 4 || nsplit < 1) return -1;
     const long n = rows * (p / 4);
-    ple_gate_split_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(part, nsplit, stride, ple, ple_ld, ple_off, out,
-                                                                      rows, p);
+    ple_gate_split_kernel<TO><<<(unsigned)((n + 255) / 256), 256, 0, s>>>(part, nsplit, stride, ple, ple_ld, ple_off, out,
+                                                                          rows, p);
     return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
+template int ple_gate_split<bf16_t>(const float*, int, long, const float*, long, int, bf16_t*, long, int, cudaStream_t);
+template int ple_gate_split<float>(const float*, int, long, const float*, long, int, float*, long, int, cudaStream_t);
 template int add_norm<float, float>(float*, const float*, const float*, float*, const float*, long, int, float, float, cudaStream_t);
 template int add_norm<bf16_t, bf16_t>(float*, const bf16_t*, const float*, bf16_t*, const float*, long, int, float, float, cudaStream_t);
 template int add_norm<float, bf16_t>(float*, const float*, const float*, bf16_t*, const float*, long, int, float, float, cudaStream_t);

@@ -777,7 +777,7 @@ static void ensure_work(eg2_ctx* c, long rows, long n_tiles) {
         w.ple = (float*)dalloc(c, bytes);
         w.ple_cap = cap;
     }
-    if (!w.osplit && bf16_mode(c)) w.osplit = (float*)dalloc(c, (size_t)kSplitElems * 4);
+    if (!w.osplit && (bf16_mode(c) || c->precision == EG2_TF32)) w.osplit = (float*)dalloc(c, (size_t)kSplitElems * 4);
     if (n_tiles > w.tiles_cap) {
         CK(cudaStreamSynchronize(c->stream));
         dfree(c, w.tiles);
@@ -919,6 +919,25 @@ static void gemm_add_norm(eg2_ctx* c, const void* x, long ldx, const void* W, lo
         mark(c, label);
         return;
     }
+    if (c->precision == EG2_TF32 && h == 512 && w.osplit) {
+        // TF32 passes of few rows (the short sequences of a bf16 context run here): the K range split into
+        // slices as in bf16 (32-element K blocks), f32 partials summed in slice order by the row kernel.
+        const int S = split_slices(rows, K / 32);
+        if (S >= 2 && S * rows <= kSplitElems / h) {
+            GemmEpilogue e;
+            e.mode = EPI_STORE;
+            e.out_f32 = 1;
+            e.out = w.osplit;
+            e.ldo = h;
+            e.ksplit = S;
+            e.split_stride = rows * h;
+            KL(gemm_tc(GEMM_TF32, x, ldx, W, K, (int)rows, h, K, e, c->stream), label);
+            KL(add_norm_split(w.hidden, w.osplit, S, rows * h, w1, (float*)w.t, w2, rows, h, c->tc.eps, scalar, c->stream),
+               "add_norm_split");
+            mark(c, label);
+            return;
+        }
+    }
     gemm(c, x, ldx, W, (int)rows, h, K, w.o, h, EPI_STORE, true);
     mark(c, label);
     KL((add_norm<float, T>(w.hidden, (const float*)w.o, w1, (T*)w.t, w2, rows, h, c->tc.eps, scalar, c->stream)), "add_norm");
@@ -1023,6 +1042,7 @@ static void enqueue_text(eg2_ctx* c, long rows, const std::vector<TileSet>& tset
         // t = hidden (as the per-layer-input gate's input, bf16 in bf16 mode).
         gemm_add_norm<T>(c, w.gate, ff, L.down, rows, ff, L.post_ff_ln, nullptr, 1.f, "gemm down (+ add_norm)");
         const int Sg = split_slices(rows, h / 64);
+        const int Sg32 = split_slices(rows, h / 32);  // TF32: 32-element K blocks
         if (ple_fused) {
             KL(gemm_ple_fused((const bf16_t*)t, (const bf16_t*)w.xb, (const bf16_t*)L.pg, (const bf16_t*)c->ple_proj, i,
                               c->ple_norm, powf((float)h, -0.5f), eps, (bf16_t*)w.pg, (int)rows, c->stream),
@@ -1039,6 +1059,18 @@ static void enqueue_text(eg2_ctx* c, long rows, const std::vector<TileSet>& tset
             e.split_stride = rows * p;
             KL(gemm_tc(GEMM_BF16, t, h, L.pg, h, (int)rows, p, h, e, c->stream), "gemm ple_gate");
             KL(ple_gate_split(w.osplit, Sg, rows * p, w.ple, (long)nl * p, i * p, (bf16_t*)w.pg, rows, p, c->stream),
+               "ple_gate_split");
+        } else if (c->precision == EG2_TF32 && Sg32 >= 2 && w.osplit && p == 512 && Sg32 * rows <= kSplitElems / p) {
+            // The same for TF32 passes of few rows (f32 gate output).
+            GemmEpilogue e;
+            e.mode = EPI_STORE;
+            e.out_f32 = 1;
+            e.out = w.osplit;
+            e.ldo = p;
+            e.ksplit = Sg32;
+            e.split_stride = rows * p;
+            KL(gemm_tc(GEMM_TF32, t, h, L.pg, h, (int)rows, p, h, e, c->stream), "gemm ple_gate");
+            KL(ple_gate_split(w.osplit, Sg32, rows * p, w.ple, (long)nl * p, i * p, (float*)w.pg, rows, p, c->stream),
                "ple_gate_split");
         } else {
             gemm(c, t, h, L.pg, (int)rows, p, h, w.pg, p, EPI_PLE_GATE, f32, 1.f, w.ple, (long)nl * p, i * p);
