@@ -121,6 +121,12 @@ int add_norm(float* h, const TI* o, const float* w1, TT* t, const float* w2, lon
 template <typename TO>  // bf16_t (bf16 contexts) or float (TF32)
 int ple_gate_split(const float* part, int nsplit, long stride, const float* ple, long ple_ld, int ple_off, TO* out,
                    long rows, int p, cudaStream_t s);
+// K-split partial sums (f32, stride apart, added in slice order) of the gate|up projection -> gelu(gate) * up,
+// and of the q|k|v projection -> qkv_post (TF32 passes of few rows).
+int gelu_gu_split(const float* part, int nsplit, long stride, float* out, long rows, int ff, cudaStream_t s);
+int qkv_post_split(const float* qkv, int nsplit, long split_stride, float* q, float* k, float* v, const float* wq,
+                   const float* wk, const float* cs, const float* sn, int rope_w, const int* pos, long rows, int nh,
+                   int nkv, int hd, int part, float eps, cudaStream_t s);
 // add_norm over o given as nsplit f32 partial sums o_stride elements apart (dim 512; t bf16 or f32).
 template <typename TT>
 int add_norm_split(float* h, const float* o, int nsplit, long o_stride, const float* w1, TT* t, const float* w2,

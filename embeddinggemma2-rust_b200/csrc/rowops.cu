@@ -237,7 +237,7 @@ template <typename TI, typename TO>
 __global__ void qkv_post_kernel(const TI* __restrict__ qkv, TO* __restrict__ q, TO* __restrict__ k, TO* __restrict__ v,
                                 const float* __restrict__ wq, const float* __restrict__ wk, const float* __restrict__ cs,
                                 const float* __restrict__ sn, int rope_w, const int* __restrict__ pos, long rows, int nh,
-                                int nkv, int hd, int part, float eps) {
+                                int nkv, int hd, int part, float eps, int nsplit = 1, long split_stride = 0) {
     extern __shared__ float sbuf[];
     const int S = nh + 2 * nkv;
     const long item = (long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -265,7 +265,8 @@ __global__ void qkv_post_kernel(const TI* __restrict__ qkv, TO* __restrict__ q, 
     }
     float ss = 0.f;
     for (int i = lane; i < hd; i += 32) {
-        const float x = ldf(src, i);
+        float x = ldf(src, i);
+        for (int sp = 1; sp < nsplit; sp++) x += ldf(src + sp * split_stride, i);  // K-split partials, in slice order
         buf[i] = x;
         ss = fmaf(x, x, ss);
     }
@@ -306,6 +307,18 @@ int qkv_post(const TI* qkv, TO* q, TO* k, TO* v, const float* wq, const float* w
         qkv, q, k, v, wq, wk, cs, sn, rope_w, pos, rows, nh, nkv, hd, part, eps);
     return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
+// qkv given as nsplit f32 partial sums (K slices of the producing GEMM) split_stride elements apart.
+int qkv_post_split(const float* qkv, int nsplit, long split_stride, float* q, float* k, float* v, const float* wq,
+                   const float* wk, const float* cs, const float* sn, int rope_w, const int* pos, long rows, int nh,
+                   int nkv, int hd, int part, float eps, cudaStream_t s) {
+    if (rows <= 0) return 0;
+    if (hd % 32 || hd > 1024 || part <= 0 || hd % part || part % 2 || nsplit < 1) return -1;
+    const int wpb = 8;
+    const long items = rows * (nh + 2 * nkv);
+    qkv_post_kernel<float, float><<<(unsigned)((items + wpb - 1) / wpb), 32 * wpb, wpb * hd * sizeof(float), s>>>(
+        qkv, q, k, v, wq, wk, cs, sn, rope_w, pos, rows, nh, nkv, hd, part, eps, nsplit, split_stride);
+    return cudaGetLastError() == cudaSuccess ? 0 : -3;
+}
 template int qkv_post<bf16_t, bf16_t>(const bf16_t*, bf16_t*, bf16_t*, bf16_t*, const float*, const float*, const float*,
                                       const float*, int, const int*, long, int, int, int, int, float, cudaStream_t);
 template int qkv_post<float, float>(const float*, float*, float*, float*, const float*, const float*, const float*,
@@ -331,6 +344,31 @@ int gelu_gu(const TI* gu, TO* out, long rows, int ff, cudaStream_t s) {
     return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
 template int gelu_gu<float, float>(const float*, float*, long, int, cudaStream_t);
+
+// gelu(gate) * up from nsplit f32 partial sums of the interleaved gate|up projection (stride apart),
+// summed in slice order; gelu_fast, as the EPI_GELU_GU epilogue computes it.
+__global__ void gelu_gu_split_kernel(const float* __restrict__ part, int nsplit, long stride, float* __restrict__ out,
+                                     long rows, int ff) {
+    grid_dep_launch();  // as in rms_norm_kernel
+    const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= rows * ff) return;
+    const long r = i / ff;
+    const int c = (int)(i % ff);
+    const long base = r * 2L * ff + (c / 128) * 256 + (c % 128);
+    float g = part[base], u = part[base + 128];
+    for (int sp = 1; sp < nsplit; sp++) {
+        g += part[sp * stride + base];
+        u += part[sp * stride + base + 128];
+    }
+    out[i] = gelu_fast(g) * u;
+}
+int gelu_gu_split(const float* part, int nsplit, long stride, float* out, long rows, int ff, cudaStream_t s) {
+    if (rows <= 0) return 0;
+    if (ff % 128 || nsplit < 1) return -1;
+    const long n = rows * ff;
+    gelu_gu_split_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(part, nsplit, stride, out, rows, ff);
+    return cudaGetLastError() == cudaSuccess ? 0 : -3;
+}
 
 template <typename TI, typename TO>
 __global__ void ple_gate_kernel(const TI* __restrict__ g, TO* __restrict__ out, const float* __restrict__ ple, long rows,

@@ -1017,8 +1017,24 @@ static void enqueue_text(eg2_ctx* c, long rows, const std::vector<TileSet>& tset
         const int hd = L.hd, nkv = L.nkv;
         const int nqkv = (nh + 2 * nkv) * hd;
         const RopeTab& rt = c->ropes[L.rope];
-        if (!qkv_projection(c, t, h, L.qkv, rows, w.q, w.k, w.v, L.q_norm, L.k_norm, rt.inv, w.pos, 1, nh, nkv,
-                            hd, hd, eps, L.qkv_pair)) {
+        const int Sq = split_slices(rows, h / 32);
+        if (c->precision == EG2_TF32 && w.osplit && Sq >= 2 && (long)Sq * rows * nqkv <= kSplitElems) {
+            // TF32 passes of few rows: the q|k|v projection split over K (f32 partials), then the per-head
+            // norm and RoPE with the partials summed in slice order.
+            GemmEpilogue e;
+            e.mode = EPI_STORE;
+            e.out_f32 = 1;
+            e.out = w.osplit;
+            e.ldo = nqkv;
+            e.ksplit = Sq;
+            e.split_stride = rows * nqkv;
+            KL(gemm_tc(GEMM_TF32, t, h, L.qkv, h, (int)rows, nqkv, h, e, c->stream), "gemm qkv");
+            KL(qkv_post_split(w.osplit, Sq, rows * nqkv, (float*)w.q, (float*)w.k, (float*)w.v, L.q_norm, L.k_norm, rt.cs,
+                              rt.sn, hd / 2, w.pos, rows, nh, nkv, hd, hd, eps, c->stream),
+               "qkv_post");
+            mark(c, "gemm qkv + qkv_post (K split)");
+        } else if (!qkv_projection(c, t, h, L.qkv, rows, w.q, w.k, w.v, L.q_norm, L.k_norm, rt.inv, w.pos, 1, nh, nkv,
+                                   hd, hd, eps, L.qkv_pair)) {
             gemm(c, t, h, L.qkv, (int)rows, nqkv, h, w.qkv, nqkv, EPI_STORE, true);
             mark(c, "gemm qkv");
             KL((qkv_post<float, T>((const float*)w.qkv, (T*)w.q, (T*)w.k, (T*)w.v, L.q_norm, L.k_norm, rt.cs, rt.sn, hd / 2,
@@ -1037,7 +1053,20 @@ static void enqueue_text(eg2_ctx* c, long rows, const std::vector<TileSet>& tset
                      L.sliding ? tc.window : -1, w.seq_start, w.seq_len, tiles, n_tiles);
         mark(c, hd == 256 ? "attention d256" : "attention d512");
         gemm_add_norm<T>(c, w.a, nh * hd, L.o, rows, nh * hd, L.post_attn_ln, L.pre_ff_ln, 1.f, "gemm o (+ add_norm)");
-        gemm(c, t, h, L.gu, (int)rows, 2 * ff, h, w.gate, ff, EPI_GELU_GU, f32, 1.f, nullptr, 0, 0, w.gu);
+        if (c->precision == EG2_TF32 && w.osplit && Sq >= 2 && (long)Sq * rows * 2 * ff <= kSplitElems) {
+            // TF32 passes of few rows: gate|up split over K, then gelu(gate) * up over the summed partials.
+            GemmEpilogue e;
+            e.mode = EPI_STORE;
+            e.out_f32 = 1;
+            e.out = w.osplit;
+            e.ldo = 2 * ff;
+            e.ksplit = Sq;
+            e.split_stride = rows * 2L * ff;
+            KL(gemm_tc(GEMM_TF32, t, h, L.gu, h, (int)rows, 2 * ff, h, e, c->stream), "gemm gate|up");
+            KL(gelu_gu_split(w.osplit, Sq, rows * 2L * ff, (float*)w.gate, rows, ff, c->stream), "gelu_gu_split");
+        } else {
+            gemm(c, t, h, L.gu, (int)rows, 2 * ff, h, w.gate, ff, EPI_GELU_GU, f32, 1.f, nullptr, 0, 0, w.gu);
+        }
         mark(c, "gemm gate|up + gelu");
         // t = hidden (as the per-layer-input gate's input, bf16 in bf16 mode).
         gemm_add_norm<T>(c, w.gate, ff, L.down, rows, ff, L.post_ff_ln, nullptr, 1.f, "gemm down (+ add_norm)");

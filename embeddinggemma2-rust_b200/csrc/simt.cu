@@ -90,23 +90,57 @@ __global__ void attention_simt_kernel(const T* __restrict__ q, const T* __restri
         qv[j] = (lane + 32 * j < hd) ? ldf(qr, lane + 32 * j) : 0.f;
         acc[j] = 0.f;
     }
+    // Keys in groups of up to KG: each group's K rows (then V rows) are loaded together, so a warp has KG
+    // rows in flight instead of one (short sequences are latency-bound on these loads); the running max
+    // and the rescale of l and acc are updated once per group.
+    constexpr int KG = 4;
     float m = -INFINITY, l = 0.f;
-    for (int key = lo; key < hi; key++) {
-        const T* kr = k + ((start + key) * nkv + g) * hd;
-        float sdot = 0.f;
+    for (int key0 = lo; key0 < hi; key0 += KG) {
+        const int nk = hi - key0 < KG ? hi - key0 : KG;
+        float kv[KG][NV];
 #pragma unroll
-        for (int j = 0; j < NV; j++)
-            if (lane + 32 * j < hd) sdot = fmaf(qv[j], ldf(kr, lane + 32 * j), sdot);
+        for (int kk = 0; kk < KG; kk++) {
+            const T* kr = k + ((start + key0 + kk) * nkv + g) * hd;
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) sdot += __shfl_xor_sync(0xffffffffu, sdot, o);
-        const float mn = fmaxf(m, sdot);
+            for (int j = 0; j < NV; j++) kv[kk][j] = (kk < nk && lane + 32 * j < hd) ? ldf(kr, lane + 32 * j) : 0.f;
+        }
+        float sd[KG];
+#pragma unroll
+        for (int kk = 0; kk < KG; kk++) {
+            sd[kk] = 0.f;
+#pragma unroll
+            for (int j = 0; j < NV; j++) sd[kk] = fmaf(qv[j], kv[kk][j], sd[kk]);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+            for (int kk = 0; kk < KG; kk++) sd[kk] += __shfl_xor_sync(0xffffffffu, sd[kk], o);
+        float mn = m;
+#pragma unroll
+        for (int kk = 0; kk < KG; kk++)
+            if (kk < nk) mn = fmaxf(mn, sd[kk]);
         const float corr = expf(m - mn);
-        const float p = expf(sdot - mn);
-        l = l * corr + p;
-        const T* vr = v + ((start + key) * nkv + g) * hd;
+        float pk[KG];
+        float psum = 0.f;
 #pragma unroll
-        for (int j = 0; j < NV; j++)
-            if (lane + 32 * j < hd) acc[j] = acc[j] * corr + p * ldf(vr, lane + 32 * j);
+        for (int kk = 0; kk < KG; kk++) {
+            pk[kk] = kk < nk ? expf(sd[kk] - mn) : 0.f;
+            psum += pk[kk];
+        }
+        l = l * corr + psum;
+#pragma unroll
+        for (int kk = 0; kk < KG; kk++) {
+            const T* vr = v + ((start + key0 + kk) * nkv + g) * hd;
+#pragma unroll
+            for (int j = 0; j < NV; j++) kv[kk][j] = (kk < nk && lane + 32 * j < hd) ? ldf(vr, lane + 32 * j) : 0.f;
+        }
+#pragma unroll
+        for (int j = 0; j < NV; j++) {
+            float a = acc[j] * corr;
+#pragma unroll
+            for (int kk = 0; kk < KG; kk++) a = fmaf(pk[kk], kv[kk][j], a);
+            acc[j] = a;
+        }
         m = mn;
     }
     const float inv = 1.f / l;
