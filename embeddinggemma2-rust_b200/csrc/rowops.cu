@@ -264,11 +264,25 @@ __global__ void qkv_post_kernel(const TI* __restrict__ qkv, TO* __restrict__ q, 
         rot = false;
     }
     float ss = 0.f;
-    for (int i = lane; i < hd; i += 32) {
-        float x = ldf(src, i);
-        for (int sp = 1; sp < nsplit; sp++) x += ldf(src + sp * split_stride, i);  // K-split partials, in slice order
-        buf[i] = x;
-        ss = fmaf(x, x, ss);
+    if (nsplit == 1) {
+        for (int i = lane; i < hd; i += 32) {
+            const float x = ldf(src, i);
+            buf[i] = x;
+            ss = fmaf(x, x, ss);
+        }
+    } else {
+        // K-split partials (at most 8), all loaded before they are added in slice order.
+        for (int i = lane; i < hd; i += 32) {
+            float pv[8];
+#pragma unroll
+            for (int sp = 0; sp < 8; sp++) pv[sp] = sp < nsplit ? ldf(src + sp * split_stride, i) : 0.f;
+            float x = pv[0];
+#pragma unroll
+            for (int sp = 1; sp < 8; sp++)
+                if (sp < nsplit) x += pv[sp];
+            buf[i] = x;
+            ss = fmaf(x, x, ss);
+        }
     }
     ss = warp_sum(ss);
     const float inv = 1.0f / sqrtf(ss / (float)hd + eps);
@@ -312,7 +326,7 @@ int qkv_post_split(const float* qkv, int nsplit, long split_stride, float* q, fl
                    const float* wk, const float* cs, const float* sn, int rope_w, const int* pos, long rows, int nh,
                    int nkv, int hd, int part, float eps, cudaStream_t s) {
     if (rows <= 0) return 0;
-    if (hd % 32 || hd > 1024 || part <= 0 || hd % part || part % 2 || nsplit < 1) return -1;
+    if (hd % 32 || hd > 1024 || part <= 0 || hd % part || part % 2 || nsplit < 1 || nsplit > 8) return -1;
     const int wpb = 8;
     const long items = rows * (nh + 2 * nkv);
     qkv_post_kernel<float, float><<<(unsigned)((items + wpb - 1) / wpb), 32 * wpb, wpb * hd * sizeof(float), s>>>(
