@@ -54,7 +54,9 @@ constexpr int gemm_threads(bool wide) { return wide ? 576 : GEMM_THREADS; }
 // and EPI_GELU_GU for their outputs. The main loop gives up stages for them.
 // DUAL (EPI_PLE_FUSED): two products per tile, each BN = 128 wide, in four TMEM accumulators (two per
 // epilogue set); 32 KB stages, four of them.
-template <int BN, bool PAIR = false, bool TIO = false, bool WIDE = false, bool DUAL = false>
+// NP: CTAs per row group of the add-norm cluster epilogue (2: 512-wide rows, the text tower; 3: 768, the
+// vision tower), each owning 256 columns; their row sums of squares go to every other CTA of the cluster.
+template <int BN, bool PAIR = false, bool TIO = false, bool WIDE = false, bool DUAL = false, int NP = 2>
 struct GemmCfg {
     static constexpr int NEPI = WIDE ? 16 : 8;  // epilogue warps
     static constexpr int A_BYTES = GEMM_BM * 128;
@@ -71,9 +73,9 @@ struct GemmCfg {
     // [set][slot][128 rows] at +X_OFF (2 KB), exchange barriers [set][slot] at +XB_OFF.
     // WIDE: the two half-warps' partial sums of squares [set][quadrant][slot][half][32] (4 KB) at
     // +XW_OFF, their barriers [set][quadrant][slot] at +XWB_OFF.
-    // DUAL: exchange slots [set][slot][source rank 0..3][128 rows] (8 KB).
+    // DUAL: exchange slots [set][slot][source rank 0..3][128 rows] (8 KB); NP = 3 the same with 3 sources.
     static constexpr int X_OFF = 2560;
-    static constexpr int XB_OFF = X_OFF + (DUAL ? 8192 : 2048);
+    static constexpr int XB_OFF = X_OFF + ((DUAL || NP > 2) ? 8192 : 2048);
     static constexpr int XW_OFF = XB_OFF + 64;
     static constexpr int XWB_OFF = XW_OFF + 4096;
     static constexpr int W_BYTES = WIDE ? XWB_OFF + 128 : XB_OFF + 64;
@@ -494,7 +496,7 @@ EG2_DEV void warp_load32_finish(const uint4 (&b)[8], float (&v)[32], uint8_t* st
 }
 
 // em: the tensor maps of the epilogue's TMA I/O (TIO only).
-template <typename TIn, int BN, int EPI, typename TOut, bool PAIR = false, bool TIO = false, bool WIDE = false>
+template <typename TIn, int BN, int EPI, typename TOut, bool PAIR = false, bool TIO = false, bool WIDE = false, int NP = 2>
 __global__ void __launch_bounds__(gemm_threads(WIDE), 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ EpiMaps em, int M, int N, int K, GemmEpilogue epi) {
@@ -506,7 +508,8 @@ __global__ void __launch_bounds__(gemm_threads(WIDE), 1)
                       (BN == 128 && EPI == EPI_PLE_FUSED && !PAIR),
                   "TMA epilogue I/O: the cluster epilogues, and the pair QKV / PLE-gate / GELU epilogues");
     constexpr bool DUAL = EPI == EPI_PLE_FUSED;
-    using Cfg = GemmCfg<BN, PAIR, TIO, WIDE, DUAL>;
+    static_assert(NP == 2 || (NP == 3 && EPI == EPI_ADD_NORM && !PAIR), "NP = 3: the single-CTA add-norm epilogue");
+    using Cfg = GemmCfg<BN, PAIR, TIO, WIDE, DUAL, NP>;
     constexpr int BK = InTraits<TIn>::BK;
     constexpr int STAGES = Cfg::STAGES;
     extern __shared__ uint8_t smem_raw[];
@@ -535,7 +538,8 @@ __global__ void __launch_bounds__(gemm_threads(WIDE), 1)
     constexpr bool QUAD = CL && PAIR;
     static_assert(!QUAD || EPI == EPI_ADD_NORM || EPI == EPI_GROUP_NORM, "QUAD: the add-norm and group-norm epilogues");
     static_assert(!PAIR || sizeof(TIn) == 2, "CTA-pair MMAs are bf16 only");
-    const int groups = N / 512;
+    const int GW = DUAL ? 512 : 256 * NP;  // cluster modes: columns of one row group
+    const int groups = N / GW;
     const uint32_t crank = (CL || PAIR) ? cluster_ctarank() : 0u;
     const uint32_t prow = PAIR ? (crank & 1u) : crank;       // PAIR: this CTA's row half of the pair tile
     const uint32_t pcol = QUAD ? (crank >> 1) : crank;       // cluster epilogues: column half of the group
@@ -543,9 +547,9 @@ __global__ void __launch_bounds__(gemm_threads(WIDE), 1)
     const uint32_t xpeer = QUAD ? (crank ^ 2u) : (crank ^ 1u);  // CL: the CTA with the other column half
     const bool lead = PAIR ? prow == 0 : crank == 0;
     const int tiles_mp = (tiles_m + 1) / 2;
-    constexpr int CSHIFT = (QUAD || DUAL) ? 2 : 1;  // log2 of the cluster size
-    const int t_first = (CL || PAIR) ? (int)(blockIdx.x >> CSHIFT) : (int)blockIdx.x;
-    const int t_step = (CL || PAIR) ? (int)(gridDim.x >> CSHIFT) : (int)gridDim.x;
+    constexpr int CSZ = (QUAD || DUAL) ? 4 : NP;  // cluster size
+    const int t_first = (CL || PAIR) ? (int)(blockIdx.x / CSZ) : (int)blockIdx.x;
+    const int t_step = (CL || PAIR) ? (int)(gridDim.x / CSZ) : (int)gridDim.x;
     // K split (EPI_STORE): linear id t = base tile * S + slice; slice s covers K blocks
     // [s * kbs, s * kbs + kbs).
     const int S = (EPI == EPI_STORE && epi.ksplit > 1) ? epi.ksplit : 1;
@@ -559,7 +563,7 @@ __global__ void __launch_bounds__(gemm_threads(WIDE), 1)
     };
     auto tile_n0 = [&](int t) {
         t /= S;
-        return CL ? (t % groups) * 512 + (int)pcol * BN : (t % tiles_n) * BN;
+        return CL ? (t % groups) * GW + (int)pcol * BN : (t % tiles_n) * BN;
     };
 
     if (threadIdx.x == 0) {
@@ -813,6 +817,27 @@ __global__ void __launch_bounds__(gemm_threads(WIDE), 1)
                 float* xv = reinterpret_cast<float*>(smem + Cfg::OFF_W + Cfg::X_OFF);  // [set][slot][128]
                 uint64_t* xb = reinterpret_cast<uint64_t*>(smem + Cfg::OFF_W + Cfg::XB_OFF);
                 const int rl = 32 * e + lane;
+                if constexpr (NP > 2) {
+                    // Every other CTA of the cluster gets this partial in its slot [set][slot][this rank];
+                    // all add the NP partials in rank order, so every CTA uses the same norm.
+                    const int x = set * 2 + slot;
+                    float* slots = xv + x * NP * 128;
+                    if (rl == 0) mbar_arrive_expect_tx(&xb[x], (NP - 1) * 128 * 4);
+#pragma unroll
+                    for (uint32_t pr = 0; pr < (uint32_t)NP; pr++)
+                        if (pr != crank)
+                            st_async_f32(mapa_shared(smem_u32(slots + crank * 128 + rl), pr), part,
+                                         mapa_shared(smem_u32(&xb[x]), pr));
+                    if (!mbar_wait(&xb[x], parity, EG2_DEV_TIMEOUT_GEMM, abort_flag)) {
+                        ok = false;
+                        return 0.f;
+                    }
+                    float tot = 0.f;
+#pragma unroll
+                    for (int src = 0; src < NP; src++)
+                        tot += (src == (int)crank) ? part : *reinterpret_cast<volatile float*>(slots + src * 128 + rl);
+                    return tot;
+                }
                 const uint32_t peer = xpeer;
                 const int x = set * 2 + slot;
                 float* mine = xv + x * 128 + rl;
@@ -1167,7 +1192,7 @@ __global__ void __launch_bounds__(gemm_threads(WIDE), 1)
                         ss = fmaf(__uint_as_float(r1[j]), __uint_as_float(r1[j]), ss);
                     }
                 }
-                const float inv1 = 1.0f / sqrtf(exchange(ss, 0, k & 1) / 512.f + A.eps);
+                const float inv1 = 1.0f / sqrtf(exchange(ss, 0, k & 1) / (float)(256 * NP) + A.eps);
                 if (!ok) break;
                 float ss2 = 0.f;
 #pragma unroll 1
@@ -1218,7 +1243,7 @@ __global__ void __launch_bounds__(gemm_threads(WIDE), 1)
                 // The second exchange runs even without w2: it is also the handshake that keeps the
                 // peer from writing this set's slot 0 for the next tile before it has been read here.
                 tmem_st_wait();
-                const float inv2 = 1.0f / sqrtf(exchange(ss2, 1, k & 1) / 512.f + A.eps);
+                const float inv2 = 1.0f / sqrtf(exchange(ss2, 1, k & 1) / (float)(256 * NP) + A.eps);
                 if (!ok) break;
 #pragma unroll 1
                 for (int c = 0; c < BN / 32; c++) {
@@ -1444,14 +1469,14 @@ static int launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N,
 // Clusters of two CTAs (the cluster epilogues, and CTA-pair MMAs), or of four (a cluster epilogue on
 // CTA-pair MMAs), as many as can be resident at once (the loop over tiles is persistent, so every
 // launched cluster must run concurrently with the others).
-template <int EPI, typename TOut, bool PAIR = false, bool TIO = false, bool WIDE = false, int BNT = 256>
+template <int EPI, typename TOut, bool PAIR = false, bool TIO = false, bool WIDE = false, int BNT = 256, int NP = 2>
 static int launch_cluster(const CUtensorMap& ta, const CUtensorMap& tb, const EpiMaps& em, int M, int N, int K,
                           const GemmEpilogue& epi, cudaStream_t s) {
     constexpr bool DUAL = EPI == EPI_PLE_FUSED;
-    using Cfg = GemmCfg<BNT, PAIR, TIO, WIDE, DUAL>;
-    auto kern = gemm_tc_kernel<bf16_t, BNT, EPI, TOut, PAIR, TIO, WIDE>;
+    using Cfg = GemmCfg<BNT, PAIR, TIO, WIDE, DUAL, NP>;
+    auto kern = gemm_tc_kernel<bf16_t, BNT, EPI, TOut, PAIR, TIO, WIDE, NP>;
     constexpr bool QUAD = PAIR && (EPI == EPI_ADD_NORM || EPI == EPI_GROUP_NORM);
-    constexpr int CSIZE = (QUAD || DUAL) ? 4 : 2;
+    constexpr int CSIZE = (QUAD || DUAL) ? 4 : NP;
     static int max_clusters[64] = {0};
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -3;
@@ -1477,10 +1502,10 @@ static int launch_cluster(const CUtensorMap& ta, const CUtensorMap& tb, const Ep
         max_clusters[dev] = n;
     }
     const int tiles_m = (M + GEMM_BM - 1) / GEMM_BM;
-    if (N % ((PAIR && !QUAD) ? 256 : 512)) return -1;
+    if (N % ((PAIR && !QUAD) ? 256 : 256 * NP)) return -1;
     const long tiles = QUAD ? (long)((tiles_m + 1) / 2) * (N / 512)
                        : PAIR ? (long)((tiles_m + 1) / 2) * (N / 256) * (epi.ksplit > 1 ? epi.ksplit : 1)
-                              : (long)tiles_m * (N / 512);
+                              : (long)tiles_m * (N / (DUAL ? 512 : 256 * NP));
     const int clusters = tiles < max_clusters[dev] ? (int)tiles : max_clusters[dev];
     cfg.gridDim = dim3(CSIZE * clusters, 1, 1);
     cfg.numAttrs = pdl_enabled() ? 2 : 1;
@@ -1536,7 +1561,7 @@ int gemm_tc(GemmKind kind, const void* A, long lda, const void* W, long ldw, int
     // The add-norm epilogue on CTA-pair MMAs (clusters of four, opt-in): each CTA streams half of the
     // weight tile (same results as the single-CTA main loop: both accumulate K in the same 64-element
     // blocks).
-    const bool quad = !tf32 && epi.mode == EPI_ADD_NORM && quad_enabled();
+    const bool quad = !tf32 && epi.mode == EPI_ADD_NORM && N == 512 && quad_enabled();
     if (make_tmap_2d(&tb, dt, W, K, N, ldw * esize, BK, (pair || quad) ? BN / 2 : BN)) return -1;
     const EpiMaps none = {};
     // bf16 output tensor [M, cols] (row stride ld elements) as 32 x 32 TMA store boxes.
@@ -1601,15 +1626,17 @@ int gemm_tc(GemmKind kind, const void* A, long lda, const void* W, long ldw, int
                 return launch_tc<bf16_t, BN, EPI_QKV, bf16_t>(ta, tb, M, N, K, epi, s);
             case EPI_ADD_NORM:
             {
-                if (N != 512 || !epi.an.h || !epi.an.w1 || !epi.out || epi.ldo % 8) return -1;
+                // Rows of 512 (text: clusters of two CTAs) or 768 (vision: clusters of three).
+                if ((N != 512 && N != 768) || !epi.an.h || !epi.an.w1 || !epi.out || epi.ldo % 8) return -1;
                 // The epilogue's residual I/O goes through TMA (the main loop keeps 3 stages); measured
                 // faster than the register path with 4 stages for the O, down and PLE projections.
                 // Residual h: f32 [M, 512], 16 x 32 boxes; t: bf16 [M, 512] (row stride ldo), 32 x 32.
                 EpiMaps em = {};
-                if (make_tmap_2d(&em.m[0], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, epi.an.h, 512, M, 512 * 4, 16, 32,
+                if (make_tmap_2d(&em.m[0], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, epi.an.h, N, M, (uint64_t)N * 4, 16, 32,
                                  CU_TENSOR_MAP_SWIZZLE_64B) ||
-                    out_map(&em.m[1], epi.out, 512, epi.ldo))
+                    out_map(&em.m[1], epi.out, N, epi.ldo))
                     return -1;
+                if (N == 768) return launch_cluster<EPI_ADD_NORM, bf16_t, false, true, false, 256, 3>(ta, tb, em, M, N, K, epi, s);
                 return quad ? launch_cluster<EPI_ADD_NORM, bf16_t, true, true>(ta, tb, em, M, N, K, epi, s)
                             : launch_cluster<EPI_ADD_NORM, bf16_t, false, true>(ta, tb, em, M, N, K, epi, s);
             }
