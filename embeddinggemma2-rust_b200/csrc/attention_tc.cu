@@ -26,6 +26,8 @@ struct AttParams {
     bf16_t* out;
     const int* seq_start;  // per row: first row of its sequence (null: a tile's rows are one sequence)
     const int* seq_len;
+    const bf16_t* q;  // [rows, nh, hd] (read directly by the head-512 kernel, which keeps Q in TMEM)
+    long rows;
     int nh, nkv, hd, window, G, tq, nsplit, n_tiles;
 };
 
@@ -571,6 +573,496 @@ done:
 }
 
 // ---------------------------------------------------------------------------------------------
+// Head 512 on clusters of four CTAs: S = Q K^T once per key tile, O over all 512 channels.
+//
+// A 512-channel O of 128 rows fills a CTA's TMEM (512 f32 columns), so one CTA pair cannot hold S
+// next to it. The four CTAs of a cluster split the work instead of duplicating S:
+//   ranks 0, 1  score pair: Q (bf16, TMEM columns [0, 256): brought into the ring by TMA and copied
+//               to TMEM with tcgen05.cp) and S over 256 keys (columns [256, 512)); S = Q K^T as
+//               M = 256, N = 256 pair MMAs with A read from TMEM (each CTA holds 128 of the 256 keys
+//               of K), and the softmax. The P of each 128-key half of a tile is one message: staged
+//               per warp in shared memory in the operand layout of the P V MMA and sent with bulk
+//               copies over distributed shared memory, with each row's rescale factor and partial
+//               row sum.
+//   ranks 2, 3  value pair: O in all 512 TMEM columns; per message O += P V as M = 256 pair MMAs, A =
+//               the P received in shared memory (three buffers), B = V (each CTA holds 128 of every
+//               256 channels); the correction warps rescale O when a row's maximum moved and write
+//               O / l at the end.
+// Rank 2 + i holds the same 128 query rows as rank i. Per 128 keys each pair's tensor work is 2,048
+// cycles (the two 256-channel halves of the CTA-pair kernel each recompute all of S: 3,072 per
+// half); P crosses the cluster at 32 KB per CTA per 128 keys.
+//
+//   warp 0      TMA producer (score pair: Q once per unit, then this CTA's 128 keys of K; value
+//               pair: its V channels)
+//   warp 1      TMEM allocation; in the even CTA of each pair lane 0 issues that pair's tcgen05 work
+//   warps 2..9  score pair: softmax, two threads per row (128 of the 256 columns each, maxima swapped
+//               through shared memory as in the head-256 kernel); the threads of column half h send
+//               message 2 t + h of tile t. Value pair: rescale and O / l.
+// Barriers (the same offsets in all four CTAs; each pair uses its own): the Q / K / V ring (full in
+// the pair's even CTA, empty committed to both), s_full / s_empty (S computed / read by both CTAs'
+// softmax); in the score CTAs p_empty per value buffer (committed by the value pair's MMAs: the
+// buffer's message has been consumed) and staged per column half (the half's last message has landed,
+// so its staging may be rewritten: one arrival from the value CTA); in the value CTAs p_full per
+// buffer (the bytes of a message), c_done per buffer (both value CTAs' correction threads have
+// applied its factors), pv_done per buffer, o_empty (O read out).
+// ---------------------------------------------------------------------------------------------
+struct AqCfg {
+    static constexpr int THREADS = 320;
+    static constexpr int P_BYTES = 128 * AP_BN * 2;       // one message's P: 128 keys x this CTA's 128 rows
+    static constexpr int X_BYTES = 128 * 8;               // per row: (factor, partial row sum)
+    static constexpr int MSG = P_BYTES + X_BYTES;
+    // Score CTAs: staging per column half, the Q / K ring, the split softmax's maxima.
+    static constexpr int RING = 4;                        // 32 KB units
+    static constexpr int OFF_SP = 0;                      // [2] P staging
+    static constexpr int OFF_SX = OFF_SP + 2 * P_BYTES;   // [2] (factor, l) staging
+    static constexpr int OFF_R = OFF_SX + 2 * X_BYTES;    // ring (1 KB aligned)
+    static constexpr int OFF_M = OFF_R + RING * AP_UNIT;  // [2 slots][2 halves][128] floats
+    static constexpr int S_END = OFF_M + 2 * 2 * 128 * 4;
+    // Value CTAs: three message buffers, the V ring.
+    static constexpr int NBUF = 3;
+    static constexpr int VRING = 3;
+    static constexpr int OFF_VP = 0;
+    static constexpr int OFF_VX = OFF_VP + NBUF * P_BYTES;
+    static constexpr int OFF_VR = ((OFF_VX + NBUF * X_BYTES + 1023) / 1024) * 1024;
+    static constexpr int V_END = OFF_VR + VRING * AP_UNIT;
+    static constexpr int OFF_BAR = S_END > V_END ? S_END : V_END;
+    // r_full[4] r_empty[4] s_full s_empty p_empty[3] staged[2] xpair[8] p_full[3] c_done[3] pv_done[3]
+    // o_empty drain
+    static constexpr int N_BARS = 2 * RING + 1 + 1 + NBUF + 2 + 8 + 3 * NBUF + 1 + 1;
+    static constexpr int SMEM = 1024 + OFF_BAR + N_BARS * 8 + 16;
+};
+static_assert(AqCfg::OFF_R % 1024 == 0 && AqCfg::OFF_VR % 1024 == 0 && AqCfg::SMEM <= 227 * 1024,
+              "attention quad: shared memory");
+
+__global__ void __launch_bounds__(AqCfg::THREADS, 1)
+    attention_quad_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                          const __grid_constant__ CUtensorMap tmV, AttParams prm) {
+    using Cfg = AqCfg;
+    constexpr int ARRIVALS = 2 * 256;  // the softmax / correction threads of both CTAs of a pair
+    constexpr int ST = 2 * AP_BN;      // keys per S tile
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::OFF_BAR);
+    uint64_t* r_full = bars;
+    uint64_t* r_empty = r_full + Cfg::RING;
+    uint64_t* s_full = r_empty + Cfg::RING;
+    uint64_t* s_empty = s_full + 1;
+    uint64_t* p_empty = s_empty + 1;
+    uint64_t* staged = p_empty + Cfg::NBUF;
+    uint64_t* xpair = staged + 2;
+    uint64_t* p_full = xpair + 8;
+    uint64_t* c_done = p_full + Cfg::NBUF;
+    uint64_t* pv_done = c_done + Cfg::NBUF;
+    uint64_t* o_empty = pv_done + Cfg::NBUF;
+    uint64_t* drain = o_empty + 1;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + Cfg::N_BARS);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();
+    const bool scorer = rank < 2;
+    const uint32_t lead = rank & 2u;  // the pair's even CTA
+    const bool even = (rank & 1u) == 0;
+    const int ring = scorer ? Cfg::RING : Cfg::VRING;
+    const int off_ring = scorer ? Cfg::OFF_R : Cfg::OFF_VR;
+    const int n_units = prm.n_tiles * prm.nkv;
+    const int u_first = (int)(blockIdx.x >> 2), u_step = (int)(gridDim.x >> 2);
+    const int G = prm.G, W = prm.window, tqc = prm.tq;
+    // A unit: (pair tile, K/V head); n_st S tiles of 256 keys from k_lo, i.e. 2 n_st messages of 128 keys.
+    struct Unit {
+        AttnTile tile;
+        int g, q0r, k_lo, n_st;
+    };
+    auto unit_at = [&](int cid) {
+        Unit x;
+        x.tile = prm.tiles[cid / prm.nkv];
+        x.g = cid % prm.nkv;
+        x.q0r = x.tile.q0 + (int)(rank & 1u) * tqc;
+        const int q_last = min(x.tile.q0 + 2 * tqc, x.tile.len) - 1;
+        x.k_lo = (W >= 0) ? max(0, x.tile.q0 - W) : 0;
+        const int k_hi = (W >= 0) ? min(x.tile.len, q_last + W + 1) : x.tile.len;
+        x.n_st = x.tile.len > 0 ? (k_hi - x.k_lo + ST - 1) / ST : 0;
+        return x;
+    };
+
+    if (threadIdx.x == 0) {
+        for (int u = 0; u < Cfg::RING; u++) {
+            mbar_init(&r_full[u], 1);
+            mbar_init(&r_empty[u], 1);
+        }
+        mbar_init(s_full, 1);
+        mbar_init(s_empty, ARRIVALS);
+        for (int b = 0; b < Cfg::NBUF; b++) {
+            mbar_init(&p_empty[b], 1);
+            mbar_init(&p_full[b], 1);
+            mbar_init(&c_done[b], ARRIVALS);
+            mbar_init(&pv_done[b], 1);
+        }
+        mbar_init(&staged[0], 1);
+        mbar_init(&staged[1], 1);
+        for (int x = 0; x < 8; x++) mbar_init(&xpair[x], 64);
+        mbar_init(o_empty, ARRIVALS);
+        mbar_init(drain, 1);
+        *abort_flag = 0;
+        fence_mbarrier_init();
+    }
+    if (warp == 1) tmem_alloc_pair(tmem_slot, 512);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    // A value CTA expects the first message of each buffer before any score CTA can send one.
+    if (!scorer && threadIdx.x == 64)
+        for (int b = 0; b < Cfg::NBUF; b++) mbar_arrive_expect_tx(&p_full[b], Cfg::MSG);
+    cluster_sync();
+    grid_dep_launch();
+    grid_dep_wait();
+    const uint32_t tmem = *tmem_slot;
+    auto arrive_lead = [&](uint64_t* bar) {
+        if (even) mbar_arrive(bar);
+        else mbar_arrive_remote(mapa_shared(smem_u32(bar), lead));
+    };
+
+    if (warp == 0) {
+        if (lane == 0) {
+            int u = 0;
+            uint32_t uph = 0;
+            auto next_slot = [&](uint8_t*& dst, uint32_t& bar) -> bool {
+                if (!mbar_wait(&r_empty[u], uph ^ 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) return false;
+                if (even) mbar_arrive_expect_tx(&r_full[u], 2 * AP_UNIT);
+                bar = mapa_shared(smem_u32(&r_full[u]), lead);
+                dst = smem + off_ring + u * AP_UNIT;
+                if (++u == ring) {
+                    u = 0;
+                    uph ^= 1;
+                }
+                return true;
+            };
+            for (int cid = u_first; cid < n_units; cid += u_step) {
+                const Unit x = unit_at(cid);
+                if (x.n_st == 0) continue;
+                uint8_t* dst;
+                uint32_t bar;
+                if (scorer) {
+                    // Q: 4 units of this CTA's 128 rows x 128 channels (2 boxes [G heads x tq tokens x 64 ch]).
+                    for (int part = 0; part < 4; part++) {
+                        if (!next_slot(dst, bar)) goto done;
+                        for (int c = 0; c < 2; c++)
+                            tma_load_3d_pair(dst + c * 16384, &tmQ, bar, part * 128 + c * 64, x.g * G, x.tile.row0 + x.q0r);
+                    }
+                }
+                for (int t = 0; t < x.n_st; t++) {
+                    const int key0 = x.tile.row0 + x.k_lo + t * ST;
+                    if (scorer) {
+                        // K of this CTA's 128 keys, channels [128 part, 128 part + 128): 2 boxes [128 keys x 64 ch].
+                        for (int part = 0; part < 4; part++) {
+                            if (!next_slot(dst, bar)) goto done;
+                            for (int c = 0; c < 2; c++)
+                                tma_load_3d_pair(dst + c * 16384, &tmK, bar, part * 128 + c * 64, x.g, key0 + AP_BN * (int)(rank & 1u));
+                        }
+                    } else {
+                        // Per message (128 keys): V for this CTA's 128 channels of each 256-channel half.
+                        for (int m = 0; m < 2; m++)
+                            for (int part = 0; part < 2; part++) {
+                                if (!next_slot(dst, bar)) goto done;
+                                for (int c = 0; c < 2; c++)
+                                    tma_load_3d_pair(dst + c * 16384, &tmV, bar, part * 256 + (int)(rank & 1u) * 128 + c * 64, x.g,
+                                                     key0 + AP_BN * m);
+                            }
+                    }
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (even && lane == 0) {
+            int iu = 0, Ts = 0, T = 0, U = 0;
+            auto wait_slot = [&](int& u) -> bool {
+                u = iu % ring;
+                const bool ok = mbar_wait(&r_full[u], (iu / ring) & 1, EG2_DEV_TIMEOUT_ATTN, abort_flag);
+                iu++;
+                return ok;
+            };
+            if (scorer) {
+                constexpr uint32_t idesc_s = umma_idesc(256, ST, 1);
+                const uint64_t dr0 = umma_desc_sw128(smem_u32(smem + Cfg::OFF_R), 16, 1024);
+                const uint32_t t_s = tmem + 256;
+                for (int cid = u_first; cid < n_units; cid += u_step) {
+                    const Unit x = unit_at(cid);
+                    if (x.n_st == 0) continue;
+                    // Q into TMEM (channel pairs per column), after the previous unit's S MMAs in issue order.
+                    for (int part = 0; part < 4; part++) {
+                        int u;
+                        if (!wait_slot(u)) goto done;
+                        const uint64_t dq = dr0 + (uint64_t)(u * (AP_UNIT >> 4));
+#pragma unroll
+                        for (int c = 0; c < 2; c++)
+#pragma unroll
+                            for (int kk = 0; kk < 4; kk++)
+                                tmem_cp_pair_128x256b(tmem + (uint32_t)(part * 64 + c * 32 + kk * 8), dq + (uint64_t)(c * (16384 >> 4) + 2 * kk));
+                        mma_commit_pair_both(&r_empty[u], 0);
+                    }
+                    for (int t = 0; t < x.n_st; t++, Ts++) {
+                        // S was last read by both CTAs' softmax (Ts - 1).
+                        if (Ts >= 1 && !mbar_wait(s_empty, (Ts - 1) & 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) goto done;
+                        tc_fence_after();
+                        for (int part = 0; part < 4; part++) {
+                            int u;
+                            if (!wait_slot(u)) goto done;
+                            const uint64_t db = dr0 + (uint64_t)(u * (AP_UNIT >> 4));
+#pragma unroll
+                            for (int c = 0; c < 2; c++) {
+#pragma unroll
+                                for (int kk = 0; kk < 4; kk++)
+                                    mma_bf16_pair_ts(t_s, tmem + (uint32_t)(part * 64 + c * 32 + kk * 8),
+                                                     db + (uint64_t)(c * (16384 >> 4) + 2 * kk), idesc_s, (part | c | kk) != 0);
+                            }
+                            mma_commit_pair_both(&r_empty[u], 0);
+                        }
+                        mma_commit_pair_both(s_full, 0);
+                    }
+                    U++;
+                }
+            } else {
+                constexpr uint32_t idesc_o = umma_idesc(256, ATT_DV, 1, /*b_mn_major=*/true);
+                const uint64_t dv0 = umma_desc_sw128(smem_u32(smem + Cfg::OFF_VR), 16384, 1024);
+                const uint64_t dp0 = umma_desc_sw128(smem_u32(smem + Cfg::OFF_VP), 16, 1024);
+                for (int cid = u_first; cid < n_units; cid += u_step) {
+                    const Unit x = unit_at(cid);
+                    if (x.n_st == 0) continue;
+                    for (int j = 0; j < 2 * x.n_st; j++, T++) {
+                        const int b = T % Cfg::NBUF;
+                        // Message T has landed in both value CTAs and its factors are applied to O.
+                        if (!mbar_wait(&c_done[b], (T / Cfg::NBUF) & 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) goto done;
+                        // The first P V of a unit overwrites O: the previous unit's O must have been read.
+                        if (j == 0 && U > 0 && !mbar_wait(o_empty, (U - 1) & 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) goto done;
+                        tc_fence_after();
+                        const uint64_t dp = dp0 + (uint64_t)(b * (Cfg::P_BYTES >> 4));
+                        for (int h = 0; h < 2; h++) {
+                            int u;
+                            if (!wait_slot(u)) goto done;
+                            const uint64_t dv = dv0 + (uint64_t)(u * (AP_UNIT >> 4));
+                            // 16 keys per MMA: P chunk kk / 4 (64 keys), 32 bytes into its rows; 16 V rows.
+#pragma unroll
+                            for (int kk = 0; kk < AP_BN / 16; kk++)
+                                mma_bf16_pair(tmem + (uint32_t)(256 * h), dp + (uint64_t)((kk >> 2) * (16384 >> 4) + 2 * (kk & 3)),
+                                              dv + (uint64_t)(kk * (2048 >> 4)), idesc_o, (j | kk) != 0);
+                            mma_commit_pair_both(&r_empty[u], 2);
+                        }
+                        mma_commit_pair_both(&pv_done[b], 2);
+                        mma_commit_pair_both(&p_empty[b], 0);  // to the score CTAs
+                    }
+                    U++;
+                }
+            }
+        }
+    } else {
+        const int e = warp & 3;
+        const int ch = (warp - 2) >> 2;  // score pair: S columns [128 ch, +128) (message half ch); value pair: O columns [256 ch, +256)
+        const int r = 32 * e + lane;
+        const uint32_t lane_off = (uint32_t)(32 * e) << 16;
+        const float LOG2E = 1.4426950408889634f;
+        int Ts = 0, T = 0, X = 0;
+        for (int cid = u_first; cid < n_units; cid += u_step) {
+            const Unit x = unit_at(cid);
+            if (x.n_st == 0) continue;
+            const AttnTile& tile = x.tile;
+            const int tok = x.q0r + r / G;
+            const int head = x.g * G + r % G;
+            const bool row_valid = tok < tile.len;
+            bool ok = true;
+            if (scorer) {
+                int rs = 0, re = tile.len;
+                if (prm.seq_start && row_valid) {
+                    rs = prm.seq_start[tile.row0 + tok] - tile.row0;
+                    re = rs + prm.seq_len[tile.row0 + tok];
+                }
+                float* xmax = reinterpret_cast<float*>(smem + Cfg::OFF_M);  // [slot][half][128]
+                float m_used = -INFINITY, l = 0.f;
+                for (int t = 0; t < x.n_st; t++, Ts++) {
+                    if (!mbar_wait(s_full, Ts & 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    float sv[128];
+#pragma unroll
+                    for (int c = 0; c < 4; c++) {
+                        uint32_t s0[32];
+                        tmem_ld32(tmem + (uint32_t)(256 + 128 * ch + 32 * c) + lane_off, s0);
+                        tmem_ld_wait();
+#pragma unroll
+                        for (int q = 0; q < 32; q++) sv[32 * c + q] = __uint_as_float(s0[q]);
+                    }
+                    tc_fence_before();
+                    arrive_lead(s_empty);
+                    // Valid key columns of this row in this tile, relative to this thread's first column.
+                    const int kbase = x.k_lo + t * ST + AP_BN * ch;
+                    int lo_c = max(0, rs - kbase), hi_c = min(AP_BN, re - kbase);
+                    if (W >= 0 && row_valid) {
+                        lo_c = max(lo_c, tok - W - kbase);
+                        hi_c = min(hi_c, tok + W + 1 - kbase);
+                    }
+                    if (!__all_sync(0xffffffffu, lo_c <= 0 && hi_c >= AP_BN)) {
+#pragma unroll
+                        for (int c = 0; c < AP_BN; c++) sv[c] = (c >= lo_c && c < hi_c) ? sv[c] : -INFINITY;
+                    }
+                    float mx[8];
+#pragma unroll
+                    for (int c = 0; c < 8; c++) mx[c] = sv[c];
+#pragma unroll
+                    for (int c = 8; c < AP_BN; c++) mx[c & 7] = fmaxf(mx[c & 7], sv[c]);
+                    float mt = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+                    {
+                        // The row's other half (slots alternate by handshake, as in the head-256 kernel).
+                        float* slot = xmax + (X & 1) * 256;
+                        slot[ch * 128 + r] = mt;
+                        mbar_arrive(&xpair[e * 2 + (X & 1)]);
+                        if (!mbar_wait(&xpair[e * 2 + (X & 1)], (X >> 1) & 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) {
+                            ok = false;
+                            break;
+                        }
+                        mt = fmaxf(mt, *reinterpret_cast<volatile float*>(slot + (ch ^ 1) * 128 + r));
+                        X++;
+                    }
+                    float factor = 1.f;
+                    if (mt > m_used) {
+                        if (m_used == -INFINITY) {
+                            m_used = mt;
+                        } else if ((mt - m_used) * LOG2E > ATT_RESCALE_LOG2) {
+                            factor = ex2_approx((m_used - mt) * LOG2E);
+                            m_used = mt;
+                        }
+                    }
+                    l *= factor;
+                    // Row sum over the bf16-ROUNDED probabilities that multiply V (weights sum to exactly l).
+                    const float bias = (m_used == -INFINITY) ? 0.f : -m_used * LOG2E;
+                    float lsum[4] = {0.f, 0.f, 0.f, 0.f};
+                    uint32_t pk[64];
+#pragma unroll
+                    for (int q = 0; q < 64; q++) {
+                        const float p0 = ex2_approx(fmaf(sv[2 * q], LOG2E, bias));
+                        const float p1 = ex2_approx(fmaf(sv[2 * q + 1], LOG2E, bias));
+                        pk[q] = bf16x2_bits(p0, p1);
+                        lsum[q & 3] += __uint_as_float(pk[q] << 16) + __uint_as_float(pk[q] & 0xffff0000u);
+                    }
+                    l += (lsum[0] + lsum[1]) + (lsum[2] + lsum[3]);
+                    // Message m = 2 Ts + ch: staging ch is free once the half's previous message has landed,
+                    // value buffer m % 3 once P V of message m - 3 has completed.
+                    const int m = 2 * Ts + ch, vb = m % Cfg::NBUF;
+                    if (Ts >= 1 && !mbar_wait(&staged[ch], (Ts - 1) & 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    if (m >= Cfg::NBUF && !mbar_wait(&p_empty[vb], (m / Cfg::NBUF - 1) & 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    // P row r, keys [64 c, 64 c + 64) of the message: row r of chunk c, 16-byte units swizzled by r % 8.
+                    uint8_t* prow = smem + Cfg::OFF_SP + ch * Cfg::P_BYTES + r * 128;
+#pragma unroll
+                    for (int c = 0; c < 2; c++)
+#pragma unroll
+                        for (int g = 0; g < 8; g++)
+                            *reinterpret_cast<uint4*>(prow + c * 16384 + ((g ^ (r & 7)) << 4)) =
+                                make_uint4(pk[32 * c + 4 * g], pk[32 * c + 4 * g + 1], pk[32 * c + 4 * g + 2], pk[32 * c + 4 * g + 3]);
+                    // The factor applies to O before the tile's first message; the partial sum is this half's.
+                    *reinterpret_cast<float2*>(smem + Cfg::OFF_SX + ch * Cfg::X_BYTES + r * 8) = make_float2(ch == 0 ? factor : 1.f, l);
+                    fence_proxy_async();
+                    __syncwarp();
+                    if (lane == 0) {
+                        // The warp's 32 rows: 2 x 4 KB of P and 256 bytes of (factor, l), into value buffer vb of CTA rank + 2.
+                        const uint32_t peer = rank + 2;
+                        const uint32_t pbar = mapa_shared(smem_u32(&p_full[vb]), peer);
+                        for (int c = 0; c < 2; c++)
+                            bulk_copy_to_peer(mapa_shared(smem_u32(smem + Cfg::OFF_VP + vb * Cfg::P_BYTES + c * 16384 + 32 * e * 128), peer),
+                                              smem_u32(smem + Cfg::OFF_SP + ch * Cfg::P_BYTES + c * 16384 + 32 * e * 128), 4096, pbar);
+                        bulk_copy_to_peer(mapa_shared(smem_u32(smem + Cfg::OFF_VX + vb * Cfg::X_BYTES + 32 * e * 8), peer),
+                                          smem_u32(smem + Cfg::OFF_SX + ch * Cfg::X_BYTES + 32 * e * 8), 256, pbar);
+                    }
+                }
+            } else {
+                float lh0 = 0.f, lh1 = 0.f;  // latest partial row sums of the two column halves
+                for (int j = 0; j < 2 * x.n_st; j++, T++) {
+                    const int b = T % Cfg::NBUF;
+                    if (!mbar_wait(&p_full[b], (T / Cfg::NBUF) & 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    if (warp == 2 && lane == 0) {
+                        // The buffer's next message (T + 3) is sent only after P V(T), which waits for c_done(T).
+                        mbar_arrive_expect_tx(&p_full[b], Cfg::MSG);
+                        // The sender's staging of column half T % 2 may be rewritten.
+                        mbar_arrive_remote(mapa_shared(smem_u32(&staged[T & 1]), rank - 2));
+                    }
+                    const float2 xv = reinterpret_cast<const float2*>(smem + Cfg::OFF_VX + b * Cfg::X_BYTES)[r];
+                    const float factor = xv.x;
+                    if (T & 1) lh1 = xv.y;
+                    else lh0 = xv.y;
+                    if (__any_sync(0xffffffffu, factor != 1.f) && j >= 1) {
+                        // O must hold every P V up to message T - 1 before it is rescaled.
+                        const int tp = T - 1;
+                        if (!mbar_wait(&pv_done[tp % Cfg::NBUF], (tp / Cfg::NBUF) & 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+#pragma unroll 1
+                        for (int c = 0; c < 8; c++) {
+                            uint32_t o[32];
+                            tmem_ld32(tmem + (uint32_t)(256 * ch + 32 * c) + lane_off, o);
+                            tmem_ld_wait();
+#pragma unroll
+                            for (int q = 0; q < 32; q++) o[q] = __float_as_uint(__uint_as_float(o[q]) * factor);
+                            tmem_st32(tmem + (uint32_t)(256 * ch + 32 * c) + lane_off, o);
+                        }
+                        tmem_st_wait();
+                    }
+                    tc_fence_before();
+                    arrive_lead(&c_done[b]);
+                }
+                if (!ok || *abort_flag) break;
+                // O / l once the unit's last P V has completed; then the next unit may overwrite O.
+                const int Tl = T - 1;
+                if (!mbar_wait(&pv_done[Tl % Cfg::NBUF], (Tl / Cfg::NBUF) & 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) break;
+                tc_fence_after();
+                const float lrow = lh0 + lh1;
+                const float inv = (lrow > 0.f) ? 1.f / lrow : 0.f;
+                bf16_t* orow = prm.out + ((long)(tile.row0 + tok) * prm.nh + head) * prm.hd + 256 * ch;
+                tmem_pipelined<32>(tmem + (uint32_t)(256 * ch) + lane_off, 8, [&](int c, uint32_t(&o)[32]) -> bool {
+                    if (row_valid) {
+#pragma unroll
+                        for (int q = 0; q < 2; q++) {
+                            uint32_t pw[8];
+#pragma unroll
+                            for (int i = 0; i < 8; i++)
+                                pw[i] = bf16x2_bits(__uint_as_float(o[16 * q + 2 * i]) * inv, __uint_as_float(o[16 * q + 2 * i + 1]) * inv);
+                            st_global_v8(orow + c * 32 + 16 * q, pw);
+                        }
+                    }
+                    return true;
+                });
+                tc_fence_before();
+                arrive_lead(o_empty);
+            }
+            if (!ok || *abort_flag) break;
+        }
+    }
+done:
+    // Every tcgen05 operation a pair's even CTA issued (into both CTAs' TMEM) has completed before
+    // either frees it.
+    if (even && warp == 1 && lane == 0) {
+        mma_commit_pair(smem_u32(drain));
+        mbar_wait(drain, 0, EG2_DEV_TIMEOUT_ATTN, nullptr);
+    }
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc_pair(tmem, 512);
+    }
+}
+
+// ---------------------------------------------------------------------------------------------
 // Head 64 (the vision tower: 12 query heads, each with its own K/V head), one CTA per (256 query
 // tokens, head): two 128-row query tiles share every K / V tile.
 //
@@ -916,6 +1408,56 @@ static int launch_pair(const CUtensorMap& mq, const CUtensorMap& mk, const CUten
     return cudaLaunchKernelEx(&cfg, kern, mq, mk, mv, mo, prm) == cudaSuccess ? 0 : -3;
 }
 
+// Head 512: clusters of four (as many as can be resident, at most one per unit), each walking its units.
+static int launch_quad(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const AttParams& prm,
+                       cudaStream_t s) {
+    using Cfg = AqCfg;
+    static int max_clusters[64] = {0};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -3;
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute la[2];
+    la[0].id = cudaLaunchAttributeClusterDimension;
+    la[0].val.clusterDim.x = 4;
+    la[0].val.clusterDim.y = 1;
+    la[0].val.clusterDim.z = 1;
+    la[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    la[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.blockDim = dim3(Cfg::THREADS, 1, 1);
+    cfg.dynamicSmemBytes = Cfg::SMEM;
+    cfg.stream = s;
+    cfg.attrs = la;
+    cfg.numAttrs = 1;
+    if (!max_clusters[dev]) {
+        if (cudaFuncSetAttribute(attention_quad_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM) != cudaSuccess)
+            return -3;
+        cfg.gridDim = dim3(4 * num_sms(), 1, 1);
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, attention_quad_kernel, &cfg) != cudaSuccess || n <= 0) return -3;
+        max_clusters[dev] = n;
+    }
+    const long units = (long)prm.n_tiles * prm.nkv;
+    const int clusters = units < max_clusters[dev] ? (int)units : max_clusters[dev];
+    cfg.gridDim = dim3((unsigned)(4 * clusters), 1, 1);
+    cfg.numAttrs = pdl_enabled() ? 2 : 1;
+    return cudaLaunchKernelEx(&cfg, attention_quad_kernel, mq, mk, mv, prm) == cudaSuccess ? 0 : -3;
+}
+
+// Head 512 runs on clusters of four for passes of at least ATT512_QUAD_ROWS rows and on the CTA-pair
+// kernel (two clusters per query-tile pair, one per 256-channel half of O, each computing all of S)
+// below: one 2,208-token document is 35 units, two waves of the 33 resident clusters of four but
+// one of the 74 CTA-pair cluster pairs; from ~130 units on the four-CTA kernel's 1.25x shorter key
+// tiles win. The regime depends only on the pass's rows, so a sequence gets the same bits in any pass
+// of its regime. EG2_ATT512_PAIR=1 keeps every pass on the CTA pairs.
+constexpr long ATT512_QUAD_ROWS = 8192;
+static bool att512_pair() {
+    static const bool v = [] {
+        const char* e = getenv("EG2_ATT512_PAIR");
+        return e && *e && *e != '0';
+    }();
+    return v;
+}
+
 int attention_tc(const bf16_t* q, const bf16_t* k, const bf16_t* v, bf16_t* out, long rows, const AttnTile* tiles,
                  int n_tiles, int nh, int nkv, int hd, int window, cudaStream_t s, const int* seq_start,
                  const int* seq_len) {
@@ -972,6 +1514,15 @@ int attention_tc(const bf16_t* q, const bf16_t* k, const bf16_t* v, bf16_t* out,
     prm.tq = tq;
     prm.nsplit = hd / ATT_DV;
     prm.n_tiles = n_tiles;
+    prm.q = q;
+    prm.rows = rows;
+    if (hd == 512 && rows >= ATT512_QUAD_ROWS && !att512_pair()) {
+        // K in boxes of 128 keys (a CTA's half of a 256-key S tile).
+        CUtensorMap mk2;
+        if (make_tmap_3d(&mk2, dt, k, hd, nkv, rows, (uint64_t)hd * 2, (uint64_t)nkv * hd * 2, 64, 1, AP_BN)) return -1;
+        prm.nsplit = 1;
+        return launch_quad(mq, mk2, mv, prm, s);
+    }
     // CTA pairs: clusters of 2 walking the (pair tile, K/V head, 256-channel half of O) units.
     return hd == 256 ? launch_pair<256>(mq, mk, mv, mo, prm, s) : launch_pair<512>(mq, mk, mv, mo, prm, s);
 }

@@ -203,6 +203,16 @@ EG2_DEV void st_async_f32(uint32_t remote_addr, float v, uint32_t remote_bar) {
                  "r"(remote_bar)
                  : "memory");
 }
+// Bulk copy of `bytes` (a multiple of 16, both addresses 16-byte aligned) from this CTA's shared
+// memory at `src` to shared::cluster address `dst` of another CTA, completing the bytes on that
+// CTA's mbarrier `remote_bar`. Writer threads make their stores to `src` visible to the copy with
+// fence.proxy.async before it is issued; `src` may be rewritten once the destination barrier says
+// the bytes have landed.
+EG2_DEV void bulk_copy_to_peer(uint32_t dst, uint32_t src, uint32_t bytes, uint32_t remote_bar) {
+    asm volatile("cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+                 "r"(src), "r"(bytes), "r"(remote_bar)
+                 : "memory");
+}
 // ---------------------------------------------------------------------------------------------
 // TMA (tiled tensor loads into this CTA's own shared memory)
 // ---------------------------------------------------------------------------------------------
@@ -324,6 +334,12 @@ EG2_DEV void mma_bf16_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint
         "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
         "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+// Copy a 128-row x 32-byte matrix (described like an MMA operand: here a 16-element K step of a
+// 128-byte-swizzled K-major tile) from shared memory into TMEM lanes 0..127, 8 columns from taddr, in
+// both CTAs of the pair (each from its own shared memory). Ordered with the issuing thread's MMAs.
+EG2_DEV void tmem_cp_pair_128x256b(uint32_t taddr, uint64_t sdesc) {
+    asm volatile("tcgen05.cp.cta_group::2.128x256b [%0], %1;" ::"r"(taddr), "l"(sdesc));
 }
 EG2_DEV void mma_bf16_pair_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
     asm volatile(

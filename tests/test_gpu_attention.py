@@ -125,3 +125,77 @@ def test_flash_bf16_long_global_sequence():
     full = exact_attention(qi, k[inner], v[inner], [seq], nh, nkv, hd, None)
     rel = np.abs(o[inner][pick] - full[pick]) / np.maximum(1.0, np.abs(full[pick]))
     assert rel.max() <= 2.5e-2
+
+
+def exact_rows(q, k, v, start, seq, rows_, nh, nkv, hd, window):
+    """Exact (float64) attention outputs of the selected query rows of one sequence starting at row
+    `start`: every key of the sequence, or those within `window` of the query."""
+    G = nh // nkv
+    out = np.zeros((len(rows_), nh * hd))
+    for n, i in enumerate(rows_):
+        lo, hi = start, start + seq
+        if window is not None:
+            lo, hi = max(lo, i - window), min(hi, i + window + 1)
+        for h in range(nh):
+            g = h // G
+            qi = q[i, h * hd:(h + 1) * hd].astype(np.float64)
+            kk = k[lo:hi, g * hd:(g + 1) * hd].astype(np.float64)
+            s = kk @ qi
+            p = np.exp(s - s.max())
+            out[n, h * hd:(h + 1) * hd] = (p / p.sum()) @ v[lo:hi, g * hd:(g + 1) * hd].astype(np.float64)
+    return out
+
+
+@pytest.mark.parametrize("window", [None, 7])
+def test_flash_bf16_global_layers_in_the_four_cta_regime(window):
+    """Passes of at least 8,192 rows run head 512 on clusters of four (S once per key tile, P sent to
+    the CTAs that hold O): four long sequences against exact attention at their first, middle and last
+    rows (with a window the sliding masks of the same kernel)."""
+    rng = np.random.default_rng(23)
+    nh, nkv, hd = 4, 1, 512
+    lens = [2208, 2208, 2208, 1700]
+    rows = PAD_BEFORE + sum(lens) + PAD_AFTER
+    assert rows >= 8192
+    sigma = hd ** -0.25
+    q, k = sample(rng, rows, nh * hd, sigma, True), sample(rng, rows, nkv * hd, sigma, True)
+    v = sample(rng, rows, nkv * hd, 1.0, True)
+    o = run_attention(L.EG2_BF16, q, k, v, lens, nh, nkv, hd, window)
+    assert np.isfinite(o).all()
+    off = PAD_BEFORE
+    worst = 0.0
+    for seq in lens:
+        pick = [off + i for i in list(range(0, 12)) + list(range(seq // 2, seq // 2 + 12)) + list(range(seq - 12, seq))]
+        want = exact_rows(q, k, v, off, seq, pick, nh, nkv, hd, window)
+        rel = np.abs(o[pick] - want) / np.maximum(1.0, np.abs(want))
+        worst = max(worst, float(rel.max()))
+        assert rel.max() <= 2.5e-2, (seq, float(rel.max()))
+        off += seq
+    print(f"worst relative error {worst:.3e}")
+
+
+def test_four_cta_regime_result_independent_of_neighbours():
+    """In the four-CTA regime a sequence's rows depend only on that sequence: the same bits behind
+    two different sets of filler sequences."""
+    rng = np.random.default_rng(31)
+    nh, nkv, hd = 4, 1, 512
+    sigma = hd ** -0.25
+    seq = 300
+    outs = []
+    for fill in ([4000, 4400], [2208, 3000, 3100]):
+        lens = fill + [seq]
+        rows = PAD_BEFORE + sum(lens) + PAD_AFTER
+        assert rows >= 8192
+        q, k = sample(rng, rows, nh * hd, sigma, True), sample(rng, rows, nkv * hd, sigma, True)
+        v = sample(rng, rows, nkv * hd, 1.0, True)
+        outs.append((q, k, v, lens, rows))
+    # The sequence itself is the same in both calls.
+    base = np.random.default_rng(77)
+    sq, sk = sample(base, seq, nh * hd, sigma, True), sample(base, seq, nkv * hd, sigma, True)
+    sv = sample(base, seq, nkv * hd, 1.0, True)
+    got = []
+    for q, k, v, lens, rows in outs:
+        s0 = PAD_BEFORE + sum(lens[:-1])
+        q[s0:s0 + seq], k[s0:s0 + seq], v[s0:s0 + seq] = sq, sk, sv
+        o = run_attention(L.EG2_BF16, q, k, v, lens, nh, nkv, hd, None)
+        got.append(o[s0:s0 + seq])
+    np.testing.assert_array_equal(got[0], got[1])
