@@ -596,18 +596,23 @@ done:
 //               pair: its V channels)
 //   warp 1      TMEM allocation; in the even CTA of each pair lane 0 issues that pair's tcgen05 work
 //   warps 2..9  score pair: softmax, two threads per row (128 of the 256 columns each, maxima swapped
-//               through shared memory as in the head-256 kernel); the threads of column half h send
+//               through shared memory as in the head-256 kernel); the threads of column half h stage
 //               message 2 t + h of tile t. Value pair: rescale and O / l.
+//   warp 10     score pair: lane 0 sends each staged message (two 16 KB chunks of P and 1 KB of
+//               factors and sums) once its value buffer is free. Bulk copies queue behind the K tiles'
+//               TMA loads on the SM's copy engine; issued by the softmax threads they held the softmax up
+//               ~2,300 cycles on every other tile.
 // Barriers (the same offsets in all four CTAs; each pair uses its own): the Q / K / V ring (full in
 // the pair's even CTA, empty committed to both), s_full / s_empty (S computed / read by both CTAs'
 // softmax); in the score CTAs p_empty per value buffer (committed by the value pair's MMAs: the
 // buffer's message has been consumed) and staged per column half (the half's last message has landed,
-// so its staging may be rewritten: one arrival from the value CTA); in the value CTAs p_full per
+// so its staging may be rewritten: one arrival from the value CTA) and stg_ready per column half (its
+// four softmax warps have staged the half's message); in the value CTAs p_full per
 // buffer (the bytes of a message), c_done per buffer (both value CTAs' correction threads have
 // applied its factors), pv_done per buffer, o_empty (O read out).
 // ---------------------------------------------------------------------------------------------
 struct AqCfg {
-    static constexpr int THREADS = 320;
+    static constexpr int THREADS = 352;
     static constexpr int P_BYTES = 128 * AP_BN * 2;       // one message's P: 128 keys x this CTA's 128 rows
     static constexpr int X_BYTES = 128 * 8;               // per row: (factor, partial row sum)
     static constexpr int MSG = P_BYTES + X_BYTES;
@@ -626,9 +631,9 @@ struct AqCfg {
     static constexpr int OFF_VR = ((OFF_VX + NBUF * X_BYTES + 1023) / 1024) * 1024;
     static constexpr int V_END = OFF_VR + VRING * AP_UNIT;
     static constexpr int OFF_BAR = S_END > V_END ? S_END : V_END;
-    // r_full[4] r_empty[4] s_full s_empty p_empty[3] staged[2] xpair[8] p_full[3] c_done[3] pv_done[3]
-    // o_empty drain
-    static constexpr int N_BARS = 2 * RING + 1 + 1 + NBUF + 2 + 8 + 3 * NBUF + 1 + 1;
+    // r_full[4] r_empty[4] s_full s_empty p_empty[3] staged[2] stg_ready[2] xpair[8] p_full[3] c_done[3]
+    // pv_done[3] o_empty drain
+    static constexpr int N_BARS = 2 * RING + 1 + 1 + NBUF + 2 + 2 + 8 + 3 * NBUF + 1 + 1;
     static constexpr int SMEM = 1024 + OFF_BAR + N_BARS * 8 + 16;
 };
 static_assert(AqCfg::OFF_R % 1024 == 0 && AqCfg::OFF_VR % 1024 == 0 && AqCfg::SMEM <= 227 * 1024,
@@ -649,7 +654,8 @@ __global__ void __launch_bounds__(AqCfg::THREADS, 1)
     uint64_t* s_empty = s_full + 1;
     uint64_t* p_empty = s_empty + 1;
     uint64_t* staged = p_empty + Cfg::NBUF;
-    uint64_t* xpair = staged + 2;
+    uint64_t* stg_ready = staged + 2;
+    uint64_t* xpair = stg_ready + 2;
     uint64_t* p_full = xpair + 8;
     uint64_t* c_done = p_full + Cfg::NBUF;
     uint64_t* pv_done = c_done + Cfg::NBUF;
@@ -698,8 +704,10 @@ __global__ void __launch_bounds__(AqCfg::THREADS, 1)
             mbar_init(&c_done[b], ARRIVALS);
             mbar_init(&pv_done[b], 1);
         }
-        mbar_init(&staged[0], 1);
-        mbar_init(&staged[1], 1);
+        for (int h = 0; h < 2; h++) {
+            mbar_init(&staged[h], 1);
+            mbar_init(&stg_ready[h], 4);
+        }
         for (int x = 0; x < 8; x++) mbar_init(&xpair[x], 64);
         mbar_init(o_empty, ARRIVALS);
         mbar_init(drain, 1);
@@ -854,6 +862,29 @@ __global__ void __launch_bounds__(AqCfg::THREADS, 1)
                 }
             }
         }
+    } else if (warp == 10) {
+        if (scorer && lane == 0) {
+            int Ts = 0;
+            for (int cid = u_first; cid < n_units; cid += u_step) {
+                const Unit x = unit_at(cid);
+                for (int t = 0; t < x.n_st; t++, Ts++)
+                    for (int h = 0; h < 2; h++) {
+                        // Message m = 2 Ts + h from staging h into value buffer m % 3 of CTA rank + 2, once the
+                        // half has staged it and P V of message m - 3 has completed.
+                        const int m = 2 * Ts + h, vb = m % Cfg::NBUF;
+                        if (!mbar_wait(&stg_ready[h], Ts & 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) goto done;
+                        if (m >= Cfg::NBUF && !mbar_wait(&p_empty[vb], (m / Cfg::NBUF - 1) & 1, EG2_DEV_TIMEOUT_ATTN, abort_flag))
+                            goto done;
+                        const uint32_t peer = rank + 2;
+                        const uint32_t pbar = mapa_shared(smem_u32(&p_full[vb]), peer);
+                        for (int c = 0; c < 2; c++)
+                            bulk_copy_to_peer(mapa_shared(smem_u32(smem + Cfg::OFF_VP + vb * Cfg::P_BYTES + c * 16384), peer),
+                                              smem_u32(smem + Cfg::OFF_SP + h * Cfg::P_BYTES + c * 16384), 16384, pbar);
+                        bulk_copy_to_peer(mapa_shared(smem_u32(smem + Cfg::OFF_VX + vb * Cfg::X_BYTES), peer),
+                                          smem_u32(smem + Cfg::OFF_SX + h * Cfg::X_BYTES), Cfg::X_BYTES, pbar);
+                    }
+            }
+        }
     } else {
         const int e = warp & 3;
         const int ch = (warp - 2) >> 2;  // score pair: S columns [128 ch, +128) (message half ch); value pair: O columns [256 ch, +256)
@@ -945,14 +976,8 @@ __global__ void __launch_bounds__(AqCfg::THREADS, 1)
                         lsum[q & 3] += __uint_as_float(pk[q] << 16) + __uint_as_float(pk[q] & 0xffff0000u);
                     }
                     l += (lsum[0] + lsum[1]) + (lsum[2] + lsum[3]);
-                    // Message m = 2 Ts + ch: staging ch is free once the half's previous message has landed,
-                    // value buffer m % 3 once P V of message m - 3 has completed.
-                    const int m = 2 * Ts + ch, vb = m % Cfg::NBUF;
+                    // Staging ch (message 2 Ts + ch) is free once the half's previous message has landed.
                     if (Ts >= 1 && !mbar_wait(&staged[ch], (Ts - 1) & 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) {
-                        ok = false;
-                        break;
-                    }
-                    if (m >= Cfg::NBUF && !mbar_wait(&p_empty[vb], (m / Cfg::NBUF - 1) & 1, EG2_DEV_TIMEOUT_ATTN, abort_flag)) {
                         ok = false;
                         break;
                     }
@@ -968,17 +993,9 @@ __global__ void __launch_bounds__(AqCfg::THREADS, 1)
                     *reinterpret_cast<float2*>(smem + Cfg::OFF_SX + ch * Cfg::X_BYTES + r * 8) = make_float2(ch == 0 ? factor : 1.f, l);
                     fence_proxy_async();
                     __syncwarp();
-                    if (lane == 0) {
-                        // The warp's 32 rows: 2 x 4 KB of P and 256 bytes of (factor, l), into value buffer vb of CTA rank + 2.
-                        const uint32_t peer = rank + 2;
-                        const uint32_t pbar = mapa_shared(smem_u32(&p_full[vb]), peer);
-                        for (int c = 0; c < 2; c++)
-                            bulk_copy_to_peer(mapa_shared(smem_u32(smem + Cfg::OFF_VP + vb * Cfg::P_BYTES + c * 16384 + 32 * e * 128), peer),
-                                              smem_u32(smem + Cfg::OFF_SP + ch * Cfg::P_BYTES + c * 16384 + 32 * e * 128), 4096, pbar);
-                        bulk_copy_to_peer(mapa_shared(smem_u32(smem + Cfg::OFF_VX + vb * Cfg::X_BYTES + 32 * e * 8), peer),
-                                          smem_u32(smem + Cfg::OFF_SX + ch * Cfg::X_BYTES + 32 * e * 8), 256, pbar);
-                    }
+                    if (lane == 0) mbar_arrive(&stg_ready[ch]);  // the copy warp sends it
                 }
+                if (!ok || *abort_flag) break;
             } else {
                 float lh0 = 0.f, lh1 = 0.f;  // latest partial row sums of the two column halves
                 for (int j = 0; j < 2 * x.n_st; j++, T++) {
