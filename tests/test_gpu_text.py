@@ -229,3 +229,17 @@ def test_ple_slices_fused_into_the_gate_match_the_ple_tensor_path(request, monke
         cos = (fused[d] * tensor[d]).sum(1) / (np.linalg.norm(fused[d], axis=1) * np.linalg.norm(tensor[d], axis=1))
         print(f"fused PLE vs PLE tensor @{d}: max|d| {diff:.2e} min cos {cos.min():.9f}")
         assert diff <= 1e-3 and cos.min() >= 0.99999
+
+
+def test_short_sequences_sharing_tiles_in_the_four_cta_regime(dev_bf16, oracle_text):
+    """300 sequences of 17-63 tokens in one bf16 pass of more than 8,192 rows: the global layers' attention
+    runs on clusters of four with several sequences per query tile (each row masking the keys of the
+    other sequences), the sliding layers' on CTA pairs. A spread of the sequences against the oracle."""
+    rng = np.random.default_rng(8192)
+    lens = [int(x) for x in rng.integers(17, 64, size=300)]
+    assert sum(lens) >= 8192
+    seqs = ids_for(lens, 91)
+    got = B.TextBackend(dev_bf16).embed_ids(seqs)
+    pick = list(range(0, 300, 13))
+    want = oracle_text.embed_ids([seqs[i] for i in pick])
+    check_embeddings({d: got[d][pick] for d in (768, 512, 256, 128)}, want, V.BF16, "bf16/shared-tiles-8192+")
