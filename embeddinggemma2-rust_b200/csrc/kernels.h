@@ -145,6 +145,8 @@ int ple_gate(const TI* g, TO* out, const float* ple, long rows, int p, int n_lay
 int pool_scratch_doubles(int n_seq, int max_len, int dim);
 int pool_rows(const float* x, const int* seq_start, const int* seq_len, int n_seq, int max_len, int dim,
               const int* dims_dev, int n_dims, int out_stride, float* out, double* scratch, cudaStream_t s);
+// pos / seq_start / seq_len of every row of a pass from its n_seq + 1 sequence offsets (device memory).
+int row_meta(const int* off, int n_seq, long rows, int* pos, int* st, int* ln, cudaStream_t s);
 int embed_gather(const bf16_t* table, long vocab, int h, const uint32_t* ids, long n, float scale, float* out,
                  int* bad, cudaStream_t s);
 template <typename TO>

@@ -501,6 +501,31 @@ int embed_gather(const bf16_t* table, long vocab, int h, const uint32_t* ids, lo
     return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
 
+// Per-row metadata of a pass from its sequence offsets (off[s] = first row of sequence s, off[n_seq] =
+// rows): the row's position in its sequence, the sequence's first row and its length -- what the
+// host used to expand row by row and upload (12 bytes per row).
+__global__ void row_meta_kernel(const int* __restrict__ off, int n_seq, long rows, int* __restrict__ pos,
+                                int* __restrict__ st, int* __restrict__ ln) {
+    const long r = (long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= rows) return;
+    int lo = 0, hi = n_seq - 1;  // the last s with off[s] <= r
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (off[mid] <= r) lo = mid;
+        else hi = mid - 1;
+    }
+    const int s0 = off[lo];
+    pos[r] = (int)(r - s0);
+    st[r] = s0;
+    ln[r] = off[lo + 1] - s0;
+}
+
+int row_meta(const int* off, int n_seq, long rows, int* pos, int* st, int* ln, cudaStream_t s) {
+    if (rows <= 0 || n_seq <= 0) return 0;
+    row_meta_kernel<<<(unsigned)((rows + 255) / 256), 256, 0, s>>>(off, n_seq, rows, pos, st, ln);
+    return cudaGetLastError() == cudaSuccess ? 0 : -3;
+}
+
 template <typename TO>
 __global__ void cast_kernel(const float* __restrict__ x, TO* __restrict__ out, long n, float mul, float add) {
     const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;

@@ -379,6 +379,7 @@ struct Work {
          *gate = nullptr, *pg = nullptr, *gu = nullptr;
     void* xb = nullptr;  // bf16 mode: the pass's input embeddings in bf16 (the PLE projection's input)
     int *pos = nullptr, *seq_start = nullptr, *seq_len = nullptr;
+    int* seq_off = nullptr;  // the pass's n_seq + 1 sequence offsets (row_meta expands them per row)
     uint32_t* ids = nullptr;
     long tiles_cap = 0;
     AttnTile* tiles = nullptr;
@@ -729,7 +730,7 @@ static void ensure_work(eg2_ctx* c, long rows, long n_tiles) {
         void** bufs[] = {(void**)&w.hidden, (void**)&w.out, (void**)&w.t, (void**)&w.qkv, (void**)&w.q,
                          (void**)&w.k, (void**)&w.v, (void**)&w.a, (void**)&w.o, (void**)&w.gate, (void**)&w.pg,
                          (void**)&w.gu, (void**)&w.pos, (void**)&w.seq_start, (void**)&w.seq_len, (void**)&w.ids,
-                         (void**)&w.xb};
+                         (void**)&w.xb, (void**)&w.seq_off};
         for (void** b : bufs) {
             dfree(c, *b);
             *b = nullptr;
@@ -762,6 +763,7 @@ static void ensure_work(eg2_ctx* c, long rows, long n_tiles) {
         w.pos = (int*)dalloc(c, cap * 4);
         w.seq_start = (int*)dalloc(c, cap * 4);
         w.seq_len = (int*)dalloc(c, cap * 4);
+        w.seq_off = (int*)dalloc(c, (cap + 1) * 4);
         w.ids = (uint32_t*)dalloc(c, cap * 4);
         w.cap = cap;
     }
@@ -1117,15 +1119,12 @@ static void enqueue_text(eg2_ctx* c, long rows, const std::vector<TileSet>& tset
 // captured graph's grid sizes stay valid for any sequence split of the same row count.
 static std::vector<TileSet> prepare_pass(eg2_ctx* c, const int32_t* lens, int n_seq, long rows, int tile_slots = 0) {
     const TextCfg& tc = c->tc;
-    std::vector<int> pos(rows), st(rows), ln(rows);
-    long r = 0;
+    // Sequence offsets only: the per-row position and sequence bounds are expanded on the device.
+    std::vector<int> off(n_seq + 1);
     long max_len = 0;
+    off[0] = 0;
     for (int s = 0; s < n_seq; s++) {
-        for (int i = 0; i < lens[s]; i++, r++) {
-            pos[r] = i;
-            st[r] = (int)(r - i);
-            ln[r] = lens[s];
-        }
+        off[s + 1] = off[s] + lens[s];
         max_len = std::max<long>(max_len, lens[s]);
     }
     std::vector<std::pair<int, int>> kinds;  // (nkv, head_dim) of the layers
@@ -1175,9 +1174,8 @@ static std::vector<TileSet> prepare_pass(eg2_ctx* c, const int32_t* lens, int n_
     ensure_work(c, rows, (long)tiles.size());
     ensure_rope(c, max_len);
     Work& w = c->w;
-    CK(cudaMemcpyAsync(w.pos, pos.data(), rows * 4, cudaMemcpyHostToDevice, c->stream));
-    CK(cudaMemcpyAsync(w.seq_start, st.data(), rows * 4, cudaMemcpyHostToDevice, c->stream));
-    CK(cudaMemcpyAsync(w.seq_len, ln.data(), rows * 4, cudaMemcpyHostToDevice, c->stream));
+    CK(cudaMemcpyAsync(w.seq_off, off.data(), (size_t)(n_seq + 1) * 4, cudaMemcpyHostToDevice, c->stream));
+    KL(row_meta(w.seq_off, n_seq, rows, w.pos, w.seq_start, w.seq_len, c->stream), "row_meta");
     if (!tiles.empty())
         CK(cudaMemcpyAsync(w.tiles, tiles.data(), tiles.size() * sizeof(AttnTile), cudaMemcpyHostToDevice, c->stream));
     // The host vectors die at return: make the copies complete first.
