@@ -147,6 +147,9 @@ int pool_rows(const float* x, const int* seq_start, const int* seq_len, int n_se
               const int* dims_dev, int n_dims, int out_stride, float* out, double* scratch, cudaStream_t s);
 // pos / seq_start / seq_len of every row of a pass from its n_seq + 1 sequence offsets (device memory).
 int row_meta(const int* off, int n_seq, long rows, int* pos, int* st, int* ln, cudaStream_t s);
+// embed_gather, the bf16 copy of its result and the first pre-norm in one kernel (h = 512).
+int embed_gather_norm(const bf16_t* table, long vocab, int h, const uint32_t* ids, long n, float scale, float* hidden,
+                      bf16_t* xb, bf16_t* t, const float* w, float eps, int* bad, cudaStream_t s);
 int embed_gather(const bf16_t* table, long vocab, int h, const uint32_t* ids, long n, float scale, float* out,
                  int* bad, cudaStream_t s);
 template <typename TO>

@@ -501,6 +501,54 @@ int embed_gather(const bf16_t* table, long vocab, int h, const uint32_t* ids, lo
     return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
 
+// The text pass's first three steps in one row kernel (bf16 contexts, 512-wide rows): the embedding
+// gather times scale (f32 hidden), its bf16 copy (the PLE projection's input) and the first layer's
+// pre-norm (bf16 t) -- the arithmetic of embed_gather_kernel, cast_kernel and rms_norm_kernel in turn,
+// with one read of the table row instead of two more of hidden.
+template <int VPL>
+__global__ void embed_gather_norm_kernel(const bf16_t* __restrict__ table, long vocab, const uint32_t* __restrict__ ids,
+                                         long n, float scale, float* __restrict__ hidden, bf16_t* __restrict__ xb,
+                                         bf16_t* __restrict__ t, const float* __restrict__ w, float eps, int* bad) {
+    grid_dep_launch();  // as in rms_norm_kernel
+    const long row = (long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (row >= n) return;
+    constexpr int dim = 32 * VPL;
+    const int lane = threadIdx.x & 31;
+    const uint32_t id = ids[row];
+    float v[VPL];
+    if ((long)id >= vocab) {
+        if (lane == 0) atomicExch(bad, 1);
+#pragma unroll
+        for (int i = 0; i < VPL; i++) v[i] = 0.f;
+    } else {
+        ld_row<VPL>(table + (long)id * dim + lane * VPL, v);
+#pragma unroll
+        for (int i = 0; i < VPL; i++) v[i] *= scale;
+    }
+    const long base = row * dim + lane * VPL;
+    st_row<VPL>(hidden + base, v);
+    st_row<VPL>(xb + base, v);
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < VPL; i++) ss = fmaf(v[i], v[i], ss);
+    ss = warp_sum(ss);
+    const float inv = 1.0f / sqrtf(ss / (float)dim + eps);
+    float wv[VPL];
+    ld_row<VPL>(w + lane * VPL, wv);
+#pragma unroll
+    for (int i = 0; i < VPL; i++) v[i] = v[i] * inv * wv[i];
+    st_row<VPL>(t + base, v);
+}
+int embed_gather_norm(const bf16_t* table, long vocab, int h, const uint32_t* ids, long n, float scale, float* hidden,
+                      bf16_t* xb, bf16_t* t, const float* w, float eps, int* bad, cudaStream_t s) {
+    if (n <= 0) return 0;
+    if (h != 512) return -1;
+    const int wpb = 8;
+    embed_gather_norm_kernel<16><<<(unsigned)((n + wpb - 1) / wpb), 32 * wpb, 0, s>>>(table, vocab, ids, n, scale, hidden, xb,
+                                                                                    t, w, eps, bad);
+    return cudaGetLastError() == cudaSuccess ? 0 : -3;
+}
+
 // Per-row metadata of a pass from its sequence offsets (off[s] = first row of sequence s, off[n_seq] =
 // rows): the row's position in its sequence, the sequence's first row and its length -- what the
 // host used to expand row by row and upload (12 bytes per row).

@@ -410,6 +410,7 @@ struct eg2_ctx {
     void *ple_proj = nullptr, *emb_proj = nullptr;
     float *ple_norm = nullptr, *final_norm = nullptr;
     uint16_t* embed_table = nullptr;  // bf16 [vocab, hidden] on the device
+    bool pre_normed = false;          // this pass's gather also wrote the bf16 input copy and the first pre-norm
     std::vector<eg2::RopeTab> ropes;
     // vision weights
     std::vector<eg2::VLayerW> vlayers;
@@ -990,8 +991,10 @@ static void enqueue_text(eg2_ctx* c, long rows, const std::vector<TileSet>& tset
     const bool ple_fused = !f32 && ple_fused_pass(c, rows);
     if (!ple_fused && w.ple_cap < rows) fail(EG2_ERR_INVALID, "PLE tensor smaller than the pass (switch changed between set-up and launch)");
     const void* x_in = w.hidden;
+    const bool pre_done = c->pre_normed;  // (embed_gather_norm: w.xb and t are written already)
+    c->pre_normed = false;
     if (!f32) {
-        KL(cast_rows<bf16_t>(w.hidden, (bf16_t*)w.xb, rows * h, 1.f, 0.f, c->stream), "cast");
+        if (!pre_done) KL(cast_rows<bf16_t>(w.hidden, (bf16_t*)w.xb, rows * h, 1.f, 0.f, c->stream), "cast");
         x_in = w.xb;
     }
     if (ple_fused) {
@@ -1012,7 +1015,7 @@ static void enqueue_text(eg2_ctx* c, long rows, const std::vector<TileSet>& tset
         mark(c, "gemm ple_model");
         KL(rms_norm_inplace(w.ple, c->ple_norm, rows * nl, p, eps, 1.f, c->stream), "rms_norm ple");
     }
-    KL(rms_norm_rows<T>(w.hidden, t, c->layers[0].input_ln, rows, h, eps, 1.f, c->stream), "rms_norm");
+    if (!pre_done) KL(rms_norm_rows<T>(w.hidden, t, c->layers[0].input_ln, rows, h, eps, 1.f, c->stream), "rms_norm");
     mark(c, (!f32 && bf16_mode(c) && p == 512) ? "norm (first)" : "norms (ple, first)");
     for (int i = 0; i < nl; i++) {
         const LayerW& L = c->layers[i];
@@ -1119,6 +1122,7 @@ static void enqueue_text(eg2_ctx* c, long rows, const std::vector<TileSet>& tset
 // captured graph's grid sizes stay valid for any sequence split of the same row count.
 static std::vector<TileSet> prepare_pass(eg2_ctx* c, const int32_t* lens, int n_seq, long rows, int tile_slots = 0) {
     const TextCfg& tc = c->tc;
+    c->pre_normed = false;
     // Sequence offsets only: the per-row position and sequence bounds are expanded on the device.
     std::vector<int> off(n_seq + 1);
     long max_len = 0;
@@ -1641,6 +1645,22 @@ int eg2_forward_packed_device(eg2_ctx* c, const float* embeds, const int32_t* le
 // (bucket, dims) into a CUDA graph and replayed with new metadata: ~175 launches become one (the
 // reference captures graphs per row bucket for the same reason, src/gpu/text.rs:475-516). The pooled
 // results are left in c->w.pooled.
+// The gather of a text pass's embeddings; bf16 contexts with 512-wide rows also write the bf16 input
+// copy and the first pre-norm in the same kernel (enqueue_text then skips them).
+static void gather_pass(eg2_ctx* c, long rows) {
+    Work& w = c->w;
+    const int h = c->tc.hidden;
+    if (bf16_mode(c) && h == 512) {
+        KL(embed_gather_norm(c->embed_table, c->tc.vocab, h, w.ids, rows, sqrtf((float)h), w.hidden, (bf16_t*)w.xb,
+                             (bf16_t*)w.t, c->layers[0].input_ln, c->tc.eps, c->bad_flag, c->stream),
+           "embed_gather_norm");
+        c->pre_normed = true;
+    } else {
+        KL(embed_gather(c->embed_table, c->tc.vocab, h, w.ids, rows, sqrtf((float)h), w.hidden, c->bad_flag, c->stream),
+           "embed_gather");
+    }
+}
+
 static void embed_graph(eg2_ctx* c, const uint32_t* ids, const int32_t* lens, int n_seq, long rows, const int32_t* dims,
                         int n_dims, int total, bool ids_on_device) {
     const int B = rows <= 16 ? 16 : rows <= 32 ? 32 : rows <= 64 ? 64 : 128;
@@ -1683,9 +1703,7 @@ static void embed_graph(eg2_ctx* c, const uint32_t* ids, const int32_t* lens, in
     CK(cudaMemsetAsync(w.ids, 0, (size_t)B * 4, c->stream));
     CK(cudaMemcpyAsync(w.ids, ids, rows * 4, ids_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, c->stream));
     auto body = [&]() {
-        KL(embed_gather(c->embed_table, c->tc.vocab, c->tc.hidden, w.ids, B, sqrtf((float)c->tc.hidden), w.hidden,
-                        c->bad_flag, c->stream),
-           "embed_gather");
+        gather_pass(c, B);
         run_text(c, B, sets);
         KL(pool_rows(w.out, seq_meta, seq_meta + S, S, B, c->tc.emb, w.dims, n_dims, total, w.pooled, w.pool_scratch,
                      c->stream),
@@ -1772,9 +1790,7 @@ static void embed_pass(eg2_ctx* c, const uint32_t* ids, bool ids_on_device, cons
     CK(cudaMemcpyAsync(seq_meta + n_seq, ln.data(), n_seq * 4, cudaMemcpyHostToDevice, c->stream));
     CK(cudaMemcpyAsync(w.dims, dims, n_dims * 4, cudaMemcpyHostToDevice, c->stream));
     CK(cudaMemcpyAsync(w.ids, ids, rows * 4, ids_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, c->stream));
-    KL(embed_gather(c->embed_table, c->tc.vocab, c->tc.hidden, w.ids, rows, sqrtf((float)c->tc.hidden), w.hidden,
-                    c->bad_flag, c->stream),
-       "embed_gather");
+    gather_pass(c, rows);
     run_text(c, rows, sets);
     int max_len = 0;
     for (int s2 = 0; s2 < n_seq; s2++) max_len = std::max(max_len, (int)lens[s2]);
